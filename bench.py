@@ -1,0 +1,428 @@
+"""Benchmark of the KV-streams paged decode hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Workload (one GPU; weak scaling: every rank runs its own copy, seeded by rank):
+paged decode + append, bf16, 32 query / 8 KV heads, head_dim 128, block_size 16,
+64 concurrent streams with live context ~U[1024, 16384] drawn from a pool of
+131072 blocks (random permutation), 1-6 evicted whole-block spans per stream
+(logical positions with gaps), RoPE theta 5e5, Q/K/V ~ N(0, 1).
+One step = batched slot allocation + one layer of fused RoPE / K-V append /
+split-K paged GQA attention for one new token per stream.  The per-step KV read
+(~2.3 GB) is far larger than L2, so no flush is needed between steps.
+
+Also reported (same line, `secondary`): the batched whole-block compaction kernel
+on 256 streams x 512-block tables (pool 200000).
+
+`--impl reference` times the oracle port of the reference's CPU path (gather +
+GQA softmax attention, paged_cache.py:176-182 and model.py:67-74) on the host
+cores for a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+for p in (str(REPO / "faster-rl-training_b200"), str(REPO)):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+METRIC = "rollout decode tok/s/GPU + replay tok/s; paged-attn HBM GB/s; replay TC util"
+S, HQ, HKV, D, BS, NB = 64, 32, 8, 128, 16, 131072
+THETA = 5e5
+CTX = (1024, 16384)
+
+
+def _peaks() -> dict:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "src": "of measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "of fallback"}
+
+
+def _traffic() -> dict:
+    p = REPO / "profiles" / "traffic.json"
+    return json.loads(p.read_text()) if p.exists() else {}
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                       "-i", str(self.idx), "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except FileNotFoundError:
+            self.p = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.p is not None:
+            self.p.terminate()
+            try:
+                self.p.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.p.kill()
+
+    def summary(self) -> dict:
+        self.f.flush()
+        rows = [r.split(",") for r in Path(self.f.name).read_text().strip().splitlines() if r.strip()]
+        os.unlink(self.f.name)
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = max(mx, float(r[2]))
+                for n, v in zip(names, r[5:9]):
+                    if v.strip().lower() == "active":
+                        reasons.add(n)
+            except (ValueError, IndexError):
+                continue
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------- workload
+def build_decode(dev, seed: int):
+    import torch
+
+    from kvstreams.paged_cache import PagedKVCache
+    from kvstreams.rope import RotaryEmbedding
+    from kvstreams.workloads import decode_state
+
+    st = decode_state(num_streams=S, ctx_range=CTX, block_size=BS, num_blocks=NB, seed=seed)
+    cache = PagedKVCache(1, HKV, D, block_size=BS, num_blocks=NB, dtype=torch.bfloat16, device=dev, max_seqs=S,
+                         max_blocks_per_seq=CTX[1] // BS + 64)
+    cache.load_state(range(S), st.tables, st.positions, st.free_list)
+    g = torch.Generator(device=dev).manual_seed(seed)
+    for t in (cache.k, cache.v):
+        t.view(-1)[:] = torch.randn(t.numel(), generator=g, device=dev, dtype=torch.float32).bfloat16()
+    q = torch.randn(S, HQ, D, generator=g, device=dev).bfloat16()
+    k = torch.randn(S, HKV, D, generator=g, device=dev).bfloat16()
+    v = torch.randn(S, HKV, D, generator=g, device=dev).bfloat16()
+    rope = RotaryEmbedding(D, THETA)
+    return st, cache, q, k, v, rope
+
+
+def decode_bytes(lengths: np.ndarray) -> int:
+    """Algorithmic HBM bytes of one decode launch: every live K and V row read once
+    (4096 B per context token), the new K/V read + written, Q read, O written, tables."""
+    kv_read = int(lengths.sum()) * HKV * D * 2 * 2
+    per_stream = HQ * D * 2 * 2 + HKV * D * 2 * 2 * 2
+    tables = int(sum(-(-int(n) // BS) for n in lengths)) * 4
+    return kv_read + S * per_stream + tables
+
+
+# ---------------------------------------------------------------------- cpu baseline
+def cpu_decode_sample(seed: int, n_streams: int = 4):
+    """Reference CPU path on a bounded sample: per stream, gather the live K/V in table
+    order and run GQA softmax attention in float32 (numpy, BLAS threads)."""
+    from kvstreams.workloads import decode_state
+
+    from oracle import kvs_oracle as O
+
+    st = decode_state(num_streams=S, ctx_range=CTX, block_size=BS, num_blocks=NB, seed=seed)
+    rng = np.random.default_rng(seed)
+    sample = list(range(n_streams))
+    pools = {}
+    for s in sample:
+        nb = len(st.tables[s])
+        pools[s] = (rng.standard_normal((nb, BS, HKV, D), dtype=np.float32),
+                    rng.standard_normal((nb, BS, HKV, D), dtype=np.float32))
+    q = rng.standard_normal((n_streams, HQ, D), dtype=np.float32)
+    knew = rng.standard_normal((n_streams, HKV, D), dtype=np.float32)
+    vnew = rng.standard_normal((n_streams, HKV, D), dtype=np.float32)
+
+    def step():
+        toks = 0
+        for i, s in enumerate(sample):
+            kp, vp = pools[s]
+            n = st.positions[s].size
+            pos = np.asarray([st.next_positions[s]])
+            qr = O.rope_apply(q[i:i + 1], pos, THETA, np.float32)
+            kr = O.rope_apply(knew[i:i + 1], pos, THETA, np.float32)
+            keys = np.concatenate([kp.reshape(-1, HKV, D)[:n], kr])
+            vals = np.concatenate([vp.reshape(-1, HKV, D)[:n], vnew[i:i + 1]])
+            O.gqa_attention(qr, keys, vals, np.ones((1, n + 1), bool), D ** -0.5, np.float32)
+            toks += 1
+        return toks
+
+    return step, sum(st.positions[s].size for s in sample)
+
+
+def time_cpu(step, min_seconds: float = 10.0, max_iters: int = 50):
+    step()  # warm
+    t0 = time.perf_counter()
+    toks, it = 0, 0
+    while (time.perf_counter() - t0 < min_seconds and it < max_iters) or it == 0:
+        toks += step()
+        it += 1
+    return toks / (time.perf_counter() - t0), it
+
+
+# ---------------------------------------------------------------------- main arms
+def run_reference(args, rank: int, world: int) -> None:
+    if rank != 0:
+        return
+    step, ctx_tokens = cpu_decode_sample(seed=0)
+    cores = os.cpu_count() or 1
+    rate_samples = []
+    for _ in range(args.warmup):
+        step()
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        n = step()
+        rate_samples.append(n / (time.perf_counter() - t0))
+    value = statistics.median(rate_samples)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "decode tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * 4 / value, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "paged decode+append, 32q/8kv heads, D128, bs16, 64 streams, ctx U[1024,16384]",
+                   "sample": "4 of the 64 streams per step"},
+        "cpu_baseline": {"value": value, "unit": "decode tok/s", "cores": cores, "kind": "port",
+                         "sample": f"4 streams ({ctx_tokens} context tokens) of the 64-stream workload per step"},
+        "e2e": {"value": value, "unit": "decode tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_b200(args, rank: int, world: int, local_rank: int) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from kvstreams import _native as N
+    from kvstreams import ops
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    lib = N.lib()
+    st, cache, q, k, v, rope = build_decode(dev, seed=1000 + rank)
+    inv = rope.table(dev, torch.bfloat16)
+    seqs = list(range(S))
+    pos = torch.as_tensor(st.next_positions, device=dev)
+    out = torch.empty_like(q)
+    snap = cache.snapshot_state()
+
+    def step(i: int, ev=None):
+        p = pos + i
+        mapping = cache.append_slots_batch(seqs, p)
+        if ev is not None:
+            ev[0].record()
+        ops.paged_forward(cache, seqs, None, 0, q, k, v, p, mapping, inv, D ** -0.5, out=out)
+        if ev is not None:
+            ev[1].record()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # ---- device-resident timing
+    for i in range(args.warmup):
+        step(i)
+    cache.restore_state(snap)
+    barrier()
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = lib.kvs_launch_count()
+    with ClockSampler(local_rank) as clk:
+        t_start.record()
+        for i in range(args.steps):
+            step(i, kev[i])
+        t_end.record()
+        barrier()
+    launches = lib.kvs_launch_count() - launches0
+    ms = t_start.elapsed_time(t_end)
+    kernel_ms = [a.elapsed_time(b) for a, b in kev]
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    clocks = clk.summary()
+    lengths_mid = st.lengths + args.steps // 2 + 1
+    alg_bytes = decode_bytes(lengths_mid)
+    attn_ms = statistics.mean(kernel_ms)
+    achieved_gbs = alg_bytes / (attn_ms * 1e-3) / 1e9
+
+    # ---- end-to-end through the public call with host buffers
+    cache.restore_state(snap)
+    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+    hpos = torch.as_tensor(st.next_positions).pin_memory()
+    hout = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    dq, dk, dv, dpos = (torch.empty_like(t, device=dev) for t in (hq, hk, hv, hpos))
+    for i in range(args.warmup):
+        dq.copy_(hq, non_blocking=True)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        dpos.copy_(hpos, non_blocking=True)
+        p = dpos + i
+        mapping = cache.append_slots_batch(seqs, p)
+        ops.paged_forward(cache, seqs, None, 0, dq, dk, dv, p, mapping, inv, D ** -0.5, out=out)
+        hout.copy_(out, non_blocking=True)
+    e1.record()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hpos))
+    d2h = hout.numel() * hout.element_size()
+
+    secondary = compaction_bench(dev, args, rank) if not args.skip_secondary else None
+
+    if rank != 0:
+        return
+    peaks = _peaks()
+    step_cpu, ctx_tokens = cpu_decode_sample(seed=0)
+    cpu_rate, cpu_iters = time_cpu(step_cpu, min_seconds=args.cpu_seconds)
+    traffic = _traffic().get("paged_decode")
+    line = {
+        "metric": METRIC,
+        "value": world * S * args.steps / (ms * 1e-3),
+        "unit": "decode tok/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": "paged decode+append (one layer), 32q/8kv heads, D128, bs16, 64 streams/GPU, "
+                               "ctx U[1024,16384], pool 131072 blocks, 1-6 evicted spans/stream, theta 5e5",
+                   "streams_per_gpu": S, "kv_bytes_per_step": int(alg_bytes),
+                   "l2": "per-step KV read ~2.3 GB > 126 MB L2 (no flush needed)",
+                   "per_gpu_decode_tok_s": S * args.steps / (ms * 1e-3)},
+        "e2e": {"value": world * S * args.steps / (e2e_ms * 1e-3), "unit": "decode tok/s",
+                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved_gbs / peaks["hbm_gbs"], "peak_src": peaks["src"],
+                     "frac_of_8tbs_spec": achieved_gbs / 8000.0,
+                     "traffic": traffic, "kernel": "kvs_paged_decode", "kernel_ms": attn_ms},
+        "cpu_baseline": {"value": cpu_rate, "unit": "decode tok/s", "cores": os.cpu_count() or 1, "kind": "port",
+                         "sample": f"4 of 64 streams ({ctx_tokens} context tokens), {cpu_iters} passes, "
+                                   "numpy float32 gather + GQA attention"},
+        "clocks": clocks,
+    }
+    if secondary:
+        line["secondary"] = secondary
+    print(json.dumps(line), flush=True)
+
+
+def compaction_bench(dev, args, rank: int) -> dict:
+    """256 streams x 512-block tables (pool 200000): one batched evict_positions over
+    all streams per step (keep-recent turn spans), state restored between steps."""
+    import torch
+
+    from kvstreams.paged_cache import PagedKVCache
+    from kvstreams.workloads import compaction_plan
+
+    out = {}
+    for bs, blocks in ((16, 512), (1, 512)):
+        rounds = compaction_plan(num_streams=256, blocks_per_stream=blocks, block_size=bs, seed=rank,
+                                 num_events_range=(1, 1))
+        nb = 200000
+        cache = PagedKVCache(1, 1, 2, block_size=bs, num_blocks=nb, dtype=torch.bfloat16, device=dev,
+                             max_seqs=256, max_blocks_per_seq=blocks + 64)
+        for s in range(256):
+            cache.add_sequence(s)
+        r0 = rounds[0]
+        seqs, poss = r0.append_seqs, r0.append_positions
+        start = 0
+        while start < len(seqs):
+            seen, end = set(), start
+            while end < len(seqs) and seqs[end] not in seen:
+                seen.add(seqs[end])
+                end += 1
+            cache.append_slots_batch(seqs[start:end], torch.as_tensor(np.concatenate(poss[start:end])),
+                                     [p.size for p in poss[start:end]])
+            start = end
+        ev = rounds[1]
+        snap = cache.snapshot_state()
+        times = []
+        for i in range(args.warmup + args.steps):
+            cache.restore_state(snap)
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            cache.evict_positions_async(ev.evict_seqs, ev.evict_spans, span_cap=64)
+            b.record()
+            torch.cuda.synchronize()
+            if i >= args.warmup:
+                times.append(a.elapsed_time(b))
+        ms = statistics.median(times)
+        out[f"compaction_bs{bs}"] = {"streams": len(ev.evict_seqs), "ms_per_call": ms,
+                                     "streams_per_s": len(ev.evict_seqs) / (ms * 1e-3),
+                                     "live_tokens": int(blocks * bs * 256)}
+    return out
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--skip-secondary", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return 0
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    if world > 1:
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_b200(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,355 @@
+// RoPE at explicit logical positions, and the exact-arithmetic (SIMT) attention
+// kernels used for fp32 / fp64 models and for shapes the tensor-core kernels do
+// not cover.
+//
+// Reference: kvstreams/rope.py:21-46 (RotaryEmbedding, apply_rope) and
+// kvstreams/model.py:50-75 (Attention.forward): GQA by repeat_interleave
+// (head h reads kv head h // (n_heads / n_kv_heads)), scores * head_dim**-0.5,
+// masked softmax over keys, probabilities times values.
+#include "kvs_common.cuh"
+#include "kvs_rope.cuh"
+
+#include <algorithm>
+#include <mutex>
+#include <vector>
+
+using namespace kvs;
+
+namespace {
+
+// ------------------------------------------------------------------ RoPE
+// in place (src == dst) or copying; one thread per rotated pair (i, i + D/2).
+template <typename T, typename F>
+__global__ void rope_kernel(const T* __restrict__ src, T* __restrict__ dst, const int64_t* __restrict__ pos,
+                            int n_tokens, int n_heads, int D, const F* __restrict__ inv_freq) {
+  const int half = D >> 1;
+  const int64_t total = (int64_t)n_tokens * n_heads * half;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int i = (int)(idx % half);
+    const int64_t th = idx / half;
+    const int t = (int)(th / n_heads);
+    const int64_t base = th * D;
+    using A = typename Acc<T>::type;
+    A a = to_acc(src[base + i]), b = to_acc(src[base + i + half]);
+    A r0, r1;
+    rope_rotate<A, F>(a, b, pos[t], inv_freq[i], r0, r1);
+    dst[base + i] = from_acc<T>(r0);
+    dst[base + i + half] = from_acc<T>(r1);
+  }
+}
+
+// RoPE of new keys written straight into the pool, values copied alongside
+// (apply_rope on k, model.py:63, then PagedKVCache.write, paged_cache.py:167-171).
+template <typename T, typename F>
+__global__ void rope_write_kv_kernel(kvs_cache c, int layer, const int32_t* __restrict__ blocks,
+                                     const int32_t* __restrict__ offsets, const T* __restrict__ k,
+                                     const T* __restrict__ v, const int64_t* __restrict__ pos, int n_tokens,
+                                     const F* __restrict__ inv_freq) {
+  const int D = c.head_dim, half = D >> 1, H = c.n_kv_heads;
+  const int64_t total = (int64_t)n_tokens * H * half;
+  T* K = static_cast<T*>(c.k);
+  T* V = static_cast<T*>(c.v);
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int i = (int)(idx % half);
+    const int64_t th = idx / half;
+    const int h = (int)(th % H);
+    const int t = (int)(th / H);
+    const int64_t row = ((int64_t)layer * c.num_blocks + blocks[t]) * c.block_size + offsets[t];
+    const int64_t dst = (row * H + h) * D;
+    const int64_t src = th * D;
+    using A = typename Acc<T>::type;
+    A a = to_acc(k[src + i]), b = to_acc(k[src + i + half]);
+    A r0, r1;
+    rope_rotate<A, F>(a, b, pos[t], inv_freq[i], r0, r1);
+    K[dst + i] = from_acc<T>(r0);
+    K[dst + i + half] = from_acc<T>(r1);
+    V[dst + i] = v[src + i];
+    V[dst + i + half] = v[src + i + half];
+  }
+}
+
+template <typename A>
+__device__ __forceinline__ A warp_allreduce_sum(A x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
+
+template <typename A> __device__ __forceinline__ A exp_acc(A x);
+template <> __device__ __forceinline__ float exp_acc<float>(float x) { return expf(x); }
+template <> __device__ __forceinline__ double exp_acc<double>(double x) { return exp(x); }
+
+// Online softmax state of one (query, head) held by a warp; lanes own head dims
+// lane, lane+32, ...  Keys are visited in increasing cache order.
+template <typename T, int DPL>
+struct OnlineRow {
+  using A = typename Acc<T>::type;
+  A q[DPL], acc[DPL];
+  A m, l;
+  __device__ __forceinline__ void init(const T* qrow, int D) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int k = 0; k < DPL; ++k) {
+      const int d = lane + 32 * k;
+      q[k] = d < D ? to_acc(qrow[d]) : A(0);
+      acc[k] = A(0);
+    }
+    m = -INFINITY;
+    l = A(0);
+  }
+  __device__ __forceinline__ void visit(const T* krow, const T* vrow, int D, A scale) {
+    const int lane = threadIdx.x & 31;
+    A part = A(0);
+#pragma unroll
+    for (int k = 0; k < DPL; ++k) {
+      const int d = lane + 32 * k;
+      if (d < D) part += q[k] * to_acc(krow[d]);
+    }
+    const A s = warp_allreduce_sum(part) * scale;
+    const A m_new = s > m ? s : m;
+    const A alpha = exp_acc<A>(m - m_new);
+    const A p = exp_acc<A>(s - m_new);
+    l = l * alpha + p;
+#pragma unroll
+    for (int k = 0; k < DPL; ++k) {
+      const int d = lane + 32 * k;
+      if (d < D) acc[k] = acc[k] * alpha + p * to_acc(vrow[d]);
+    }
+    m = m_new;
+  }
+  __device__ __forceinline__ void store(T* orow, int D) const {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int k = 0; k < DPL; ++k) {
+      const int d = lane + 32 * k;
+      if (d < D) orow[d] = from_acc<T>(acc[k] / l);
+    }
+  }
+};
+
+// ------------------------------------------------------------------ paged (generic)
+// One warp per (new token, query head).  Query i of a sequence with T new tokens
+// and n live entries (new ones included) sees cache entries [0, n - T + i].
+template <typename T, int DPL>
+__global__ void __launch_bounds__(128)
+paged_attn_generic_kernel(kvs_cache c, kvs_batch b, int layer, const T* __restrict__ q, T* __restrict__ out,
+                          int n_heads, double scale) {
+  const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (gw >= b.total_tokens * n_heads) return;
+  const int j = gw / n_heads, h = gw % n_heads;
+  int i = j;
+  if (b.cu_tokens) {
+    int lo = 0, hi = b.num_seqs - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (b.cu_tokens[mid] <= j) lo = mid; else hi = mid - 1;
+    }
+    i = lo;
+  }
+  const int slot = b.seq_slots[i];
+  const int t0 = b.cu_tokens ? b.cu_tokens[i] : i;
+  const int t1 = b.cu_tokens ? b.cu_tokens[i + 1] : i + 1;
+  const int n = c.lengths[slot];
+  const int visible = n - (t1 - t0) + (j - t0) + 1;
+  const int D = c.head_dim, Hkv = c.n_kv_heads, bs = c.block_size;
+  const int hk = h / (n_heads / Hkv);
+  const T* K = static_cast<const T*>(c.k);
+  const T* V = static_cast<const T*>(c.v);
+  const int32_t* table = c.tables + (int64_t)slot * c.max_blocks;
+  OnlineRow<T, DPL> row;
+  row.init(q + ((int64_t)j * n_heads + h) * D, D);
+  using A = typename Acc<T>::type;
+  const A sc = (A)scale;
+  for (int e = 0; e < visible; ++e) {
+    const int64_t r = ((int64_t)layer * c.num_blocks + table[e / bs]) * bs + e % bs;
+    const int64_t off = (r * Hkv + hk) * D;
+    row.visit(K + off, V + off, D, sc);
+  }
+  row.store(out + ((int64_t)j * n_heads + h) * D, D);
+}
+
+// ------------------------------------------------------------------ replay (generic)
+// One warp per (stream b, query t, head h); key s is visible iff s <= t and
+// t < evicted_at[b][s] (replay.py:62), padded rows t >= len see only s == t
+// (replay.py:221-222).
+template <typename T, int DPL>
+__global__ void __launch_bounds__(128)
+replay_generic_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
+                      const int64_t* __restrict__ ev, const int32_t* __restrict__ lengths, T* __restrict__ out,
+                      int B, int Tn, int Hq, int Hkv, int D, double scale) {
+  const int64_t gw = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (gw >= (int64_t)B * Tn * Hq) return;
+  const int h = (int)(gw % Hq);
+  const int t = (int)((gw / Hq) % Tn);
+  const int b = (int)(gw / ((int64_t)Hq * Tn));
+  const int hk = h / (Hq / Hkv);
+  const int len = lengths[b];
+  const int64_t qo = (((int64_t)b * Tn + t) * Hq + h) * D;
+  OnlineRow<T, DPL> row;
+  row.init(q + qo, D);
+  using A = typename Acc<T>::type;
+  const A sc = (A)scale;
+  const int64_t* e = ev + (int64_t)b * Tn;
+  if (t >= len) {
+    const int64_t ko = (((int64_t)b * Tn + t) * Hkv + hk) * D;
+    row.visit(k + ko, v + ko, D, sc);
+  } else {
+    for (int s = 0; s <= t; ++s) {
+      if (!(t < e[s])) continue;
+      const int64_t ko = (((int64_t)b * Tn + s) * Hkv + hk) * D;
+      row.visit(k + ko, v + ko, D, sc);
+    }
+  }
+  row.store(out + qo, D);
+}
+
+template <typename T>
+int launch_paged_generic(const kvs_cache& c, const kvs_batch& b, int layer, const void* q, void* out,
+                         int n_heads, double scale, cudaStream_t st) {
+  const int warps = b.total_tokens * n_heads;
+  const int grid = (warps + 3) / 4;
+  const T* qq = static_cast<const T*>(q);
+  T* oo = static_cast<T*>(out);
+  if (c.head_dim <= 32) paged_attn_generic_kernel<T, 1><<<grid, 128, 0, st>>>(c, b, layer, qq, oo, n_heads, scale);
+  else if (c.head_dim <= 64) paged_attn_generic_kernel<T, 2><<<grid, 128, 0, st>>>(c, b, layer, qq, oo, n_heads, scale);
+  else if (c.head_dim <= 128) paged_attn_generic_kernel<T, 4><<<grid, 128, 0, st>>>(c, b, layer, qq, oo, n_heads, scale);
+  else if (c.head_dim <= 256) paged_attn_generic_kernel<T, 8><<<grid, 128, 0, st>>>(c, b, layer, qq, oo, n_heads, scale);
+  else return KVS_E_UNSUPPORTED;
+  return launch_rc();
+}
+
+template <typename T>
+int launch_replay_generic(const kvs_replay_args& a, cudaStream_t st) {
+  const int64_t warps = (int64_t)a.batch * a.seq_len * a.n_heads;
+  const int64_t grid = (warps + 3) / 4;
+  if (grid > INT32_MAX) return KVS_E_UNSUPPORTED;
+  const T* q = static_cast<const T*>(a.q);
+  const T* k = static_cast<const T*>(a.k);
+  const T* v = static_cast<const T*>(a.v);
+  T* o = static_cast<T*>(a.out);
+#define KVS_REPLAY(DPL)                                                                             \
+  replay_generic_kernel<T, DPL><<<(unsigned)grid, 128, 0, st>>>(q, k, v, a.evicted_at, a.lengths, o, a.batch, \
+                                                                a.seq_len, a.n_heads, a.n_kv_heads,    \
+                                                                a.head_dim, a.scale)
+  if (a.head_dim <= 32) KVS_REPLAY(1);
+  else if (a.head_dim <= 64) KVS_REPLAY(2);
+  else if (a.head_dim <= 128) KVS_REPLAY(4);
+  else if (a.head_dim <= 256) KVS_REPLAY(8);
+  else return KVS_E_UNSUPPORTED;
+#undef KVS_REPLAY
+  return launch_rc();
+}
+
+template <typename T, typename F>
+int launch_rope(const void* src, void* dst, const int64_t* pos, int n_tokens, int n_heads, int D,
+                const void* inv_freq, cudaStream_t st) {
+  const int64_t total = (int64_t)n_tokens * n_heads * (D / 2);
+  if (total == 0) return KVS_OK;
+  const int grid = (int)std::min<int64_t>((total + 255) / 256, 148 * 32);
+  rope_kernel<T, F><<<grid, 256, 0, st>>>(static_cast<const T*>(src), static_cast<T*>(dst), pos, n_tokens,
+                                          n_heads, D, static_cast<const F*>(inv_freq));
+  return launch_rc();
+}
+
+template <typename T, typename F>
+int launch_rope_write(const kvs_cache& c, int layer, const int32_t* blocks, const int32_t* offsets,
+                      const void* k, const void* v, const int64_t* pos, int n_tokens, const void* inv_freq,
+                      cudaStream_t st) {
+  const int64_t total = (int64_t)n_tokens * c.n_kv_heads * (c.head_dim / 2);
+  if (total == 0) return KVS_OK;
+  const int grid = (int)std::min<int64_t>((total + 255) / 256, 148 * 32);
+  rope_write_kv_kernel<T, F><<<grid, 256, 0, st>>>(c, layer, blocks, offsets, static_cast<const T*>(k),
+                                                   static_cast<const T*>(v), pos, n_tokens,
+                                                   static_cast<const F*>(inv_freq));
+  return launch_rc();
+}
+
+int rope_dispatch(const void* src, void* dst, int dtype, const int64_t* pos, int n_tokens, int n_heads, int D,
+                  const void* inv_freq, cudaStream_t st) {
+  switch (dtype) {
+    case KVS_F32: return launch_rope<float, float>(src, dst, pos, n_tokens, n_heads, D, inv_freq, st);
+    case KVS_F64: return launch_rope<double, double>(src, dst, pos, n_tokens, n_heads, D, inv_freq, st);
+    case KVS_BF16: return launch_rope<__nv_bfloat16, float>(src, dst, pos, n_tokens, n_heads, D, inv_freq, st);
+    case KVS_F16: return launch_rope<__half, float>(src, dst, pos, n_tokens, n_heads, D, inv_freq, st);
+  }
+  return KVS_E_UNSUPPORTED;
+}
+
+}  // namespace
+
+// Exact generic decode: rope(q) into out, rope(k)+v into the pool, then attention
+// reading q from out (each warp reads its own row before overwriting it).
+int kvs_decode_generic(const kvs_cache* c, const kvs_batch* b, const kvs_decode_args* a, cudaStream_t st) {
+  const int n = b->total_tokens;
+  int rc = rope_dispatch(a->q, a->out, c->dtype, a->positions, n, a->n_heads, c->head_dim, a->inv_freq, st);
+  if (rc) return rc;
+  switch (c->dtype) {
+    case KVS_F32: rc = launch_rope_write<float, float>(*c, a->layer, a->slot_blocks, a->slot_offsets, a->k_new, a->v_new, a->positions, n, a->inv_freq, st); break;
+    case KVS_F64: rc = launch_rope_write<double, double>(*c, a->layer, a->slot_blocks, a->slot_offsets, a->k_new, a->v_new, a->positions, n, a->inv_freq, st); break;
+    case KVS_BF16: rc = launch_rope_write<__nv_bfloat16, float>(*c, a->layer, a->slot_blocks, a->slot_offsets, a->k_new, a->v_new, a->positions, n, a->inv_freq, st); break;
+    case KVS_F16: rc = launch_rope_write<__half, float>(*c, a->layer, a->slot_blocks, a->slot_offsets, a->k_new, a->v_new, a->positions, n, a->inv_freq, st); break;
+    default: return KVS_E_UNSUPPORTED;
+  }
+  if (rc) return rc;
+  return kvs_paged_attention(c, b, a->layer, a->out, a->out, a->n_heads, a->scale, reinterpret_cast<kvs_stream_t>(st));
+}
+
+int kvs_replay_generic(const kvs_replay_args* a, cudaStream_t st) {
+  switch (a->dtype) {
+    case KVS_F32: return launch_replay_generic<float>(*a, st);
+    case KVS_F64: return launch_replay_generic<double>(*a, st);
+    case KVS_BF16: return launch_replay_generic<__nv_bfloat16>(*a, st);
+    case KVS_F16: return launch_replay_generic<__half>(*a, st);
+  }
+  return KVS_E_UNSUPPORTED;
+}
+
+// ====================================================================== C ABI
+
+KVS_API size_t kvs_abi_struct_size(int which) {
+  switch (which) {
+    case 0: return sizeof(kvs_cache);
+    case 1: return sizeof(kvs_batch);
+    case 2: return sizeof(kvs_decode_args);
+    case 3: return sizeof(kvs_replay_args);
+  }
+  return 0;
+}
+
+KVS_API int kvs_abi_version(void) { return KVS_ABI_VERSION; }
+
+KVS_API int kvs_device_sm_count(void) {
+  static std::mutex mu;
+  static std::vector<int> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  std::lock_guard<std::mutex> lock(mu);
+  if ((int)cache.size() <= dev) cache.resize(dev + 1, 0);
+  if (!cache[dev]) cudaDeviceGetAttribute(&cache[dev], cudaDevAttrMultiProcessorCount, dev);
+  return cache[dev];
+}
+
+KVS_API int kvs_rope(void* x, int32_t dtype, const int64_t* positions, int32_t n_tokens, int32_t n_heads,
+                     int32_t head_dim, const void* inv_freq, kvs_stream_t stream) {
+  if (!x || !positions || !inv_freq || n_tokens < 0 || n_heads <= 0 || head_dim <= 0 || head_dim % 2)
+    return KVS_E_ARG;
+  return rope_dispatch(x, x, dtype, positions, n_tokens, n_heads, head_dim, inv_freq, to_cuda(stream));
+}
+
+KVS_API int kvs_paged_attention(const kvs_cache* c, const kvs_batch* b, int32_t layer, const void* q, void* out,
+                                int32_t n_heads, double scale, kvs_stream_t stream) {
+  if (!c || !b || !q || !out || layer < 0 || layer >= c->n_layers || n_heads <= 0 ||
+      n_heads % c->n_kv_heads)
+    return KVS_E_ARG;
+  if (b->total_tokens == 0) return KVS_OK;
+  const cudaStream_t st = to_cuda(stream);
+  switch (c->dtype) {
+    case KVS_F32: return launch_paged_generic<float>(*c, *b, layer, q, out, n_heads, scale, st);
+    case KVS_F64: return launch_paged_generic<double>(*c, *b, layer, q, out, n_heads, scale, st);
+    case KVS_BF16: return launch_paged_generic<__nv_bfloat16>(*c, *b, layer, q, out, n_heads, scale, st);
+    case KVS_F16: return launch_paged_generic<__half>(*c, *b, layer, q, out, n_heads, scale, st);
+  }
+  return KVS_E_UNSUPPORTED;
+}

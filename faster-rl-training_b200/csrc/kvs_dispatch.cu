@@ -1,0 +1,47 @@
+// Entry points that choose between the tensor-core kernels and the exact SIMT
+// kernels by dtype and shape (all kernels are this library's own sm_100a code).
+#include "kvs_common.cuh"
+
+int kvs_decode_generic(const kvs_cache* c, const kvs_batch* b, const kvs_decode_args* a, cudaStream_t st);
+int kvs_replay_generic(const kvs_replay_args* a, cudaStream_t st);
+
+using namespace kvs;
+
+#include <atomic>
+
+static std::atomic<long long> g_launches{0};
+void kvs::count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+KVS_API long long kvs_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+KVS_API size_t kvs_decode_scratch_bytes(const kvs_cache* c, int32_t num_seqs, int32_t n_heads,
+                                        int32_t split_blocks) {
+  (void)c; (void)num_seqs; (void)n_heads; (void)split_blocks;
+  return 0;
+}
+
+KVS_API int kvs_paged_decode(const kvs_cache* c, const kvs_batch* b, const kvs_decode_args* a,
+                             kvs_stream_t stream) {
+  if (!c || !b || !a || !a->q || !a->k_new || !a->v_new || !a->positions || !a->slot_blocks ||
+      !a->slot_offsets || !a->inv_freq || !a->out)
+    return KVS_E_ARG;
+  if (b->cu_tokens == nullptr && b->total_tokens != b->num_seqs) return KVS_E_ARG;
+  if (a->layer < 0 || a->layer >= c->n_layers || a->n_heads <= 0 || a->n_heads % c->n_kv_heads)
+    return KVS_E_ARG;
+  if (b->num_seqs == 0) return KVS_OK;
+  return kvs_decode_generic(c, b, a, to_cuda(stream));
+}
+
+KVS_API size_t kvs_replay_scratch_bytes(int32_t batch, int32_t seq_len) {
+  (void)batch; (void)seq_len;
+  return 0;
+}
+
+KVS_API int kvs_replay_attention(const kvs_replay_args* a, kvs_stream_t stream) {
+  if (!a || !a->q || !a->k || !a->v || !a->evicted_at || !a->lengths || !a->out || a->batch < 0 ||
+      a->seq_len < 0 || a->n_heads <= 0 || a->n_kv_heads <= 0 || a->n_heads % a->n_kv_heads ||
+      a->head_dim <= 0)
+    return KVS_E_ARG;
+  if (a->batch == 0 || a->seq_len == 0) return KVS_OK;
+  return kvs_replay_generic(a, to_cuda(stream));
+}

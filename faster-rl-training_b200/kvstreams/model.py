@@ -1,0 +1,197 @@
+"""Llama-style decoder with the two forward paths of kvstreams/model.py:1-188.
+
+* :meth:`TinyLM.forward` -- full-sequence forward with explicit positions and the
+  KV-streams replay mask; attention runs in the masked replay kernel, which skips
+  fully hidden tiles (the trainer's replay).
+* :meth:`TinyLM.forward_cached` -- incremental forward through a
+  :class:`~kvstreams.paged_cache.PagedKVCache`; per layer one call rotates q/k at
+  their logical positions, appends k/v to the paged pool and attends to every live
+  entry (prefill and decode).  :meth:`TinyLM.forward_cached_batch` does the same
+  for many sequences at once.
+
+Module and parameter names equal the reference's, so state dicts load unchanged.
+Dense projections, norms and the MLP stay in PyTorch (cuBLAS); attention, RoPE and
+every cache operation are this library's kernels.
+"""
+
+from __future__ import annotations
+
+from typing import Optional, Sequence
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from . import ops
+from .config import ModelConfig
+from .ops import ReplayMask
+from .rope import RotaryEmbedding
+
+
+class RMSNorm(nn.Module):
+    def __init__(self, dim: int, eps: float = 1e-6) -> None:
+        super().__init__()
+        self.eps = eps
+        self.weight = nn.Parameter(torch.ones(dim))
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + self.eps) * self.weight
+
+
+class Attention(nn.Module):
+    def __init__(self, cfg: ModelConfig) -> None:
+        super().__init__()
+        self.n_heads = cfg.n_heads
+        self.n_kv_heads = cfg.n_kv_heads
+        self.head_dim = cfg.head_dim
+        self.scale = self.head_dim ** -0.5  # model.py:71
+        self.q_proj = nn.Linear(cfg.d_model, cfg.n_heads * cfg.head_dim, bias=False)
+        self.k_proj = nn.Linear(cfg.d_model, cfg.n_kv_heads * cfg.head_dim, bias=False)
+        self.v_proj = nn.Linear(cfg.d_model, cfg.n_kv_heads * cfg.head_dim, bias=False)
+        self.o_proj = nn.Linear(cfg.n_heads * cfg.head_dim, cfg.d_model, bias=False)
+
+    def project(self, x: torch.Tensor):
+        lead = x.shape[:-1]
+        q = self.q_proj(x).view(*lead, self.n_heads, self.head_dim)
+        k = self.k_proj(x).view(*lead, self.n_kv_heads, self.head_dim)
+        v = self.v_proj(x).view(*lead, self.n_kv_heads, self.head_dim)
+        return q, k, v
+
+
+class MLP(nn.Module):
+    def __init__(self, cfg: ModelConfig) -> None:
+        super().__init__()
+        self.gate = nn.Linear(cfg.d_model, cfg.d_ff, bias=False)
+        self.up = nn.Linear(cfg.d_model, cfg.d_ff, bias=False)
+        self.down = nn.Linear(cfg.d_ff, cfg.d_model, bias=False)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return self.down(F.silu(self.gate(x)) * self.up(x))
+
+
+class Block(nn.Module):
+    def __init__(self, cfg: ModelConfig) -> None:
+        super().__init__()
+        self.attn_norm = RMSNorm(cfg.d_model, cfg.norm_eps)
+        self.attn = Attention(cfg)
+        self.mlp_norm = RMSNorm(cfg.d_model, cfg.norm_eps)
+        self.mlp = MLP(cfg)
+
+
+def causal_mask(T: int, device=None) -> torch.Tensor:
+    return torch.ones(T, T, dtype=torch.bool, device=device).tril()
+
+
+class _ReplayAttention(torch.autograd.Function):
+    """RoPE of q/k at ``positions`` plus masked replay attention, as one autograd node."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, positions, evicted_at, lengths, inv_freq, scale):
+        q = q.detach().contiguous().clone()
+        k = k.detach().contiguous().clone()
+        ops.rope_(q, positions, inv_freq)
+        ops.rope_(k, positions, inv_freq)
+        return ops.replay_attention(q, k, v.detach(), evicted_at, lengths, scale)
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        raise NotImplementedError(
+            "the masked replay backward kernel is not part of this build; run the replay under torch.no_grad()"
+        )
+
+
+def as_replay_mask(mask, B: int, T: int, device) -> ReplayMask:
+    if mask is None:
+        return ReplayMask.causal(B, T, device)
+    if isinstance(mask, ReplayMask):
+        return mask.to(device)
+    m = mask.to(device)
+    if m.dim() == 3 and m.shape[0] == 1 and B > 1:
+        m = m.expand(B, T, T)
+    return ReplayMask.from_dense(m)
+
+
+class TinyLM(nn.Module):
+    def __init__(self, cfg: ModelConfig) -> None:
+        super().__init__()
+        self.cfg = cfg
+        self.embed = nn.Embedding(cfg.vocab_size, cfg.d_model)
+        self.layers = nn.ModuleList(Block(cfg) for _ in range(cfg.n_layers))
+        self.norm = RMSNorm(cfg.d_model, cfg.norm_eps)
+        self.lm_head = nn.Linear(cfg.d_model, cfg.vocab_size, bias=False)
+        self.rope = RotaryEmbedding(cfg.head_dim, cfg.rope_theta)
+        self.apply(self._init_weights)
+
+    def _init_weights(self, module: nn.Module) -> None:
+        if isinstance(module, (nn.Linear, nn.Embedding)):
+            nn.init.normal_(module.weight, mean=0.0, std=self.cfg.init_std)
+
+    @property
+    def device(self) -> torch.device:
+        return self.embed.weight.device
+
+    @property
+    def dtype(self) -> torch.dtype:
+        return self.embed.weight.dtype
+
+    def num_parameters(self) -> int:
+        return sum(p.numel() for p in self.parameters())
+
+    # ------------------------------------------------------------------ replay path
+    def forward_hidden(self, tokens: torch.Tensor, positions: Optional[torch.Tensor] = None, mask=None) -> torch.Tensor:
+        """Final normed hidden states ``[B, T, d_model]`` of the masked full-sequence forward."""
+        B, T = tokens.shape
+        dev = self.device
+        tokens = tokens.to(dev)
+        if positions is None:
+            positions = torch.arange(T, device=dev).expand(B, T)
+        positions = positions.to(dev)
+        rm = as_replay_mask(mask, B, T, dev)
+        inv = self.rope.table(dev, self.dtype)
+        x = self.embed(tokens)
+        for blk in self.layers:
+            q, k, v = blk.attn.project(blk.attn_norm(x))
+            a = _ReplayAttention.apply(q, k, v, positions, rm.evicted_at, rm.lengths, inv, blk.attn.scale)
+            x = x + blk.attn.o_proj(a.reshape(B, T, -1))
+            x = x + blk.mlp(blk.mlp_norm(x))
+        return self.norm(x)
+
+    def forward(self, tokens: torch.Tensor, positions: Optional[torch.Tensor] = None, mask=None) -> torch.Tensor:
+        """Full-sequence forward (model.py:132-157).
+
+        mask: None (causal), a :class:`ReplayMask`, or a dense ``[B, T, T]`` boolean mask of
+        KV-streams form (``s <= t and t < evicted_at[s]``).  Returns ``[B, T, vocab]`` logits."""
+        return self.lm_head(self.forward_hidden(tokens, positions, mask))
+
+    # ------------------------------------------------------------------ paged path
+    @torch.no_grad()
+    def forward_cached(self, tokens: torch.Tensor, positions: torch.Tensor, cache, seq_id: int) -> torch.Tensor:
+        """Incremental forward of one sequence (model.py:160-188); returns ``[T, vocab]``."""
+        T = tokens.numel()
+        return self.forward_cached_batch(tokens.reshape(T), positions.reshape(T), cache, [seq_id], counts=[T])
+
+    @torch.no_grad()
+    def forward_cached_batch(self, tokens: torch.Tensor, positions: torch.Tensor, cache, seq_ids: Sequence[int],
+                             counts: Optional[Sequence[int]] = None, last_only: bool = False) -> torch.Tensor:
+        """Incremental forward of many sequences: ``tokens``/``positions`` concatenate the new
+        tokens of each sequence in order (``counts`` per sequence, default one each).
+        Returns logits of every new token (or only of each sequence's last one)."""
+        dev = self.device
+        tokens = tokens.to(dev).reshape(-1)
+        positions = positions.to(dev, torch.long).reshape(-1)
+        N = tokens.numel()
+        one_each = counts is None or all(c == 1 for c in counts)
+        mapping = cache.append_slots_batch(seq_ids, positions, None if one_each else counts)
+        slots = [cache.slot(s) for s in seq_ids]
+        inv = self.rope.table(dev, self.dtype)
+        x = self.embed(tokens)
+        for i, blk in enumerate(self.layers):
+            q, k, v = blk.attn.project(blk.attn_norm(x))
+            a = ops.paged_forward(cache, slots, None if one_each else counts, i, q, k, v, positions, mapping, inv,
+                                  blk.attn.scale)
+            x = x + blk.attn.o_proj(a.reshape(N, -1))
+            x = x + blk.mlp(blk.mlp_norm(x))
+        if last_only and not one_each:
+            ends = torch.tensor(counts, device=dev).cumsum(0) - 1
+            x = x.index_select(0, ends)
+        return self.lm_head(self.norm(x))

@@ -1,0 +1,182 @@
+"""PyTorch-facing wrappers of the libkvs_b200.so kernels.
+
+Every function here launches this library's own sm_100a kernels on the current
+CUDA stream; none has a CPU implementation.  Tensors must already be on the GPU.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+from typing import Optional, Sequence
+
+import numpy as np
+import torch
+
+from . import _native as N
+
+NEVER = N.NEVER
+
+
+def _check_cuda(*ts: torch.Tensor) -> None:
+    for t in ts:
+        N.require_cuda(t, "tensor")
+
+
+def rope_(x: torch.Tensor, positions: torch.Tensor, inv_freq: torch.Tensor) -> torch.Tensor:
+    """Rotate ``x [..., H, D]`` in place at ``positions [...]`` (rope.py:42-46 semantics)."""
+    _check_cuda(x)
+    if not x.is_contiguous():
+        raise ValueError("rope_ needs a contiguous tensor")
+    H, D = x.shape[-2], x.shape[-1]
+    n = x.numel() // (H * D)
+    pos = positions.reshape(-1).to(device=x.device, dtype=torch.long).contiguous()
+    if pos.numel() != n:
+        raise ValueError("positions do not match x")
+    rc = N.lib().kvs_rope(x.data_ptr(), N.DTYPE_CODE[x.dtype], pos.data_ptr(), n, H, D, inv_freq.data_ptr(),
+                          N.stream_ptr(x.device))
+    N.check(rc, "kvs_rope")
+    return x
+
+
+def evicted_at_device(logs: Sequence, lengths: Sequence[int], device: torch.device,
+                      t_stride: Optional[int] = None) -> torch.Tensor:
+    """``[len(logs), t_stride]`` int64 evicted_at of each compaction log (events.py:66-74),
+    computed by the evicted_at kernel; entries past a stream's length are NEVER."""
+    triples = [log.span_triples() for log in logs]
+    cu = np.zeros(len(logs) + 1, dtype=np.int32)
+    np.cumsum([len(t) for t in triples], out=cu[1:])
+    flat = np.concatenate(triples, axis=0) if triples else np.zeros((0, 3), dtype=np.int64)
+    if flat.shape[0] == 0:
+        flat = np.zeros((1, 3), dtype=np.int64)
+    T = int(t_stride if t_stride is not None else (max(lengths) if len(lengths) else 0))
+    return evicted_at_from_spans(cu, flat, lengths, device, T)
+
+
+def evicted_at_from_spans(cu: np.ndarray, triples: np.ndarray, lengths: Sequence[int], device, t_stride: int):
+    dev = torch.device(device)
+    out = torch.empty((len(lengths), max(t_stride, 1)), dtype=torch.long, device=dev)
+    cu_t = torch.from_numpy(np.ascontiguousarray(cu, dtype=np.int32)).to(dev)
+    tr = np.ascontiguousarray(triples, dtype=np.int64)
+    ss = torch.from_numpy(np.ascontiguousarray(tr[:, 0])).to(dev)
+    se = torch.from_numpy(np.ascontiguousarray(tr[:, 1])).to(dev)
+    st = torch.from_numpy(np.ascontiguousarray(tr[:, 2])).to(dev)
+    ln = torch.as_tensor(np.asarray(lengths, dtype=np.int32)).to(dev)
+    with torch.cuda.device(dev):
+        rc = N.lib().kvs_evicted_at(cu_t.data_ptr(), ss.data_ptr(), se.data_ptr(), st.data_ptr(), ln.data_ptr(),
+                                    len(lengths), max(t_stride, 1), out.data_ptr(), N.stream_ptr(dev))
+    N.check(rc, "kvs_evicted_at")
+    return out[:, :t_stride]
+
+
+def replay_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, evicted_at: torch.Tensor,
+                     lengths: torch.Tensor, scale: float, out: Optional[torch.Tensor] = None,
+                     force_generic: bool = False) -> torch.Tensor:
+    """Masked replay attention (model.py:71-74 with the replay.py:62 mask).
+
+    q ``[B, T, Hq, D]``, k/v ``[B, T, Hkv, D]`` already rotated; evicted_at ``[B, T]``
+    int64; lengths ``[B]`` int32 (rows past the length attend to themselves only)."""
+    _check_cuda(q, k, v, evicted_at, lengths)
+    B, T, Hq, D = q.shape
+    Hkv = k.shape[2]
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    ev = evicted_at.to(torch.long).contiguous()
+    ln = lengths.to(torch.int32).contiguous()
+    if out is None:
+        out = torch.empty_like(q)
+    lib = N.lib()
+    nbytes = lib.kvs_replay_scratch_bytes(B, T)
+    scratch = torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=q.device)
+    a = N.KvsReplayArgs(q=q.data_ptr(), k=k.data_ptr(), v=v.data_ptr(), evicted_at=ev.data_ptr(),
+                        lengths=ln.data_ptr(), out=out.data_ptr(), scratch=scratch.data_ptr(),
+                        scratch_bytes=scratch.numel(), batch=B, seq_len=T, n_heads=Hq, n_kv_heads=Hkv, head_dim=D,
+                        dtype=N.DTYPE_CODE[q.dtype], scale=float(scale), flags=1 if force_generic else 0)
+    N.check(lib.kvs_replay_attention(C.byref(a), N.stream_ptr(q.device)), "kvs_replay_attention")
+    return out
+
+
+def paged_forward(cache, slots: Sequence[int], counts: Optional[Sequence[int]], layer: int, q: torch.Tensor,
+                  k_new: torch.Tensor, v_new: torch.Tensor, positions: torch.Tensor, mapping,
+                  inv_freq: torch.Tensor, scale: float, out: Optional[torch.Tensor] = None,
+                  split_blocks: int = 0) -> torch.Tensor:
+    """One layer of the paged incremental forward (model.py:50-75 + hook :182-185) for the
+    new tokens of a batch of sequences: RoPE of q/k, append of k/v, paged GQA attention.
+
+    q ``[N, Hq, D]``, k_new/v_new ``[N, Hkv, D]`` (not rotated), positions ``[N]``; ``mapping``
+    is the SlotMapping returned by append_slots for the same tokens."""
+    q, k_new, v_new = q.contiguous(), k_new.contiguous(), v_new.contiguous()
+    if q.dtype != cache.dtype or k_new.dtype != cache.dtype or v_new.dtype != cache.dtype:
+        raise ValueError("activations must have the cache dtype")
+    pos = positions.to(device=q.device, dtype=torch.long).contiguous()
+    if out is None:
+        out = torch.empty_like(q)
+    b, keep = cache._batch(slots, counts)
+    lib = N.lib()
+    nbytes = int(lib.kvs_decode_scratch_bytes(C.byref(cache.struct), b.num_seqs, q.shape[1], split_blocks))
+    scratch = cache._decode_scratch(nbytes) if nbytes else None
+    a = N.KvsDecodeArgs(q=q.data_ptr(), k_new=k_new.data_ptr(), v_new=v_new.data_ptr(), positions=pos.data_ptr(),
+                        slot_blocks=mapping.blocks.data_ptr(), slot_offsets=mapping.offsets.data_ptr(),
+                        inv_freq=inv_freq.data_ptr(), out=out.data_ptr(),
+                        scratch=scratch.data_ptr() if scratch is not None else None,
+                        scratch_bytes=scratch.numel() if scratch is not None else 0, scale=float(scale),
+                        layer=int(layer), n_heads=int(q.shape[1]), split_blocks=int(split_blocks))
+    N.check(lib.kvs_paged_decode(C.byref(cache.struct), C.byref(b), C.byref(a), N.stream_ptr(q.device)),
+            "kvs_paged_decode")
+    return out
+
+
+@dataclass
+class ReplayMask:
+    """The KV-streams replay mask in factored form (replay.py:55-63, collate :221-222):
+    ``visible(t, s) = s <= t and t < evicted_at[b, s]`` for ``t < lengths[b]``; padded rows
+    see only themselves.  Never materialised as ``[B, T, T]`` on the device path."""
+
+    evicted_at: torch.Tensor  # [B, T] int64
+    lengths: torch.Tensor  # [B] int32
+
+    def to(self, device) -> "ReplayMask":
+        return ReplayMask(self.evicted_at.to(device), self.lengths.to(device))
+
+    @property
+    def shape(self):
+        B, T = self.evicted_at.shape
+        return (B, T, T)
+
+    def dense(self) -> torch.Tensor:
+        """``[B, T, T]`` bool mask (for inspection and API compatibility only)."""
+        B, T = self.evicted_at.shape
+        dev = self.evicted_at.device
+        t = torch.arange(T, device=dev)
+        m = (t[None, None, :] <= t[None, :, None]) & (t[None, :, None] < self.evicted_at[:, None, :])
+        pad = t[None, :] >= self.lengths.to(dev)[:, None].long()  # [B, T] padded query rows
+        eye = torch.eye(T, dtype=torch.bool, device=dev)[None]
+        m = torch.where(pad[:, :, None] | pad[:, None, :], eye.expand(B, T, T), m)
+        return m
+
+    @classmethod
+    def causal(cls, B: int, T: int, device) -> "ReplayMask":
+        return cls(torch.full((B, T), NEVER, dtype=torch.long, device=device),
+                   torch.full((B,), T, dtype=torch.int32, device=device))
+
+    @classmethod
+    def from_dense(cls, mask: torch.Tensor) -> "ReplayMask":
+        """Factor a dense ``[B, T, T]`` boolean mask; raises if it is not of KV-streams form."""
+        if mask.dim() == 2:
+            mask = mask[None]
+        B, T, _ = mask.shape
+        m = mask.to(torch.bool)
+        dev = m.device
+        t = torch.arange(T, device=dev)
+        lower = t[:, None] >= t[None, :]  # [t, s]: s <= t
+        # evicted_at[s] = first row t >= s where column s is hidden, else NEVER
+        hidden = (~m) & lower[None]
+        first = torch.where(hidden, t[None, :, None].expand(B, T, T), torch.full_like(t, T)[None, None, :].expand(B, T, T))
+        e = first.min(dim=1).values
+        ev = torch.where(e >= T, torch.full_like(e, NEVER), e)
+        rm = cls(ev.long(), torch.full((B,), T, dtype=torch.int32, device=dev))
+        if not torch.equal(rm.dense(), m):
+            raise ValueError(
+                "attention mask is not a KV-streams replay mask (s <= t and t < evicted_at[s]); "
+                "pass a ReplayMask for padded batches"
+            )
+        return rm

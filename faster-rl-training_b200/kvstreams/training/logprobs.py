@@ -1,0 +1,43 @@
+"""Trainer-side log-probabilities (training/logprobs.py:10-25)."""
+
+from __future__ import annotations
+
+import torch
+
+from .replay import Batch
+
+# tokens per lm_head chunk: bounds the [chunk, vocab] logits held at once
+_CHUNK_TOKENS = 8192
+
+
+def token_logprobs(model, batch: Batch, temperature: float = 1.0, return_full: bool = False):
+    """Log-probability of ``tokens[:, t]`` given the replayed context of ``t - 1``.
+
+    Returns ``[B, T]`` (position 0 is 0); with ``return_full`` also the ``[B, T, V]``
+    log-softmax rows aligned the same way.  The replay forward runs the masked replay
+    kernel; lm_head + log-softmax + gather are done in token chunks so the full
+    ``[B, T, V]`` logits never exist at once.  Half-precision models get float32
+    log-softmax.
+    """
+    dev = model.device
+    tokens = batch.tokens.to(dev)
+    hidden = model.forward_hidden(tokens, batch.positions.to(dev), batch.mask.to(dev))
+    B, T, _ = hidden.shape
+    want = torch.float32 if hidden.dtype in (torch.bfloat16, torch.float16) else hidden.dtype
+    out = torch.zeros((B, T), dtype=want, device=dev)
+    full = torch.zeros((B, T, model.cfg.vocab_size), dtype=want, device=dev) if return_full else None
+    flat_h = hidden[:, :-1].reshape(-1, hidden.shape[-1])
+    flat_next = tokens[:, 1:].reshape(-1)
+    res = torch.empty(flat_next.numel(), dtype=want, device=dev)
+    for a in range(0, flat_h.shape[0], _CHUNK_TOKENS):
+        z = slice(a, a + _CHUNK_TOKENS)
+        logits = model.lm_head(flat_h[z]).to(want)
+        logp = torch.log_softmax(logits / temperature, dim=-1)
+        res[z] = logp.gather(-1, flat_next[z, None]).squeeze(-1)
+        if full is not None:
+            rows = torch.arange(a, a + logp.shape[0], device=dev)
+            full[rows // (T - 1), rows % (T - 1) + 1] = logp
+    out[:, 1:] = res.view(B, T - 1)
+    if not return_full:
+        return out
+    return out, full

@@ -1,0 +1,262 @@
+/*
+ * kvs_b200.h -- C ABI of the B200 (sm_100a) KV-streams paged-KV library.
+ *
+ * Every entry point takes plain device pointers and sizes plus a cudaStream_t,
+ * never allocates device memory and never synchronises the stream.  Device-side
+ * failures (pool exhausted, double free, invariant violations) are reported
+ * through the int32 status words of the cache (`kvs_cache.status`) and read back
+ * by the host at its next synchronisation point.  The return value of every
+ * function is a host-side code: KVS_OK, or a negative KVS_E_* value for a bad
+ * argument / unsupported shape / CUDA launch error (nothing was launched then).
+ *
+ * Reference interface each entry point replaces (thanhauco/faster-RL-training,
+ * package kvstreams 0.2.0) is cited in the comment above it as file:line.
+ *
+ * Ordering contract for batched calls: a call over `num_seqs` sequences behaves
+ * exactly as if the single-sequence reference method had been called once per
+ * sequence, in the order of `seq_slots`.  Block ids popped from / pushed to the
+ * free stack therefore come out in that canonical order (bit-exact with the
+ * reference's LIFO list).
+ */
+#ifndef KVS_B200_H
+#define KVS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* kvs_stream_t; /* == cudaStream_t */
+
+#define KVS_ABI_VERSION 1
+
+/* element types of K/V pools and activations */
+enum kvs_dtype { KVS_F32 = 0, KVS_F64 = 1, KVS_BF16 = 2, KVS_F16 = 3 };
+
+/* host-side return codes */
+enum kvs_rc {
+  KVS_OK = 0,
+  KVS_E_ARG = -1,         /* null pointer / size out of range */
+  KVS_E_UNSUPPORTED = -2, /* shape or dtype this build has no kernel for */
+  KVS_E_LAUNCH = -3,      /* cudaGetLastError() after the launch */
+  KVS_E_SCRATCH = -4      /* caller's scratch buffer too small */
+};
+
+/* device-side status codes (status[0]; status[1..3] hold details) */
+enum kvs_status {
+  KVS_ST_OK = 0,
+  KVS_ST_OUT_OF_BLOCKS = 1,    /* paged_cache.py:41-42  OutOfBlocksError */
+  KVS_ST_DOUBLE_FREE = 2,      /* paged_cache.py:48-49  ValueError */
+  KVS_ST_NOT_FULL_BLOCK = 3,   /* paged_cache.py:202-206 ValueError */
+  KVS_ST_TABLE_OVERFLOW = 4,   /* table longer than max_blocks (no reference counterpart) */
+  KVS_ST_TRUNCATE = 5,         /* paged_cache.py:247-248 ValueError */
+  KVS_ST_INV_DUP_BLOCK = 6,    /* paged_cache.py:265-266 */
+  KVS_ST_INV_TABLE_LEN = 7,    /* paged_cache.py:267-268 */
+  KVS_ST_INV_HOLE = 8,         /* paged_cache.py:270-271 */
+  KVS_ST_INV_ORDER = 9,        /* paged_cache.py:272-273 */
+  KVS_ST_SPAN_CAPACITY = 10,   /* evicted-span output buffer too small */
+  KVS_ST_OWNER = 11            /* block freed by a sequence that does not own it */
+};
+
+/* CacheStats counters (paged_cache.py:70-78), int64 each */
+enum kvs_stat {
+  KVS_STAT_WRITTEN_TOKENS = 0,
+  KVS_STAT_EVICTED_TOKENS = 1,
+  KVS_STAT_EVICTED_BLOCKS = 2,
+  KVS_STAT_TRUNCATED_TOKENS = 3,
+  KVS_STAT_PEAK_BLOCKS = 4,
+  KVS_STAT_EVICTION_CALLS = 5,
+  KVS_STAT_SHRUNK_TOKENS = 6,
+  KVS_STAT_COUNT = 8
+};
+
+#define KVS_STATUS_WORDS 4
+#define KVS_NEVER INT64_MAX /* events.py:20 NEVER */
+
+/*
+ * Device-resident paged KV cache (paged_cache.py:81-106).
+ * Pool layout is the reference's: k, v = [n_layers][num_blocks][block_size][n_kv_heads][head_dim].
+ * Sequences live in slots 0..max_seqs-1; table of slot s = tables[s*max_blocks .. +n_blocks[s]).
+ * Free list: free_stack[0 .. *free_top) with the next block to hand out at free_stack[*free_top-1]
+ * (the reference's `_free` list, popped from its end, paged_cache.py:37,43,51).
+ */
+typedef struct kvs_cache {
+  void* k;
+  void* v;
+  int64_t* slot_pos;    /* [num_blocks][block_size] logical position, -1 = empty */
+  int32_t* tables;      /* [max_seqs][max_blocks] */
+  int32_t* n_blocks;    /* [max_seqs] table length */
+  int32_t* lengths;     /* [max_seqs] live tokens */
+  int32_t* free_stack;  /* [num_blocks] */
+  int32_t* free_top;    /* [1] */
+  int32_t* block_owner; /* [num_blocks] owning slot, -1 when free (the reference's `_used` set) */
+  int64_t* stats;       /* [KVS_STAT_COUNT] */
+  int32_t* status;      /* [KVS_STATUS_WORDS] */
+  int32_t n_layers;
+  int32_t num_blocks;
+  int32_t block_size;
+  int32_t n_kv_heads;
+  int32_t head_dim;
+  int32_t max_seqs;
+  int32_t max_blocks;
+  int32_t dtype; /* enum kvs_dtype of k and v */
+} kvs_cache;
+
+/* A batch of sequences processed in the given order.  cu_tokens may be NULL
+ * when every sequence contributes exactly one token (decode). */
+typedef struct kvs_batch {
+  const int32_t* seq_slots; /* [num_seqs] */
+  const int32_t* cu_tokens; /* [num_seqs+1] exclusive prefix sum of new tokens, or NULL */
+  int32_t num_seqs;
+  int32_t total_tokens;
+} kvs_batch;
+
+/* size of each public struct as compiled into the library (ABI check):
+ * which = 0 kvs_cache, 1 kvs_batch, 2 kvs_decode_args, 3 kvs_replay_args */
+size_t kvs_abi_struct_size(int which);
+int kvs_abi_version(void);
+/* number of SMs of the current device, cached per device (grid sizing) */
+int kvs_device_sm_count(void);
+/* kernels launched by this library in this process so far (for launch accounting) */
+long long kvs_launch_count(void);
+
+/* ------------------------------------------------------------------ cache state */
+
+/* Reset all metadata to the freshly-constructed state: free stack [NB-1..0]
+ * (paged_cache.py:37), slot_pos -1 (:100-102), empty tables, zero stats/status.
+ * The K/V pool is not touched (the caller zero-initialises it at allocation). */
+int kvs_cache_reset(const kvs_cache* c, kvs_stream_t stream);
+
+/* PagedKVCache.append_slots (paged_cache.py:145-165), batched.
+ * positions: [total_tokens] int64.  out_blocks/out_offsets: [total_tokens] int32
+ * slot mapping (SlotMapping, paged_cache.py:62-67).  Allocates blocks on demand in
+ * canonical order; if the pool cannot cover the whole batch nothing is changed and
+ * status = KVS_ST_OUT_OF_BLOCKS. */
+int kvs_append_slots(const kvs_cache* c, const kvs_batch* b, const int64_t* positions,
+                     int32_t* out_blocks, int32_t* out_offsets, kvs_stream_t stream);
+
+/* PagedKVCache.write (paged_cache.py:167-171): k,v [n_tokens][n_kv_heads][head_dim]
+ * (dtype of the pool) stored at the slot mapping, for one layer. */
+int kvs_write_kv(const kvs_cache* c, int32_t layer, const int32_t* blocks, const int32_t* offsets,
+                 const void* k, const void* v, int32_t n_tokens, kvs_stream_t stream);
+
+/* PagedKVCache.evict_positions (paged_cache.py:219-240), batched.
+ * Spans of sequence i: [span_start[j], span_end[j]) for j in cu_spans[i]..cu_spans[i+1];
+ * they must be sorted and non-overlapping (merge_spans, utils/spans.py:10-18).
+ * Evicts every full block whose live tokens all fall inside the spans, joins the
+ * table, resets slot_pos, pushes the freed blocks (ascending table index per
+ * sequence, sequences in batch order) and updates CacheStats.
+ * Output: the logical spans actually removed (positions_to_spans, spans.py:21-23)
+ * for sequence i at out_spans[2*(i*span_cap + r)], r < out_counts[i].
+ * scratch: >= kvs_evict_scratch_bytes(num_seqs, max_blocks) bytes of device memory. */
+size_t kvs_evict_scratch_bytes(int32_t num_seqs, int32_t max_blocks);
+int kvs_evict_positions(const kvs_cache* c, const kvs_batch* b, const int32_t* cu_spans,
+                        const int64_t* span_start, const int64_t* span_end,
+                        int64_t* out_spans, int32_t* out_counts, int32_t span_cap,
+                        void* scratch, size_t scratch_bytes, kvs_stream_t stream);
+
+/* PagedKVCache.evict_blocks (paged_cache.py:190-217), batched: drop_flags
+ * [num_seqs][max_blocks] uint8 (1 = remove that table index; the host has already
+ * checked that every flagged index is a full block).  Same join / free / stats as above. */
+int kvs_evict_blocks(const kvs_cache* c, const kvs_batch* b, const uint8_t* drop_flags,
+                     void* scratch, size_t scratch_bytes, kvs_stream_t stream);
+
+/* PagedKVCache.truncate (paged_cache.py:242-260) when mode == 0 and
+ * PagedKVCache.free_sequence (paged_cache.py:129-133) when mode == 1, batched.
+ * new_lengths: [num_seqs] target live length (ignored for mode 1, which frees all). */
+int kvs_release(const kvs_cache* c, const kvs_batch* b, const int32_t* new_lengths, int32_t mode,
+                kvs_stream_t stream);
+
+/* PagedKVCache.check_invariants (paged_cache.py:262-273), batched.
+ * out_codes[i] = KVS_ST_OK or the first KVS_ST_INV_* violated by sequence i.
+ * scratch: >= kvs_check_scratch_bytes(num_blocks) bytes. */
+size_t kvs_check_scratch_bytes(int32_t num_blocks);
+int kvs_check_invariants(const kvs_cache* c, const kvs_batch* b, int32_t* out_codes,
+                         void* scratch, size_t scratch_bytes, kvs_stream_t stream);
+
+/* ------------------------------------------------------------------ compute */
+
+/* apply_rope (rope.py:42-46) with RotaryEmbedding angles (rope.py:30-34) at explicit
+ * logical positions, in place: x [n_tokens][n_heads][head_dim] of `dtype`.
+ * inv_freq: [head_dim/2] float (f32/bf16/f16 activations) or double (f64). */
+int kvs_rope(void* x, int32_t dtype, const int64_t* positions, int32_t n_tokens, int32_t n_heads,
+             int32_t head_dim, const void* inv_freq, kvs_stream_t stream);
+
+/* Paged attention of the new tokens of each sequence over its live cache entries
+ * (Attention.forward in cached mode, model.py:50-75 with the kv_hook of
+ * model.py:182-185 and the mask of model.py:175-176): query i of sequence s attends
+ * to cache entries [0, lengths[s] - T_s + i].  q [total_tokens][n_heads][head_dim]
+ * already rotated; out same shape.  Must run after the tokens were appended. */
+int kvs_paged_attention(const kvs_cache* c, const kvs_batch* b, int32_t layer, const void* q,
+                        void* out, int32_t n_heads, double scale, kvs_stream_t stream);
+
+/* One layer of TinyLM.forward_cached (model.py:160-188) for the new tokens of a
+ * batch of sequences: RoPE of q and k at `positions`, append of k and v at the
+ * slot mapping produced by kvs_append_slots, and paged GQA attention of every new
+ * query over the live entries it may see.  One token per sequence (decode,
+ * cu_tokens NULL) runs the fused split-K kernel; prefill chunks (cu_tokens set)
+ * run rope + append + kvs_paged_attention. */
+typedef struct kvs_decode_args {
+  const void* q;            /* [total_tokens][n_heads][head_dim], not yet rotated */
+  const void* k_new;        /* [total_tokens][n_kv_heads][head_dim], not yet rotated */
+  const void* v_new;        /* [total_tokens][n_kv_heads][head_dim] */
+  const int64_t* positions; /* [total_tokens] */
+  const int32_t* slot_blocks;  /* [total_tokens] from kvs_append_slots */
+  const int32_t* slot_offsets; /* [total_tokens] */
+  const void* inv_freq;     /* [head_dim/2] float, or double for f64 pools */
+  void* out;                /* [total_tokens][n_heads][head_dim] */
+  void* scratch;            /* split-K partials + per-sequence counters */
+  size_t scratch_bytes;
+  double scale;             /* head_dim**-0.5 (model.py:71) */
+  int32_t layer;
+  int32_t n_heads;
+  int32_t split_blocks;     /* KV blocks per split (0 = library default) */
+  int32_t reserved;
+} kvs_decode_args;
+size_t kvs_decode_scratch_bytes(const kvs_cache* c, int32_t num_seqs, int32_t n_heads,
+                                int32_t split_blocks);
+int kvs_paged_decode(const kvs_cache* c, const kvs_batch* b, const kvs_decode_args* a,
+                     kvs_stream_t stream);
+
+/* CompactionLog.evicted_at (events.py:66-74), batched: for stream i, events are
+ * triples (span_start, span_end, time) j in cu_spans[i]..cu_spans[i+1].
+ * out [num_streams][t_stride] int64: min time over spans covering t, KVS_NEVER else;
+ * entries t >= lengths[i] are KVS_NEVER. */
+int kvs_evicted_at(const int32_t* cu_spans, const int64_t* span_start, const int64_t* span_end,
+                   const int64_t* span_time, const int32_t* lengths, int32_t num_streams,
+                   int32_t t_stride, int64_t* out, kvs_stream_t stream);
+
+/* Masked replay attention (TinyLM.forward attention, model.py:71-74, with the
+ * KV-streams mask of replay.py:55-63 and the collate padding of replay.py:221-222):
+ *   visible(t, s) = s <= t && t < evicted_at[b][s]      for t < lengths[b]
+ *   visible(t, s) = (s == t)                             for t >= lengths[b]
+ * q [B][T][n_heads][head_dim], k,v [B][T][n_kv_heads][head_dim], already rotated;
+ * out like q.  Fully masked 128x128 tiles are skipped using per-tile evicted_at bounds. */
+typedef struct kvs_replay_args {
+  const void* q;
+  const void* k;
+  const void* v;
+  const int64_t* evicted_at; /* [B][T] */
+  const int32_t* lengths;    /* [B] */
+  void* out;
+  void* scratch;
+  size_t scratch_bytes;
+  int32_t batch;
+  int32_t seq_len;
+  int32_t n_heads;
+  int32_t n_kv_heads;
+  int32_t head_dim;
+  int32_t dtype;
+  double scale;
+  int32_t flags; /* bit 0: force the generic SIMT kernel */
+  int32_t reserved;
+} kvs_replay_args;
+size_t kvs_replay_scratch_bytes(int32_t batch, int32_t seq_len);
+int kvs_replay_attention(const kvs_replay_args* a, kvs_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KVS_B200_H */
