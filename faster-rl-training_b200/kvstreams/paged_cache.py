@@ -320,7 +320,7 @@ class PagedKVCache:
         total = len(slots)
         if counts is not None:
             cu = np.zeros(len(slots) + 1, dtype=np.int32)
-            np.cumsum(np.asarray(counts, dtype=np.int64), out=cu[1:], casting="unsafe")
+            cu[1:] = np.cumsum(np.asarray(counts, dtype=np.int64))
             total = int(cu[-1])
             cu_t = torch.from_numpy(cu).to(self.device, non_blocking=True)
             keep.append(cu_t)
