@@ -34,7 +34,8 @@ ST_INV_ORDER = 9
 ST_SPAN_CAPACITY = 10
 ST_OWNER = 11
 
-RC_NAMES = {-1: "bad argument", -2: "unsupported shape/dtype", -3: "CUDA launch error", -4: "scratch too small"}
+RC_NAMES = {-1: "bad argument", -2: "unsupported shape/dtype", -3: "CUDA launch error", -4: "scratch too small",
+            -5: "request exceeds the built-in scratch of a no-alloc entry point"}
 
 STAT_FIELDS = (
     "written_tokens",
@@ -140,6 +141,7 @@ SIGNATURES = {
     "kvs_write_kv": (C.c_int, [_P, _I, _P, _P, _P, _P, _I, _P]),
     "kvs_evict_scratch_bytes": (_Z, [_I, _I]),
     "kvs_evict_positions": (C.c_int, [_P, _P, _P, _P, _P, _P, _P, _I, _P, _Z, _P]),
+    "kvs_evict_positions_noalloc": (C.c_int, [_P, _P, _P, _P, _P, _P, _P, _I, _P]),
     "kvs_evict_blocks": (C.c_int, [_P, _P, _P, _P, _Z, _P]),
     "kvs_release": (C.c_int, [_P, _P, _P, _I, _P]),
     "kvs_check_scratch_bytes": (_Z, [_I]),

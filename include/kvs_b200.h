@@ -41,7 +41,8 @@ enum kvs_rc {
   KVS_E_ARG = -1,         /* null pointer / size out of range */
   KVS_E_UNSUPPORTED = -2, /* shape or dtype this build has no kernel for */
   KVS_E_LAUNCH = -3,      /* cudaGetLastError() after the launch */
-  KVS_E_SCRATCH = -4      /* caller's scratch buffer too small */
+  KVS_E_SCRATCH = -4,     /* caller's scratch buffer too small */
+  KVS_E_NOALLOC_LIMIT = -5 /* request larger than the built-in scratch of a *_noalloc entry point */
 };
 
 /* device-side status codes (status[0]; status[1..3] hold details) */
@@ -156,6 +157,22 @@ int kvs_evict_positions(const kvs_cache* c, const kvs_batch* b, const int32_t* c
                         const int64_t* span_start, const int64_t* span_end,
                         int64_t* out_spans, int32_t* out_counts, int32_t span_cap,
                         void* scratch, size_t scratch_bytes, kvs_stream_t stream);
+
+/* No counterpart in the reference.  kvs_evict_positions for callers that cannot
+ * allocate device memory (hosts binding this C ABI without a device allocator of
+ * their own, or rollout loops that must not cudaMalloc between steps because it
+ * can synchronise the device).  Same arguments and results as
+ * kvs_evict_positions minus the scratch buffer: the scratch comes from one
+ * ~1.25 MiB array compiled into the library (held by every GPU that loads it
+ * until exit).  Limits: num_seqs <= 256 and c->max_blocks <= 1024, else
+ * KVS_E_NOALLOC_LIMIT and nothing is launched.  Calls share that array, so calls
+ * whose kernels overlap on the GPU race.  The first call on each device looks up
+ * the array's device address (cudaGetSymbolAddress); make it before any stream
+ * capture.  Allocates nothing. */
+int kvs_evict_positions_noalloc(const kvs_cache* c, const kvs_batch* b, const int32_t* cu_spans,
+                                const int64_t* span_start, const int64_t* span_end,
+                                int64_t* out_spans, int32_t* out_counts, int32_t span_cap,
+                                kvs_stream_t stream);
 
 /* PagedKVCache.evict_blocks (paged_cache.py:190-217), batched: drop_flags
  * [num_seqs][max_blocks] uint8 (1 = remove that table index; the host has already
