@@ -1,0 +1,466 @@
+// Fused paged decode for bf16, head_dim 128, block_size 16, 8 KV heads, GQA group 4
+// (the Llama-3-8B attention geometry): one new token per sequence.
+//
+// One launch does, for every sequence of the batch (TinyLM.forward_cached,
+// model.py:160-188, decode step, one layer):
+//   * RoPE of q and of the new k at the token's logical position (rope.py:42-46),
+//   * append of the rotated k and of v at the slot kvs_append_slots reserved
+//     (PagedKVCache.write, paged_cache.py:167-171),
+//   * GQA attention of q over every live entry of the block table
+//     (Attention.forward, model.py:67-74: head h reads KV head h / 4, scores * D^-0.5,
+//     softmax, weighted V).
+//
+// Work split ("stream-K"): the blocks of all sequences, concatenated in batch order,
+// are cut into gridDim.x equal contiguous ranges, one per CTA (one CTA per SM), so
+// every SM streams the same number of KV bytes whatever the context lengths.  A
+// sequence cut by range boundaries yields one partial (m, l, O) per CTA; the last
+// CTA to finish a sequence (per-sequence arrival counter) merges its partials.
+//
+// Per CTA: 8 warps, warp w <-> KV head w (4 query heads).  A 3-stage cp.async
+// pipeline stages whole 16-token blocks (K and V of all heads, 64 KiB) in shared
+// memory with a 16-byte-chunk XOR swizzle (chunk ^ token%8), so ldmatrix reads are
+// conflict free.  Per block and warp: S^T[16 tokens x 8] = K[16x128] . Q^T (4 real
+// heads + 4 zero columns) with 8 mma.m16n8k16 (bf16 in, fp32 accumulate), online
+// softmax in fp32 (base 2), P^T brought into B-fragment layout with movmatrix, and
+// O^T[128 x 8] += V^T . P^T with 8 more mma.
+#include "kvs_common.cuh"
+#include "kvs_rope.cuh"
+
+#include <mutex>
+
+using namespace kvs;
+
+namespace {
+
+constexpr int D = 128;
+constexpr int BS = 16;
+constexpr int HKV = 8;
+constexpr int G = 4;
+constexpr int HQ = HKV * G;
+constexpr int NTHREADS = 32 * HKV;
+constexpr int ROW_BYTES = D * 2;                       // one token of one head
+constexpr int KV_BLOCK_BYTES = BS * HKV * ROW_BYTES;   // 32 KiB: K (or V) of one block, all heads
+constexpr int STAGES = 3;
+constexpr int STAGE_BYTES = 2 * KV_BLOCK_BYTES;
+constexpr int MAX_SEQS = 1024;
+constexpr int CHUNKS = KV_BLOCK_BYTES / 16;            // 2048 16-byte chunks per K (or V) block
+
+constexpr int SMEM_STAGES = STAGES * STAGE_BYTES;
+constexpr int SMEM_Q = HQ * D * 2;
+constexpr int SMEM_NEW = 2 * HKV * D * 2;
+constexpr int SMEM_PREF = (MAX_SEQS + 1) * 4;
+constexpr int SMEM_TOTAL = SMEM_STAGES + SMEM_Q + SMEM_NEW + SMEM_PREF + 64;
+
+struct DecodeParams {
+  kvs_cache c;
+  const int32_t* seq_slots;
+  int num_seqs;
+  int layer;
+  const __nv_bfloat16* q;      // [S][HQ][D]
+  const __nv_bfloat16* k_new;  // [S][HKV][D]
+  const __nv_bfloat16* v_new;
+  const int64_t* positions;    // [S]
+  const int32_t* slot_blocks;  // [S]
+  const int32_t* slot_offsets; // [S]
+  const float* inv_freq;       // [D/2]
+  __nv_bfloat16* out;          // [S][HQ][D]
+  float* part_o;               // [slots][HQ][D]
+  float* part_ml;              // [slots][HQ][2]
+  int32_t* counters;           // [S]
+  float scale_log2;            // D^-0.5 * log2(e)
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ uint32_t movm_t(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;\n" : "=r"(y) : "r"(x));
+  return y;
+}
+__device__ __forceinline__ void mma_bf16(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// byte offset of 16-byte chunk `c` (0..15) of row `r` (= token*HKV + head) inside a K or V stage
+__device__ __forceinline__ uint32_t swz(int r, int c) {
+  return static_cast<uint32_t>(r * ROW_BYTES + ((c ^ ((r >> 3) & 7)) << 4));
+}
+
+__device__ __forceinline__ float warp_max_rows(float v) {
+  v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 4));
+  v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 8));
+  v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 16));
+  return v;
+}
+__device__ __forceinline__ float warp_sum_rows(float v) {
+  v += __shfl_xor_sync(0xffffffffu, v, 4);
+  v += __shfl_xor_sync(0xffffffffu, v, 8);
+  v += __shfl_xor_sync(0xffffffffu, v, 16);
+  return v;
+}
+
+__global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodeParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* stages = smem;
+  __nv_bfloat16* q_s = reinterpret_cast<__nv_bfloat16*>(smem + SMEM_STAGES);
+  __nv_bfloat16* knew_s = reinterpret_cast<__nv_bfloat16*>(smem + SMEM_STAGES + SMEM_Q);
+  __nv_bfloat16* vnew_s = knew_s + HKV * D;
+  int* s_pref = reinterpret_cast<int*>(smem + SMEM_STAGES + SMEM_Q + SMEM_NEW);
+  int* s_flag = s_pref + MAX_SEQS + 1;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const kvs_cache& c = p.c;
+  const int S = p.num_seqs;
+
+  // prefix sums of table lengths (blocks) over the batch
+  if (tid == 0) {
+    int acc = 0;
+    s_pref[0] = 0;
+    for (int i = 0; i < S; ++i) {
+      acc += (c.lengths[p.seq_slots[i]] + BS - 1) / BS;
+      s_pref[i + 1] = acc;
+    }
+  }
+  __syncthreads();
+  const int total = s_pref[S];
+  const int R = (total + gridDim.x - 1) / gridDim.x;
+  const int g0 = blockIdx.x * R;
+  const int g1 = min(total, g0 + R);
+  if (g0 >= g1) return;
+
+  const uint8_t* Kpool = static_cast<const uint8_t*>(c.k);
+  const uint8_t* Vpool = static_cast<const uint8_t*>(c.v);
+  const int64_t layer_rows = (int64_t)p.layer * c.num_blocks;
+
+  auto seq_of = [&](int gb) {
+    int lo = 0, hi = S - 1;  // last i with s_pref[i] <= gb
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (s_pref[mid] <= gb) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+  };
+
+  auto issue = [&](int gb, int st) {
+    const int i = seq_of(gb);
+    const int j = gb - s_pref[i];
+    const int slot = p.seq_slots[i];
+    const int64_t blk = c.tables[(int64_t)slot * c.max_blocks + j];
+    const uint8_t* ks = Kpool + (layer_rows + blk) * KV_BLOCK_BYTES;
+    const uint8_t* vs = Vpool + (layer_rows + blk) * KV_BLOCK_BYTES;
+    const uint32_t kd = smem_u32(stages + st * STAGE_BYTES);
+    const uint32_t vd = kd + KV_BLOCK_BYTES;
+#pragma unroll
+    for (int k = 0; k < CHUNKS / NTHREADS; ++k) {
+      const int q = tid + k * NTHREADS;
+      const int r = q >> 4, ch = q & 15;
+      cp_async16(kd + swz(r, ch), ks + (q << 4));
+      cp_async16(vd + swz(r, ch), vs + (q << 4));
+    }
+  };
+
+  // prologue
+#pragma unroll
+  for (int k = 0; k < STAGES - 1; ++k) {
+    if (g0 + k < g1) issue(g0 + k, k);
+    cp_async_commit();
+  }
+
+  // per-warp state of the current segment (one sequence inside this CTA's range)
+  uint32_t bq[8][2];
+  float acc[8][4];
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  int cur = -1;
+
+  auto finish = [&](int i) {
+    // sequence i: this CTA's part is done; write it (or the final output) and merge if last
+    const int P0 = s_pref[i], nb = s_pref[i + 1] - P0;
+    const int c0 = P0 / R, c1 = (P0 + nb - 1) / R;
+    const int expected = c1 - c0 + 1;
+    const float lt0 = warp_sum_rows(l0), lt1 = warp_sum_rows(l1);
+    const int hq0 = warp * G + 2 * t;  // query heads hq0, hq0+1 (valid for t < 2)
+    if (expected == 1) {
+      if (t < 2) {
+        __nv_bfloat16* o = p.out + ((int64_t)i * HQ + hq0) * D;
+        const float r0 = 1.f / lt0, r1 = 1.f / lt1;
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+          const int d = mt * 16 + g;
+          o[d] = __float2bfloat16_rn(acc[mt][0] * r0);
+          o[D + d] = __float2bfloat16_rn(acc[mt][1] * r1);
+          o[d + 8] = __float2bfloat16_rn(acc[mt][2] * r0);
+          o[D + d + 8] = __float2bfloat16_rn(acc[mt][3] * r1);
+        }
+      }
+      return;
+    }
+    const int slot_id = blockIdx.x + i;  // unique per (CTA, sequence) pair
+    if (t < 2) {
+      float* o = p.part_o + ((int64_t)slot_id * HQ + hq0) * D;
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        const int d = mt * 16 + g;
+        o[d] = acc[mt][0];
+        o[D + d] = acc[mt][1];
+        o[d + 8] = acc[mt][2];
+        o[D + d + 8] = acc[mt][3];
+      }
+      if (g == 0) {
+        float* ml = p.part_ml + ((int64_t)slot_id * HQ + hq0) * 2;
+        ml[0] = m0;
+        ml[1] = lt0;
+        ml[2] = m1;
+        ml[3] = lt1;
+      }
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+      const int arrived = atomicAdd(&p.counters[i], 1);
+      *s_flag = (arrived == expected - 1);
+    }
+    __syncthreads();
+    if (*s_flag) {
+      __threadfence();
+      for (int e = tid; e < HQ * D; e += NTHREADS) {
+        const int h = e / D;
+        float M = -INFINITY;
+        for (int cc = c0; cc <= c1; ++cc)
+          M = fmaxf(M, __ldcg(p.part_ml + ((int64_t)(cc + i) * HQ + h) * 2));
+        float num = 0.f, den = 0.f;
+        for (int cc = c0; cc <= c1; ++cc) {
+          const float* ml = p.part_ml + ((int64_t)(cc + i) * HQ + h) * 2;
+          const float w = exp2f(__ldcg(ml) - M);
+          den += w * __ldcg(ml + 1);
+          num += w * __ldcg(p.part_o + (int64_t)(cc + i) * HQ * D + e);
+        }
+        p.out[(int64_t)i * HQ * D + e] = __float2bfloat16_rn(num / den);
+      }
+      if (tid == 0) p.counters[i] = 0;  // ready for the next launch
+    }
+    __syncthreads();
+  };
+
+  auto start = [&](int i) {
+    const int slot = p.seq_slots[i];
+    const int64_t pos = p.positions[i];
+    // RoPE of q into shared memory (same rotation as every other kernel of the library)
+    for (int e = tid; e < HQ * (D / 2); e += NTHREADS) {
+      const int h = e / (D / 2), d = e % (D / 2);
+      const __nv_bfloat16* qr = p.q + ((int64_t)i * HQ + h) * D;
+      float r0, r1;
+      rope_rotate<float, float>(__bfloat162float(qr[d]), __bfloat162float(qr[d + D / 2]), pos, p.inv_freq[d], r0, r1);
+      q_s[h * D + d] = __float2bfloat16_rn(r0);
+      q_s[h * D + d + D / 2] = __float2bfloat16_rn(r1);
+    }
+    const int last = s_pref[i + 1] - 1;
+    if (last >= g0 && last < g1) {
+      // this CTA owns the sequence's last block: rotate + append the new token
+      const int64_t row = ((layer_rows + p.slot_blocks[i]) * BS + p.slot_offsets[i]) * HKV;
+      __nv_bfloat16* K = static_cast<__nv_bfloat16*>(c.k);
+      __nv_bfloat16* V = static_cast<__nv_bfloat16*>(c.v);
+      for (int e = tid; e < HKV * (D / 2); e += NTHREADS) {
+        const int h = e / (D / 2), d = e % (D / 2);
+        const __nv_bfloat16* kr = p.k_new + ((int64_t)i * HKV + h) * D;
+        float r0, r1;
+        rope_rotate<float, float>(__bfloat162float(kr[d]), __bfloat162float(kr[d + D / 2]), pos, p.inv_freq[d], r0, r1);
+        const __nv_bfloat16 b0 = __float2bfloat16_rn(r0), b1 = __float2bfloat16_rn(r1);
+        knew_s[h * D + d] = b0;
+        knew_s[h * D + d + D / 2] = b1;
+        K[(row + h) * D + d] = b0;
+        K[(row + h) * D + d + D / 2] = b1;
+      }
+      for (int e = tid; e < HKV * D; e += NTHREADS) {
+        const __nv_bfloat16 x = p.v_new[(int64_t)i * HKV * D + e];
+        vnew_s[e] = x;
+        V[row * D + e] = x;
+      }
+    }
+    (void)slot;
+    __syncthreads();
+    const __nv_bfloat16* qh = q_s + (warp * G + g) * D;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      bq[kk][0] = g < G ? *reinterpret_cast<const uint32_t*>(qh + kk * 16 + 2 * t) : 0u;
+      bq[kk][1] = g < G ? *reinterpret_cast<const uint32_t*>(qh + kk * 16 + 2 * t + 8) : 0u;
+    }
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
+    m0 = m1 = -INFINITY;
+    l0 = l1 = 0.f;
+  };
+
+  for (int gb = g0; gb < g1; ++gb) {
+    const int it = gb - g0;
+    const int st = it % STAGES;
+    if (gb + STAGES - 1 < g1) issue(gb + STAGES - 1, (it + STAGES - 1) % STAGES);
+    cp_async_commit();
+    cp_async_wait<STAGES - 1>();
+    __syncthreads();
+
+    const int i = seq_of(gb);
+    if (i != cur) {
+      if (cur >= 0) finish(cur);
+      start(i);
+      cur = i;
+    }
+    const int j = gb - s_pref[i];
+    const int nb = s_pref[i + 1] - s_pref[i];
+    const int n = c.lengths[p.seq_slots[i]];
+    const int valid = (j == nb - 1) ? n - j * BS : BS;
+    uint8_t* kst = stages + st * STAGE_BYTES;
+    uint8_t* vst = kst + KV_BLOCK_BYTES;
+    if (j == nb - 1) {
+      // the prefetch may predate the append: patch the new token's rows in shared memory
+      const int off = p.slot_offsets[i];
+      const int r = off * HKV + (tid >> 4) % HKV, ch = tid & 15;  // 256 threads = 8 heads x 16 chunks
+      const __nv_bfloat16* srck = (tid < HKV * 16) ? knew_s + ((tid >> 4)) * D + ch * 8 : nullptr;
+      if (tid < HKV * 16) {
+        *reinterpret_cast<int4*>(kst + swz(r, ch)) = *reinterpret_cast<const int4*>(srck);
+        *reinterpret_cast<int4*>(vst + swz(r, ch)) =
+            *reinterpret_cast<const int4*>(vnew_s + (tid >> 4) * D + ch * 8);
+      }
+      __syncthreads();
+    }
+
+    // ---- S^T = K . Q^T  (16 tokens x 8 head columns)
+    const uint32_t kbase = smem_u32(kst), vbase = smem_u32(vst);
+    float sc[4] = {0.f, 0.f, 0.f, 0.f};
+    {
+      const int mi = lane >> 3, rr = lane & 7;
+      const int tok = rr + ((mi & 1) << 3);
+      const int row = tok * HKV + warp;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(kbase + swz(row, 2 * kk + (mi >> 1)), a0, a1, a2, a3);
+        mma_bf16(sc, a0, a1, a2, a3, bq[kk][0], bq[kk][1]);
+      }
+    }
+    // ---- online softmax (base 2); lane holds tokens g, g+8 and heads 2t, 2t+1
+    float s0 = sc[0] * p.scale_log2, s1 = sc[1] * p.scale_log2;
+    float s2 = sc[2] * p.scale_log2, s3 = sc[3] * p.scale_log2;
+    if (g >= valid) s0 = s1 = -INFINITY;
+    if (g + 8 >= valid) s2 = s3 = -INFINITY;
+    const float bm0 = warp_max_rows(fmaxf(s0, s2));
+    const float bm1 = warp_max_rows(fmaxf(s1, s3));
+    const float mn0 = fmaxf(m0, bm0), mn1 = fmaxf(m1, bm1);
+    const float al0 = exp2f(m0 - mn0), al1 = exp2f(m1 - mn1);
+    const float p0 = exp2f(s0 - mn0), p1 = exp2f(s1 - mn1);
+    const float p2 = exp2f(s2 - mn0), p3 = exp2f(s3 - mn1);
+    l0 = l0 * al0 + p0 + p2;
+    l1 = l1 * al1 + p1 + p3;
+    m0 = mn0;
+    m1 = mn1;
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) {
+      acc[mt][0] *= al0;
+      acc[mt][1] *= al1;
+      acc[mt][2] *= al0;
+      acc[mt][3] *= al1;
+    }
+    const uint32_t pb0 = movm_t(pack_bf16(p0, p1));  // P[head g][tokens 2t, 2t+1]
+    const uint32_t pb1 = movm_t(pack_bf16(p2, p3));  // P[head g][tokens 8+2t, 9+2t]
+    // ---- O^T += V^T . P^T
+    {
+      const int mi = lane >> 3, rr = lane & 7;
+      const int tok = rr + ((mi >> 1) << 3);
+      const int row = tok * HKV + warp;
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4_t(vbase + swz(row, 2 * mt + (mi & 1)), a0, a1, a2, a3);
+        mma_bf16(acc[mt], a0, a1, a2, a3, pb0, pb1);
+      }
+    }
+    __syncthreads();  // the stage is refilled by the next iteration's prefetch
+  }
+  cp_async_wait<0>();
+  if (cur >= 0) finish(cur);
+}
+
+std::mutex g_attr_mu;
+bool g_attr_done[64] = {};
+
+}  // namespace
+
+// ---------------------------------------------------------------------------- host
+size_t kvs_decode_bf16_scratch(int num_seqs, int grid) {
+  const size_t slots = (size_t)grid + num_seqs;
+  return align_up(slots * HQ * D * 4, 256) + align_up(slots * HQ * 2 * 4, 256) + align_up((size_t)num_seqs * 4, 256);
+}
+
+bool kvs_decode_bf16_supported(const kvs_cache* c, const kvs_batch* b, int n_heads) {
+  return c->dtype == KVS_BF16 && c->head_dim == D && c->block_size == BS && c->n_kv_heads == HKV &&
+         n_heads == HQ && b->cu_tokens == nullptr && b->num_seqs <= MAX_SEQS;
+}
+
+int kvs_decode_bf16_grid(int override_ctas) {
+  if (override_ctas > 0) return override_ctas;
+  const int sms = kvs_device_sm_count();
+  return sms > 0 ? sms : 148;
+}
+
+int kvs_decode_bf16_launch(const kvs_cache* c, const kvs_batch* b, const kvs_decode_args* a, int grid,
+                           cudaStream_t st) {
+  if (a->scratch_bytes < kvs_decode_bf16_scratch(b->num_seqs, grid) || !a->scratch) return KVS_E_SCRATCH;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> lock(g_attr_mu);
+    if (dev < 64 && !g_attr_done[dev]) {
+      if (cudaFuncSetAttribute(decode_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_TOTAL) !=
+          cudaSuccess)
+        return KVS_E_LAUNCH;
+      g_attr_done[dev] = true;
+    }
+  }
+  DecodeParams p;
+  p.c = *c;
+  p.seq_slots = b->seq_slots;
+  p.num_seqs = b->num_seqs;
+  p.layer = a->layer;
+  p.q = static_cast<const __nv_bfloat16*>(a->q);
+  p.k_new = static_cast<const __nv_bfloat16*>(a->k_new);
+  p.v_new = static_cast<const __nv_bfloat16*>(a->v_new);
+  p.positions = a->positions;
+  p.slot_blocks = a->slot_blocks;
+  p.slot_offsets = a->slot_offsets;
+  p.inv_freq = static_cast<const float*>(a->inv_freq);
+  p.out = static_cast<__nv_bfloat16*>(a->out);
+  const size_t slots = (size_t)grid + b->num_seqs;
+  uint8_t* s = static_cast<uint8_t*>(a->scratch);
+  p.part_o = reinterpret_cast<float*>(s);
+  p.part_ml = reinterpret_cast<float*>(s + align_up(slots * HQ * D * 4, 256));
+  p.counters = reinterpret_cast<int32_t*>(s + align_up(slots * HQ * D * 4, 256) + align_up(slots * HQ * 2 * 4, 256));
+  p.scale_log2 = (float)(a->scale * 1.4426950408889634);
+  decode_bf16_kernel<<<grid, NTHREADS, SMEM_TOTAL, st>>>(p);
+  return launch_rc();
+}

@@ -3,6 +3,11 @@
 #include "kvs_common.cuh"
 
 int kvs_decode_generic(const kvs_cache* c, const kvs_batch* b, const kvs_decode_args* a, cudaStream_t st);
+size_t kvs_decode_bf16_scratch(int num_seqs, int grid);
+bool kvs_decode_bf16_supported(const kvs_cache* c, const kvs_batch* b, int n_heads);
+int kvs_decode_bf16_grid(int override_ctas);
+int kvs_decode_bf16_launch(const kvs_cache* c, const kvs_batch* b, const kvs_decode_args* a, int grid,
+                           cudaStream_t st);
 int kvs_replay_generic(const kvs_replay_args* a, cudaStream_t st);
 
 using namespace kvs;
@@ -15,9 +20,11 @@ void kvs::count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 KVS_API long long kvs_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 KVS_API size_t kvs_decode_scratch_bytes(const kvs_cache* c, int32_t num_seqs, int32_t n_heads,
-                                        int32_t split_blocks) {
-  (void)c; (void)num_seqs; (void)n_heads; (void)split_blocks;
-  return 0;
+                                        int32_t grid_ctas) {
+  if (!c || num_seqs <= 0) return 0;
+  const kvs_batch probe = {nullptr, nullptr, num_seqs, num_seqs};
+  if (!kvs_decode_bf16_supported(c, &probe, n_heads)) return 0;
+  return kvs_decode_bf16_scratch(num_seqs, kvs_decode_bf16_grid(grid_ctas));
 }
 
 KVS_API int kvs_paged_decode(const kvs_cache* c, const kvs_batch* b, const kvs_decode_args* a,
@@ -29,6 +36,8 @@ KVS_API int kvs_paged_decode(const kvs_cache* c, const kvs_batch* b, const kvs_d
   if (a->layer < 0 || a->layer >= c->n_layers || a->n_heads <= 0 || a->n_heads % c->n_kv_heads)
     return KVS_E_ARG;
   if (b->num_seqs == 0) return KVS_OK;
+  if (kvs_decode_bf16_supported(c, b, a->n_heads))
+    return kvs_decode_bf16_launch(c, b, a, kvs_decode_bf16_grid(a->grid_ctas), to_cuda(stream));
   return kvs_decode_generic(c, b, a, to_cuda(stream));
 }
 

@@ -99,7 +99,7 @@ class KvsDecodeArgs(C.Structure):
         ("scale", C.c_double),
         ("layer", C.c_int32),
         ("n_heads", C.c_int32),
-        ("split_blocks", C.c_int32),
+        ("grid_ctas", C.c_int32),
         ("reserved", C.c_int32),
     ]
 

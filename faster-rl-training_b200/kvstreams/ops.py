@@ -98,7 +98,7 @@ def replay_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, evicted_
 def paged_forward(cache, slots: Sequence[int], counts: Optional[Sequence[int]], layer: int, q: torch.Tensor,
                   k_new: torch.Tensor, v_new: torch.Tensor, positions: torch.Tensor, mapping,
                   inv_freq: torch.Tensor, scale: float, out: Optional[torch.Tensor] = None,
-                  split_blocks: int = 0) -> torch.Tensor:
+                  grid_ctas: int = 0) -> torch.Tensor:
     """One layer of the paged incremental forward (model.py:50-75 + hook :182-185) for the
     new tokens of a batch of sequences: RoPE of q/k, append of k/v, paged GQA attention.
 
@@ -112,14 +112,14 @@ def paged_forward(cache, slots: Sequence[int], counts: Optional[Sequence[int]], 
         out = torch.empty_like(q)
     b, keep = cache._batch(slots, counts)
     lib = N.lib()
-    nbytes = int(lib.kvs_decode_scratch_bytes(C.byref(cache.struct), b.num_seqs, q.shape[1], split_blocks))
+    nbytes = int(lib.kvs_decode_scratch_bytes(C.byref(cache.struct), b.num_seqs, q.shape[1], grid_ctas))
     scratch = cache._decode_scratch(nbytes) if nbytes else None
     a = N.KvsDecodeArgs(q=q.data_ptr(), k_new=k_new.data_ptr(), v_new=v_new.data_ptr(), positions=pos.data_ptr(),
                         slot_blocks=mapping.blocks.data_ptr(), slot_offsets=mapping.offsets.data_ptr(),
                         inv_freq=inv_freq.data_ptr(), out=out.data_ptr(),
                         scratch=scratch.data_ptr() if scratch is not None else None,
                         scratch_bytes=scratch.numel() if scratch is not None else 0, scale=float(scale),
-                        layer=int(layer), n_heads=int(q.shape[1]), split_blocks=int(split_blocks))
+                        layer=int(layer), n_heads=int(q.shape[1]), grid_ctas=int(grid_ctas))
     N.check(lib.kvs_paged_decode(C.byref(cache.struct), C.byref(b), C.byref(a), N.stream_ptr(q.device)),
             "kvs_paged_decode")
     return out

@@ -229,11 +229,13 @@ typedef struct kvs_decode_args {
   double scale;             /* head_dim**-0.5 (model.py:71) */
   int32_t layer;
   int32_t n_heads;
-  int32_t split_blocks;     /* KV blocks per split (0 = library default) */
+  int32_t grid_ctas;        /* CTAs of the fused decode kernel (0 = one per SM) */
   int32_t reserved;
 } kvs_decode_args;
+/* scratch of kvs_paged_decode: split partials and per-sequence arrival counters;
+ * zero it once when allocated (the kernel leaves the counters at zero). */
 size_t kvs_decode_scratch_bytes(const kvs_cache* c, int32_t num_seqs, int32_t n_heads,
-                                int32_t split_blocks);
+                                int32_t grid_ctas);
 int kvs_paged_decode(const kvs_cache* c, const kvs_batch* b, const kvs_decode_args* a,
                      kvs_stream_t stream);
 
