@@ -45,11 +45,14 @@ constexpr int STAGE_BYTES = 2 * KV_BLOCK_BYTES;
 constexpr int MAX_SEQS = 1024;
 constexpr int CHUNKS = KV_BLOCK_BYTES / 16;            // 2048 16-byte chunks per K (or V) block
 
+constexpr int TAB_CAP = 2048;  // table entries of one CTA's range staged in shared memory
+
 constexpr int SMEM_STAGES = STAGES * STAGE_BYTES;
 constexpr int SMEM_Q = HQ * D * 2;
 constexpr int SMEM_NEW = 2 * HKV * D * 2;
 constexpr int SMEM_PREF = (MAX_SEQS + 1) * 4;
-constexpr int SMEM_TOTAL = SMEM_STAGES + SMEM_Q + SMEM_NEW + SMEM_PREF + 64;
+constexpr int SMEM_TAB = TAB_CAP * 4;
+constexpr int SMEM_TOTAL = SMEM_STAGES + SMEM_Q + SMEM_NEW + SMEM_PREF + SMEM_TAB + 256;
 
 struct DecodeParams {
   kvs_cache c;
@@ -132,21 +135,34 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
   __nv_bfloat16* knew_s = reinterpret_cast<__nv_bfloat16*>(smem + SMEM_STAGES + SMEM_Q);
   __nv_bfloat16* vnew_s = knew_s + HKV * D;
   int* s_pref = reinterpret_cast<int*>(smem + SMEM_STAGES + SMEM_Q + SMEM_NEW);
-  int* s_flag = s_pref + MAX_SEQS + 1;
+  int* s_tab = s_pref + MAX_SEQS + 1;
+  int* s_flag = s_tab + TAB_CAP;
+  int* s_scan = s_flag + 4;  // 33 ints
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;
   const kvs_cache& c = p.c;
   const int S = p.num_seqs;
 
-  // prefix sums of table lengths (blocks) over the batch
-  if (tid == 0) {
-    int acc = 0;
-    s_pref[0] = 0;
-    for (int i = 0; i < S; ++i) {
-      acc += (c.lengths[p.seq_slots[i]] + BS - 1) / BS;
-      s_pref[i + 1] = acc;
+  // prefix sums of table lengths (blocks) over the batch: thread tid owns sequences
+  // 4*tid .. 4*tid+3 (MAX_SEQS = 4 * NTHREADS), one block-wide scan
+  {
+    int nb[4], sum = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int i = 4 * tid + k;
+      nb[k] = i < S ? (c.lengths[p.seq_slots[i]] + BS - 1) / BS : 0;
+      sum += nb[k];
     }
+    int total_nb = 0;
+    int run = block_exclusive_scan(sum, s_scan, &total_nb);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int i = 4 * tid + k;
+      if (i < S) s_pref[i] = run;
+      run += nb[k];
+    }
+    if (tid == 0) s_pref[S] = total_nb;
   }
   __syncthreads();
   const int total = s_pref[S];
@@ -168,11 +184,24 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
     return lo;
   };
 
+  // block ids of this CTA's range, gathered once (the copies below then need no global lookups)
+  const bool tab_in_smem = (g1 - g0) <= TAB_CAP;
+  if (tab_in_smem) {
+    for (int gb = g0 + tid; gb < g1; gb += NTHREADS) {
+      const int i = seq_of(gb);
+      s_tab[gb - g0] = c.tables[(int64_t)p.seq_slots[i] * c.max_blocks + (gb - s_pref[i])];
+    }
+    __syncthreads();
+  }
+
   auto issue = [&](int gb, int st) {
-    const int i = seq_of(gb);
-    const int j = gb - s_pref[i];
-    const int slot = p.seq_slots[i];
-    const int64_t blk = c.tables[(int64_t)slot * c.max_blocks + j];
+    int64_t blk;
+    if (tab_in_smem) {
+      blk = s_tab[gb - g0];
+    } else {
+      const int i = seq_of(gb);
+      blk = c.tables[(int64_t)p.seq_slots[i] * c.max_blocks + (gb - s_pref[i])];
+    }
     const uint8_t* ks = Kpool + (layer_rows + blk) * KV_BLOCK_BYTES;
     const uint8_t* vs = Vpool + (layer_rows + blk) * KV_BLOCK_BYTES;
     const uint32_t kd = smem_u32(stages + st * STAGE_BYTES);
@@ -249,19 +278,68 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
     __syncthreads();
     if (*s_flag) {
       __threadfence();
-      for (int e = tid; e < HQ * D; e += NTHREADS) {
-        const int h = e / D;
-        float M = -INFINITY;
-        for (int cc = c0; cc <= c1; ++cc)
-          M = fmaxf(M, __ldcg(p.part_ml + ((int64_t)(cc + i) * HQ + h) * 2));
-        float num = 0.f, den = 0.f;
-        for (int cc = c0; cc <= c1; ++cc) {
-          const float* ml = p.part_ml + ((int64_t)(cc + i) * HQ + h) * 2;
-          const float w = exp2f(__ldcg(ml) - M);
-          den += w * __ldcg(ml + 1);
-          num += w * __ldcg(p.part_o + (int64_t)(cc + i) * HQ * D + e);
+      // weights w[h][k] = 2^(m_k - M_h) / sum_k 2^(m_k - M_h) l_k, kept in q_s (its q is already in
+      // registers; start() rewrites it); partials beyond COMBINE_CAP fall back to direct loops
+      constexpr int COMBINE_CAP = SMEM_Q / 4 / HQ;  // 64 partials
+      float* w_s = reinterpret_cast<float*>(q_s);
+      if (expected <= COMBINE_CAP) {
+        for (int e = tid; e < HQ * expected; e += NTHREADS) {
+          const int h = e / expected, k = e % expected;
+          w_s[h * COMBINE_CAP + k] = __ldcg(p.part_ml + ((int64_t)(c0 + k + i) * HQ + h) * 2);
         }
-        p.out[(int64_t)i * HQ * D + e] = __float2bfloat16_rn(num / den);
+        __syncthreads();
+        if (tid < HQ) {
+          float M = -INFINITY, den = 0.f;
+          for (int k = 0; k < expected; ++k) M = fmaxf(M, w_s[tid * COMBINE_CAP + k]);
+          for (int k = 0; k < expected; ++k) {
+            const float wk = exp2f(w_s[tid * COMBINE_CAP + k] - M);
+            den += wk * __ldcg(p.part_ml + ((int64_t)(c0 + k + i) * HQ + tid) * 2 + 1);
+            w_s[tid * COMBINE_CAP + k] = wk;
+          }
+          const float inv = 1.f / den;
+          for (int k = 0; k < expected; ++k) w_s[tid * COMBINE_CAP + k] *= inv;
+        }
+        __syncthreads();
+        // thread -> head tid/8, dims 16*(tid%8) .. +16: four independent float4 loads per partial
+        const int h = tid >> 3, d0 = (tid & 7) * 16;
+        float4 o[4] = {};
+#pragma unroll 4
+        for (int k = 0; k < expected; ++k) {
+          const float wk = w_s[h * COMBINE_CAP + k];
+          const float4* src = reinterpret_cast<const float4*>(p.part_o + ((int64_t)(c0 + k + i) * HQ + h) * D + d0);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            const float4 x = __ldcg(src + v);
+            o[v].x += wk * x.x;
+            o[v].y += wk * x.y;
+            o[v].z += wk * x.z;
+            o[v].w += wk * x.w;
+          }
+        }
+        uint32_t packed[8];
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          packed[2 * v] = pack_bf16(o[v].x, o[v].y);
+          packed[2 * v + 1] = pack_bf16(o[v].z, o[v].w);
+        }
+        int4* dst = reinterpret_cast<int4*>(p.out + ((int64_t)i * HQ + h) * D + d0);
+        dst[0] = make_int4(packed[0], packed[1], packed[2], packed[3]);
+        dst[1] = make_int4(packed[4], packed[5], packed[6], packed[7]);
+      } else {
+        for (int e = tid; e < HQ * D; e += NTHREADS) {
+          const int h = e / D;
+          float M = -INFINITY;
+          for (int cc = c0; cc <= c1; ++cc)
+            M = fmaxf(M, __ldcg(p.part_ml + ((int64_t)(cc + i) * HQ + h) * 2));
+          float num = 0.f, den = 0.f;
+          for (int cc = c0; cc <= c1; ++cc) {
+            const float* ml = p.part_ml + ((int64_t)(cc + i) * HQ + h) * 2;
+            const float w = exp2f(__ldcg(ml) - M);
+            den += w * __ldcg(ml + 1);
+            num += w * __ldcg(p.part_o + (int64_t)(cc + i) * HQ * D + e);
+          }
+          p.out[(int64_t)i * HQ * D + e] = __float2bfloat16_rn(num / den);
+        }
       }
       if (tid == 0) p.counters[i] = 0;  // ready for the next launch
     }
@@ -333,8 +411,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
     }
     const int j = gb - s_pref[i];
     const int nb = s_pref[i + 1] - s_pref[i];
-    const int n = c.lengths[p.seq_slots[i]];
-    const int valid = (j == nb - 1) ? n - j * BS : BS;
+    // the new token is the last live entry, at offset slot_offsets[i] of the last block
+    const int valid = (j == nb - 1) ? p.slot_offsets[i] + 1 : BS;
     uint8_t* kst = stages + st * STAGE_BYTES;
     uint8_t* vst = kst + KV_BLOCK_BYTES;
     if (j == nb - 1) {

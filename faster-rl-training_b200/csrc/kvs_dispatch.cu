@@ -36,7 +36,9 @@ KVS_API int kvs_paged_decode(const kvs_cache* c, const kvs_batch* b, const kvs_d
   if (a->layer < 0 || a->layer >= c->n_layers || a->n_heads <= 0 || a->n_heads % c->n_kv_heads)
     return KVS_E_ARG;
   if (b->num_seqs == 0) return KVS_OK;
-  if (kvs_decode_bf16_supported(c, b, a->n_heads))
+  // the fused kernel stores outputs with 16-byte vector writes
+  const bool out_aligned = (reinterpret_cast<uintptr_t>(a->out) & 15) == 0;
+  if (out_aligned && kvs_decode_bf16_supported(c, b, a->n_heads))
     return kvs_decode_bf16_launch(c, b, a, kvs_decode_bf16_grid(a->grid_ctas), to_cuda(stream));
   return kvs_decode_generic(c, b, a, to_cuda(stream));
 }

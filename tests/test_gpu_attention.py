@@ -48,21 +48,23 @@ def _setup_cache(dtype, D, Hkv, bs, S, ctx, seed):
     return cache, st
 
 
-@pytest.mark.parametrize("dtype,D,Hq,Hkv,bs,T", [
-    (torch.float64, 16, 4, 2, 16, 1),
-    (torch.float64, 16, 4, 2, 4, 5),
-    (torch.float32, 16, 4, 2, 16, 1),
-    (torch.float32, 32, 8, 2, 1, 3),
-    (torch.bfloat16, 128, 32, 8, 16, 1),
-    (torch.bfloat16, 128, 32, 8, 16, 7),
-    (torch.bfloat16, 64, 8, 8, 1, 1),
+@pytest.mark.parametrize("dtype,D,Hq,Hkv,bs,T,S,ctx", [
+    (torch.float64, 16, 4, 2, 16, 1, 5, (3, 200)),
+    (torch.float64, 16, 4, 2, 4, 5, 5, (3, 200)),
+    (torch.float32, 16, 4, 2, 16, 1, 5, (3, 200)),
+    (torch.float32, 32, 8, 2, 1, 3, 5, (3, 200)),
+    (torch.bfloat16, 128, 32, 8, 16, 1, 5, (3, 200)),
+    # fused kernel with CTA ranges spanning several sequences and sequences spanning several CTAs
+    (torch.bfloat16, 128, 32, 8, 16, 1, 12, (500, 3000)),
+    (torch.bfloat16, 128, 32, 8, 16, 1, 40, (16, 40)),
+    (torch.bfloat16, 128, 32, 8, 16, 7, 5, (3, 200)),
+    (torch.bfloat16, 64, 8, 8, 1, 1, 5, (3, 200)),
 ])
-def test_paged_forward_matches_oracle(dtype, D, Hq, Hkv, bs, T):
+def test_paged_forward_matches_oracle(dtype, D, Hq, Hkv, bs, T, S, ctx):
     from kvstreams import ops
     from kvstreams.rope import RotaryEmbedding
 
-    S = 5
-    cache, st = _setup_cache(dtype, D, Hkv, bs, S, (3, 200), seed=D + T)
+    cache, st = _setup_cache(dtype, D, Hkv, bs, S, ctx, seed=D + T + S)
     theta = 5e5 if D == 128 else 1e4
     rope = RotaryEmbedding(D, theta)
     g = torch.Generator(device="cuda").manual_seed(7)
