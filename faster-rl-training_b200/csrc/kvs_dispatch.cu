@@ -9,6 +9,9 @@ int kvs_decode_bf16_grid(int override_ctas);
 int kvs_decode_bf16_launch(const kvs_cache* c, const kvs_batch* b, const kvs_decode_args* a, int grid,
                            cudaStream_t st);
 int kvs_replay_generic(const kvs_replay_args* a, cudaStream_t st);
+size_t kvs_replay_tc_scratch(int B, int T);
+bool kvs_replay_tc_supported(const kvs_replay_args* a);
+int kvs_replay_tc_launch(const kvs_replay_args* a, cudaStream_t st);
 
 using namespace kvs;
 
@@ -44,8 +47,8 @@ KVS_API int kvs_paged_decode(const kvs_cache* c, const kvs_batch* b, const kvs_d
 }
 
 KVS_API size_t kvs_replay_scratch_bytes(int32_t batch, int32_t seq_len) {
-  (void)batch; (void)seq_len;
-  return 0;
+  if (batch <= 0 || seq_len <= 0) return 0;
+  return kvs_replay_tc_scratch(batch, seq_len);
 }
 
 KVS_API int kvs_replay_attention(const kvs_replay_args* a, kvs_stream_t stream) {
@@ -54,5 +57,6 @@ KVS_API int kvs_replay_attention(const kvs_replay_args* a, kvs_stream_t stream) 
       a->head_dim <= 0)
     return KVS_E_ARG;
   if (a->batch == 0 || a->seq_len == 0) return KVS_OK;
+  if (!(a->flags & 1) && kvs_replay_tc_supported(a)) return kvs_replay_tc_launch(a, to_cuda(stream));
   return kvs_replay_generic(a, to_cuda(stream));
 }

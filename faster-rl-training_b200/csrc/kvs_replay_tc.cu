@@ -1,0 +1,562 @@
+// Masked replay attention on the 5th-generation tensor cores (tcgen05 / TMEM), bf16,
+// head_dim 128: the trainer's one-pass replay of a KV-streams rollout
+// (TinyLM.forward attention, model.py:71-74, under the mask of replay.py:55-63):
+//
+//   visible(t, s) = s <= t && t < evicted_at[b][s]     (t < lengths[b])
+//   visible(t, s) = s == t                             (padded rows, collate replay.py:221-222)
+//
+// CTA = (stream b, query head h, 128-query tile).  Warp roles (192 threads):
+//   warp 0      TMA producer: Q tile once; per active key tile the K and V tiles
+//               (128 keys x 128 dims, 128-byte swizzle) and the tile's evicted_at
+//               values, into a 2-slot ring;
+//   warp 1      TMEM owner + UMMA issuer: S[k%2] = Q K^T (8 x M128 N128 K16) into
+//               TMEM, then O += P V (P from shared memory, V MN-major) into TMEM;
+//   warps 2..5  softmax: one thread per query row (TMEM lane), online softmax in
+//               fp32 base 2 with a lazy rescale (O is only rescaled when the row max
+//               grew by more than 2^8), P written as bf16 into a 2-slot smem ring.
+// TMEM: S0 cols [0,128), S1 [128,256), O [256,384) of a 512-column allocation.
+//
+// Tile skipping: per 128-key tile the prepass records min/max evicted_at; a key
+// tile is skipped when every key in it was evicted at or before the tile's first
+// query, or lies above the diagonal; tiles fully visible to every row of the query
+// tile run without per-element masking.
+#include "kvs_common.cuh"
+#include "kvs_sm100.cuh"
+
+#include <mutex>
+
+using namespace kvs;
+using namespace kvs::sm100;
+
+namespace {
+
+constexpr int BM = 128, BN = 128, HD = 128;
+constexpr int NT = 192;
+constexpr int HALF_BYTES = 128 * 64 * 2;  // 128 rows x 64 bf16 (one 128-byte swizzled half tile)
+constexpr int TILE_BYTES = 2 * HALF_BYTES;  // 128 x 128 bf16
+constexpr int E_BYTES = BN * 4;
+
+// shared memory map (offsets from a 1024-byte aligned base)
+constexpr int OFF_Q = 0;
+constexpr int OFF_K = OFF_Q + TILE_BYTES;          // 2 slots
+constexpr int OFF_V = OFF_K + 2 * TILE_BYTES;      // 2 slots
+constexpr int OFF_P = OFF_V + 2 * TILE_BYTES;      // 2 slots
+constexpr int OFF_E = OFF_P + 2 * TILE_BYTES;      // 2 slots of 128 int32
+constexpr int OFF_LIST = OFF_E + 2 * E_BYTES;      // active key tiles (<= 512 entries)
+constexpr int MAX_KT = 256;  // key tiles per stream: T <= 32768
+constexpr int OFF_BAR = OFF_LIST + MAX_KT * 2;
+constexpr int NBAR = 13;
+constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+constexpr int SMEM_BYTES = OFF_MISC + 64 + 33 * 4 + 1024;  // + alignment slack
+static_assert(SMEM_BYTES <= 232448, "replay kernel shared memory");
+
+enum { B_FULL0 = 0, B_FULL1, B_EMPTY0, B_EMPTY1, B_QFULL, B_SFULL0, B_SFULL1, B_SFREE0, B_SFREE1,
+       B_PFULL0, B_PFULL1, B_ODONE, B_FINAL };
+
+struct ReplayParams {
+  const int32_t* e32;      // [B][T_pad] evicted_at clamped to int32, 0 past T
+  const int32_t* tile_min; // [B][n_kt]
+  const int32_t* tile_max; // [B][n_kt]
+  const int32_t* lengths;  // [B]
+  __nv_bfloat16* out;      // [B][T][Hq][D]
+  int32_t* error;          // [1]
+  int B, T, T_pad, Hq, Hkv, n_qt, n_kt;
+  float scale_log2;
+};
+
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__global__ void __launch_bounds__(NT, 1)
+replay_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                 const __grid_constant__ CUtensorMap tm_v, const ReplayParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* Qs = smem + OFF_Q;
+  uint16_t* list = reinterpret_cast<uint16_t*>(smem + OFF_LIST);  // key tile | 0x8000 if masked
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + 4);
+  int* s_n = reinterpret_cast<int*>(smem + OFF_MISC + 8);
+  int* s_scan = reinterpret_cast<int*>(smem + OFF_MISC + 64);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // heaviest query tiles (most key tiles) first
+  const int bh_count = p.B * p.Hq;
+  const int qt = p.n_qt - 1 - (int)(blockIdx.x / bh_count);
+  const int bh = (int)(blockIdx.x % bh_count);
+  const int b = bh / p.Hq, h = bh % p.Hq;
+  const int hk = h / (p.Hq / p.Hkv);
+  const int t0 = qt * BM, t1 = t0 + BM - 1;
+  const int L = p.lengths[b];
+
+  if (tid == 0) {
+    for (int i = 0; i < NBAR; ++i) mbar_init(&bar[i], 1);
+    mbar_init(&bar[B_SFREE0], 128);
+    mbar_init(&bar[B_SFREE1], 128);
+    mbar_init(&bar[B_PFULL0], 128);
+    mbar_init(&bar[B_PFULL1], 128);
+    *abort_flag = 0;
+    mbar_fence_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+
+  // ---- active key tiles for this query tile (same list for every role)
+  {
+    const int real_last = min(t1, L - 1);
+    int carry = 0;
+    for (int base = 0; base <= qt; base += NT) {
+      const int j = base + tid;
+      int flag = 0;
+      if (j <= qt) {
+        const int emin = p.tile_min[b * p.n_kt + j], emax = p.tile_max[b * p.n_kt + j];
+        const bool active = (j == qt) || (j * BN <= real_last && emax > t0);
+        const bool masked = (j == qt) || (emin <= t1) || (t1 >= L);
+        flag = (active ? 1 : 0) | (masked ? 2 : 0);
+      }
+      int tot = 0;
+      const int pre = block_exclusive_scan(flag & 1, s_scan, &tot);
+      if (flag & 1) list[carry + pre] = (uint16_t)(j | ((flag & 2) ? 0x8000 : 0));
+      carry += tot;
+      __syncthreads();
+    }
+    if (tid == 0) *s_n = carry;
+  }
+  __syncthreads();
+  tc_fence_after();
+  const int n = *s_n;
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t S_col = 0, O_col = 256;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&bar[B_QFULL], TILE_BYTES);
+      tma_load_3d(Qs, &tm_q, 0, h, b * p.T + t0, &bar[B_QFULL]);
+      tma_load_3d(Qs + HALF_BYTES, &tm_q, 64, h, b * p.T + t0, &bar[B_QFULL]);
+      for (int k = 0; k < n; ++k) {
+        const int slot = k & 1;
+        if (k >= 2 && !mbar_wait(&bar[B_EMPTY0 + slot], ((k >> 1) - 1) & 1, abort_flag)) {
+          *abort_flag = 1;
+          atomicExch(p.error, 1);
+          break;
+        }
+        const int j = list[k] & 0x7fff;
+        const int row = b * p.T + j * BN;
+        uint8_t* Ks = smem + OFF_K + slot * TILE_BYTES;
+        uint8_t* Vs = smem + OFF_V + slot * TILE_BYTES;
+        mbar_arrive_expect_tx(&bar[B_FULL0 + slot], 2 * TILE_BYTES + E_BYTES);
+        tma_load_3d(Ks, &tm_k, 0, hk, row, &bar[B_FULL0 + slot]);
+        tma_load_3d(Ks + HALF_BYTES, &tm_k, 64, hk, row, &bar[B_FULL0 + slot]);
+        tma_load_3d(Vs, &tm_v, 0, hk, row, &bar[B_FULL0 + slot]);
+        tma_load_3d(Vs + HALF_BYTES, &tm_v, 64, hk, row, &bar[B_FULL0 + slot]);
+        bulk_load(smem + OFF_E + slot * E_BYTES, p.e32 + (int64_t)b * p.T_pad + j * BN, E_BYTES,
+                  &bar[B_FULL0 + slot]);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ UMMA issuer
+    if (lane == 0) {
+      constexpr uint32_t ID_QK = idesc_bf16(128, 128, 0);
+      constexpr uint32_t ID_PV = idesc_bf16(128, 128, 1);
+      const uint32_t q_base = smem_addr(Qs);
+      bool ok = mbar_wait(&bar[B_QFULL], 0, abort_flag);
+      for (int k = 0; ok && k <= n; ++k) {
+        if (k < n) {
+          const int slot = k & 1;
+          ok = mbar_wait(&bar[B_FULL0 + slot], (k >> 1) & 1, abort_flag);
+          if (ok && k >= 2) ok = mbar_wait(&bar[B_SFREE0 + slot], ((k >> 1) - 1) & 1, abort_flag);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t k_base = smem_addr(smem + OFF_K + slot * TILE_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint32_t off = (kk >> 2) * HALF_BYTES + (kk & 3) * 32;
+            umma_bf16(tmem + S_col + slot * 128, desc_kmajor_sw128(q_base + off), desc_kmajor_sw128(k_base + off),
+                      ID_QK, kk > 0);
+          }
+          umma_commit(&bar[B_SFULL0 + slot]);
+        }
+        if (k >= 1) {
+          const int pk = k - 1, ps = pk & 1;
+          ok = mbar_wait(&bar[B_PFULL0 + ps], (pk >> 1) & 1, abort_flag);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t p_base = smem_addr(smem + OFF_P + ps * TILE_BYTES);
+          const uint32_t v_base = smem_addr(smem + OFF_V + ps * TILE_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint32_t a_off = (kk >> 2) * HALF_BYTES + (kk & 3) * 32;
+            umma_bf16(tmem + O_col, desc_kmajor_sw128(p_base + a_off),
+                      desc_mnmajor_sw128(v_base + kk * 2048, HALF_BYTES), ID_PV, (pk > 0 || kk > 0));
+          }
+          umma_commit(&bar[B_EMPTY0 + ps]);
+          umma_commit(&bar[B_ODONE]);
+        }
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        atomicExch(p.error, 2);
+      }
+      // every issued UMMA has finished before TMEM is released
+      umma_commit(&bar[B_FINAL]);
+      mbar_wait(&bar[B_FINAL], 0, nullptr);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax (one row per thread)
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const int t = t0 + r;
+    const bool real = t < L;
+    const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16);
+    const float sl2 = p.scale_log2;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int k = 0; k < n && ok; ++k) {
+      const int slot = k & 1;
+      const int j = list[k] & 0x7fff;
+      const bool masked = (list[k] >> 15) & 1;
+      const int s0 = j * BN;
+      ok = mbar_wait(&bar[B_SFULL0 + slot], (k >> 1) & 1, abort_flag);
+      if (ok && masked) ok = mbar_wait(&bar[B_FULL0 + slot], (k >> 1) & 1, abort_flag);
+      if (!ok) break;
+      tc_fence_after();
+      const int32_t* E = reinterpret_cast<const int32_t*>(smem + OFF_E + slot * E_BYTES);
+      // pass 1: row max over visible keys
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tl + S_col + slot * 128 + c * 32, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int s = s0 + c * 32 + i;
+          const bool vis = !masked || (real ? (s <= t && t < E[c * 32 + i]) : (s == t));
+          const float x = __uint_as_float(v[i]) * sl2;
+          mx = vis ? fmaxf(mx, x) : mx;
+        }
+      }
+      float alpha = 1.f;
+      bool rescale = false;
+      if (m == -INFINITY) {
+        m = mx;
+      } else if (mx > m + 8.f) {
+        alpha = exp2f(m - mx);
+        m = mx;
+        rescale = true;
+      }
+      const float m_eff = (m == -INFINITY) ? 0.f : m;
+      // pass 2: probabilities -> bf16 P row (128-byte swizzled K-major, like the TMA tiles)
+      float sum = 0.f;
+      uint8_t* Prow = smem + OFF_P + slot * TILE_BYTES + r * 128;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tl + S_col + slot * 128 + c * 32, v);
+        tmem_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const int s = s0 + c * 32 + i;
+          const bool v0 = !masked || (real ? (s <= t && t < E[c * 32 + i]) : (s == t));
+          const bool v1 = !masked || (real ? (s + 1 <= t && t < E[c * 32 + i + 1]) : (s + 1 == t));
+          const float p0 = v0 ? exp2f(__uint_as_float(v[i]) * sl2 - m_eff) : 0.f;
+          const float p1 = v1 ? exp2f(__uint_as_float(v[i + 1]) * sl2 - m_eff) : 0.f;
+          sum += p0 + p1;
+          pk[i >> 1] = pack2(p0, p1);
+        }
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const int ch = c * 4 + q4;  // 16-byte chunk 0..15 of the 256-byte row
+          const int half = ch >> 3, cidx = ch & 7;
+          uint8_t* dst = Prow + half * HALF_BYTES + ((cidx ^ (r & 7)) << 4);
+          *reinterpret_cast<uint4*>(dst) = make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
+        }
+      }
+      l = l * alpha + sum;
+      tc_fence_before();
+      mbar_arrive(&bar[B_SFREE0 + slot]);
+      // O holds every earlier P V once the previous UMMA group is done
+      if (k >= 1) {
+        ok = mbar_wait(&bar[B_ODONE], (k - 1) & 1, abort_flag);
+        if (!ok) break;
+      }
+      if (__any_sync(0xffffffffu, rescale)) {
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t v[32];
+          tmem_ld32(tl + O_col + c * 32, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+          tmem_st32(tl + O_col + c * 32, v);
+        }
+        tmem_wait_st();
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&bar[B_PFULL0 + slot]);
+    }
+    if (ok) ok = mbar_wait(&bar[B_ODONE], (n - 1) & 1, abort_flag);
+    if (!ok) {
+      *abort_flag = 1;
+      atomicExch(p.error, 3);
+    } else {
+      tc_fence_after();
+      const float inv = 1.f / l;
+      __nv_bfloat16* orow = p.out + (((int64_t)b * p.T + t) * p.Hq + h) * HD;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tl + O_col + c * 32, v);
+        tmem_wait_ld();
+        if (t < p.T) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) pk[i >> 1] = pack2(__uint_as_float(v[i]) * inv, __uint_as_float(v[i + 1]) * inv);
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) dst[q4] = make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// per-(stream, key tile) min / max of evicted_at and the padded int32 copy
+__global__ void replay_prepass_kernel(const int64_t* __restrict__ ev, int T, int T_pad, int n_kt,
+                                      int32_t* __restrict__ e32, int32_t* __restrict__ tmin, int32_t* __restrict__ tmax) {
+  const int b = blockIdx.y, j = blockIdx.x;  // one CTA of 128 threads per key tile
+  const int s = j * BN + threadIdx.x;
+  int32_t e = 0;
+  int32_t lo = INT32_MAX, hi = INT32_MIN;
+  if (s < T) {
+    const int64_t x = ev[(int64_t)b * T + s];
+    e = x > INT32_MAX ? INT32_MAX : (int32_t)x;
+    lo = hi = e;
+  }
+  if (s < T_pad) e32[(int64_t)b * T_pad + s] = e;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+    hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+  }
+  __shared__ int32_t slo[4], shi[4];
+  if ((threadIdx.x & 31) == 0) {
+    slo[threadIdx.x >> 5] = lo;
+    shi[threadIdx.x >> 5] = hi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    tmin[b * n_kt + j] = min(min(slo[0], slo[1]), min(slo[2], slo[3]));
+    tmax[b * n_kt + j] = max(max(shi[0], shi[1]), max(shi[2], shi[3]));
+  }
+}
+
+// ------------------------------------------------------------------ UMMA self-test
+// C[128][128] (f32) = A[128][128] (bf16, row-major = K-major) x B, with B given as
+// Bt[128 n][128 k] (K-major, b_mn = 0) or B[128 k][128 n] (MN-major, b_mn = 1).
+__global__ void __launch_bounds__(128, 1)
+umma_selftest_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b, int b_mn,
+                     float* __restrict__ c, int32_t* __restrict__ error) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* As = smem;
+  uint8_t* Bs = smem + TILE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * TILE_BYTES);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + 2 * TILE_BYTES + 64);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    mbar_fence_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tslot, 128);
+    tmem_relinquish();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  bool ok = true;
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(&bars[0], 2 * TILE_BYTES);
+    tma_load_3d(As, &tm_a, 0, 0, 0, &bars[0]);
+    tma_load_3d(As + HALF_BYTES, &tm_a, 64, 0, 0, &bars[0]);
+    tma_load_3d(Bs, &tm_b, 0, 0, 0, &bars[0]);
+    tma_load_3d(Bs + HALF_BYTES, &tm_b, 64, 0, 0, &bars[0]);
+    ok = mbar_wait(&bars[0], 0, nullptr);
+    if (ok) {
+      tc_fence_after();
+      const uint32_t a0 = smem_addr(As), b0 = smem_addr(Bs);
+      const uint32_t id = idesc_bf16(128, 128, b_mn);
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t off = (kk >> 2) * HALF_BYTES + (kk & 3) * 32;
+        const uint64_t bd = b_mn ? desc_mnmajor_sw128(b0 + kk * 2048, HALF_BYTES) : desc_kmajor_sw128(b0 + off);
+        umma_bf16(tmem, desc_kmajor_sw128(a0 + off), bd, id, kk > 0);
+      }
+      umma_commit(&bars[1]);
+    } else {
+      atomicExch(error, 1);
+    }
+  }
+  __syncthreads();
+  if (mbar_wait(&bars[1], 0, nullptr)) {
+    tc_fence_after();
+    const int r = warp * 32 + lane;
+    for (int cc = 0; cc < 4; ++cc) {
+      uint32_t v[32];
+      tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + cc * 32, v);
+      tmem_wait_ld();
+      for (int i = 0; i < 32; ++i) c[r * 128 + cc * 32 + i] = __uint_as_float(v[i]);
+    }
+  } else if (threadIdx.x == 0) {
+    atomicExch(error, 2);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 128);
+  }
+}
+
+// ------------------------------------------------------------------ host helpers
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static std::once_flag once;
+  static EncodeTiledFn fn = nullptr;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 3-D bf16 map over rows of `inner` elements: dims {inner, mid, outer}, box {64, 1, 128}, 128-byte swizzle
+bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t mid, uint64_t outer) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[3] = {inner, mid, outer};
+  const cuuint64_t strides[2] = {inner * 2, inner * mid * 2};
+  const cuuint32_t box[3] = {64, 1, 128};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+std::mutex g_attr_mu;
+bool g_attr_done[64][2] = {};
+
+bool set_smem_attr(const void* fn, int which, int bytes) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(g_attr_mu);
+  if (dev < 64 && !g_attr_done[dev][which]) {
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) return false;
+    g_attr_done[dev][which] = true;
+  }
+  return true;
+}
+
+struct ReplayScratch {
+  int32_t* e32;
+  int32_t* tmin;
+  int32_t* tmax;
+  int32_t* error;
+};
+
+size_t replay_scratch_layout(int B, int T, void* base, ReplayScratch* s) {
+  const int T_pad = (T + BN - 1) / BN * BN;
+  const int n_kt = T_pad / BN;
+  size_t off = 0;
+  const size_t o_e = off; off = align_up(off + (size_t)B * T_pad * 4, 256);
+  const size_t o_lo = off; off = align_up(off + (size_t)B * n_kt * 4, 256);
+  const size_t o_hi = off; off = align_up(off + (size_t)B * n_kt * 4, 256);
+  const size_t o_err = off; off = align_up(off + 4, 256);
+  if (s) {
+    uint8_t* p = static_cast<uint8_t*>(base);
+    s->e32 = reinterpret_cast<int32_t*>(p + o_e);
+    s->tmin = reinterpret_cast<int32_t*>(p + o_lo);
+    s->tmax = reinterpret_cast<int32_t*>(p + o_hi);
+    s->error = reinterpret_cast<int32_t*>(p + o_err);
+  }
+  return off;
+}
+
+}  // namespace
+
+size_t kvs_replay_tc_scratch(int B, int T) { return replay_scratch_layout(B, T, nullptr, nullptr); }
+
+bool kvs_replay_tc_supported(const kvs_replay_args* a) {
+  return a->dtype == KVS_BF16 && a->head_dim == HD && (a->n_heads % a->n_kv_heads) == 0 &&
+         (a->seq_len + BN - 1) / BN <= MAX_KT && (reinterpret_cast<uintptr_t>(a->out) & 15) == 0 &&
+         (reinterpret_cast<uintptr_t>(a->q) & 15) == 0 && (reinterpret_cast<uintptr_t>(a->k) & 15) == 0 &&
+         (reinterpret_cast<uintptr_t>(a->v) & 15) == 0 && encode_fn() != nullptr;
+}
+
+int kvs_replay_tc_launch(const kvs_replay_args* a, cudaStream_t st) {
+  ReplayScratch s;
+  const size_t need = replay_scratch_layout(a->batch, a->seq_len, a->scratch, &s);
+  if (!a->scratch || a->scratch_bytes < need) return KVS_E_SCRATCH;
+  const int T = a->seq_len, B = a->batch;
+  const int T_pad = (T + BN - 1) / BN * BN, n_kt = T_pad / BN;
+  CUtensorMap mq, mk, mv;
+  if (!make_map(&mq, a->q, HD, a->n_heads, (uint64_t)B * T) || !make_map(&mk, a->k, HD, a->n_kv_heads, (uint64_t)B * T) ||
+      !make_map(&mv, a->v, HD, a->n_kv_heads, (uint64_t)B * T))
+    return KVS_E_UNSUPPORTED;
+  if (!set_smem_attr(reinterpret_cast<const void*>(replay_tc_kernel), 0, SMEM_BYTES)) return KVS_E_LAUNCH;
+  if (cudaMemsetAsync(s.error, 0, 4, st) != cudaSuccess) return KVS_E_LAUNCH;
+  replay_prepass_kernel<<<dim3(n_kt, B), BN, 0, st>>>(a->evicted_at, T, T_pad, n_kt, s.e32, s.tmin, s.tmax);
+  int rc = launch_rc();
+  if (rc) return rc;
+  ReplayParams p;
+  p.e32 = s.e32;
+  p.tile_min = s.tmin;
+  p.tile_max = s.tmax;
+  p.lengths = a->lengths;
+  p.out = static_cast<__nv_bfloat16*>(a->out);
+  p.error = s.error;
+  p.B = B;
+  p.T = T;
+  p.T_pad = T_pad;
+  p.Hq = a->n_heads;
+  p.Hkv = a->n_kv_heads;
+  p.n_qt = n_kt;
+  p.n_kt = n_kt;
+  p.scale_log2 = (float)(a->scale * 1.4426950408889634);
+  const int64_t grid = (int64_t)B * a->n_heads * n_kt;
+  replay_tc_kernel<<<(unsigned)grid, NT, SMEM_BYTES, st>>>(mq, mk, mv, p);
+  return launch_rc();
+}
+
+KVS_API int kvs_selftest_umma(const void* a, const void* b, float* c, int32_t b_mn, int32_t* error,
+                              kvs_stream_t stream) {
+  if (!a || !b || !c || !error || (b_mn != 0 && b_mn != 1)) return KVS_E_ARG;
+  CUtensorMap ma, mb;
+  if (!make_map(&ma, a, 128, 1, 128) || !make_map(&mb, b, 128, 1, 128)) return KVS_E_UNSUPPORTED;
+  const int smem = 2 * TILE_BYTES + 128 + 1024;
+  if (!set_smem_attr(reinterpret_cast<const void*>(umma_selftest_kernel), 1, smem)) return KVS_E_LAUNCH;
+  umma_selftest_kernel<<<1, 128, smem, to_cuda(stream)>>>(ma, mb, b_mn, c, error);
+  return launch_rc();
+}

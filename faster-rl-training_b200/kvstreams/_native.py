@@ -153,6 +153,7 @@ SIGNATURES = {
     "kvs_evicted_at": (C.c_int, [_P, _P, _P, _P, _P, _I, _I, _P, _P]),
     "kvs_replay_scratch_bytes": (_Z, [_I, _I]),
     "kvs_replay_attention": (C.c_int, [_P, _P]),
+    "kvs_selftest_umma": (C.c_int, [_P, _P, _P, _I, _P, _P]),
 }
 
 STRUCTS = {0: KvsCache, 1: KvsBatch, 2: KvsDecodeArgs, 3: KvsReplayArgs}

@@ -275,6 +275,14 @@ typedef struct kvs_replay_args {
 size_t kvs_replay_scratch_bytes(int32_t batch, int32_t seq_len);
 int kvs_replay_attention(const kvs_replay_args* a, kvs_stream_t stream);
 
+/* Self-test of the tcgen05 path (no reference counterpart): c[128][128] f32 =
+ * a[128][128] (bf16 row-major) x B, with B given as bt[128 n][128 k] (b_mn = 0,
+ * K-major operand) or b[128 k][128 n] (b_mn = 1, MN-major operand).  *error is set
+ * non-zero if an internal wait timed out.  Validates the UMMA descriptors, TMA
+ * swizzle and TMEM read-back that the replay kernel relies on. */
+int kvs_selftest_umma(const void* a, const void* b, float* c, int32_t b_mn, int32_t* error,
+                      kvs_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
