@@ -312,7 +312,11 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hpos))
     d2h = hout.numel() * hout.element_size()
 
-    secondary = compaction_bench(dev, args, rank) if not args.skip_secondary else None
+    secondary = None
+    if not args.skip_secondary:
+        del hq, hk, hv, hout
+        secondary = compaction_bench(dev, args, rank)
+        secondary["replay_attention"] = replay_bench(dev, args, rank)
 
     if rank != 0:
         return
@@ -404,6 +408,48 @@ def compaction_bench(dev, args, rank: int) -> dict:
     return out
 
 
+def replay_bench(dev, args, rank: int) -> dict:
+    """Masked replay attention, one layer of the Llama-3-8B geometry (32 q / 8 kv heads,
+    D 128, bf16): B streams x T tokens with 3-8 keep-recent compaction events each.
+    Algorithmic work = 4 * Hq * D FLOP per visible (query, key) pair."""
+    import torch
+
+    from kvstreams import _native as N
+    from kvstreams import ops
+    from kvstreams.workloads import replay_evicted_at, visible_pairs
+
+    B, T = args.replay_b, args.replay_t
+    ev, _ = replay_evicted_at(batch=B, seq_len=T, seed=rank)
+    pairs = visible_pairs(ev)
+    causal = B * T * (T + 1) // 2
+    g = torch.Generator(device=dev).manual_seed(rank)
+    q = torch.randn(B, T, HQ, D, generator=g, device=dev).bfloat16()
+    k = torch.randn(B, T, HKV, D, generator=g, device=dev).bfloat16()
+    v = torch.randn(B, T, HKV, D, generator=g, device=dev).bfloat16()
+    ev_t = torch.from_numpy(ev).to(dev)
+    ln_t = torch.full((B,), T, dtype=torch.int32, device=dev)
+    out = torch.empty_like(q)
+    lib = N.lib()
+    times = []
+    for i in range(2 + args.replay_steps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        ops.replay_attention(q, k, v, ev_t, ln_t, D ** -0.5, out=out)
+        b.record()
+        torch.cuda.synchronize()
+        if i >= 2:
+            times.append(a.elapsed_time(b))
+    ms = statistics.median(times)
+    flops = 4.0 * HQ * D * pairs
+    peaks = _peaks()
+    tf = flops / (ms * 1e-3) / 1e12
+    del q, k, v, out
+    return {"workload": f"B={B} T={T} 32q/8kv D128 bf16, 3-8 keep-recent events/stream (one layer)",
+            "ms": ms, "visible_pairs": pairs, "visible_frac_of_causal": pairs / causal,
+            "tflops": tf, "tc_frac": tf / peaks["bf16_tflops"], "peak_src": peaks["src"],
+            "replay_attn_tok_s": B * T / (ms * 1e-3), "kernel": "replay_tc_kernel (tcgen05/TMEM)"}
+
+
 def main() -> int:
     global S, NB, CTX
     ap = argparse.ArgumentParser()
@@ -416,6 +462,10 @@ def main() -> int:
     ap.add_argument("--streams", type=int, default=S, help="decode streams per GPU (profiling: smaller case)")
     ap.add_argument("--pool-blocks", type=int, default=NB)
     ap.add_argument("--ctx-max", type=int, default=CTX[1])
+    ap.add_argument("--replay-b", type=int, default=16)
+    ap.add_argument("--replay-t", type=int, default=32768)
+    ap.add_argument("--replay-steps", type=int, default=2)
+    ap.add_argument("--replay-only", action="store_true", help="only the replay attention measurement")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -436,7 +486,13 @@ def main() -> int:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        run_b200(args, rank, world, local_rank)
+        if args.replay_only:
+            torch.cuda.set_device(local_rank)
+            r = replay_bench(torch.device("cuda", local_rank), args, rank)
+            if rank == 0:
+                print(json.dumps({"replay_attention": r}), flush=True)
+        else:
+            run_b200(args, rank, world, local_rank)
     finally:
         if world > 1:
             dist.destroy_process_group()

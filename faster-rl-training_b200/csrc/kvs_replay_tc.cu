@@ -226,62 +226,67 @@ replay_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       if (ok && masked) ok = mbar_wait(&bar[B_FULL0 + slot], (k >> 1) & 1, abort_flag);
       if (!ok) break;
       tc_fence_after();
-      const int32_t* E = reinterpret_cast<const int32_t*>(smem + OFF_E + slot * E_BYTES);
-      // pass 1: row max over visible keys
-      float mx = -INFINITY;
+      // the tile's whole S row in registers (one TMEM pass), then the S buffer is free
+      uint32_t v[128];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld32(tl + S_col + slot * 128 + c * 32, v);
-        tmem_wait_ld();
+      for (int c = 0; c < 4; ++c)
+        tmem_ld32(tl + S_col + slot * 128 + c * 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32 * c));
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&bar[B_SFREE0 + slot]);
+      if (masked) {
+        // key i of the tile is visible to row t iff i <= t - s0 and t < evicted_at (real rows),
+        // or i == t - s0 (padded rows); hidden scores become -inf (predicated, no branches)
+        const int lim = t - s0;
+        const int4* E4 = reinterpret_cast<const int4*>(smem + OFF_E + slot * E_BYTES);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int s = s0 + c * 32 + i;
-          const bool vis = !masked || (real ? (s <= t && t < E[c * 32 + i]) : (s == t));
-          const float x = __uint_as_float(v[i]) * sl2;
-          mx = vis ? fmaxf(mx, x) : mx;
+        for (int q = 0; q < 32; ++q) {
+          const int4 e = E4[q];
+          const int ev[4] = {e.x, e.y, e.z, e.w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int i = 4 * q + u;
+            const bool vis = (i <= lim) && (real ? (t < ev[u]) : (i >= lim));
+            v[i] = vis ? v[i] : 0xff800000u;
+          }
         }
       }
+      float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 128; i += 4) {
+        mx0 = fmaxf(mx0, __uint_as_float(v[i]));
+        mx1 = fmaxf(mx1, __uint_as_float(v[i + 1]));
+        mx2 = fmaxf(mx2, __uint_as_float(v[i + 2]));
+        mx3 = fmaxf(mx3, __uint_as_float(v[i + 3]));
+      }
+      const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2;  // sl2 > 0: max commutes
       float alpha = 1.f;
       bool rescale = false;
       if (m == -INFINITY) {
         m = mx;
       } else if (mx > m + 8.f) {
-        alpha = exp2f(m - mx);
+        alpha = ex2_approx(m - mx);
         m = mx;
         rescale = true;
       }
-      const float m_eff = (m == -INFINITY) ? 0.f : m;
-      // pass 2: probabilities -> bf16 P row (128-byte swizzled K-major, like the TMA tiles)
-      float sum = 0.f;
+      const float neg_m = (m == -INFINITY) ? 0.f : -m;
+      // probabilities 2^(s*sl2 - m) -> bf16 P row (128-byte swizzled K-major, like the TMA tiles)
+      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
       uint8_t* Prow = smem + OFF_P + slot * TILE_BYTES + r * 128;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld32(tl + S_col + slot * 128 + c * 32, v);
-        tmem_wait_ld();
-        uint32_t pk[16];
+      for (int ch = 0; ch < 16; ++ch) {  // 16-byte chunk = 8 keys
+        float pv[8];
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const int s = s0 + c * 32 + i;
-          const bool v0 = !masked || (real ? (s <= t && t < E[c * 32 + i]) : (s == t));
-          const bool v1 = !masked || (real ? (s + 1 <= t && t < E[c * 32 + i + 1]) : (s + 1 == t));
-          const float p0 = v0 ? exp2f(__uint_as_float(v[i]) * sl2 - m_eff) : 0.f;
-          const float p1 = v1 ? exp2f(__uint_as_float(v[i + 1]) * sl2 - m_eff) : 0.f;
-          sum += p0 + p1;
-          pk[i >> 1] = pack2(p0, p1);
-        }
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          const int ch = c * 4 + q4;  // 16-byte chunk 0..15 of the 256-byte row
-          const int half = ch >> 3, cidx = ch & 7;
-          uint8_t* dst = Prow + half * HALF_BYTES + ((cidx ^ (r & 7)) << 4);
-          *reinterpret_cast<uint4*>(dst) = make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
-        }
+        for (int u = 0; u < 8; ++u) pv[u] = ex2_approx(fmaf(__uint_as_float(v[ch * 8 + u]), sl2, neg_m));
+        a0 += pv[0] + pv[4];
+        a1 += pv[1] + pv[5];
+        a2 += pv[2] + pv[6];
+        a3 += pv[3] + pv[7];
+        uint8_t* dst = Prow + (ch >> 3) * HALF_BYTES + (((ch & 7) ^ (r & 7)) << 4);
+        *reinterpret_cast<uint4*>(dst) =
+            make_uint4(pack2(pv[0], pv[1]), pack2(pv[2], pv[3]), pack2(pv[4], pv[5]), pack2(pv[6], pv[7]));
       }
-      l = l * alpha + sum;
-      tc_fence_before();
-      mbar_arrive(&bar[B_SFREE0 + slot]);
+      l = l * alpha + ((a0 + a1) + (a2 + a3));
       // O holds every earlier P V once the previous UMMA group is done
       if (k >= 1) {
         ok = mbar_wait(&bar[B_ODONE], (k - 1) & 1, abort_flag);

@@ -37,27 +37,36 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_addr(bar)), "r"(bytes)
                : "memory");
 }
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+// try_wait with a suspend-time hint: a waiting thread sleeps until the phase
+// completes or about `hint_ns` nanoseconds pass, instead of spinning on issue slots.
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity, uint32_t hint_ns = 100000) {
   uint32_t ok;
   asm volatile(
       "{\n.reg .pred p;\n"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
       "selp.u32 %0, 1, 0, p;\n}\n"
       : "=r"(ok)
-      : "r"(smem_addr(bar)), "r"(parity)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
       : "memory");
   return ok != 0;
 }
-// Wait for phase `parity` of `bar` to complete, giving up after `limit` polls
-// (each try_wait itself blocks for a hardware-defined time slice).  Returns false
-// on timeout; the caller records an error and winds down instead of hanging.
+// Wait for phase `parity` of `bar` to complete, giving up after `limit` suspended
+// polls of at most 100 us each (~2 s in all).  Returns false on timeout; the caller
+// records an error and winds down instead of hanging.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const volatile int* abort_flag,
-                                          uint32_t limit = 1u << 22) {
+                                          uint32_t limit = 20000) {
   for (uint32_t i = 0; i < limit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if (abort_flag && *abort_flag) return false;
   }
   return false;
+}
+
+// 2^x on the MUFU unit (hardware approximation, flush-to-zero; 2^-inf = +0)
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+  return y;
 }
 
 // ------------------------------------------------------------------ TMA
