@@ -31,7 +31,8 @@ using namespace kvs::sm100;
 namespace {
 
 constexpr int BM = 128, BN = 128, HD = 128;
-constexpr int NT = 192;
+constexpr int NSOFT = 256;                 // 8 softmax warps: two per TMEM lane quadrant
+constexpr int NT = 64 + NSOFT;             // + producer warp + UMMA warp
 constexpr int HALF_BYTES = 128 * 64 * 2;  // 128 rows x 64 bf16 (one 128-byte swizzled half tile)
 constexpr int TILE_BYTES = 2 * HALF_BYTES;  // 128 x 128 bf16
 constexpr int E_BYTES = BN * 4;
@@ -40,18 +41,22 @@ constexpr int E_BYTES = BN * 4;
 constexpr int OFF_Q = 0;
 constexpr int OFF_K = OFF_Q + TILE_BYTES;          // 2 slots
 constexpr int OFF_V = OFF_K + 2 * TILE_BYTES;      // 2 slots
-constexpr int OFF_P = OFF_V + 2 * TILE_BYTES;      // 2 slots
-constexpr int OFF_E = OFF_P + 2 * TILE_BYTES;      // 2 slots of 128 int32
-constexpr int OFF_LIST = OFF_E + 2 * E_BYTES;      // active key tiles (<= 512 entries)
+constexpr int OFF_P = OFF_V + 2 * TILE_BYTES;      // 1 tile of probabilities
+constexpr int OFF_E = OFF_P + TILE_BYTES;          // 2 slots of 128 int32
+constexpr int OFF_RED = OFF_E + 2 * E_BYTES;       // [2 tiles][2 halves][128 rows] f32 row maxima
+constexpr int OFF_LIST = OFF_RED + 2 * 2 * BM * 4; // active key tiles
 constexpr int MAX_KT = 256;  // key tiles per stream: T <= 32768
 constexpr int OFF_BAR = OFF_LIST + MAX_KT * 2;
-constexpr int NBAR = 13;
+constexpr int NBAR = 12;
 constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
 constexpr int SMEM_BYTES = OFF_MISC + 64 + 33 * 4 + 1024;  // + alignment slack
 static_assert(SMEM_BYTES <= 232448, "replay kernel shared memory");
 
 enum { B_FULL0 = 0, B_FULL1, B_EMPTY0, B_EMPTY1, B_QFULL, B_SFULL0, B_SFULL1, B_SFREE0, B_SFREE1,
-       B_PFULL0, B_PFULL1, B_ODONE, B_FINAL };
+       B_PFULL, B_ODONE, B_FINAL };
+
+// named barrier over the softmax warps only (id 1; id 0 is __syncthreads)
+__device__ __forceinline__ void softmax_bar() { asm volatile("bar.sync 1, %0;\n" ::"n"(NSOFT) : "memory"); }
 
 struct ReplayParams {
   const int32_t* e32;      // [B][T_pad] evicted_at clamped to int32, 0 past T
@@ -83,21 +88,23 @@ replay_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   int* s_scan = reinterpret_cast<int*>(smem + OFF_MISC + 64);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  // heaviest query tiles (most key tiles) first
-  const int bh_count = p.B * p.Hq;
-  const int qt = p.n_qt - 1 - (int)(blockIdx.x / bh_count);
-  const int bh = (int)(blockIdx.x % bh_count);
-  const int b = bh / p.Hq, h = bh % p.Hq;
-  const int hk = h / (p.Hq / p.Hkv);
+  // CTA order: (stream, KV head) slowest, then query tiles heaviest first, then the query
+  // heads of the GQA group -- CTAs resident together read the same K/V tiles (L2 reuse)
+  const int G = p.Hq / p.Hkv;
+  const int g = (int)(blockIdx.x % G);
+  const int rest = (int)(blockIdx.x / G);
+  const int qt = p.n_qt - 1 - rest % p.n_qt;
+  const int bhk = rest / p.n_qt;
+  const int b = bhk / p.Hkv, hk = bhk % p.Hkv;
+  const int h = hk * G + g;
   const int t0 = qt * BM, t1 = t0 + BM - 1;
   const int L = p.lengths[b];
 
   if (tid == 0) {
     for (int i = 0; i < NBAR; ++i) mbar_init(&bar[i], 1);
-    mbar_init(&bar[B_SFREE0], 128);
-    mbar_init(&bar[B_SFREE1], 128);
-    mbar_init(&bar[B_PFULL0], 128);
-    mbar_init(&bar[B_PFULL1], 128);
+    mbar_init(&bar[B_SFREE0], NSOFT);
+    mbar_init(&bar[B_SFREE1], NSOFT);
+    mbar_init(&bar[B_PFULL], NSOFT);
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -184,10 +191,10 @@ replay_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         }
         if (k >= 1) {
           const int pk = k - 1, ps = pk & 1;
-          ok = mbar_wait(&bar[B_PFULL0 + ps], (pk >> 1) & 1, abort_flag);
+          ok = mbar_wait(&bar[B_PFULL], pk & 1, abort_flag);
           if (!ok) break;
           tc_fence_after();
-          const uint32_t p_base = smem_addr(smem + OFF_P + ps * TILE_BYTES);
+          const uint32_t p_base = smem_addr(smem + OFF_P);
           const uint32_t v_base = smem_addr(smem + OFF_V + ps * TILE_BYTES);
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
@@ -208,39 +215,51 @@ replay_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       mbar_wait(&bar[B_FINAL], 0, nullptr);
     }
   } else {
-    // ------------------------------------------------------------ softmax (one row per thread)
+    // ------------------------------------------------------------ softmax
+    // 8 warps; warps w and w+4 share TMEM lane quadrant w%4 (32 query rows).  The first of
+    // the pair owns key / output columns 0..63 of those rows, the second 64..127; the row
+    // maximum is exchanged through shared memory once per key tile.
+    const int sw = warp - 2;
     const int quad = warp & 3;
+    const int half = sw >> 2;
+    const int cbase = half * 64;
     const int r = quad * 32 + lane;
     const int t = t0 + r;
     const bool real = t < L;
     const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16);
     const float sl2 = p.scale_log2;
-    float m = -INFINITY, l = 0.f;
+    float* red = reinterpret_cast<float*>(smem + OFF_RED);  // [2 tiles][2 halves][128 rows]
+    float m = -INFINITY, l = 0.f;  // l: this half's partial row sum
+    // `ok` stays warp-uniform; after a timeout a thread keeps passing the named barrier once
+    // per tile (so its partner warp is never left waiting) but does no further work.
     bool ok = true;
-    for (int k = 0; k < n && ok; ++k) {
+    for (int k = 0; k < n; ++k) {
       const int slot = k & 1;
       const int j = list[k] & 0x7fff;
       const bool masked = (list[k] >> 15) & 1;
-      const int s0 = j * BN;
-      ok = mbar_wait(&bar[B_SFULL0 + slot], (k >> 1) & 1, abort_flag);
+      const int s0 = j * BN + cbase;
+      if (ok) ok = mbar_wait(&bar[B_SFULL0 + slot], (k >> 1) & 1, abort_flag);
       if (ok && masked) ok = mbar_wait(&bar[B_FULL0 + slot], (k >> 1) & 1, abort_flag);
-      if (!ok) break;
-      tc_fence_after();
-      // the tile's whole S row in registers (one TMEM pass), then the S buffer is free
-      uint32_t v[128];
+      ok = __all_sync(0xffffffffu, ok);
+      uint32_t v[64];
+      if (ok) {
+        tc_fence_after();
+        tmem_ld32(tl + S_col + slot * 128 + cbase, *reinterpret_cast<uint32_t(*)[32]>(v));
+        tmem_ld32(tl + S_col + slot * 128 + cbase + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(&bar[B_SFREE0 + slot]);
+      } else {
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
-        tmem_ld32(tl + S_col + slot * 128 + c * 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32 * c));
-      tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(&bar[B_SFREE0 + slot]);
+        for (int i = 0; i < 64; ++i) v[i] = 0xff800000u;
+      }
       if (masked) {
-        // key i of the tile is visible to row t iff i <= t - s0 and t < evicted_at (real rows),
-        // or i == t - s0 (padded rows); hidden scores become -inf (predicated, no branches)
+        // key i (of this half) is visible to row t iff i <= t - s0 and t < evicted_at (real
+        // rows), or i == t - s0 (padded rows); hidden scores become -inf, branch-free
         const int lim = t - s0;
-        const int4* E4 = reinterpret_cast<const int4*>(smem + OFF_E + slot * E_BYTES);
+        const int4* E4 = reinterpret_cast<const int4*>(smem + OFF_E + slot * E_BYTES + cbase * 4);
 #pragma unroll
-        for (int q = 0; q < 32; ++q) {
+        for (int q = 0; q < 16; ++q) {
           const int4 e = E4[q];
           const int ev[4] = {e.x, e.y, e.z, e.w};
 #pragma unroll
@@ -253,82 +272,94 @@ replay_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       }
       float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < 128; i += 4) {
+      for (int i = 0; i < 64; i += 4) {
         mx0 = fmaxf(mx0, __uint_as_float(v[i]));
         mx1 = fmaxf(mx1, __uint_as_float(v[i + 1]));
         mx2 = fmaxf(mx2, __uint_as_float(v[i + 2]));
         mx3 = fmaxf(mx3, __uint_as_float(v[i + 3]));
       }
-      const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2;  // sl2 > 0: max commutes
+      const float mh = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+      red[(slot * 2 + half) * BM + r] = mh;
+      softmax_bar();
+      const float mx = fmaxf(mh, red[(slot * 2 + (half ^ 1)) * BM + r]) * sl2;  // sl2 > 0: max commutes
       float alpha = 1.f;
       bool rescale = false;
       if (m == -INFINITY) {
         m = mx;
-      } else if (mx > m + 8.f) {
+      } else if (mx > m + 8.f) {  // lazy rescale: exact, p <= 2^8 in between
         alpha = ex2_approx(m - mx);
         m = mx;
         rescale = true;
       }
       const float neg_m = (m == -INFINITY) ? 0.f : -m;
-      // probabilities 2^(s*sl2 - m) -> bf16 P row (128-byte swizzled K-major, like the TMA tiles)
+      float pv[64];
       float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-      uint8_t* Prow = smem + OFF_P + slot * TILE_BYTES + r * 128;
 #pragma unroll
-      for (int ch = 0; ch < 16; ++ch) {  // 16-byte chunk = 8 keys
-        float pv[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) pv[u] = ex2_approx(fmaf(__uint_as_float(v[ch * 8 + u]), sl2, neg_m));
-        a0 += pv[0] + pv[4];
-        a1 += pv[1] + pv[5];
-        a2 += pv[2] + pv[6];
-        a3 += pv[3] + pv[7];
-        uint8_t* dst = Prow + (ch >> 3) * HALF_BYTES + (((ch & 7) ^ (r & 7)) << 4);
-        *reinterpret_cast<uint4*>(dst) =
-            make_uint4(pack2(pv[0], pv[1]), pack2(pv[2], pv[3]), pack2(pv[4], pv[5]), pack2(pv[6], pv[7]));
+      for (int i = 0; i < 64; i += 4) {
+        pv[i] = ex2_approx(fmaf(__uint_as_float(v[i]), sl2, neg_m));
+        pv[i + 1] = ex2_approx(fmaf(__uint_as_float(v[i + 1]), sl2, neg_m));
+        pv[i + 2] = ex2_approx(fmaf(__uint_as_float(v[i + 2]), sl2, neg_m));
+        pv[i + 3] = ex2_approx(fmaf(__uint_as_float(v[i + 3]), sl2, neg_m));
+        a0 += pv[i];
+        a1 += pv[i + 1];
+        a2 += pv[i + 2];
+        a3 += pv[i + 3];
       }
       l = l * alpha + ((a0 + a1) + (a2 + a3));
-      // O holds every earlier P V once the previous UMMA group is done
-      if (k >= 1) {
-        ok = mbar_wait(&bar[B_ODONE], (k - 1) & 1, abort_flag);
-        if (!ok) break;
+      // P is single-buffered and O must hold every earlier P V: wait for the previous UMMA group
+      if (ok && k >= 1) ok = mbar_wait(&bar[B_ODONE], (k - 1) & 1, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) continue;
+      // bf16 P (this half's 64 keys = 8 chunks of 16 B, 128-byte swizzle like the TMA tiles)
+      uint8_t* Prow = smem + OFF_P + half * HALF_BYTES + r * 128;
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        *reinterpret_cast<uint4*>(Prow + ((ch ^ (r & 7)) << 4)) =
+            make_uint4(pack2(pv[ch * 8], pv[ch * 8 + 1]), pack2(pv[ch * 8 + 2], pv[ch * 8 + 3]),
+                       pack2(pv[ch * 8 + 4], pv[ch * 8 + 5]), pack2(pv[ch * 8 + 6], pv[ch * 8 + 7]));
       }
       if (__any_sync(0xffffffffu, rescale)) {
         tc_fence_after();
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t v[32];
-          tmem_ld32(tl + O_col + c * 32, v);
+        for (int c = 0; c < 2; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tl + O_col + cbase + c * 32, o);
           tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
-          tmem_st32(tl + O_col + c * 32, v);
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(tl + O_col + cbase + c * 32, o);
         }
         tmem_wait_st();
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(&bar[B_PFULL0 + slot]);
+      mbar_arrive(&bar[B_PFULL]);
     }
     if (ok) ok = mbar_wait(&bar[B_ODONE], (n - 1) & 1, abort_flag);
+    // full row sum from the two halves (buffer n&1 was last read at tile n-2)
+    red[((n & 1) * 2 + half) * BM + r] = l;
+    softmax_bar();
+    const float lsum = l + red[((n & 1) * 2 + (half ^ 1)) * BM + r];
     if (!ok) {
       *abort_flag = 1;
       atomicExch(p.error, 3);
     } else {
       tc_fence_after();
-      const float inv = 1.f / l;
-      __nv_bfloat16* orow = p.out + (((int64_t)b * p.T + t) * p.Hq + h) * HD;
+      const float inv = 1.f / lsum;
+      __nv_bfloat16* orow = p.out + (((int64_t)b * p.T + t) * p.Hq + h) * HD + cbase;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld32(tl + O_col + c * 32, v);
+      for (int c = 0; c < 2; ++c) {
+        uint32_t o[32];
+        tmem_ld32(tl + O_col + cbase + c * 32, o);
         tmem_wait_ld();
         if (t < p.T) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int i = 0; i < 32; i += 2) pk[i >> 1] = pack2(__uint_as_float(v[i]) * inv, __uint_as_float(v[i + 1]) * inv);
           uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
 #pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4) dst[q4] = make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
+          for (int q4 = 0; q4 < 4; ++q4)
+            dst[q4] = make_uint4(pack2(__uint_as_float(o[8 * q4]) * inv, __uint_as_float(o[8 * q4 + 1]) * inv),
+                                 pack2(__uint_as_float(o[8 * q4 + 2]) * inv, __uint_as_float(o[8 * q4 + 3]) * inv),
+                                 pack2(__uint_as_float(o[8 * q4 + 4]) * inv, __uint_as_float(o[8 * q4 + 5]) * inv),
+                                 pack2(__uint_as_float(o[8 * q4 + 6]) * inv, __uint_as_float(o[8 * q4 + 7]) * inv));
         }
       }
     }
