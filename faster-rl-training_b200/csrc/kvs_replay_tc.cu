@@ -47,13 +47,15 @@ constexpr int OFF_RED = OFF_E + 2 * E_BYTES;       // [2 tiles][2 halves][128 ro
 constexpr int OFF_LIST = OFF_RED + 2 * 2 * BM * 4; // active key tiles
 constexpr int MAX_KT = 256;  // key tiles per stream: T <= 32768
 constexpr int OFF_BAR = OFF_LIST + MAX_KT * 2;
-constexpr int NBAR = 12;
+constexpr int NBAR = 16;
 constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
 constexpr int SMEM_BYTES = OFF_MISC + 64 + 33 * 4 + 1024;  // + alignment slack
 static_assert(SMEM_BYTES <= 232448, "replay kernel shared memory");
 
-enum { B_FULL0 = 0, B_FULL1, B_EMPTY0, B_EMPTY1, B_QFULL, B_SFULL0, B_SFULL1, B_SFREE0, B_SFREE1,
-       B_PFULL, B_ODONE, B_FINAL };
+// K and V rings are refilled independently: a K slot as soon as Q K^T has read it, a V slot
+// (with the tile's evicted_at values) once P V has read it.
+enum { B_KFULL0 = 0, B_KFULL1, B_VFULL0, B_VFULL1, B_KEMPTY0, B_KEMPTY1, B_VEMPTY0, B_VEMPTY1, B_QFULL,
+       B_SFULL0, B_SFULL1, B_SFREE0, B_SFREE1, B_PFULL, B_ODONE, B_FINAL };
 
 // named barrier over the softmax warps only (id 1; id 0 is __syncthreads)
 __device__ __forceinline__ void softmax_bar() { asm volatile("bar.sync 1, %0;\n" ::"n"(NSOFT) : "memory"); }
@@ -141,29 +143,41 @@ replay_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   const uint32_t S_col = 0, O_col = 256;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ producer
+    // ------------------------------------------------------------ producers
+    // lane 0: Q once, then the K ring; lane 1: the V ring (+ evicted_at of each tile)
     if (lane == 0) {
       mbar_arrive_expect_tx(&bar[B_QFULL], TILE_BYTES);
       tma_load_3d(Qs, &tm_q, 0, h, b * p.T + t0, &bar[B_QFULL]);
       tma_load_3d(Qs + HALF_BYTES, &tm_q, 64, h, b * p.T + t0, &bar[B_QFULL]);
       for (int k = 0; k < n; ++k) {
         const int slot = k & 1;
-        if (k >= 2 && !mbar_wait(&bar[B_EMPTY0 + slot], ((k >> 1) - 1) & 1, abort_flag)) {
+        if (k >= 2 && !mbar_wait(&bar[B_KEMPTY0 + slot], ((k >> 1) - 1) & 1, abort_flag)) {
+          *abort_flag = 1;
+          atomicExch(p.error, 1);
+          break;
+        }
+        const int row = b * p.T + (list[k] & 0x7fff) * BN;
+        uint8_t* Ks = smem + OFF_K + slot * TILE_BYTES;
+        mbar_arrive_expect_tx(&bar[B_KFULL0 + slot], TILE_BYTES);
+        tma_load_3d(Ks, &tm_k, 0, hk, row, &bar[B_KFULL0 + slot]);
+        tma_load_3d(Ks + HALF_BYTES, &tm_k, 64, hk, row, &bar[B_KFULL0 + slot]);
+      }
+    } else if (lane == 1) {
+      for (int k = 0; k < n; ++k) {
+        const int slot = k & 1;
+        if (k >= 2 && !mbar_wait(&bar[B_VEMPTY0 + slot], ((k >> 1) - 1) & 1, abort_flag)) {
           *abort_flag = 1;
           atomicExch(p.error, 1);
           break;
         }
         const int j = list[k] & 0x7fff;
         const int row = b * p.T + j * BN;
-        uint8_t* Ks = smem + OFF_K + slot * TILE_BYTES;
         uint8_t* Vs = smem + OFF_V + slot * TILE_BYTES;
-        mbar_arrive_expect_tx(&bar[B_FULL0 + slot], 2 * TILE_BYTES + E_BYTES);
-        tma_load_3d(Ks, &tm_k, 0, hk, row, &bar[B_FULL0 + slot]);
-        tma_load_3d(Ks + HALF_BYTES, &tm_k, 64, hk, row, &bar[B_FULL0 + slot]);
-        tma_load_3d(Vs, &tm_v, 0, hk, row, &bar[B_FULL0 + slot]);
-        tma_load_3d(Vs + HALF_BYTES, &tm_v, 64, hk, row, &bar[B_FULL0 + slot]);
+        mbar_arrive_expect_tx(&bar[B_VFULL0 + slot], TILE_BYTES + E_BYTES);
+        tma_load_3d(Vs, &tm_v, 0, hk, row, &bar[B_VFULL0 + slot]);
+        tma_load_3d(Vs + HALF_BYTES, &tm_v, 64, hk, row, &bar[B_VFULL0 + slot]);
         bulk_load(smem + OFF_E + slot * E_BYTES, p.e32 + (int64_t)b * p.T_pad + j * BN, E_BYTES,
-                  &bar[B_FULL0 + slot]);
+                  &bar[B_VFULL0 + slot]);
       }
     }
   } else if (warp == 1) {
@@ -176,7 +190,7 @@ replay_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       for (int k = 0; ok && k <= n; ++k) {
         if (k < n) {
           const int slot = k & 1;
-          ok = mbar_wait(&bar[B_FULL0 + slot], (k >> 1) & 1, abort_flag);
+          ok = mbar_wait(&bar[B_KFULL0 + slot], (k >> 1) & 1, abort_flag);
           if (ok && k >= 2) ok = mbar_wait(&bar[B_SFREE0 + slot], ((k >> 1) - 1) & 1, abort_flag);
           if (!ok) break;
           tc_fence_after();
@@ -187,11 +201,13 @@ replay_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
             umma_bf16(tmem + S_col + slot * 128, desc_kmajor_sw128(q_base + off), desc_kmajor_sw128(k_base + off),
                       ID_QK, kk > 0);
           }
+          umma_commit(&bar[B_KEMPTY0 + slot]);
           umma_commit(&bar[B_SFULL0 + slot]);
         }
         if (k >= 1) {
           const int pk = k - 1, ps = pk & 1;
           ok = mbar_wait(&bar[B_PFULL], pk & 1, abort_flag);
+          if (ok) ok = mbar_wait(&bar[B_VFULL0 + ps], (pk >> 1) & 1, abort_flag);
           if (!ok) break;
           tc_fence_after();
           const uint32_t p_base = smem_addr(smem + OFF_P);
@@ -202,7 +218,7 @@ replay_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
             umma_bf16(tmem + O_col, desc_kmajor_sw128(p_base + a_off),
                       desc_mnmajor_sw128(v_base + kk * 2048, HALF_BYTES), ID_PV, (pk > 0 || kk > 0));
           }
-          umma_commit(&bar[B_EMPTY0 + ps]);
+          umma_commit(&bar[B_VEMPTY0 + ps]);
           umma_commit(&bar[B_ODONE]);
         }
       }
@@ -239,7 +255,8 @@ replay_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       const bool masked = (list[k] >> 15) & 1;
       const int s0 = j * BN + cbase;
       if (ok) ok = mbar_wait(&bar[B_SFULL0 + slot], (k >> 1) & 1, abort_flag);
-      if (ok && masked) ok = mbar_wait(&bar[B_FULL0 + slot], (k >> 1) & 1, abort_flag);
+      // evicted_at of the tile arrives with its V slot, which outlives this softmax step
+      if (ok && masked) ok = mbar_wait(&bar[B_VFULL0 + slot], (k >> 1) & 1, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
       uint32_t v[64];
       if (ok) {
