@@ -190,8 +190,8 @@ replay_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       for (int k = 0; ok && k <= n; ++k) {
         if (k < n) {
           const int slot = k & 1;
-          ok = mbar_wait(&bar[B_KFULL0 + slot], (k >> 1) & 1, abort_flag);
-          if (ok && k >= 2) ok = mbar_wait(&bar[B_SFREE0 + slot], ((k >> 1) - 1) & 1, abort_flag);
+          ok = mbar_wait_fast(&bar[B_KFULL0 + slot], (k >> 1) & 1, abort_flag);
+          if (ok && k >= 2) ok = mbar_wait_fast(&bar[B_SFREE0 + slot], ((k >> 1) - 1) & 1, abort_flag);
           if (!ok) break;
           tc_fence_after();
           const uint32_t k_base = smem_addr(smem + OFF_K + slot * TILE_BYTES);
@@ -206,8 +206,8 @@ replay_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         }
         if (k >= 1) {
           const int pk = k - 1, ps = pk & 1;
-          ok = mbar_wait(&bar[B_PFULL], pk & 1, abort_flag);
-          if (ok) ok = mbar_wait(&bar[B_VFULL0 + ps], (pk >> 1) & 1, abort_flag);
+          ok = mbar_wait_fast(&bar[B_PFULL], pk & 1, abort_flag);
+          if (ok) ok = mbar_wait_fast(&bar[B_VFULL0 + ps], (pk >> 1) & 1, abort_flag);
           if (!ok) break;
           tc_fence_after();
           const uint32_t p_base = smem_addr(smem + OFF_P);
@@ -254,7 +254,7 @@ replay_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       const int j = list[k] & 0x7fff;
       const bool masked = (list[k] >> 15) & 1;
       const int s0 = j * BN + cbase;
-      if (ok) ok = mbar_wait(&bar[B_SFULL0 + slot], (k >> 1) & 1, abort_flag);
+      if (ok) ok = mbar_wait_fast(&bar[B_SFULL0 + slot], (k >> 1) & 1, abort_flag);
       // evicted_at of the tile arrives with its V slot, which outlives this softmax step
       if (ok && masked) ok = mbar_wait(&bar[B_VFULL0 + slot], (k >> 1) & 1, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
@@ -309,22 +309,24 @@ replay_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         rescale = true;
       }
       const float neg_m = (m == -INFINITY) ? 0.f : -m;
-      float pv[64];
+      uint32_t pk[32];  // bf16 pairs of this half's probabilities
       float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
 #pragma unroll
       for (int i = 0; i < 64; i += 4) {
-        pv[i] = ex2_approx(fmaf(__uint_as_float(v[i]), sl2, neg_m));
-        pv[i + 1] = ex2_approx(fmaf(__uint_as_float(v[i + 1]), sl2, neg_m));
-        pv[i + 2] = ex2_approx(fmaf(__uint_as_float(v[i + 2]), sl2, neg_m));
-        pv[i + 3] = ex2_approx(fmaf(__uint_as_float(v[i + 3]), sl2, neg_m));
-        a0 += pv[i];
-        a1 += pv[i + 1];
-        a2 += pv[i + 2];
-        a3 += pv[i + 3];
+        const float p0 = ex2_approx(fmaf(__uint_as_float(v[i]), sl2, neg_m));
+        const float p1 = ex2_approx(fmaf(__uint_as_float(v[i + 1]), sl2, neg_m));
+        const float p2 = ex2_approx(fmaf(__uint_as_float(v[i + 2]), sl2, neg_m));
+        const float p3 = ex2_approx(fmaf(__uint_as_float(v[i + 3]), sl2, neg_m));
+        a0 += p0;
+        a1 += p1;
+        a2 += p2;
+        a3 += p3;
+        pk[i >> 1] = pack2(p0, p1);
+        pk[(i >> 1) + 1] = pack2(p2, p3);
       }
       l = l * alpha + ((a0 + a1) + (a2 + a3));
       // P is single-buffered and O must hold every earlier P V: wait for the previous UMMA group
-      if (ok && k >= 1) ok = mbar_wait(&bar[B_ODONE], (k - 1) & 1, abort_flag);
+      if (ok && k >= 1) ok = mbar_wait_fast(&bar[B_ODONE], (k - 1) & 1, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) continue;
       // bf16 P (this half's 64 keys = 8 chunks of 16 B, 128-byte swizzle like the TMA tiles)
@@ -332,8 +334,7 @@ replay_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
 #pragma unroll
       for (int ch = 0; ch < 8; ++ch) {
         *reinterpret_cast<uint4*>(Prow + ((ch ^ (r & 7)) << 4)) =
-            make_uint4(pack2(pv[ch * 8], pv[ch * 8 + 1]), pack2(pv[ch * 8 + 2], pv[ch * 8 + 3]),
-                       pack2(pv[ch * 8 + 4], pv[ch * 8 + 5]), pack2(pv[ch * 8 + 6], pv[ch * 8 + 7]));
+            make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
       }
       if (__any_sync(0xffffffffu, rescale)) {
         tc_fence_after();

@@ -62,11 +62,51 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
   return false;
 }
 
+// try_wait without a suspend hint (the hardware's default time slice)
+__device__ __forceinline__ bool mbar_try_wait_default(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n.reg .pred p;\n"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      "selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Latency-critical wait: default time slices, bounded by `limit` polls (several seconds).
+__device__ __forceinline__ bool mbar_wait_fast(uint64_t* bar, uint32_t parity, const volatile int* abort_flag,
+                                               uint32_t limit = 1u << 24) {
+  for (uint32_t i = 0; i < limit; ++i) {
+    if (mbar_try_wait_default(bar, parity)) return true;
+    if (abort_flag && *abort_flag) return false;
+  }
+  return false;
+}
+
 // 2^x on the MUFU unit (hardware approximation, flush-to-zero; 2^-inf = +0)
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
   return y;
+}
+
+// 2^x on the FMA/ALU pipes, for x <= 64 (arguments below -125 give +0): x = j + f with
+// j = round(x) taken from the low mantissa bits of x + 1.5*2^23 and f in [-0.5, 0.5];
+// 2^f ~ 1 + f*(c1 + f*(c2 + f*c3)), a cubic fitted here by relative least squares on
+// Chebyshev nodes (max relative error 1.14e-4, below bf16 rounding); 2^j is added to
+// the exponent field.  Used for part of the softmax exponentials so that they do not
+// all queue on the MUFU unit.
+__device__ __forceinline__ float exp2_poly(float x) {
+  const float magic = 12582912.0f;  // 1.5 * 2^23
+  const float xc = fmaxf(x, -125.0f);
+  const float t = xc + magic;
+  const float f = xc - (t - magic);
+  float p = fmaf(0.05459282547235489f, f, 0.24221783876419067f);
+  p = fmaf(p, f, 0.6933686137199402f);
+  p = fmaf(p, f, 1.0f);
+  const float r = __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+  return x < -125.0f ? 0.0f : r;
 }
 
 // ------------------------------------------------------------------ TMA
