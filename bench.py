@@ -230,6 +230,7 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
 
     from kvstreams import _native as N
     from kvstreams import ops
+    from kvstreams.distributed import reduce_max
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
@@ -272,10 +273,7 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     launches = lib.kvs_launch_count() - launches0
     ms = t_start.elapsed_time(t_end)
     kernel_ms = [a.elapsed_time(b) for a, b in kev]
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = reduce_max(ms, dev)  # slowest rank (weak scaling: every rank times its own streams)
     clocks = clk.summary()
     lengths_mid = st.lengths + args.steps // 2 + 1
     alg_bytes = decode_bytes(lengths_mid)
@@ -305,10 +303,7 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     e1.record()
     barrier()
     e2e_ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    e2e_ms = reduce_max(e2e_ms, dev)
     h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hpos))
     d2h = hout.numel() * hout.element_size()
 
