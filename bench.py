@@ -318,7 +318,10 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     peaks = _peaks()
     step_cpu, ctx_tokens = cpu_decode_sample(seed=0)
     cpu_rate, cpu_iters = time_cpu(step_cpu, min_seconds=args.cpu_seconds)
-    traffic = _traffic().get("paged_decode")
+    # DRAM bytes of one decode launch: ncu-measured traffic/algorithmic ratio (small-case
+    # capture, profiles/) scaled by this launch's algorithmic bytes
+    ratio = _traffic().get("paged_decode", {}).get("traffic_over_algorithmic")
+    traffic = int(ratio * alg_bytes) if ratio else None
     line = {
         "metric": METRIC,
         "value": world * S * args.steps / (ms * 1e-3),
