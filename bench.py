@@ -120,7 +120,9 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------- workload
-def build_decode(dev, seed: int):
+def build_decode(dev, seed: int, value_seed: int):
+    """Same stream shapes on every rank (weak scaling: identical work per GPU); the K/V,
+    q, k, v values are drawn with a per-rank seed."""
     import torch
 
     from kvstreams.paged_cache import PagedKVCache
@@ -131,7 +133,7 @@ def build_decode(dev, seed: int):
     cache = PagedKVCache(1, HKV, D, block_size=BS, num_blocks=NB, dtype=torch.bfloat16, device=dev, max_seqs=S,
                          max_blocks_per_seq=CTX[1] // BS + 256)
     cache.load_state(range(S), st.tables, st.positions, st.free_list)
-    g = torch.Generator(device=dev).manual_seed(seed)
+    g = torch.Generator(device=dev).manual_seed(value_seed)
     for t in (cache.k, cache.v):
         t.view(-1)[:] = torch.randn(t.numel(), generator=g, device=dev, dtype=torch.float32).bfloat16()
     q = torch.randn(S, HQ, D, generator=g, device=dev).bfloat16()
@@ -235,7 +237,7 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     lib = N.lib()
-    st, cache, q, k, v, rope = build_decode(dev, seed=1000 + rank)
+    st, cache, q, k, v, rope = build_decode(dev, seed=1000, value_seed=1000 + rank)
     inv = rope.table(dev, torch.bfloat16)
     seqs = list(range(S))
     pos = torch.as_tensor(st.next_positions, device=dev)
