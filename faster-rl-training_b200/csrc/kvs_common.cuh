@@ -6,7 +6,7 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
-#include "../../include/kvs_b200.h"
+#include "kvs_b200.h"  // include/ (the build passes -I<repo>/include)
 
 #define KVS_API extern "C" __attribute__((visibility("default")))
 

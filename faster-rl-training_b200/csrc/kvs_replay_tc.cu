@@ -41,21 +41,21 @@ constexpr int E_BYTES = BN * 4;
 constexpr int OFF_Q = 0;
 constexpr int OFF_K = OFF_Q + TILE_BYTES;          // 2 slots
 constexpr int OFF_V = OFF_K + 2 * TILE_BYTES;      // 2 slots
-constexpr int OFF_P = OFF_V + 2 * TILE_BYTES;      // 1 tile of probabilities
-constexpr int OFF_E = OFF_P + TILE_BYTES;          // 2 slots of 128 int32
+constexpr int OFF_E = OFF_V + 2 * TILE_BYTES;      // 2 slots of 128 int32
 constexpr int OFF_RED = OFF_E + 2 * E_BYTES;       // [2 tiles][2 halves][128 rows] f32 row maxima
 constexpr int OFF_LIST = OFF_RED + 2 * 2 * BM * 4; // active key tiles
 constexpr int MAX_KT = 256;  // key tiles per stream: T <= 32768
 constexpr int OFF_BAR = OFF_LIST + MAX_KT * 2;
-constexpr int NBAR = 16;
+constexpr int NBAR = 18;
 constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
 constexpr int SMEM_BYTES = OFF_MISC + 64 + 33 * 4 + 1024;  // + alignment slack
 static_assert(SMEM_BYTES <= 232448, "replay kernel shared memory");
 
 // K and V rings are refilled independently: a K slot as soon as Q K^T has read it, a V slot
-// (with the tile's evicted_at values) once P V has read it.
+// (with the tile's evicted_at values) once P V has read it.  P lives in TMEM, two buffers:
+// PFULLb = P of the tile using buffer b written, PVDONEb = the P V that read buffer b done.
 enum { B_KFULL0 = 0, B_KFULL1, B_VFULL0, B_VFULL1, B_KEMPTY0, B_KEMPTY1, B_VEMPTY0, B_VEMPTY1, B_QFULL,
-       B_SFULL0, B_SFULL1, B_SFREE0, B_SFREE1, B_PFULL, B_ODONE, B_FINAL };
+       B_SFULL0, B_SFULL1, B_SFREE0, B_SFREE1, B_PFULL0, B_PFULL1, B_PVDONE0, B_PVDONE1, B_FINAL };
 
 // named barrier over the softmax warps only (id 1; id 0 is __syncthreads)
 __device__ __forceinline__ void softmax_bar() { asm volatile("bar.sync 1, %0;\n" ::"n"(NSOFT) : "memory"); }
@@ -106,7 +106,8 @@ replay_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     for (int i = 0; i < NBAR; ++i) mbar_init(&bar[i], 1);
     mbar_init(&bar[B_SFREE0], NSOFT);
     mbar_init(&bar[B_SFREE1], NSOFT);
-    mbar_init(&bar[B_PFULL], NSOFT);
+    mbar_init(&bar[B_PFULL0], NSOFT);
+    mbar_init(&bar[B_PFULL1], NSOFT);
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -140,7 +141,8 @@ replay_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   tc_fence_after();
   const int n = *s_n;
   const uint32_t tmem = *tmem_slot;
-  const uint32_t S_col = 0, O_col = 256;
+  // TMEM columns: S buffers [0,128) [128,256), O [256,384), P buffers (bf16 pairs) [384,448) [448,512)
+  const uint32_t S_col = 0, O_col = 256, P_col = 384;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producers
@@ -206,20 +208,17 @@ replay_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         }
         if (k >= 1) {
           const int pk = k - 1, ps = pk & 1;
-          ok = mbar_wait_fast(&bar[B_PFULL], pk & 1, abort_flag);
+          ok = mbar_wait_fast(&bar[B_PFULL0 + ps], (pk >> 1) & 1, abort_flag);
           if (ok) ok = mbar_wait_fast(&bar[B_VFULL0 + ps], (pk >> 1) & 1, abort_flag);
           if (!ok) break;
           tc_fence_after();
-          const uint32_t p_base = smem_addr(smem + OFF_P);
           const uint32_t v_base = smem_addr(smem + OFF_V + ps * TILE_BYTES);
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint32_t a_off = (kk >> 2) * HALF_BYTES + (kk & 3) * 32;
-            umma_bf16(tmem + O_col, desc_kmajor_sw128(p_base + a_off),
-                      desc_mnmajor_sw128(v_base + kk * 2048, HALF_BYTES), ID_PV, (pk > 0 || kk > 0));
-          }
+          for (int kk = 0; kk < 8; ++kk)  // A = P from TMEM: 16 keys = 8 columns per step
+            umma_bf16_tmem_a(tmem + O_col, tmem + P_col + ps * 64 + kk * 8,
+                             desc_mnmajor_sw128(v_base + kk * 2048, HALF_BYTES), ID_PV, (pk > 0 || kk > 0));
           umma_commit(&bar[B_VEMPTY0 + ps]);
-          umma_commit(&bar[B_ODONE]);
+          umma_commit(&bar[B_PVDONE0 + ps]);
         }
       }
       if (!ok) {
@@ -325,19 +324,18 @@ replay_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         pk[(i >> 1) + 1] = pack2(p2, p3);
       }
       l = l * alpha + ((a0 + a1) + (a2 + a3));
-      // P is single-buffered and O must hold every earlier P V: wait for the previous UMMA group
-      if (ok && k >= 1) ok = mbar_wait_fast(&bar[B_ODONE], (k - 1) & 1, abort_flag);
+      // P buffer `slot` was last read by the P V of tile k-2; a rescale of O additionally
+      // needs the P V of tile k-1 (the other buffer) to have landed in O
+      const bool any_rescale = __any_sync(0xffffffffu, rescale);
+      if (ok && k >= 2) ok = mbar_wait_fast(&bar[B_PVDONE0 + slot], ((k >> 1) - 1) & 1, abort_flag);
+      if (ok && k >= 1 && any_rescale)
+        ok = mbar_wait_fast(&bar[B_PVDONE0 + (slot ^ 1)], ((k - 1) >> 1) & 1, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) continue;
-      // bf16 P (this half's 64 keys = 8 chunks of 16 B, 128-byte swizzle like the TMA tiles)
-      uint8_t* Prow = smem + OFF_P + half * HALF_BYTES + r * 128;
-#pragma unroll
-      for (int ch = 0; ch < 8; ++ch) {
-        *reinterpret_cast<uint4*>(Prow + ((ch ^ (r & 7)) << 4)) =
-            make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
-      }
-      if (__any_sync(0xffffffffu, rescale)) {
-        tc_fence_after();
+      tc_fence_after();
+      // bf16 P of this half's 64 keys -> 32 TMEM columns of P buffer `slot`
+      tmem_st32(tl + P_col + slot * 64 + half * 32, pk);
+      if (any_rescale) {
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           uint32_t o[32];
@@ -347,13 +345,12 @@ replay_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
           for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
           tmem_st32(tl + O_col + cbase + c * 32, o);
         }
-        tmem_wait_st();
       }
-      fence_proxy_async_smem();
+      tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&bar[B_PFULL]);
+      mbar_arrive(&bar[B_PFULL0 + slot]);
     }
-    if (ok) ok = mbar_wait(&bar[B_ODONE], (n - 1) & 1, abort_flag);
+    if (ok) ok = mbar_wait(&bar[B_PVDONE0 + ((n - 1) & 1)], ((n - 1) >> 1) & 1, abort_flag);
     // full row sum from the two halves (buffer n&1 was last read at tile n-2)
     red[((n & 1) * 2 + half) * BM + r] = l;
     softmax_bar();
@@ -424,8 +421,9 @@ __global__ void replay_prepass_kernel(const int64_t* __restrict__ ev, int T, int
 // C[128][128] (f32) = A[128][128] (bf16, row-major = K-major) x B, with B given as
 // Bt[128 n][128 k] (K-major, b_mn = 0) or B[128 k][128 n] (MN-major, b_mn = 1).
 __global__ void __launch_bounds__(128, 1)
-umma_selftest_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b, int b_mn,
-                     float* __restrict__ c, int32_t* __restrict__ error) {
+umma_selftest_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b, int mode,
+                     const uint32_t* __restrict__ a_raw, float* __restrict__ c, int32_t* __restrict__ error) {
+  // mode bit 0: B is MN-major; bit 1: A is staged in TMEM (row = lane, bf16 pairs per column)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* As = smem;
@@ -433,20 +431,35 @@ umma_selftest_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_cons
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * TILE_BYTES);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + 2 * TILE_BYTES + 64);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b_mn = mode & 1, a_tmem = (mode >> 1) & 1;
   if (threadIdx.x == 0) {
     mbar_init(&bars[0], 1);
     mbar_init(&bars[1], 1);
     mbar_fence_init();
   }
   if (warp == 0) {
-    tmem_alloc(tslot, 128);
+    tmem_alloc(tslot, 256);
     tmem_relinquish();
   }
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
+  if (a_tmem) {
+    // row r of A -> TMEM lane r, columns 128..191 (64 columns of bf16 pairs)
+    const int r = warp * 32 + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16) + 128;
+    for (int cc = 0; cc < 2; ++cc) {
+      uint32_t v[32];
+      for (int i = 0; i < 32; ++i) v[i] = a_raw[r * 64 + cc * 32 + i];
+      tmem_st32(lane_base + cc * 32, v);
+    }
+    tmem_wait_st();
+  }
+  tc_fence_before();
+  __syncthreads();
   bool ok = true;
   if (threadIdx.x == 0) {
+    tc_fence_after();
     mbar_arrive_expect_tx(&bars[0], 2 * TILE_BYTES);
     tma_load_3d(As, &tm_a, 0, 0, 0, &bars[0]);
     tma_load_3d(As + HALF_BYTES, &tm_a, 64, 0, 0, &bars[0]);
@@ -460,7 +473,10 @@ umma_selftest_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_cons
       for (int kk = 0; kk < 8; ++kk) {
         const uint32_t off = (kk >> 2) * HALF_BYTES + (kk & 3) * 32;
         const uint64_t bd = b_mn ? desc_mnmajor_sw128(b0 + kk * 2048, HALF_BYTES) : desc_kmajor_sw128(b0 + off);
-        umma_bf16(tmem, desc_kmajor_sw128(a0 + off), bd, id, kk > 0);
+        if (a_tmem)
+          umma_bf16_tmem_a(tmem, tmem + 128 + kk * 8, bd, id, kk > 0);
+        else
+          umma_bf16(tmem, desc_kmajor_sw128(a0 + off), bd, id, kk > 0);
       }
       umma_commit(&bars[1]);
     } else {
@@ -484,7 +500,7 @@ umma_selftest_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_cons
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc(tmem, 128);
+    tmem_dealloc(tmem, 256);
   }
 }
 
@@ -604,13 +620,14 @@ int kvs_replay_tc_launch(const kvs_replay_args* a, cudaStream_t st) {
   return launch_rc();
 }
 
-KVS_API int kvs_selftest_umma(const void* a, const void* b, float* c, int32_t b_mn, int32_t* error,
+KVS_API int kvs_selftest_umma(const void* a, const void* b, float* c, int32_t mode, int32_t* error,
                               kvs_stream_t stream) {
-  if (!a || !b || !c || !error || (b_mn != 0 && b_mn != 1)) return KVS_E_ARG;
+  if (!a || !b || !c || !error || mode < 0 || mode > 3) return KVS_E_ARG;
+  if ((reinterpret_cast<uintptr_t>(a) & 15) || (reinterpret_cast<uintptr_t>(b) & 15)) return KVS_E_ARG;
   CUtensorMap ma, mb;
   if (!make_map(&ma, a, 128, 1, 128) || !make_map(&mb, b, 128, 1, 128)) return KVS_E_UNSUPPORTED;
   const int smem = 2 * TILE_BYTES + 128 + 1024;
   if (!set_smem_attr(reinterpret_cast<const void*>(umma_selftest_kernel), 1, smem)) return KVS_E_LAUNCH;
-  umma_selftest_kernel<<<1, 128, smem, to_cuda(stream)>>>(ma, mb, b_mn, c, error);
+  umma_selftest_kernel<<<1, 128, smem, to_cuda(stream)>>>(ma, mb, mode, static_cast<const uint32_t*>(a), c, error);
   return launch_rc();
 }

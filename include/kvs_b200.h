@@ -276,11 +276,12 @@ size_t kvs_replay_scratch_bytes(int32_t batch, int32_t seq_len);
 int kvs_replay_attention(const kvs_replay_args* a, kvs_stream_t stream);
 
 /* Self-test of the tcgen05 path (no reference counterpart): c[128][128] f32 =
- * a[128][128] (bf16 row-major) x B, with B given as bt[128 n][128 k] (b_mn = 0,
- * K-major operand) or b[128 k][128 n] (b_mn = 1, MN-major operand).  *error is set
- * non-zero if an internal wait timed out.  Validates the UMMA descriptors, TMA
- * swizzle and TMEM read-back that the replay kernel relies on. */
-int kvs_selftest_umma(const void* a, const void* b, float* c, int32_t b_mn, int32_t* error,
+ * a[128][128] (bf16 row-major) x B, with B given as bt[128 n][128 k] (mode bit 0 = 0,
+ * K-major operand) or b[128 k][128 n] (bit 0 = 1, MN-major operand); mode bit 1 = 1
+ * stages A in TMEM (the operand form of the replay kernel's P V) instead of shared
+ * memory.  *error is set non-zero if an internal wait timed out.  Validates the UMMA
+ * descriptors, TMA swizzle and TMEM layouts that the replay kernel relies on. */
+int kvs_selftest_umma(const void* a, const void* b, float* c, int32_t mode, int32_t* error,
                       kvs_stream_t stream);
 
 #ifdef __cplusplus

@@ -12,16 +12,18 @@ from oracle import kvs_oracle as O
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("b_mn", [0, 1])
-def test_umma_selftest_matches_matmul(b_mn):
+@pytest.mark.parametrize("mode", [0, 1, 2, 3])
+def test_umma_selftest_matches_matmul(mode):
+    """mode bit 0: B MN-major (else K-major); bit 1: A staged in TMEM (else shared memory)."""
     from kvstreams import _native as N
 
-    g = torch.Generator(device="cuda").manual_seed(b_mn)
+    b_mn = mode & 1
+    g = torch.Generator(device="cuda").manual_seed(mode)
     a = torch.randn(128, 128, generator=g, device="cuda").bfloat16()
     b = torch.randn(128, 128, generator=g, device="cuda").bfloat16()  # bt[n][k] or b[k][n]
     c = torch.zeros(128, 128, device="cuda")
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
-    rc = N.lib().kvs_selftest_umma(a.data_ptr(), b.data_ptr(), c.data_ptr(), b_mn, err.data_ptr(),
+    rc = N.lib().kvs_selftest_umma(a.data_ptr(), b.data_ptr(), c.data_ptr(), mode, err.data_ptr(),
                                    N.stream_ptr())
     assert rc == 0
     torch.cuda.synchronize()
