@@ -447,7 +447,8 @@ def replay_bench(dev, args, rank: int) -> dict:
     return {"workload": f"B={B} T={T} 32q/8kv D128 bf16, 3-8 keep-recent events/stream (one layer)",
             "ms": ms, "visible_pairs": pairs, "visible_frac_of_causal": pairs / causal,
             "tflops": tf, "tc_frac": tf / peaks["bf16_tflops"], "peak_src": peaks["src"],
-            "replay_attn_tok_s": B * T / (ms * 1e-3), "kernel": "replay_tc_kernel (tcgen05/TMEM)"}
+            "replay_attn_tok_s": B * T / (ms * 1e-3),
+            "kernel": "replay_pair_kernel (tcgen05/TMEM, two query heads of a GQA group per CTA)"}
 
 
 def main() -> int:

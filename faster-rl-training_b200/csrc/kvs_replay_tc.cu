@@ -5,16 +5,23 @@
 //   visible(t, s) = s <= t && t < evicted_at[b][s]     (t < lengths[b])
 //   visible(t, s) = s == t                             (padded rows, collate replay.py:221-222)
 //
-// CTA = (stream b, query head h, 128-query tile).  Warp roles (192 threads):
+// Two kernels share the tile skipping, the TMA/UMMA plumbing and the mask:
+//   replay_pair_kernel (GQA group size even, the default there): a CTA takes two query
+//     heads of one KV head at the same 128 positions, so every staged K/V tile feeds four
+//     UMMA tiles and two softmax warpgroups (one full row per thread) alternate with the
+//     tensor pipe; described at the kernel.
+//   replay_tc_kernel (any group size): CTA = (stream b, query head h, 128-query tile),
+//     320 threads:
 //   warp 0      TMA producer: Q tile once; per active key tile the K and V tiles
 //               (128 keys x 128 dims, 128-byte swizzle) and the tile's evicted_at
-//               values, into a 2-slot ring;
+//               values, into 2-slot rings;
 //   warp 1      TMEM owner + UMMA issuer: S[k%2] = Q K^T (8 x M128 N128 K16) into
-//               TMEM, then O += P V (P from shared memory, V MN-major) into TMEM;
-//   warps 2..5  softmax: one thread per query row (TMEM lane), online softmax in
-//               fp32 base 2 with a lazy rescale (O is only rescaled when the row max
-//               grew by more than 2^8), P written as bf16 into a 2-slot smem ring.
-// TMEM: S0 cols [0,128), S1 [128,256), O [256,384) of a 512-column allocation.
+//               TMEM, then O += P V (P from TMEM, V MN-major) into TMEM;
+//   warps 2..9  softmax: two warps per TMEM lane quadrant, each owning 64 key columns of
+//               32 query rows; online softmax in fp32 base 2 with a lazy rescale (O is
+//               only rescaled when the row max grew by more than 2^8), the row maximum
+//               exchanged through shared memory, P written as bf16 into TMEM.
+//     TMEM: S0 [0,128), S1 [128,256), O [256,384), P buffers [384,448) [448,512).
 //
 // Tile skipping: per 128-key tile the prepass records min/max evicted_at; a key
 // tile is skipped when every key in it was evicted at or before the tile's first
@@ -187,7 +194,12 @@ replay_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     if (lane == 0) {
       constexpr uint32_t ID_QK = idesc_bf16(128, 128, 0);
       constexpr uint32_t ID_PV = idesc_bf16(128, 128, 1);
-      const uint32_t q_base = smem_addr(Qs);
+      // descriptors built once, K16 steps add their byte offset >> 4 (see the head-pair kernel)
+      const uint64_t dq = desc_kmajor_sw128(smem_addr(Qs));
+      const uint64_t dk0 = desc_kmajor_sw128(smem_addr(smem + OFF_K));
+      const uint64_t dk1 = desc_kmajor_sw128(smem_addr(smem + OFF_K + TILE_BYTES));
+      const uint64_t dv0 = desc_mnmajor_sw128(smem_addr(smem + OFF_V), HALF_BYTES);
+      const uint64_t dv1 = desc_mnmajor_sw128(smem_addr(smem + OFF_V + TILE_BYTES), HALF_BYTES);
       bool ok = mbar_wait(&bar[B_QFULL], 0, abort_flag);
       for (int k = 0; ok && k <= n; ++k) {
         if (k < n) {
@@ -196,12 +208,11 @@ replay_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
           if (ok && k >= 2) ok = mbar_wait_fast(&bar[B_SFREE0 + slot], ((k >> 1) - 1) & 1, abort_flag);
           if (!ok) break;
           tc_fence_after();
-          const uint32_t k_base = smem_addr(smem + OFF_K + slot * TILE_BYTES);
+          const uint64_t b = slot ? dk1 : dk0;
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
-            const uint32_t off = (kk >> 2) * HALF_BYTES + (kk & 3) * 32;
-            umma_bf16(tmem + S_col + slot * 128, desc_kmajor_sw128(q_base + off), desc_kmajor_sw128(k_base + off),
-                      ID_QK, kk > 0);
+            const uint32_t off = ((kk >> 2) * HALF_BYTES + (kk & 3) * 32) >> 4;
+            umma_bf16(tmem + S_col + slot * 128, dq + off, b + off, ID_QK, kk > 0);
           }
           umma_commit(&bar[B_KEMPTY0 + slot]);
           umma_commit(&bar[B_SFULL0 + slot]);
@@ -212,11 +223,11 @@ replay_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
           if (ok) ok = mbar_wait_fast(&bar[B_VFULL0 + ps], (pk >> 1) & 1, abort_flag);
           if (!ok) break;
           tc_fence_after();
-          const uint32_t v_base = smem_addr(smem + OFF_V + ps * TILE_BYTES);
+          const uint64_t b = ps ? dv1 : dv0;
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)  // A = P from TMEM: 16 keys = 8 columns per step
-            umma_bf16_tmem_a(tmem + O_col, tmem + P_col + ps * 64 + kk * 8,
-                             desc_mnmajor_sw128(v_base + kk * 2048, HALF_BYTES), ID_PV, (pk > 0 || kk > 0));
+            umma_bf16_tmem_a(tmem + O_col, tmem + P_col + ps * 64 + kk * 8, b + ((kk * 2048) >> 4), ID_PV,
+                             (pk > 0 || kk > 0));
           umma_commit(&bar[B_VEMPTY0 + ps]);
           umma_commit(&bar[B_PVDONE0 + ps]);
         }
@@ -366,6 +377,368 @@ replay_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       for (int c = 0; c < 2; ++c) {
         uint32_t o[32];
         tmem_ld32(tl + O_col + cbase + c * 32, o);
+        tmem_wait_ld();
+        if (t < p.T) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4)
+            dst[q4] = make_uint4(pack2(__uint_as_float(o[8 * q4]) * inv, __uint_as_float(o[8 * q4 + 1]) * inv),
+                                 pack2(__uint_as_float(o[8 * q4 + 2]) * inv, __uint_as_float(o[8 * q4 + 3]) * inv),
+                                 pack2(__uint_as_float(o[8 * q4 + 4]) * inv, __uint_as_float(o[8 * q4 + 5]) * inv),
+                                 pack2(__uint_as_float(o[8 * q4 + 6]) * inv, __uint_as_float(o[8 * q4 + 7]) * inv));
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------ head-pair kernel
+// CTA = (stream b, KV head, 128-query tile, pair of query heads h0, h0+1 of the GQA group).
+// Both heads see the same positions, hence the same mask and the same key-tile list, so
+// each K/V tile staged in shared memory feeds four UMMA tiles.  Roles (384 threads):
+//   warpgroup 0   warp 0 TMA producer (lane 0: both Q tiles, then the K ring; lane 1: the
+//                 V ring with each tile's evicted_at values); warp 1 TMEM owner + UMMA
+//                 issuer; warps 2-3 idle.  Registers trimmed to 56 per thread.
+//   warpgroup 1   softmax of head h0: one thread per query row (TMEM lane), all 128 key
+//                 columns of the row in registers, so no cross-warp reduction;
+//   warpgroup 2   softmax of head h0+1.  Both at 224 registers per thread.
+// TMEM: S0 [0,128), S1 [128,256), O0 [256,384), O1 [384,512).  The bf16 probabilities
+// P_t overwrite the first 64 columns of S_t once the row is in registers.
+// UMMA issue order per key tile k:  S0(k), P1(k-1) V(k-1), S1(k), P0(k) V(k).  tcgen05.mma
+// ops of one thread run in issue order, so S_t(k+1) is issued right behind the P_t V
+// that reads the columns it overwrites, and the commit that signals S_t(k+1) also
+// covers that P V: softmax t may rescale O_t as soon as S_t(k+1) is signalled.
+constexpr int NT2 = 384;
+constexpr int REGS_CTRL = 56, REGS_SOFT = 224;
+static_assert(REGS_CTRL * 128 + REGS_SOFT * 256 <= 168 * NT2, "register split exceeds the launch budget");
+constexpr int OFF2_Q = 0;                          // 2 query tiles
+constexpr int OFF2_K = OFF2_Q + 2 * TILE_BYTES;    // 2 slots
+constexpr int OFF2_V = OFF2_K + 2 * TILE_BYTES;    // 2 slots
+constexpr int OFF2_E = OFF2_V + 2 * TILE_BYTES;    // 2 slots of 128 int32
+constexpr int OFF2_LIST = OFF2_E + 2 * E_BYTES;
+constexpr int OFF2_BAR = OFF2_LIST + MAX_KT * 2;
+constexpr int NBAR2 = 14;
+constexpr int OFF2_MISC = OFF2_BAR + NBAR2 * 8;
+constexpr int SMEM2_BYTES = OFF2_MISC + 64 + 33 * 4 + 1024;
+static_assert(SMEM2_BYTES <= 232448, "head-pair replay kernel shared memory");
+static_assert(232448 + 1024 < (1 << 18), "descriptor start-address field (addr >> 4, 14 bits) must not carry");
+
+// descriptor start-address offsets (bytes >> 4) of K16 step kk: for a K-major 128x128 tile,
+// half kk/4 (16 KB apart) and 32 bytes into the 128-byte swizzled row; for the MN-major V
+// tile, rows 16kk.. (2 KB per step).  P supplies 8 TMEM columns (bf16 pairs) per step.
+__host__ __device__ constexpr uint32_t s_step(int kk) { return (uint32_t)(((kk >> 2) * HALF_BYTES + (kk & 3) * 32) >> 4); }
+__host__ __device__ constexpr uint32_t pv_step(int kk) { return (uint32_t)((kk * 2048) >> 4); }
+
+enum { C_KFULL0 = 0, C_KFULL1, C_VFULL0, C_VFULL1, C_KEMPTY0, C_KEMPTY1, C_VEMPTY0, C_VEMPTY1, C_QFULL,
+       C_SFULL0, C_SFULL1, C_PFULL0, C_PFULL1, C_FINAL };
+
+__global__ void __launch_bounds__(NT2, 1)
+replay_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                   const __grid_constant__ CUtensorMap tm_v, const ReplayParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* Qs = smem + OFF2_Q;
+  uint16_t* list = reinterpret_cast<uint16_t*>(smem + OFF2_LIST);  // key tile | 0x8000 if masked
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + OFF2_BAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF2_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF2_MISC + 4);
+  int* s_n = reinterpret_cast<int*>(smem + OFF2_MISC + 8);
+  int* s_scan = reinterpret_cast<int*>(smem + OFF2_MISC + 64);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // CTA order: (stream, KV head) slowest, then query tiles heaviest first, then head pairs
+  const int G = p.Hq / p.Hkv, GP = G >> 1;
+  const int gp = (int)(blockIdx.x % GP);
+  const int rest = (int)(blockIdx.x / GP);
+  const int qt = p.n_qt - 1 - rest % p.n_qt;
+  const int bhk = rest / p.n_qt;
+  const int b = bhk / p.Hkv, hk = bhk % p.Hkv;
+  const int h0 = hk * G + 2 * gp;
+  const int t0 = qt * BM, t1 = t0 + BM - 1;
+  const int L = p.lengths[b];
+
+  if (tid == 0) {
+    for (int i = 0; i < NBAR2; ++i) mbar_init(&bar[i], 1);
+    mbar_init(&bar[C_PFULL0], 128);
+    mbar_init(&bar[C_PFULL1], 128);
+    *abort_flag = 0;
+    mbar_fence_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+
+  // ---- active key tiles for this query tile (same list for every role)
+  {
+    const int real_last = min(t1, L - 1);
+    int carry = 0;
+    for (int base = 0; base <= qt; base += NT2) {
+      const int j = base + tid;
+      int flag = 0;
+      if (j <= qt) {
+        const int emin = p.tile_min[b * p.n_kt + j], emax = p.tile_max[b * p.n_kt + j];
+        const bool active = (j == qt) || (j * BN <= real_last && emax > t0);
+        const bool masked = (j == qt) || (emin <= t1) || (t1 >= L);
+        flag = (active ? 1 : 0) | (masked ? 2 : 0);
+      }
+      int tot = 0;
+      const int pre = block_exclusive_scan(flag & 1, s_scan, &tot);
+      if (flag & 1) list[carry + pre] = (uint16_t)(j | ((flag & 2) ? 0x8000 : 0));
+      carry += tot;
+      __syncthreads();
+    }
+    if (tid == 0) *s_n = carry;
+  }
+  __syncthreads();
+  tc_fence_after();
+  const int n = *s_n;  // >= 1: the diagonal tile is always active
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp < 4) {
+    regs_dealloc<REGS_CTRL>();
+    if (warp == 0 && lane == 0) {
+      // ---------------------------------------------------------- producer: Q tiles, K ring
+      mbar_arrive_expect_tx(&bar[C_QFULL], 2 * TILE_BYTES);
+      for (int t = 0; t < 2; ++t) {
+        tma_load_3d(Qs + t * TILE_BYTES, &tm_q, 0, h0 + t, b * p.T + t0, &bar[C_QFULL]);
+        tma_load_3d(Qs + t * TILE_BYTES + HALF_BYTES, &tm_q, 64, h0 + t, b * p.T + t0, &bar[C_QFULL]);
+      }
+      for (int k = 0; k < n; ++k) {
+        const int slot = k & 1;
+        if (k >= 2 && !mbar_wait(&bar[C_KEMPTY0 + slot], ((k >> 1) - 1) & 1, abort_flag)) {
+          *abort_flag = 1;
+          atomicExch(p.error, 1);
+          break;
+        }
+        const int row = b * p.T + (list[k] & 0x7fff) * BN;
+        uint8_t* Ks = smem + OFF2_K + slot * TILE_BYTES;
+        mbar_arrive_expect_tx(&bar[C_KFULL0 + slot], TILE_BYTES);
+        tma_load_3d(Ks, &tm_k, 0, hk, row, &bar[C_KFULL0 + slot]);
+        tma_load_3d(Ks + HALF_BYTES, &tm_k, 64, hk, row, &bar[C_KFULL0 + slot]);
+      }
+    } else if (warp == 0 && lane == 1) {
+      // ---------------------------------------------------------- producer: V ring + evicted_at
+      for (int k = 0; k < n; ++k) {
+        const int slot = k & 1;
+        if (k >= 2 && !mbar_wait(&bar[C_VEMPTY0 + slot], ((k >> 1) - 1) & 1, abort_flag)) {
+          *abort_flag = 1;
+          atomicExch(p.error, 1);
+          break;
+        }
+        const int j = list[k] & 0x7fff;
+        const int row = b * p.T + j * BN;
+        uint8_t* Vs = smem + OFF2_V + slot * TILE_BYTES;
+        mbar_arrive_expect_tx(&bar[C_VFULL0 + slot], TILE_BYTES + E_BYTES);
+        tma_load_3d(Vs, &tm_v, 0, hk, row, &bar[C_VFULL0 + slot]);
+        tma_load_3d(Vs + HALF_BYTES, &tm_v, 64, hk, row, &bar[C_VFULL0 + slot]);
+        bulk_load(smem + OFF2_E + slot * E_BYTES, p.e32 + (int64_t)b * p.T_pad + j * BN, E_BYTES,
+                  &bar[C_VFULL0 + slot]);
+      }
+    } else if (warp == 1) {
+      // ---------------------------------------------------------- UMMA issuer (whole warp,
+      // one elected lane issues; every value on this path is warp-uniform)
+      constexpr uint32_t ID_QK = idesc_bf16(128, 128, 0);
+      constexpr uint32_t ID_PV = idesc_bf16(128, 128, 1);
+      // Descriptors are built once; each K16 step adds its byte offset >> 4 to the start-address
+      // field (no carry: shared addresses stay below 2^18).
+      const uint64_t dq0 = desc_kmajor_sw128(smem_addr(Qs)), dq1 = desc_kmajor_sw128(smem_addr(Qs + TILE_BYTES));
+      const uint64_t dk0 = desc_kmajor_sw128(smem_addr(smem + OFF2_K));
+      const uint64_t dk1 = desc_kmajor_sw128(smem_addr(smem + OFF2_K + TILE_BYTES));
+      const uint64_t dv0 = desc_mnmajor_sw128(smem_addr(smem + OFF2_V), HALF_BYTES);
+      const uint64_t dv1 = desc_mnmajor_sw128(smem_addr(smem + OFF2_V + TILE_BYTES), HALF_BYTES);
+      // S_t = Q_t K^T (8 x K16 steps over the two 64-column halves)
+      auto issue_s = [&](int t, int slot) {
+        const uint64_t a = t ? dq1 : dq0, b = slot ? dk1 : dk0;
+        const uint32_t d = tmem + t * 128;
+#define KVS_S_STEP(kk) umma_bf16_warp_at<s_step(kk), s_step(kk)>(d, a, b, ID_QK, kk > 0)
+        KVS_S_STEP(0); KVS_S_STEP(1); KVS_S_STEP(2); KVS_S_STEP(3);
+        KVS_S_STEP(4); KVS_S_STEP(5); KVS_S_STEP(6); KVS_S_STEP(7);
+#undef KVS_S_STEP
+      };
+      // O_t (+)= P_t V: P_t from TMEM (16 keys = 8 columns per step), V MN-major
+      auto issue_pv = [&](int t, int slot, bool acc) {
+        const uint64_t b = slot ? dv1 : dv0;
+        const uint32_t d = tmem + 256 + t * 128, a = tmem + t * 128;
+#define KVS_PV_STEP(kk) umma_bf16_tmem_a_warp_at<kk * 8, pv_step(kk)>(d, a, b, ID_PV, (kk > 0) || acc)
+        KVS_PV_STEP(0); KVS_PV_STEP(1); KVS_PV_STEP(2); KVS_PV_STEP(3);
+        KVS_PV_STEP(4); KVS_PV_STEP(5); KVS_PV_STEP(6); KVS_PV_STEP(7);
+#undef KVS_PV_STEP
+      };
+      // all lanes poll; `ok` is made warp-uniform after every wait
+      auto wait = [&](uint64_t* b, int parity) {
+        return __all_sync(0xffffffffu, mbar_wait_fast(b, parity, abort_flag));
+      };
+      bool ok = __all_sync(0xffffffffu, mbar_wait(&bar[C_QFULL], 0, abort_flag));
+      for (int k = 0; ok && k < n; ++k) {
+        const int slot = k & 1, ph = (k >> 1) & 1;
+        ok = wait(&bar[C_KFULL0 + slot], ph);
+        if (!ok) break;
+        tc_fence_after();
+        issue_s(0, slot);
+        umma_commit_warp(&bar[C_SFULL0]);
+        if (k >= 1) {
+          ok = wait(&bar[C_PFULL1], (k - 1) & 1);
+          if (!ok) break;
+          tc_fence_after();
+          issue_pv(1, slot ^ 1, k > 1);
+          umma_commit_warp(&bar[C_VEMPTY0 + (slot ^ 1)]);
+        }
+        issue_s(1, slot);
+        umma_commit_warp(&bar[C_KEMPTY0 + slot]);
+        umma_commit_warp(&bar[C_SFULL1]);
+        ok = wait(&bar[C_PFULL0], k & 1);
+        if (ok) ok = wait(&bar[C_VFULL0 + slot], ph);
+        if (!ok) break;
+        tc_fence_after();
+        issue_pv(0, slot, k > 0);
+      }
+      if (ok) {
+        ok = wait(&bar[C_PFULL1], (n - 1) & 1);
+        if (ok) {
+          tc_fence_after();
+          issue_pv(1, (n - 1) & 1, n > 1);
+        }
+      }
+      if (!ok && lane == 0) {
+        *abort_flag = 1;
+        atomicExch(p.error, 2);
+      }
+      // every issued UMMA has finished before the softmax warps read O and TMEM is released
+      umma_commit_warp(&bar[C_FINAL]);
+      mbar_wait(&bar[C_FINAL], 0, nullptr);
+      __syncwarp();
+    }
+  } else {
+    regs_alloc<REGS_SOFT>();
+    // ------------------------------------------------------------ softmax of head h0 + team
+    const int team = (warp - 4) >> 2;
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const int t = t0 + r;
+    const bool real = t < L;
+    const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16);
+    const uint32_t S_col = team * 128, O_col = 256 + team * 128;
+    uint64_t* sfull = &bar[C_SFULL0 + team];
+    uint64_t* pfull = &bar[C_PFULL0 + team];
+    const float sl2 = p.scale_log2;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int k = 0; k < n; ++k) {
+      const int slot = k & 1;
+      const int j = list[k] & 0x7fff;
+      const bool masked = (list[k] >> 15) & 1;
+      ok = mbar_wait_fast(sfull, k & 1, abort_flag);
+      // evicted_at of the tile arrives with its V slot, which outlives both softmax steps
+      if (ok && masked) ok = mbar_wait_fast(&bar[C_VFULL0 + slot], (k >> 1) & 1, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t v[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(tl + S_col + c * 32, *reinterpret_cast<uint32_t(*)[32]>(v + c * 32));
+      tmem_wait_ld();
+      if (masked) {
+        // key i is visible to row t iff i <= t - j*BN and t < evicted_at (real rows), or
+        // i == t - j*BN (padded rows).  The 128 visibility bits are gathered into four words
+        // first (so the tile's evicted_at values are never all live in registers at once),
+        // then hidden scores become -inf, branch-free.
+        const int lim = t - j * BN;
+        const int4* E4 = reinterpret_cast<const int4*>(smem + OFF2_E + slot * E_BYTES);
+        uint32_t bits[4];
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          uint32_t bw = 0;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const int4 e = E4[w * 8 + q];
+            const int ev[4] = {e.x, e.y, e.z, e.w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int i = 32 * w + 4 * q + u;
+              const bool vis = (i <= lim) && (real ? (t < ev[u]) : (i >= lim));
+              bw |= (vis ? 1u : 0u) << (4 * q + u);
+            }
+          }
+          bits[w] = bw;
+        }
+#pragma unroll
+        for (int i = 0; i < 128; ++i) v[i] = ((bits[i >> 5] >> (i & 31)) & 1) ? v[i] : 0xff800000u;
+      }
+      float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 128; i += 8) {
+        mx0 = fmax3(mx0, __uint_as_float(v[i]), __uint_as_float(v[i + 1]));
+        mx1 = fmax3(mx1, __uint_as_float(v[i + 2]), __uint_as_float(v[i + 3]));
+        mx2 = fmax3(mx2, __uint_as_float(v[i + 4]), __uint_as_float(v[i + 5]));
+        mx3 = fmax3(mx3, __uint_as_float(v[i + 6]), __uint_as_float(v[i + 7]));
+      }
+      const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2;  // sl2 > 0: max commutes
+      float alpha = 1.f;
+      bool rescale = false;
+      if (m == -INFINITY) {
+        m = mx;
+      } else if (mx > m + 8.f) {  // lazy rescale: exact, p <= 2^8 in between
+        alpha = ex2_approx(m - mx);
+        m = mx;
+        rescale = true;
+      }
+      const float neg_m = (m == -INFINITY) ? 0.f : -m;
+      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t pk[16];  // bf16 pairs of keys 32c .. 32c+31
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+          const int e = 32 * c + i;
+          const float p0 = ex2_approx(fmaf(__uint_as_float(v[e]), sl2, neg_m));
+          const float p1 = ex2_approx(fmaf(__uint_as_float(v[e + 1]), sl2, neg_m));
+          const float p2 = ex2_approx(fmaf(__uint_as_float(v[e + 2]), sl2, neg_m));
+          const float p3 = ex2_approx(fmaf(__uint_as_float(v[e + 3]), sl2, neg_m));
+          a0 += p0;
+          a1 += p1;
+          a2 += p2;
+          a3 += p3;
+          pk[i >> 1] = pack2(p0, p1);
+          pk[(i >> 1) + 1] = pack2(p2, p3);
+        }
+        tmem_st16(tl + S_col + c * 16, pk);
+      }
+      l = l * alpha + ((a0 + a1) + (a2 + a3));
+      // O_t holds P V up to tile k-1: its last P V finished before S_t(k) was signalled
+      if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tl + O_col + c * 32, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(tl + O_col + c * 32, o);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(pfull);
+    }
+    if (ok) ok = mbar_wait(&bar[C_FINAL], 0, abort_flag);
+    if (!ok) {
+      *abort_flag = 1;
+      atomicExch(p.error, 3);
+    } else {
+      tc_fence_after();
+      const float inv = 1.f / l;
+      __nv_bfloat16* orow = p.out + (((int64_t)b * p.T + t) * p.Hq + h0 + team) * HD;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[32];
+        tmem_ld32(tl + O_col + c * 32, o);
         tmem_wait_ld();
         if (t < p.T) {
           uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
@@ -549,6 +922,28 @@ bool set_smem_attr(const void* fn, int which, int bytes) {
   return true;
 }
 
+// The head-pair kernel redistributes registers between its warpgroups with setmaxnreg;
+// that is only sound when the block is launched with at least the budget the split adds
+// up to, so the launch register count is checked once per device before its first use.
+bool pair_kernel_ready() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static std::mutex mu;
+  static int state[64] = {};  // 0 unknown, 1 ready, 2 unusable
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev >= 64) return false;
+  if (state[dev] == 0) {
+    cudaFuncAttributes fa;
+    bool ok = cudaFuncGetAttributes(&fa, reinterpret_cast<const void*>(replay_pair_kernel)) == cudaSuccess &&
+              fa.numRegs * NT2 >= REGS_CTRL * 128 + REGS_SOFT * 256 &&
+              cudaFuncSetAttribute(reinterpret_cast<const void*>(replay_pair_kernel),
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES) == cudaSuccess;
+    if (!ok) (void)cudaGetLastError();  // leave no error behind for the next launch check
+    state[dev] = ok ? 1 : 2;
+  }
+  return state[dev] == 1;
+}
+
 struct ReplayScratch {
   int32_t* e32;
   int32_t* tmin;
@@ -615,8 +1010,14 @@ int kvs_replay_tc_launch(const kvs_replay_args* a, cudaStream_t st) {
   p.n_qt = n_kt;
   p.n_kt = n_kt;
   p.scale_log2 = (float)(a->scale * 1.4426950408889634);
-  const int64_t grid = (int64_t)B * a->n_heads * n_kt;
-  replay_tc_kernel<<<(unsigned)grid, NT, SMEM_BYTES, st>>>(mq, mk, mv, p);
+  const int G = a->n_heads / a->n_kv_heads;
+  if (G % 2 == 0 && !(a->flags & 2) && pair_kernel_ready()) {
+    const int64_t grid = (int64_t)B * a->n_heads / 2 * n_kt;
+    replay_pair_kernel<<<(unsigned)grid, NT2, SMEM2_BYTES, st>>>(mq, mk, mv, p);
+  } else {
+    const int64_t grid = (int64_t)B * a->n_heads * n_kt;
+    replay_tc_kernel<<<(unsigned)grid, NT, SMEM_BYTES, st>>>(mq, mk, mv, p);
+  }
   return launch_rc();
 }
 

@@ -71,11 +71,13 @@ def evicted_at_from_spans(cu: np.ndarray, triples: np.ndarray, lengths: Sequence
 
 def replay_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, evicted_at: torch.Tensor,
                      lengths: torch.Tensor, scale: float, out: Optional[torch.Tensor] = None,
-                     force_generic: bool = False) -> torch.Tensor:
+                     force_generic: bool = False, one_head_per_cta: bool = False) -> torch.Tensor:
     """Masked replay attention (model.py:71-74 with the replay.py:62 mask).
 
     q ``[B, T, Hq, D]``, k/v ``[B, T, Hkv, D]`` already rotated; evicted_at ``[B, T]``
-    int64; lengths ``[B]`` int32 (rows past the length attend to themselves only)."""
+    int64; lengths ``[B]`` int32 (rows past the length attend to themselves only).
+    ``force_generic`` selects the exact SIMT kernel; ``one_head_per_cta`` keeps the
+    tensor-core path on its one-query-head-per-CTA kernel for even GQA group sizes."""
     _check_cuda(q, k, v, evicted_at, lengths)
     B, T, Hq, D = q.shape
     Hkv = k.shape[2]
@@ -90,7 +92,8 @@ def replay_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, evicted_
     a = N.KvsReplayArgs(q=q.data_ptr(), k=k.data_ptr(), v=v.data_ptr(), evicted_at=ev.data_ptr(),
                         lengths=ln.data_ptr(), out=out.data_ptr(), scratch=scratch.data_ptr(),
                         scratch_bytes=scratch.numel(), batch=B, seq_len=T, n_heads=Hq, n_kv_heads=Hkv, head_dim=D,
-                        dtype=N.DTYPE_CODE[q.dtype], scale=float(scale), flags=1 if force_generic else 0)
+                        dtype=N.DTYPE_CODE[q.dtype], scale=float(scale),
+                        flags=(1 if force_generic else 0) | (2 if one_head_per_cta else 0))
     N.check(lib.kvs_replay_attention(C.byref(a), N.stream_ptr(q.device)), "kvs_replay_attention")
     return out
 

@@ -269,7 +269,9 @@ typedef struct kvs_replay_args {
   int32_t head_dim;
   int32_t dtype;
   double scale;
-  int32_t flags; /* bit 0: force the generic SIMT kernel */
+  int32_t flags; /* bit 0: force the generic SIMT kernel; bit 1: tensor-core kernel
+                    with one query head per CTA even when the GQA group size is even
+                    (default there: two heads of the group share each K/V tile) */
   int32_t reserved;
 } kvs_replay_args;
 size_t kvs_replay_scratch_bytes(int32_t batch, int32_t seq_len);

@@ -40,13 +40,15 @@ def _inputs(B, T, Hq, Hkv, seed):
     return q, k, v
 
 
+@pytest.mark.parametrize("one_head", [False, True])
 @pytest.mark.parametrize("B,T,Hq,Hkv,evict,lengths", [
-    (2, 1024, 8, 2, True, None),
-    (2, 1000, 4, 4, True, [1000, 700]),
+    (2, 1024, 8, 2, True, None),        # GQA group of 4: head pairs share K/V tiles
+    (2, 1000, 4, 4, True, [1000, 700]),  # group of 1: one head per CTA
     (1, 1536, 4, 1, False, None),       # causal only: unmasked fast-path tiles
     (3, 300, 8, 2, True, [300, 129, 1]),
+    (1, 600, 6, 3, True, None),         # group of 2, ragged last query tile
 ])
-def test_replay_tc_matches_exact_kernel(B, T, Hq, Hkv, evict, lengths):
+def test_replay_tc_matches_exact_kernel(B, T, Hq, Hkv, evict, lengths, one_head):
     from kvstreams import ops
     from kvstreams.workloads import replay_evicted_at
 
@@ -57,7 +59,7 @@ def test_replay_tc_matches_exact_kernel(B, T, Hq, Hkv, evict, lengths):
         ev = np.full((B, T), O.NEVER, dtype=np.int64)
     ln = np.asarray(lengths or [T] * B, dtype=np.int32)
     ev_t, ln_t = torch.from_numpy(ev).cuda(), torch.from_numpy(ln).cuda()
-    fast = ops.replay_attention(q, k, v, ev_t, ln_t, 128 ** -0.5)
+    fast = ops.replay_attention(q, k, v, ev_t, ln_t, 128 ** -0.5, one_head_per_cta=one_head)
     exact = ops.replay_attention(q, k, v, ev_t, ln_t, 128 ** -0.5, force_generic=True)
     torch.cuda.synchronize()
     torch.testing.assert_close(fast.float(), exact.float(), rtol=0, atol=3e-2)
