@@ -593,8 +593,10 @@ replay_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
         issue_s(1, slot);
         umma_commit_warp(&bar[C_KEMPTY0 + slot]);
         umma_commit_warp(&bar[C_SFULL1]);
-        ok = wait(&bar[C_PFULL0], k & 1);
-        if (ok) ok = wait(&bar[C_VFULL0 + slot], ph);
+        // V(k) normally landed long ago: take its wait before head 0's P, which is on the
+        // softmax -> P V -> S critical path
+        ok = wait(&bar[C_VFULL0 + slot], ph);
+        if (ok) ok = wait(&bar[C_PFULL0], k & 1);
         if (!ok) break;
         tc_fence_after();
         issue_pv(0, slot, k > 0);
@@ -697,14 +699,13 @@ replay_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
 #pragma unroll
         for (int i = 0; i < 32; i += 4) {
           const int e = 32 * c + i;
-          const float p0 = ex2_approx(fmaf(__uint_as_float(v[e]), sl2, neg_m));
-          const float p1 = ex2_approx(fmaf(__uint_as_float(v[e + 1]), sl2, neg_m));
-          const float p2 = ex2_approx(fmaf(__uint_as_float(v[e + 2]), sl2, neg_m));
-          const float p3 = ex2_approx(fmaf(__uint_as_float(v[e + 3]), sl2, neg_m));
-          a0 += p0;
-          a1 += p1;
-          a2 += p2;
-          a3 += p3;
+          // scale-and-shift and the row sums as packed pairs (one instruction per two keys)
+          float x0, x1, x2, x3;
+          ffma2(x0, x1, __uint_as_float(v[e]), __uint_as_float(v[e + 1]), sl2, neg_m);
+          ffma2(x2, x3, __uint_as_float(v[e + 2]), __uint_as_float(v[e + 3]), sl2, neg_m);
+          const float p0 = ex2_approx(x0), p1 = ex2_approx(x1), p2 = ex2_approx(x2), p3 = ex2_approx(x3);
+          fadd2(a0, a1, p0, p1);
+          fadd2(a2, a3, p2, p3);
           pk[i >> 1] = pack2(p0, p1);
           pk[(i >> 1) + 1] = pack2(p2, p3);
         }

@@ -109,6 +109,29 @@ __device__ __forceinline__ float exp2_poly(float x) {
   return x < -125.0f ? 0.0f : r;
 }
 
+// Packed fp32 pairs (sm_100 .f32x2 forms): one instruction for two lanes of work.
+// (d0, d1) = (a0, a1) * b + c
+__device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b, float c) {
+  asm("{\n.reg .b64 a, b, c, d;\n"
+      "mov.b64 a, {%2, %3};\n"
+      "mov.b64 b, {%4, %4};\n"
+      "mov.b64 c, {%5, %5};\n"
+      "fma.rn.f32x2 d, a, b, c;\n"
+      "mov.b64 {%0, %1}, d;\n}\n"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b), "f"(c));
+}
+// (s0, s1) += (a0, a1)
+__device__ __forceinline__ void fadd2(float& s0, float& s1, float a0, float a1) {
+  asm("{\n.reg .b64 a, s;\n"
+      "mov.b64 a, {%2, %3};\n"
+      "mov.b64 s, {%0, %1};\n"
+      "add.rn.f32x2 s, s, a;\n"
+      "mov.b64 {%0, %1}, s;\n}\n"
+      : "+f"(s0), "+f"(s1)
+      : "f"(a0), "f"(a1));
+}
+
 // max of three (sm_100 three-input form)
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;
