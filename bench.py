@@ -314,6 +314,7 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
         del hq, hk, hv, hout
         secondary = compaction_bench(dev, args, rank)
         secondary["replay_attention"] = replay_bench(dev, args, rank)
+        secondary["rollout"] = rollout_bench(dev, args, rank)
 
     if rank != 0:
         return
@@ -408,6 +409,83 @@ def compaction_bench(dev, args, rank: int) -> dict:
     return out
 
 
+def rollout_bench(dev, args, rank: int) -> dict:
+    """Config 5 on one GPU: batched KV-streams rollouts of the Llama-3-8B architecture
+    (random init, bf16; 32 layers, d 4096, 32/8 heads, FFN 14336, vocab 128256), 64 rollouts
+    of 24 turns with observation and reply lengths ~U[64, 512] (uniform random ids), Markovian
+    keep_last=1, context budget 8192, 16-token blocks padded.  Timed: ``--rollout-iters`` engine
+    iterations (each one decode step of the generating rollouts plus one batched chunk call
+    for turn starts and reply ends) after ``--rollout-warmup`` iterations, by CUDA events."""
+    import torch
+
+    from kvstreams.compaction.policies import MarkovianPolicy
+    from kvstreams.config import ModelConfig
+    from kvstreams.distributed import reduce_max
+    from kvstreams.engine.batched import BatchedKVStreams, synthetic_episodes
+    from kvstreams.model import TinyLM
+    from kvstreams.paged_cache import PagedKVCache
+
+    torch.cuda.empty_cache()
+    n, budget, turns = args.rollout_streams, 8192, 24
+    cfg = ModelConfig(vocab_size=128256, d_model=4096, n_layers=args.rollout_layers, n_heads=32, n_kv_heads=8,
+                      d_ff=14336, rope_theta=5e5)
+    torch.manual_seed(rank)
+    old = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    try:
+        with dev:
+            model = TinyLM(cfg)
+    finally:
+        torch.set_default_dtype(old)
+    model.eval()
+    # budget + the largest turn reserve (reply 512 + 1 + 15 padding) + a block, per rollout
+    blocks = n * ((budget + 512 + 16 + 16) // 16 + 1)
+    cache = PagedKVCache(cfg.n_layers, cfg.n_kv_heads, cfg.head_dim, block_size=16, num_blocks=blocks,
+                         dtype=torch.bfloat16, device=dev, max_seqs=n)
+    eng = BatchedKVStreams(model, cache, MarkovianPolicy(keep_last=1), context_budget=budget, seed=rank)
+    eps = synthetic_episodes(n, turns=turns, turn_range=(64, 512), prompt_len=64, vocab=cfg.vocab_size,
+                             seed=1000 + rank)
+    W, K = args.rollout_warmup, args.rollout_iters
+    ev = [torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
+    tally = {"decode": 0, "prefill": 0}
+
+    def hook(i, n_dec, n_pre):
+        if i == W:
+            ev[0].record()
+        elif W < i <= W + K:
+            tally["decode"] += n_dec
+            tally["prefill"] += n_pre
+            if i == W + K:
+                ev[1].record()
+
+    from kvstreams import _native as N
+
+    launches0 = N.lib().kvs_launch_count()
+    rolls = eng.run(eps, max_iterations=None if args.rollout_full else W + K, on_iteration=hook)
+    torch.cuda.synchronize(dev)
+    ms = ev[0].elapsed_time(ev[1])
+    ms = reduce_max(ms, dev)
+    out = {
+        "workload": f"{n} rollouts/GPU x {turns} turns, obs/reply ~U[64,512], Llama-3-8B arch "
+                    f"({cfg.n_layers} layers) bf16 random init, Markovian keep_last=1, budget {budget}, bs16",
+        "iterations_timed": K, "ms": ms,
+        "decode_tokens": tally["decode"], "prefill_tokens": tally["prefill"],
+        "rollout_decode_tok_s_per_gpu": tally["decode"] / (ms * 1e-3),
+        "prefill_tok_s_per_gpu": tally["prefill"] / (ms * 1e-3),
+        "ms_per_iteration": ms / K,
+        "library_launches": N.lib().kvs_launch_count() - launches0,
+        "engine_iterations": eng.last_iterations,
+    }
+    if args.rollout_full:
+        out["compactions"] = sum(r.stats.compactions for r in rolls)
+        out["episode_wall_s"] = eng.last_wall
+        out["decode_tokens_total"] = sum(r.stats.decode_tokens for r in rolls)
+        out["rollout_decode_tok_s_per_gpu_whole_episode"] = out["decode_tokens_total"] / eng.last_wall
+    del model, cache, eng, rolls
+    torch.cuda.empty_cache()
+    return out
+
+
 def replay_bench(dev, args, rank: int) -> dict:
     """Masked replay attention, one layer of the Llama-3-8B geometry (32 q / 8 kv heads,
     D 128, bf16): B streams x T tokens with 3-8 keep-recent compaction events each.
@@ -467,6 +545,12 @@ def main() -> int:
     ap.add_argument("--replay-t", type=int, default=32768)
     ap.add_argument("--replay-steps", type=int, default=2)
     ap.add_argument("--replay-only", action="store_true", help="only the replay attention measurement")
+    ap.add_argument("--rollout-streams", type=int, default=64)
+    ap.add_argument("--rollout-layers", type=int, default=32)
+    ap.add_argument("--rollout-warmup", type=int, default=20)
+    ap.add_argument("--rollout-iters", type=int, default=100)
+    ap.add_argument("--rollout-full", action="store_true", help="play the whole episodes (minutes)")
+    ap.add_argument("--rollout-only", action="store_true", help="only the batched rollout measurement")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -492,6 +576,11 @@ def main() -> int:
             r = replay_bench(torch.device("cuda", local_rank), args, rank)
             if rank == 0:
                 print(json.dumps({"replay_attention": r}), flush=True)
+        elif args.rollout_only:
+            torch.cuda.set_device(local_rank)
+            r = rollout_bench(torch.device("cuda", local_rank), args, rank)
+            if rank == 0:
+                print(json.dumps({"rollout": r}), flush=True)
         else:
             run_b200(args, rank, world, local_rank)
     finally:

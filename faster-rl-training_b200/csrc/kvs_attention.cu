@@ -281,17 +281,22 @@ int rope_dispatch(const void* src, void* dst, int dtype, const int64_t* pos, int
 
 // Exact generic decode: rope(q) into out, rope(k)+v into the pool, then attention
 // reading q from out (each warp reads its own row before overwriting it).
-int kvs_decode_generic(const kvs_cache* c, const kvs_batch* b, const kvs_decode_args* a, cudaStream_t st) {
+// RoPE of q (into a->out) and of the new k, and the append of k/v to their slots
+int kvs_rope_append(const kvs_cache* c, const kvs_batch* b, const kvs_decode_args* a, cudaStream_t st) {
   const int n = b->total_tokens;
   int rc = rope_dispatch(a->q, a->out, c->dtype, a->positions, n, a->n_heads, c->head_dim, a->inv_freq, st);
   if (rc) return rc;
   switch (c->dtype) {
-    case KVS_F32: rc = launch_rope_write<float, float>(*c, a->layer, a->slot_blocks, a->slot_offsets, a->k_new, a->v_new, a->positions, n, a->inv_freq, st); break;
-    case KVS_F64: rc = launch_rope_write<double, double>(*c, a->layer, a->slot_blocks, a->slot_offsets, a->k_new, a->v_new, a->positions, n, a->inv_freq, st); break;
-    case KVS_BF16: rc = launch_rope_write<__nv_bfloat16, float>(*c, a->layer, a->slot_blocks, a->slot_offsets, a->k_new, a->v_new, a->positions, n, a->inv_freq, st); break;
-    case KVS_F16: rc = launch_rope_write<__half, float>(*c, a->layer, a->slot_blocks, a->slot_offsets, a->k_new, a->v_new, a->positions, n, a->inv_freq, st); break;
-    default: return KVS_E_UNSUPPORTED;
+    case KVS_F32: return launch_rope_write<float, float>(*c, a->layer, a->slot_blocks, a->slot_offsets, a->k_new, a->v_new, a->positions, n, a->inv_freq, st);
+    case KVS_F64: return launch_rope_write<double, double>(*c, a->layer, a->slot_blocks, a->slot_offsets, a->k_new, a->v_new, a->positions, n, a->inv_freq, st);
+    case KVS_BF16: return launch_rope_write<__nv_bfloat16, float>(*c, a->layer, a->slot_blocks, a->slot_offsets, a->k_new, a->v_new, a->positions, n, a->inv_freq, st);
+    case KVS_F16: return launch_rope_write<__half, float>(*c, a->layer, a->slot_blocks, a->slot_offsets, a->k_new, a->v_new, a->positions, n, a->inv_freq, st);
   }
+  return KVS_E_UNSUPPORTED;
+}
+
+int kvs_decode_generic(const kvs_cache* c, const kvs_batch* b, const kvs_decode_args* a, cudaStream_t st) {
+  const int rc = kvs_rope_append(c, b, a, st);
   if (rc) return rc;
   return kvs_paged_attention(c, b, a->layer, a->out, a->out, a->n_heads, a->scale, reinterpret_cast<kvs_stream_t>(st));
 }

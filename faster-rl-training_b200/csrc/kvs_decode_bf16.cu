@@ -490,9 +490,15 @@ bool g_attr_done[64] = {};
 }  // namespace
 
 // ---------------------------------------------------------------------------- host
+// Scratch: arrival counters first, at a fixed offset and for the largest batch, so that a
+// buffer reused by calls of different batch sizes always finds them where the previous call
+// left them at zero; then the partial rows (data, written before they are read).
+constexpr size_t COUNTER_BYTES = (size_t)MAX_SEQS * 4;
+static_assert(COUNTER_BYTES % 256 == 0, "partials stay 256-byte aligned");
+
 size_t kvs_decode_bf16_scratch(int num_seqs, int grid) {
   const size_t slots = (size_t)grid + num_seqs;
-  return align_up(slots * HQ * D * 4, 256) + align_up(slots * HQ * 2 * 4, 256) + align_up((size_t)num_seqs * 4, 256);
+  return COUNTER_BYTES + align_up(slots * HQ * D * 4, 256) + align_up(slots * HQ * 2 * 4, 256);
 }
 
 bool kvs_decode_bf16_supported(const kvs_cache* c, const kvs_batch* b, int n_heads) {
@@ -535,9 +541,9 @@ int kvs_decode_bf16_launch(const kvs_cache* c, const kvs_batch* b, const kvs_dec
   p.out = static_cast<__nv_bfloat16*>(a->out);
   const size_t slots = (size_t)grid + b->num_seqs;
   uint8_t* s = static_cast<uint8_t*>(a->scratch);
-  p.part_o = reinterpret_cast<float*>(s);
-  p.part_ml = reinterpret_cast<float*>(s + align_up(slots * HQ * D * 4, 256));
-  p.counters = reinterpret_cast<int32_t*>(s + align_up(slots * HQ * D * 4, 256) + align_up(slots * HQ * 2 * 4, 256));
+  p.counters = reinterpret_cast<int32_t*>(s);
+  p.part_o = reinterpret_cast<float*>(s + COUNTER_BYTES);
+  p.part_ml = reinterpret_cast<float*>(s + COUNTER_BYTES + align_up(slots * HQ * D * 4, 256));
   p.scale_log2 = (float)(a->scale * 1.4426950408889634);
   decode_bf16_kernel<<<grid, NTHREADS, SMEM_TOTAL, st>>>(p);
   return launch_rc();

@@ -8,6 +8,11 @@ bool kvs_decode_bf16_supported(const kvs_cache* c, const kvs_batch* b, int n_hea
 int kvs_decode_bf16_grid(int override_ctas);
 int kvs_decode_bf16_launch(const kvs_cache* c, const kvs_batch* b, const kvs_decode_args* a, int grid,
                            cudaStream_t st);
+int kvs_rope_append(const kvs_cache* c, const kvs_batch* b, const kvs_decode_args* a, cudaStream_t st);
+size_t kvs_prefill_tc_scratch(int num_seqs);
+bool kvs_prefill_tc_capable(const kvs_cache* c, int n_heads);
+int kvs_prefill_tc_launch(const kvs_cache* c, const kvs_batch* b, int layer, void* qo, int n_heads, double scale,
+                          void* scratch, cudaStream_t st);
 int kvs_replay_generic(const kvs_replay_args* a, cudaStream_t st);
 size_t kvs_replay_tc_scratch(int B, int T);
 bool kvs_replay_tc_supported(const kvs_replay_args* a);
@@ -22,12 +27,20 @@ void kvs::count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 KVS_API long long kvs_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
-KVS_API size_t kvs_decode_scratch_bytes(const kvs_cache* c, int32_t num_seqs, int32_t n_heads,
-                                        int32_t grid_ctas) {
-  if (!c || num_seqs <= 0) return 0;
+// Scratch of one kvs_paged_decode call: the decode kernel's region (partial rows and
+// zeroed arrival counters), then the chunked-prefill region (per-sequence query-tile offsets).
+static size_t decode_region_bytes(const kvs_cache* c, int num_seqs, int n_heads, int grid_ctas) {
   const kvs_batch probe = {nullptr, nullptr, num_seqs, num_seqs};
   if (!kvs_decode_bf16_supported(c, &probe, n_heads)) return 0;
   return kvs_decode_bf16_scratch(num_seqs, kvs_decode_bf16_grid(grid_ctas));
+}
+
+KVS_API size_t kvs_decode_scratch_bytes(const kvs_cache* c, int32_t num_seqs, int32_t n_heads,
+                                        int32_t grid_ctas) {
+  if (!c || num_seqs <= 0 || n_heads <= 0) return 0;
+  size_t bytes = decode_region_bytes(c, num_seqs, n_heads, grid_ctas);
+  if (kvs_prefill_tc_capable(c, n_heads)) bytes += kvs_prefill_tc_scratch(num_seqs);
+  return bytes;
 }
 
 KVS_API int kvs_paged_decode(const kvs_cache* c, const kvs_batch* b, const kvs_decode_args* a,
@@ -39,11 +52,27 @@ KVS_API int kvs_paged_decode(const kvs_cache* c, const kvs_batch* b, const kvs_d
   if (a->layer < 0 || a->layer >= c->n_layers || a->n_heads <= 0 || a->n_heads % c->n_kv_heads)
     return KVS_E_ARG;
   if (b->num_seqs == 0) return KVS_OK;
-  // the fused kernel stores outputs with 16-byte vector writes
+  const cudaStream_t st = to_cuda(stream);
+  // the tensor-core kernels store outputs with 16-byte vector writes
   const bool out_aligned = (reinterpret_cast<uintptr_t>(a->out) & 15) == 0;
   if (out_aligned && kvs_decode_bf16_supported(c, b, a->n_heads))
-    return kvs_decode_bf16_launch(c, b, a, kvs_decode_bf16_grid(a->grid_ctas), to_cuda(stream));
-  return kvs_decode_generic(c, b, a, to_cuda(stream));
+    return kvs_decode_bf16_launch(c, b, a, kvs_decode_bf16_grid(a->grid_ctas), st);
+  if (b->cu_tokens != nullptr && out_aligned && kvs_prefill_tc_capable(c, a->n_heads)) {
+    // chunks (prefill): RoPE + append, then the tensor-core paged attention in place on `out`
+    const size_t off = decode_region_bytes(c, b->num_seqs, a->n_heads, a->grid_ctas);
+    if (a->scratch && a->scratch_bytes >= off + kvs_prefill_tc_scratch(b->num_seqs)) {
+      int rc = kvs_rope_append(c, b, a, st);
+      if (rc) return rc;
+      uint8_t* region = static_cast<uint8_t*>(a->scratch) + off;
+      rc = kvs_prefill_tc_launch(c, b, a->layer, a->out, a->n_heads, a->scale, region, st);
+      if (rc) return rc;
+      // the whole scratch buffer stays zero between calls: a later decode call with more
+      // sequences finds its arrival counters where these tile offsets were
+      return cudaMemsetAsync(region, 0, kvs_prefill_tc_scratch(b->num_seqs), st) == cudaSuccess ? KVS_OK
+                                                                                       : KVS_E_LAUNCH;
+    }
+  }
+  return kvs_decode_generic(c, b, a, st);
 }
 
 KVS_API size_t kvs_replay_scratch_bytes(int32_t batch, int32_t seq_len) {

@@ -78,6 +78,19 @@ struct ReplayParams {
   float scale_log2;
 };
 
+// Paged prefill source: queries are the new tokens of a batch of sequences (concatenated,
+// rotated), keys/values the live entries of each sequence in the paged pool.
+struct PagedParams {
+  const int32_t* seq_slots;  // [num_seqs]
+  const int32_t* cu_tokens;  // [num_seqs + 1] new-token offsets
+  const int32_t* cu_qt;      // [num_seqs + 1] 128-query tile offsets
+  const int32_t* lengths;    // cache lengths (new tokens included), by slot
+  const int32_t* tables;     // [max_seqs][max_blocks]
+  int32_t* status;           // the cache's status words
+  int num_seqs, max_blocks;
+  int pool_rows;             // num_blocks * 16: a row coordinate past the pool reads zeros
+};
+
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
   __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&v);
@@ -438,9 +451,10 @@ __host__ __device__ constexpr uint32_t pv_step(int kk) { return (uint32_t)((kk *
 enum { C_KFULL0 = 0, C_KFULL1, C_VFULL0, C_VFULL1, C_KEMPTY0, C_KEMPTY1, C_VEMPTY0, C_VEMPTY1, C_QFULL,
        C_SFULL0, C_SFULL1, C_PFULL0, C_PFULL1, C_FINAL };
 
+template <bool PAGED>
 __global__ void __launch_bounds__(NT2, 1)
-replay_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                   const __grid_constant__ CUtensorMap tm_v, const ReplayParams p) {
+pair_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                 const __grid_constant__ CUtensorMap tm_v, const ReplayParams p, const PagedParams g) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* Qs = smem + OFF2_Q;
@@ -452,16 +466,55 @@ replay_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
   int* s_scan = reinterpret_cast<int*>(smem + OFF2_MISC + 64);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  // CTA order: (stream, KV head) slowest, then query tiles heaviest first, then head pairs
+  // a bounded wait that expired: replay reports the site in its error word, the paged path
+  // in the cache's status words (KVS_ST_KERNEL_TIMEOUT, site, CTA)
+  auto fail_site = [&](int site) {
+    if (PAGED)
+      set_status(g.status, KVS_ST_KERNEL_TIMEOUT, site, (int)blockIdx.x, 0);
+    else
+      atomicExch(p.error, site);
+  };
   const int G = p.Hq / p.Hkv, GP = G >> 1;
-  const int gp = (int)(blockIdx.x % GP);
-  const int rest = (int)(blockIdx.x / GP);
-  const int qt = p.n_qt - 1 - rest % p.n_qt;
-  const int bhk = rest / p.n_qt;
-  const int b = bhk / p.Hkv, hk = bhk % p.Hkv;
+  int gp, hk, qt, b = 0, t0 = 0, t1 = 0, L = 0;  // replay: stream b, query rows t0..t1, length L
+  int seq_slot = 0, tok0 = 0, Ti = 0, n_all = 0, n_past = 0;  // paged: cache slot, new tokens, live entries
+  int q_row0;  // TMA row of the tile's first query
+  if (!PAGED) {
+    // CTA order: (stream, KV head) slowest, then query tiles heaviest first, then head pairs
+    gp = (int)(blockIdx.x % GP);
+    const int rest = (int)(blockIdx.x / GP);
+    qt = p.n_qt - 1 - rest % p.n_qt;
+    const int bhk = rest / p.n_qt;
+    b = bhk / p.Hkv;
+    hk = bhk % p.Hkv;
+    t0 = qt * BM;
+    t1 = t0 + BM - 1;
+    L = p.lengths[b];
+    q_row0 = b * p.T + t0;
+  } else {
+    // CTA order: query tiles of the batch (sequence by sequence) slowest, then KV head, then
+    // head pairs.  The grid is an upper bound on the number of tiles; surplus CTAs leave here.
+    gp = (int)(blockIdx.x % GP);
+    hk = (int)((blockIdx.x / GP) % p.Hkv);
+    const int item = (int)(blockIdx.x / (GP * p.Hkv));
+    if (item >= g.cu_qt[g.num_seqs]) return;
+    int lo = 0, hi = g.num_seqs - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (g.cu_qt[mid] <= item) lo = mid; else hi = mid - 1;
+    }
+    qt = item - g.cu_qt[lo];
+    seq_slot = g.seq_slots[lo];
+    tok0 = g.cu_tokens[lo];
+    Ti = g.cu_tokens[lo + 1] - tok0;
+    n_all = g.lengths[seq_slot];
+    n_past = n_all - Ti;
+    q_row0 = tok0 + qt * BM;
+    if ((n_all + BN - 1) / BN > MAX_KT) {  // the key-tile list holds MAX_KT tiles
+      if (tid == 0) set_status(g.status, KVS_ST_SEQ_TOO_LONG, seq_slot, n_all, 0);
+      return;
+    }
+  }
   const int h0 = hk * G + 2 * gp;
-  const int t0 = qt * BM, t1 = t0 + BM - 1;
-  const int L = p.lengths[b];
 
   if (tid == 0) {
     for (int i = 0; i < NBAR2; ++i) mbar_init(&bar[i], 1);
@@ -475,18 +528,27 @@ replay_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
     tmem_relinquish();
   }
 
-  // ---- active key tiles for this query tile (same list for every role)
+  // ---- active key tiles for this query tile (same list for every role).  Replay: tiles
+  // up to the diagonal, skipping those every key of which was evicted before the first
+  // query.  Paged: every tile up to the last visible key of the tile's last query; masked
+  // where the causal limit or the end of the sequence cuts through.
   {
     const int real_last = min(t1, L - 1);
+    const int jlast = PAGED ? (n_past + min(qt * BM + BM - 1, Ti - 1)) / BN : qt;
     int carry = 0;
-    for (int base = 0; base <= qt; base += NT2) {
+    for (int base = 0; base <= jlast; base += NT2) {
       const int j = base + tid;
       int flag = 0;
-      if (j <= qt) {
-        const int emin = p.tile_min[b * p.n_kt + j], emax = p.tile_max[b * p.n_kt + j];
-        const bool active = (j == qt) || (j * BN <= real_last && emax > t0);
-        const bool masked = (j == qt) || (emin <= t1) || (t1 >= L);
-        flag = (active ? 1 : 0) | (masked ? 2 : 0);
+      if (j <= jlast) {
+        if (PAGED) {
+          const bool masked = (j * BN + BN - 1 > n_past + qt * BM) || (j * BN + BN > n_all);
+          flag = 1 | (masked ? 2 : 0);
+        } else {
+          const int emin = p.tile_min[b * p.n_kt + j], emax = p.tile_max[b * p.n_kt + j];
+          const bool active = (j == qt) || (j * BN <= real_last && emax > t0);
+          const bool masked = (j == qt) || (emin <= t1) || (t1 >= L);
+          flag = (active ? 1 : 0) | (masked ? 2 : 0);
+        }
       }
       int tot = 0;
       const int pre = block_exclusive_scan(flag & 1, s_scan, &tot);
@@ -500,6 +562,24 @@ replay_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
   tc_fence_after();
   const int n = *s_n;  // >= 1: the diagonal tile is always active
   const uint32_t tmem = *tmem_slot;
+  // one 128-key x 128-dim tile of K or V into a 128-byte swizzled shared tile: replay rows
+  // are contiguous; paged keys come as eight 16-token pool blocks (2 KB per half each),
+  // and blocks past the sequence are read out of bounds of the pool, i.e. as zeros.
+  auto load_kv = [&](uint8_t* dst, const CUtensorMap* map, int j, uint64_t* bb) {
+    if (!PAGED) {
+      const int row = b * p.T + j * BN;
+      tma_load_3d(dst, map, 0, hk, row, bb);
+      tma_load_3d(dst + HALF_BYTES, map, 64, hk, row, bb);
+    } else {
+      const int32_t* tab = g.tables + (int64_t)seq_slot * g.max_blocks + j * (BN / 16);
+#pragma unroll 1
+      for (int b8 = 0; b8 < BN / 16; ++b8) {
+        const int row = (j * BN + b8 * 16 < n_all) ? tab[b8] * 16 : g.pool_rows;
+        tma_load_3d(dst + b8 * 2048, map, 0, hk, row, bb);
+        tma_load_3d(dst + HALF_BYTES + b8 * 2048, map, 64, hk, row, bb);
+      }
+    }
+  };
 
   if (warp < 4) {
     regs_dealloc<REGS_CTRL>();
@@ -507,39 +587,37 @@ replay_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
       // ---------------------------------------------------------- producer: Q tiles, K ring
       mbar_arrive_expect_tx(&bar[C_QFULL], 2 * TILE_BYTES);
       for (int t = 0; t < 2; ++t) {
-        tma_load_3d(Qs + t * TILE_BYTES, &tm_q, 0, h0 + t, b * p.T + t0, &bar[C_QFULL]);
-        tma_load_3d(Qs + t * TILE_BYTES + HALF_BYTES, &tm_q, 64, h0 + t, b * p.T + t0, &bar[C_QFULL]);
+        tma_load_3d(Qs + t * TILE_BYTES, &tm_q, 0, h0 + t, q_row0, &bar[C_QFULL]);
+        tma_load_3d(Qs + t * TILE_BYTES + HALF_BYTES, &tm_q, 64, h0 + t, q_row0, &bar[C_QFULL]);
       }
       for (int k = 0; k < n; ++k) {
-        const int slot = k & 1;
-        if (k >= 2 && !mbar_wait(&bar[C_KEMPTY0 + slot], ((k >> 1) - 1) & 1, abort_flag)) {
+        const int ks = k & 1;
+        if (k >= 2 && !mbar_wait(&bar[C_KEMPTY0 + ks], ((k >> 1) - 1) & 1, abort_flag)) {
           *abort_flag = 1;
-          atomicExch(p.error, 1);
+          fail_site(1);
           break;
         }
-        const int row = b * p.T + (list[k] & 0x7fff) * BN;
-        uint8_t* Ks = smem + OFF2_K + slot * TILE_BYTES;
-        mbar_arrive_expect_tx(&bar[C_KFULL0 + slot], TILE_BYTES);
-        tma_load_3d(Ks, &tm_k, 0, hk, row, &bar[C_KFULL0 + slot]);
-        tma_load_3d(Ks + HALF_BYTES, &tm_k, 64, hk, row, &bar[C_KFULL0 + slot]);
+        const int j = list[k] & 0x7fff;
+        uint8_t* Ks = smem + OFF2_K + ks * TILE_BYTES;
+        mbar_arrive_expect_tx(&bar[C_KFULL0 + ks], TILE_BYTES);
+        load_kv(Ks, &tm_k, j, &bar[C_KFULL0 + ks]);
       }
     } else if (warp == 0 && lane == 1) {
       // ---------------------------------------------------------- producer: V ring + evicted_at
       for (int k = 0; k < n; ++k) {
-        const int slot = k & 1;
-        if (k >= 2 && !mbar_wait(&bar[C_VEMPTY0 + slot], ((k >> 1) - 1) & 1, abort_flag)) {
+        const int vs = k & 1;
+        if (k >= 2 && !mbar_wait(&bar[C_VEMPTY0 + vs], ((k >> 1) - 1) & 1, abort_flag)) {
           *abort_flag = 1;
-          atomicExch(p.error, 1);
+          fail_site(1);
           break;
         }
         const int j = list[k] & 0x7fff;
-        const int row = b * p.T + j * BN;
-        uint8_t* Vs = smem + OFF2_V + slot * TILE_BYTES;
-        mbar_arrive_expect_tx(&bar[C_VFULL0 + slot], TILE_BYTES + E_BYTES);
-        tma_load_3d(Vs, &tm_v, 0, hk, row, &bar[C_VFULL0 + slot]);
-        tma_load_3d(Vs + HALF_BYTES, &tm_v, 64, hk, row, &bar[C_VFULL0 + slot]);
-        bulk_load(smem + OFF2_E + slot * E_BYTES, p.e32 + (int64_t)b * p.T_pad + j * BN, E_BYTES,
-                  &bar[C_VFULL0 + slot]);
+        uint8_t* Vs = smem + OFF2_V + vs * TILE_BYTES;
+        mbar_arrive_expect_tx(&bar[C_VFULL0 + vs], TILE_BYTES + (PAGED ? 0 : E_BYTES));
+        load_kv(Vs, &tm_v, j, &bar[C_VFULL0 + vs]);
+        if (!PAGED)
+          bulk_load(smem + OFF2_E + vs * E_BYTES, p.e32 + (int64_t)b * p.T_pad + j * BN, E_BYTES,
+                    &bar[C_VFULL0 + vs]);
       }
     } else if (warp == 1) {
       // ---------------------------------------------------------- UMMA issuer (whole warp,
@@ -610,7 +688,7 @@ replay_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
       }
       if (!ok && lane == 0) {
         *abort_flag = 1;
-        atomicExch(p.error, 2);
+        fail_site(2);
       }
       // every issued UMMA has finished before the softmax warps read O and TMEM is released
       umma_commit_warp(&bar[C_FINAL]);
@@ -623,8 +701,10 @@ replay_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
     const int team = (warp - 4) >> 2;
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
-    const int t = t0 + r;
+    const int t = t0 + r;  // replay: query position
     const bool real = t < L;
+    const int ci = qt * BM + r;                              // paged: index among the new tokens
+    const int qidx = (ci < Ti) ? n_past + ci : -1;           // paged: last visible key (-1: no row)
     const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16);
     const uint32_t S_col = team * 128, O_col = 256 + team * 128;
     uint64_t* sfull = &bar[C_SFULL0 + team];
@@ -638,7 +718,7 @@ replay_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
       const bool masked = (list[k] >> 15) & 1;
       ok = mbar_wait_fast(sfull, k & 1, abort_flag);
       // evicted_at of the tile arrives with its V slot, which outlives both softmax steps
-      if (ok && masked) ok = mbar_wait_fast(&bar[C_VFULL0 + slot], (k >> 1) & 1, abort_flag);
+      if (!PAGED && ok && masked) ok = mbar_wait_fast(&bar[C_VFULL0 + slot], (k >> 1) & 1, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
@@ -651,24 +731,32 @@ replay_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
         // i == t - j*BN (padded rows).  The 128 visibility bits are gathered into four words
         // first (so the tile's evicted_at values are never all live in registers at once),
         // then hidden scores become -inf, branch-free.
-        const int lim = t - j * BN;
-        const int4* E4 = reinterpret_cast<const int4*>(smem + OFF2_E + slot * E_BYTES);
         uint32_t bits[4];
+        if (PAGED) {
+          // key i of the tile is visible iff j*BN + i <= qidx (a prefix of the tile)
+          const int lim = qidx - j * BN;
 #pragma unroll
-        for (int w = 0; w < 4; ++w) {
-          uint32_t bw = 0;
+          for (int w = 0; w < 4; ++w)
+            bits[w] = lim >= 32 * w + 31 ? 0xffffffffu : (lim < 32 * w ? 0u : (2u << (lim - 32 * w)) - 1u);
+        } else {
+          const int lim = t - j * BN;
+          const int4* E4 = reinterpret_cast<const int4*>(smem + OFF2_E + slot * E_BYTES);
 #pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const int4 e = E4[w * 8 + q];
-            const int ev[4] = {e.x, e.y, e.z, e.w};
+          for (int w = 0; w < 4; ++w) {
+            uint32_t bw = 0;
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const int i = 32 * w + 4 * q + u;
-              const bool vis = (i <= lim) && (real ? (t < ev[u]) : (i >= lim));
-              bw |= (vis ? 1u : 0u) << (4 * q + u);
+            for (int q = 0; q < 8; ++q) {
+              const int4 e = E4[w * 8 + q];
+              const int ev[4] = {e.x, e.y, e.z, e.w};
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                const int i = 32 * w + 4 * q + u;
+                const bool vis = (i <= lim) && (real ? (t < ev[u]) : (i >= lim));
+                bw |= (vis ? 1u : 0u) << (4 * q + u);
+              }
             }
+            bits[w] = bw;
           }
-          bits[w] = bw;
         }
 #pragma unroll
         for (int i = 0; i < 128; ++i) v[i] = ((bits[i >> 5] >> (i & 31)) & 1) ? v[i] : 0xff800000u;
@@ -731,17 +819,19 @@ replay_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
     if (ok) ok = mbar_wait(&bar[C_FINAL], 0, abort_flag);
     if (!ok) {
       *abort_flag = 1;
-      atomicExch(p.error, 3);
+      fail_site(3);
     } else {
       tc_fence_after();
       const float inv = 1.f / l;
-      __nv_bfloat16* orow = p.out + (((int64_t)b * p.T + t) * p.Hq + h0 + team) * HD;
+      const int64_t orow_idx = PAGED ? (int64_t)tok0 + ci : (int64_t)b * p.T + t;
+      const bool store = PAGED ? ci < Ti : t < p.T;
+      __nv_bfloat16* orow = p.out + (orow_idx * p.Hq + h0 + team) * HD;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t o[32];
         tmem_ld32(tl + O_col + c * 32, o);
         tmem_wait_ld();
-        if (t < p.T) {
+        if (store) {
           uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
 #pragma unroll
           for (int q4 = 0; q4 < 4; ++q4)
@@ -896,13 +986,14 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// 3-D bf16 map over rows of `inner` elements: dims {inner, mid, outer}, box {64, 1, 128}, 128-byte swizzle
-bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t mid, uint64_t outer) {
+// 3-D bf16 map over rows of `inner` elements: dims {inner, mid, outer}, box {64, 1, rows},
+// 128-byte swizzle
+bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t mid, uint64_t outer, uint32_t rows = 128) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   const cuuint64_t dims[3] = {inner, mid, outer};
   const cuuint64_t strides[2] = {inner * 2, inner * mid * 2};
-  const cuuint32_t box[3] = {64, 1, 128};
+  const cuuint32_t box[3] = {64, 1, rows};
   const cuuint32_t estr[3] = {1, 1, 1};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -926,6 +1017,7 @@ bool set_smem_attr(const void* fn, int which, int bytes) {
 // The head-pair kernel redistributes registers between its warpgroups with setmaxnreg;
 // that is only sound when the block is launched with at least the budget the split adds
 // up to, so the launch register count is checked once per device before its first use.
+template <bool PAGED>
 bool pair_kernel_ready() {
   int dev = 0;
   cudaGetDevice(&dev);
@@ -935,9 +1027,9 @@ bool pair_kernel_ready() {
   if (dev >= 64) return false;
   if (state[dev] == 0) {
     cudaFuncAttributes fa;
-    bool ok = cudaFuncGetAttributes(&fa, reinterpret_cast<const void*>(replay_pair_kernel)) == cudaSuccess &&
+    bool ok = cudaFuncGetAttributes(&fa, reinterpret_cast<const void*>(pair_attn_kernel<PAGED>)) == cudaSuccess &&
               fa.numRegs * NT2 >= REGS_CTRL * 128 + REGS_SOFT * 256 &&
-              cudaFuncSetAttribute(reinterpret_cast<const void*>(replay_pair_kernel),
+              cudaFuncSetAttribute(reinterpret_cast<const void*>(pair_attn_kernel<PAGED>),
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES) == cudaSuccess;
     if (!ok) (void)cudaGetLastError();  // leave no error behind for the next launch check
     state[dev] = ok ? 1 : 2;
@@ -1012,13 +1104,80 @@ int kvs_replay_tc_launch(const kvs_replay_args* a, cudaStream_t st) {
   p.n_kt = n_kt;
   p.scale_log2 = (float)(a->scale * 1.4426950408889634);
   const int G = a->n_heads / a->n_kv_heads;
-  if (G % 2 == 0 && !(a->flags & 2) && pair_kernel_ready()) {
+  if (G % 2 == 0 && !(a->flags & 2) && pair_kernel_ready<false>()) {
     const int64_t grid = (int64_t)B * a->n_heads / 2 * n_kt;
-    replay_pair_kernel<<<(unsigned)grid, NT2, SMEM2_BYTES, st>>>(mq, mk, mv, p);
+    pair_attn_kernel<false><<<(unsigned)grid, NT2, SMEM2_BYTES, st>>>(mq, mk, mv, p, PagedParams{});
   } else {
     const int64_t grid = (int64_t)B * a->n_heads * n_kt;
     replay_tc_kernel<<<(unsigned)grid, NT, SMEM_BYTES, st>>>(mq, mk, mv, p);
   }
+  return launch_rc();
+}
+
+// ------------------------------------------------------------------ paged prefill (host)
+namespace {
+// cu_qt[i] = number of 128-query tiles of sequences 0..i-1 (one CTA)
+__global__ void prefill_tiles_kernel(const int32_t* __restrict__ cu_tokens, int num_seqs, int32_t* __restrict__ cu_qt) {
+  __shared__ int scan[33];
+  int carry = 0;
+  for (int base = 0; base < num_seqs; base += blockDim.x) {
+    const int i = base + threadIdx.x;
+    const int tiles = i < num_seqs ? (cu_tokens[i + 1] - cu_tokens[i] + BM - 1) / BM : 0;
+    int tot = 0;
+    const int pre = block_exclusive_scan(tiles, scan, &tot);
+    if (i < num_seqs) cu_qt[i] = carry + pre;
+    carry += tot;
+  }
+  if (threadIdx.x == 0) cu_qt[num_seqs] = carry;
+}
+}  // namespace
+
+size_t kvs_prefill_tc_scratch(int num_seqs) { return align_up((size_t)(num_seqs + 1) * 4, 256); }
+
+// bf16, D 128, 16-token blocks, an even GQA group (sequences longer than MAX_KT * 128 entries
+// are reported through the status words)
+bool kvs_prefill_tc_capable(const kvs_cache* c, int n_heads) {
+  return c->dtype == KVS_BF16 && c->head_dim == HD && c->block_size == 16 && n_heads % c->n_kv_heads == 0 &&
+         (n_heads / c->n_kv_heads) % 2 == 0 && (int64_t)c->num_blocks * c->block_size < INT32_MAX &&
+         encode_fn() != nullptr;
+}
+
+// Attention of the new tokens of a chunked batch (q already rotated, in `qo`; their k/v already
+// appended) over the paged pool, written back into `qo`.  `scratch` holds cu_qt.
+int kvs_prefill_tc_launch(const kvs_cache* c, const kvs_batch* b, int layer, void* qo, int n_heads, double scale,
+                          void* scratch, cudaStream_t st) {
+  if (!pair_kernel_ready<true>()) return KVS_E_UNSUPPORTED;
+  int32_t* cu_qt = static_cast<int32_t*>(scratch);
+  prefill_tiles_kernel<<<1, 1024, 0, st>>>(b->cu_tokens, b->num_seqs, cu_qt);
+  int rc = launch_rc();
+  if (rc) return rc;
+  const uint64_t pool_rows = (uint64_t)c->num_blocks * c->block_size;
+  const size_t layer_elems = (size_t)pool_rows * c->n_kv_heads * c->head_dim;
+  const __nv_bfloat16* kl = static_cast<const __nv_bfloat16*>(c->k) + (size_t)layer * layer_elems;
+  const __nv_bfloat16* vl = static_cast<const __nv_bfloat16*>(c->v) + (size_t)layer * layer_elems;
+  CUtensorMap mq, mk, mv;
+  if (!make_map(&mq, qo, HD, n_heads, (uint64_t)b->total_tokens) ||
+      !make_map(&mk, kl, HD, c->n_kv_heads, pool_rows, 16) || !make_map(&mv, vl, HD, c->n_kv_heads, pool_rows, 16))
+    return KVS_E_UNSUPPORTED;
+  ReplayParams p{};
+  p.out = static_cast<__nv_bfloat16*>(qo);
+  p.Hq = n_heads;
+  p.Hkv = c->n_kv_heads;
+  p.scale_log2 = (float)(scale * 1.4426950408889634);
+  PagedParams g;
+  g.seq_slots = b->seq_slots;
+  g.cu_tokens = b->cu_tokens;
+  g.cu_qt = cu_qt;
+  g.lengths = c->lengths;
+  g.tables = c->tables;
+  g.status = c->status;
+  g.num_seqs = b->num_seqs;
+  g.max_blocks = c->max_blocks;
+  g.pool_rows = (int)pool_rows;
+  // upper bound on the query tiles of the batch: ceil(total / 128) + one partial tile per sequence
+  const int64_t items = ((int64_t)b->total_tokens + BM - 1) / BM + b->num_seqs;
+  const int64_t grid = items * n_heads / 2;
+  pair_attn_kernel<true><<<(unsigned)grid, NT2, SMEM2_BYTES, st>>>(mq, mk, mv, p, g);
   return launch_rc();
 }
 

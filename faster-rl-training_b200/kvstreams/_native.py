@@ -33,6 +33,8 @@ ST_INV_HOLE = 8
 ST_INV_ORDER = 9
 ST_SPAN_CAPACITY = 10
 ST_OWNER = 11
+ST_KERNEL_TIMEOUT = 12
+ST_SEQ_TOO_LONG = 13
 
 RC_NAMES = {-1: "bad argument", -2: "unsupported shape/dtype", -3: "CUDA launch error", -4: "scratch too small",
             -5: "request exceeds the built-in scratch of a no-alloc entry point"}

@@ -252,6 +252,12 @@ class PagedKVCache:
             raise ValueError(f"double free of block {a}")
         if code == N.ST_TRUNCATE:
             raise ValueError("cannot truncate more tokens than are live")
+        if code == N.ST_SEQ_TOO_LONG:
+            raise RuntimeError(f"sequence in slot {a} has {b} live entries, more than the 32768 the "
+                               "tensor-core prefill attends over")
+        if code == N.ST_KERNEL_TIMEOUT:
+            raise RuntimeError(f"a tensor-core attention kernel timed out waiting (site {a}, CTA {b}); "
+                               "its outputs are invalid")
         raise RuntimeError(f"kvstreams device status {code} (details {a}, {b}, {c})")
 
     def sync(self) -> None:

@@ -58,7 +58,11 @@ enum kvs_status {
   KVS_ST_INV_HOLE = 8,         /* paged_cache.py:270-271 */
   KVS_ST_INV_ORDER = 9,        /* paged_cache.py:272-273 */
   KVS_ST_SPAN_CAPACITY = 10,   /* evicted-span output buffer too small */
-  KVS_ST_OWNER = 11            /* block freed by a sequence that does not own it */
+  KVS_ST_OWNER = 11,           /* block freed by a sequence that does not own it */
+  KVS_ST_KERNEL_TIMEOUT = 12,  /* a bounded wait inside a tensor-core kernel expired; its outputs
+                                  are invalid (no reference counterpart) */
+  KVS_ST_SEQ_TOO_LONG = 13     /* a sequence is longer than the 32768 entries the tensor-core
+                                  prefill attends over (no reference counterpart) */
 };
 
 /* CacheStats counters (paged_cache.py:70-78), int64 each */
@@ -232,8 +236,10 @@ typedef struct kvs_decode_args {
   int32_t grid_ctas;        /* CTAs of the fused decode kernel (0 = one per SM) */
   int32_t reserved;
 } kvs_decode_args;
-/* scratch of kvs_paged_decode: split partials and per-sequence arrival counters;
- * zero it once when allocated (the kernel leaves the counters at zero). */
+/* scratch of kvs_paged_decode: split partials and per-sequence arrival counters of the
+ * fused decode kernel, then (bf16, head_dim 128, 16-token blocks, even GQA group) the
+ * query-tile offsets of the tensor-core chunked prefill.  Zero it once when allocated:
+ * every call leaves it zero, whatever the batch size of the previous call. */
 size_t kvs_decode_scratch_bytes(const kvs_cache* c, int32_t num_seqs, int32_t n_heads,
                                 int32_t grid_ctas);
 int kvs_paged_decode(const kvs_cache* c, const kvs_batch* b, const kvs_decode_args* a,

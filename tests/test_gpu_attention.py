@@ -34,11 +34,12 @@ def test_rope_kernel_matches_reference(golden_rope, D, prec):
     np.testing.assert_allclose(y.cpu().numpy(), want, rtol=0, atol=tol * max(1.0, np.abs(want).max()))
 
 
-def _setup_cache(dtype, D, Hkv, bs, S, ctx, seed):
+def _setup_cache(dtype, D, Hkv, bs, S, ctx, seed, extra_tokens=0):
     from kvstreams.paged_cache import PagedKVCache
     from kvstreams.workloads import decode_state
 
-    st = decode_state(num_streams=S, ctx_range=ctx, block_size=bs, num_blocks=S * (ctx[1] // bs + 8),
+    per_stream = (ctx[1] + extra_tokens) // bs + 8
+    st = decode_state(num_streams=S, ctx_range=ctx, block_size=bs, num_blocks=S * per_stream,
                       evicted_spans_range=(1, 3), seed=seed)
     cache = PagedKVCache(1, Hkv, D, block_size=bs, num_blocks=st.num_blocks, dtype=dtype, max_seqs=S)
     cache.load_state(range(S), st.tables, st.positions, st.free_list)
@@ -157,3 +158,104 @@ def test_evicted_at_kernel_matches_reference(golden_evicted_at):
     for i in range(n):
         np.testing.assert_array_equal(out[i, : lens[i]], g[f"c{i}_out"])
         assert (out[i, lens[i]:] == O.NEVER).all()
+
+
+@pytest.mark.parametrize("Hq,Hkv,counts,ctx", [
+    (32, 8, [300, 1, 129, 128], (3, 700)),   # several query tiles, a single token, tile edges
+    (8, 2, [17, 256, 200], (1000, 2500)),    # long contexts: key tiles across many blocks
+    (4, 2, [5, 64, 130, 1, 90], (1, 40)),    # group of 2; tiny contexts
+])
+def test_paged_prefill_chunks_match_oracle(Hq, Hkv, counts, ctx):
+    """Ragged bf16 chunks (D 128, 16-token blocks, even GQA group) take the tensor-core paged
+    prefill: RoPE + append, then attention over the pool through the block tables."""
+    from kvstreams import ops
+    from kvstreams.rope import RotaryEmbedding
+
+    dtype, D, bs = torch.bfloat16, 128, 16
+    S = len(counts)
+    cache, st = _setup_cache(dtype, D, Hkv, bs, S, ctx, seed=sum(counts) + Hq, extra_tokens=max(counts))
+    rope = RotaryEmbedding(D, 5e5)
+    g = torch.Generator(device="cuda").manual_seed(11)
+    N = sum(counts)
+    q = torch.randn(N, Hq, D, generator=g, device="cuda").to(dtype)
+    k = torch.randn(N, Hkv, D, generator=g, device="cuda").to(dtype)
+    v = torch.randn(N, Hkv, D, generator=g, device="cuda").to(dtype)
+    pos = torch.cat([torch.arange(int(p), int(p) + c) for p, c in zip(st.next_positions, counts)]).cuda()
+    old_k = cache.k.clone()
+    old_tables = [cache.block_table(s) for s in range(S)]
+    old_len = [cache.num_tokens(s) for s in range(S)]
+    mapping = cache.append_slots_batch(list(range(S)), pos, counts)
+    out = ops.paged_forward(cache, list(range(S)), counts, 0, q, k, v, pos, mapping, rope.table(q.device, dtype),
+                            D ** -0.5)
+    cache.sync()
+    qn, kn, pn = _np(q), _np(k), pos.cpu().numpy()
+    q_rot = O.rope_apply(qn, pn, 5e5, np.float32).astype(np.float64)
+    k_rot = O.rope_apply(kn, pn, 5e5, np.float32).astype(np.float64)
+    pool_k, pool_v = _np(old_k)[0], _np(cache.v)[0]
+    got = _np(out)
+    start = 0
+    for s, T in enumerate(counts):
+        tab = old_tables[s] + cache.block_table(s)[len(old_tables[s]):]
+        n_old = old_len[s]
+        ks = pool_k[tab].reshape(-1, Hkv, D)[:n_old]
+        vs = pool_v[tab].reshape(-1, Hkv, D)[:n_old + T]
+        sl = slice(start, start + T)
+        keys = np.concatenate([ks, k_rot[sl]])
+        mask = np.ones((T, n_old + T), dtype=bool)
+        mask[:, n_old:] = np.tril(np.ones((T, T), dtype=bool))
+        want = O.gqa_attention(q_rot[sl], keys, vs, mask, D ** -0.5)
+        np.testing.assert_allclose(got[sl], want, rtol=0, atol=TOL[dtype], err_msg=f"stream {s}")
+        start += T
+
+
+def _oracle_paged(q_rot, k_rot, pool_k, pool_v, table, n_old, T, Hkv, D):
+    ks = pool_k[table].reshape(-1, Hkv, D)[:n_old]
+    vs = pool_v[table].reshape(-1, Hkv, D)[:n_old + T]
+    keys = np.concatenate([ks, k_rot])
+    mask = np.ones((T, n_old + T), dtype=bool)
+    mask[:, n_old:] = np.tril(np.ones((T, T), dtype=bool))
+    return O.gqa_attention(q_rot, keys, vs, mask, D ** -0.5)
+
+
+def test_prefill_then_decode_share_scratch_any_slot_order():
+    """Chunked prefills and decode steps of different batch sizes, slots in any order, one
+    after the other on one cache: they share one scratch buffer, which every call must leave
+    as the next expects (regressions: arrival counters at a batch-size dependent offset, and
+    prefill tile offsets read back as counters)."""
+    from kvstreams import ops
+    from kvstreams.rope import RotaryEmbedding
+
+    dtype, D, Hq, Hkv, bs, S = torch.bfloat16, 128, 32, 8, 16, 12
+    cache, st = _setup_cache(dtype, D, Hkv, bs, S, (50, 900), seed=5, extra_tokens=200)
+    rope = RotaryEmbedding(D, 5e5)
+    inv = rope.table("cuda", dtype)
+    g = torch.Generator(device="cuda").manual_seed(3)
+    nxt = [int(p) for p in st.next_positions]
+    steps = [([5, 2, 9], [40, 7, 130]), ([7, 0, 11, 3, 1, 10, 4, 8, 6, 2, 9, 5], None),
+             ([4, 1, 10, 6, 2], None), ([3, 8], [17, 64]), ([0, 11, 5, 9, 7, 3, 1], None),
+             (list(range(12)), None)]
+    for seqs, counts in steps:
+        c = counts or [1] * len(seqs)
+        N = sum(c)
+        q = torch.randn(N, Hq, D, generator=g, device="cuda").to(dtype)
+        k = torch.randn(N, Hkv, D, generator=g, device="cuda").to(dtype)
+        v = torch.randn(N, Hkv, D, generator=g, device="cuda").to(dtype)
+        pos = torch.cat([torch.arange(nxt[s], nxt[s] + n) for s, n in zip(seqs, c)]).cuda()
+        old_k, old_tables = cache.k.clone(), [cache.block_table(s) for s in seqs]
+        old_len = [cache.num_tokens(s) for s in seqs]
+        mapping = cache.append_slots_batch(seqs, pos, counts)
+        out = ops.paged_forward(cache, seqs, counts, 0, q, k, v, pos, mapping, inv, D ** -0.5)
+        cache.sync()
+        pn = pos.cpu().numpy()
+        q_rot = O.rope_apply(_np(q), pn, 5e5, np.float32).astype(np.float64)
+        k_rot = O.rope_apply(_np(k), pn, 5e5, np.float32).astype(np.float64)
+        pool_k, pool_v = _np(old_k)[0], _np(cache.v)[0]
+        got = _np(out)
+        start = 0
+        for i, (s, n) in enumerate(zip(seqs, c)):
+            tab = old_tables[i] + cache.block_table(s)[len(old_tables[i]):]
+            sl = slice(start, start + n)
+            want = _oracle_paged(q_rot[sl], k_rot[sl], pool_k, pool_v, tab, old_len[i], n, Hkv, D)
+            np.testing.assert_allclose(got[sl], want, rtol=0, atol=TOL[dtype], err_msg=f"sequence {s}")
+            start += n
+            nxt[s] += n
