@@ -35,7 +35,22 @@ class RMSNorm(nn.Module):
         self.weight = nn.Parameter(torch.ones(dim))
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + self.eps) * self.weight
+        # x * rsqrt(mean(x^2) + eps) * weight as one kernel (half precision reduces in float32)
+        return F.rms_norm(x, (x.shape[-1],), self.weight, self.eps)
+
+
+def _fused_weight(owner: nn.Module, name: str, parts) -> torch.Tensor:
+    """Row-concatenation of several Linear weights, cached on ``owner`` and rebuilt when any
+    of them is replaced or updated in place, so one GEMM serves several projections."""
+    key = tuple((w.data_ptr(), w._version) for w in parts)
+    cached = owner.__dict__.get(name)
+    if cached is None or cached[0] != key or torch.is_grad_enabled():
+        w = torch.cat(list(parts), dim=0)
+        if torch.is_grad_enabled():
+            return w  # differentiable, not cached
+        owner.__dict__[name] = (key, w)
+        return w
+    return cached[1]
 
 
 class Attention(nn.Module):
@@ -51,10 +66,14 @@ class Attention(nn.Module):
         self.o_proj = nn.Linear(cfg.n_heads * cfg.head_dim, cfg.d_model, bias=False)
 
     def project(self, x: torch.Tensor):
+        """q, k, v of ``x`` (one GEMM over the concatenated projection weights)."""
         lead = x.shape[:-1]
-        q = self.q_proj(x).view(*lead, self.n_heads, self.head_dim)
-        k = self.k_proj(x).view(*lead, self.n_kv_heads, self.head_dim)
-        v = self.v_proj(x).view(*lead, self.n_kv_heads, self.head_dim)
+        w = _fused_weight(self, "_qkv", (self.q_proj.weight, self.k_proj.weight, self.v_proj.weight))
+        qkv = F.linear(x, w)
+        nq, nk = self.n_heads * self.head_dim, self.n_kv_heads * self.head_dim
+        q = qkv[..., :nq].reshape(*lead, self.n_heads, self.head_dim)
+        k = qkv[..., nq:nq + nk].reshape(*lead, self.n_kv_heads, self.head_dim)
+        v = qkv[..., nq + nk:].reshape(*lead, self.n_kv_heads, self.head_dim)
         return q, k, v
 
 
@@ -66,7 +85,10 @@ class MLP(nn.Module):
         self.down = nn.Linear(cfg.d_ff, cfg.d_model, bias=False)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        return self.down(F.silu(self.gate(x)) * self.up(x))
+        # gate and up as one GEMM over the concatenated weights
+        gu = F.linear(x, _fused_weight(self, "_gate_up", (self.gate.weight, self.up.weight)))
+        g, u = gu.chunk(2, dim=-1)
+        return self.down(F.silu(g) * u)
 
 
 class Block(nn.Module):
@@ -76,6 +98,17 @@ class Block(nn.Module):
         self.attn = Attention(cfg)
         self.mlp_norm = RMSNorm(cfg.d_model, cfg.norm_eps)
         self.mlp = MLP(cfg)
+
+    # Residual updates of rows ``x [N, d_model]``: x + o_proj(a) and x + mlp(mlp_norm(x))
+    # (model.py:149-152 order), the output projection and the add as one GEMM.
+    def attn_residual(self, x: torch.Tensor, a: torch.Tensor) -> torch.Tensor:
+        return torch.addmm(x, a, self.attn.o_proj.weight.t())
+
+    def mlp_residual(self, x: torch.Tensor) -> torch.Tensor:
+        h = self.mlp_norm(x)
+        gu = F.linear(h, _fused_weight(self.mlp, "_gate_up", (self.mlp.gate.weight, self.mlp.up.weight)))
+        g, u = gu.chunk(2, dim=-1)
+        return torch.addmm(x, F.silu(g) * u, self.mlp.down.weight.t())
 
 
 def causal_mask(T: int, device=None) -> torch.Tensor:
@@ -137,6 +170,16 @@ class TinyLM(nn.Module):
     def num_parameters(self) -> int:
         return sum(p.numel() for p in self.parameters())
 
+    def logits(self, h: torch.Tensor) -> torch.Tensor:
+        """lm_head of final hidden states.  Half-precision models accumulate and return the
+        logits in float32 (one GEMM with a float32 result): a bf16 logit of magnitude ~4 would
+        carry a rounding step of 2^-5, more than the replay-vs-inference log-prob tolerance."""
+        w = self.lm_head.weight
+        if w.dtype in (torch.bfloat16, torch.float16) and h.is_cuda:
+            flat = h.reshape(-1, h.shape[-1])
+            return torch.mm(flat, w.t(), out_dtype=torch.float32).view(*h.shape[:-1], w.shape[0])
+        return self.lm_head(h)
+
     # ------------------------------------------------------------------ replay path
     def forward_hidden(self, tokens: torch.Tensor, positions: Optional[torch.Tensor] = None, mask=None) -> torch.Tensor:
         """Final normed hidden states ``[B, T, d_model]`` of the masked full-sequence forward."""
@@ -152,8 +195,8 @@ class TinyLM(nn.Module):
         for blk in self.layers:
             q, k, v = blk.attn.project(blk.attn_norm(x))
             a = _ReplayAttention.apply(q, k, v, positions, rm.evicted_at, rm.lengths, inv, blk.attn.scale)
-            x = x + blk.attn.o_proj(a.reshape(B, T, -1))
-            x = x + blk.mlp(blk.mlp_norm(x))
+            x2 = blk.attn_residual(x.reshape(B * T, -1), a.reshape(B * T, -1))
+            x = blk.mlp_residual(x2).view(B, T, -1)
         return self.norm(x)
 
     def forward(self, tokens: torch.Tensor, positions: Optional[torch.Tensor] = None, mask=None) -> torch.Tensor:
@@ -161,7 +204,7 @@ class TinyLM(nn.Module):
 
         mask: None (causal), a :class:`ReplayMask`, or a dense ``[B, T, T]`` boolean mask of
         KV-streams form (``s <= t and t < evicted_at[s]``).  Returns ``[B, T, vocab]`` logits."""
-        return self.lm_head(self.forward_hidden(tokens, positions, mask))
+        return self.logits(self.forward_hidden(tokens, positions, mask))
 
     # ------------------------------------------------------------------ paged path
     @torch.no_grad()
@@ -183,15 +226,15 @@ class TinyLM(nn.Module):
         one_each = counts is None or all(c == 1 for c in counts)
         mapping = cache.append_slots_batch(seq_ids, positions, None if one_each else counts)
         slots = [cache.slot(s) for s in seq_ids]
+        batch = cache._batch(slots, None if one_each else counts)  # shared by every layer
         inv = self.rope.table(dev, self.dtype)
         x = self.embed(tokens)
         for i, blk in enumerate(self.layers):
             q, k, v = blk.attn.project(blk.attn_norm(x))
             a = ops.paged_forward(cache, slots, None if one_each else counts, i, q, k, v, positions, mapping, inv,
-                                  blk.attn.scale)
-            x = x + blk.attn.o_proj(a.reshape(N, -1))
-            x = x + blk.mlp(blk.mlp_norm(x))
+                                  blk.attn.scale, batch=batch)
+            x = blk.mlp_residual(blk.attn_residual(x, a.reshape(N, -1)))
         if last_only and not one_each:
             ends = torch.tensor(counts, device=dev).cumsum(0) - 1
             x = x.index_select(0, ends)
-        return self.lm_head(self.norm(x))
+        return self.logits(self.norm(x))

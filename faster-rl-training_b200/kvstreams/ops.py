@@ -101,19 +101,20 @@ def replay_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, evicted_
 def paged_forward(cache, slots: Sequence[int], counts: Optional[Sequence[int]], layer: int, q: torch.Tensor,
                   k_new: torch.Tensor, v_new: torch.Tensor, positions: torch.Tensor, mapping,
                   inv_freq: torch.Tensor, scale: float, out: Optional[torch.Tensor] = None,
-                  grid_ctas: int = 0) -> torch.Tensor:
+                  grid_ctas: int = 0, batch=None) -> torch.Tensor:
     """One layer of the paged incremental forward (model.py:50-75 + hook :182-185) for the
     new tokens of a batch of sequences: RoPE of q/k, append of k/v, paged GQA attention.
 
     q ``[N, Hq, D]``, k_new/v_new ``[N, Hkv, D]`` (not rotated), positions ``[N]``; ``mapping``
-    is the SlotMapping returned by append_slots for the same tokens."""
+    is the SlotMapping returned by append_slots for the same tokens; ``batch`` a descriptor from
+    ``cache._batch(slots, counts)`` that the layers of one forward can share."""
     q, k_new, v_new = q.contiguous(), k_new.contiguous(), v_new.contiguous()
     if q.dtype != cache.dtype or k_new.dtype != cache.dtype or v_new.dtype != cache.dtype:
         raise ValueError("activations must have the cache dtype")
     pos = positions.to(device=q.device, dtype=torch.long).contiguous()
     if out is None:
         out = torch.empty_like(q)
-    b, keep = cache._batch(slots, counts)
+    b, keep = batch if batch is not None else cache._batch(slots, counts)
     lib = N.lib()
     nbytes = int(lib.kvs_decode_scratch_bytes(C.byref(cache.struct), b.num_seqs, q.shape[1], grid_ctas))
     scratch = cache._decode_scratch(nbytes) if nbytes else None

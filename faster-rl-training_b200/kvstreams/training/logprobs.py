@@ -16,8 +16,8 @@ def token_logprobs(model, batch: Batch, temperature: float = 1.0, return_full: b
     Returns ``[B, T]`` (position 0 is 0); with ``return_full`` also the ``[B, T, V]``
     log-softmax rows aligned the same way.  The replay forward runs the masked replay
     kernel; lm_head + log-softmax + gather are done in token chunks so the full
-    ``[B, T, V]`` logits never exist at once.  Half-precision models get float32
-    log-softmax.
+    ``[B, T, V]`` logits never exist at once.  Half-precision models get float32 logits
+    (float32 accumulation, no half-precision rounding) and float32 log-softmax.
     """
     dev = model.device
     tokens = batch.tokens.to(dev)
@@ -31,7 +31,7 @@ def token_logprobs(model, batch: Batch, temperature: float = 1.0, return_full: b
     res = torch.empty(flat_next.numel(), dtype=want, device=dev)
     for a in range(0, flat_h.shape[0], _CHUNK_TOKENS):
         z = slice(a, a + _CHUNK_TOKENS)
-        logits = model.lm_head(flat_h[z]).to(want)
+        logits = model.logits(flat_h[z]).to(want)
         logp = torch.log_softmax(logits / temperature, dim=-1)
         res[z] = logp.gather(-1, flat_next[z, None]).squeeze(-1)
         if full is not None:
