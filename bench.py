@@ -442,7 +442,8 @@ def rollout_bench(dev, args, rank: int) -> dict:
     blocks = n * ((budget + 512 + 16 + 16) // 16 + 1)
     cache = PagedKVCache(cfg.n_layers, cfg.n_kv_heads, cfg.head_dim, block_size=16, num_blocks=blocks,
                          dtype=torch.bfloat16, device=dev, max_seqs=n)
-    eng = BatchedKVStreams(model, cache, MarkovianPolicy(keep_last=1), context_budget=budget, seed=rank)
+    eng = BatchedKVStreams(model, cache, MarkovianPolicy(keep_last=1), context_budget=budget, seed=rank,
+                           cuda_graphs=not args.rollout_eager)
     eps = synthetic_episodes(n, turns=turns, turn_range=(64, 512), prompt_len=64, vocab=cfg.vocab_size,
                              seed=1000 + rank)
     W, K = args.rollout_warmup, args.rollout_iters
@@ -475,6 +476,7 @@ def rollout_bench(dev, args, rank: int) -> dict:
         "ms_per_iteration": ms / K,
         "library_launches": N.lib().kvs_launch_count() - launches0,
         "engine_iterations": eng.last_iterations,
+        "cuda_graphs": not args.rollout_eager,
     }
     if args.rollout_full:
         out["compactions"] = sum(r.stats.compactions for r in rolls)
@@ -550,6 +552,7 @@ def main() -> int:
     ap.add_argument("--rollout-warmup", type=int, default=20)
     ap.add_argument("--rollout-iters", type=int, default=100)
     ap.add_argument("--rollout-full", action="store_true", help="play the whole episodes (minutes)")
+    ap.add_argument("--rollout-eager", action="store_true", help="decode steps without CUDA graphs")
     ap.add_argument("--rollout-only", action="store_true", help="only the batched rollout measurement")
     args = ap.parse_args()
     if args.warmup < 3:

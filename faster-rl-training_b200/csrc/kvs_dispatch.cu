@@ -55,6 +55,32 @@ KVS_API int kvs_paged_decode(const kvs_cache* c, const kvs_batch* b, const kvs_d
   const cudaStream_t st = to_cuda(stream);
   // the tensor-core kernels store outputs with 16-byte vector writes
   const bool out_aligned = (reinterpret_cast<uintptr_t>(a->out) & 15) == 0;
+  if (b->cu_tokens != nullptr && a->tail_singles > 0) {
+    // mixed step: chunks first, then tail_singles one-token sequences (a decode sub-batch)
+    const int ns = a->tail_singles, nc = b->num_seqs - ns, tok1 = b->total_tokens - ns;
+    if (ns > b->num_seqs || tok1 < nc) return KVS_E_ARG;
+    const size_t qrow = (size_t)a->n_heads * c->head_dim, kvrow = (size_t)c->n_kv_heads * c->head_dim;
+    const size_t esz = c->dtype == KVS_F64 ? 8 : (c->dtype == KVS_F32 ? 4 : 2);
+    kvs_batch bs_ = {b->seq_slots + nc, nullptr, ns, ns};
+    kvs_decode_args as_ = *a;
+    as_.q = static_cast<const uint8_t*>(a->q) + tok1 * qrow * esz;
+    as_.k_new = static_cast<const uint8_t*>(a->k_new) + tok1 * kvrow * esz;
+    as_.v_new = static_cast<const uint8_t*>(a->v_new) + tok1 * kvrow * esz;
+    as_.positions = a->positions + tok1;
+    as_.slot_blocks = a->slot_blocks + tok1;
+    as_.slot_offsets = a->slot_offsets + tok1;
+    as_.out = static_cast<uint8_t*>(a->out) + tok1 * qrow * esz;
+    as_.tail_singles = 0;
+    int rc = KVS_OK;
+    if (nc > 0) {
+      kvs_batch bc = {b->seq_slots, b->cu_tokens, nc, tok1};
+      kvs_decode_args ac = *a;
+      ac.tail_singles = 0;
+      rc = kvs_paged_decode(c, &bc, &ac, stream);
+      if (rc) return rc;
+    }
+    return kvs_paged_decode(c, &bs_, &as_, stream);
+  }
   if (out_aligned && kvs_decode_bf16_supported(c, b, a->n_heads))
     return kvs_decode_bf16_launch(c, b, a, kvs_decode_bf16_grid(a->grid_ctas), st);
   if (b->cu_tokens != nullptr && out_aligned && kvs_prefill_tc_capable(c, a->n_heads)) {

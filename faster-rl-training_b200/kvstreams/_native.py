@@ -102,7 +102,7 @@ class KvsDecodeArgs(C.Structure):
         ("layer", C.c_int32),
         ("n_heads", C.c_int32),
         ("grid_ctas", C.c_int32),
-        ("reserved", C.c_int32),
+        ("tail_singles", C.c_int32),
     ]
 
 

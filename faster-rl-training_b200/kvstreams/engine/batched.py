@@ -97,7 +97,8 @@ class BatchedKVStreams:
     name = "kvstream"
 
     def __init__(self, model, cache, policy: CompactionPolicy, context_budget: int = 8192, pad_to_block: bool = True,
-                 pad_id: int = 0, temperature: float = 1.0, greedy: bool = False, seed: int = 0) -> None:
+                 pad_id: int = 0, temperature: float = 1.0, greedy: bool = False, seed: int = 0,
+                 cuda_graphs: bool = False) -> None:
         self.model = model
         self.cache = cache
         self.policy = policy
@@ -109,6 +110,9 @@ class BatchedKVStreams:
         self.greedy = greedy
         self.gen = torch.Generator(device=model.device).manual_seed(seed)
         self._next_seq = 0
+        # decode steps replayed as CUDA graphs (one per batch size), see engine/graphs.py
+        self.cuda_graphs = cuda_graphs
+        self._graphs = None
 
     # ------------------------------------------------------------------ helpers
     def _reserve(self, run: _Run) -> int:
@@ -216,6 +220,25 @@ class BatchedKVStreams:
             it += 1
             n_dec = n_pre = 0
             starting = [r for r in active if r.phase == _PREFILL]
+
+            def decode_step(logits: torch.Tensor) -> None:
+                """Sample the next token of every generating rollout from its logits row."""
+                rows = torch.tensor([r.idx for r in decoding], device=dev)
+                idx = torch.tensor([gen_base[r.idx] + gen_used[r.idx] for r in decoding], device=dev)
+                forced = forced_all.index_select(0, idx) if forced_all is not None else None
+                tok, lp = self._sample(logits, forced)
+                gen_tok.index_copy_(0, idx, tok)
+                gen_logp.index_copy_(0, idx, lp)
+                cur.index_copy_(0, rows, tok)
+                for r in decoding:
+                    r.n_tokens += 1
+                    r.live += 1
+                    r.step += 1
+                    gen_used[r.idx] += 1
+                    r.stats.decode_tokens += 1
+                    r.stats.tokens_forwarded += 1
+                    r.stats.peak_live_tokens = max(r.stats.peak_live_tokens, r.live)
+
             # a rollout forwarding the last token of its reply sends it with the turn's block
             # padding as one chunk: the padding is in the cache before the next compaction
             # check, as in the reference (engine/base.py:241-245, then :260)
@@ -262,16 +285,28 @@ class BatchedKVStreams:
                     base += 1 + pads
                 n_pre = base - len(finishing)
                 n_dec = len(finishing)
+                # the generating rollouts ride along in the same forward (one weight read per
+                # iteration): one token each, after the chunks (the decode kernel's sub-batch)
+                merged = list(decoding)
+                for r in merged:
+                    dev_rows.append(r.idx)
+                    dev_at.append(base)
+                    host_tok.append(np.zeros(1, dtype=np.int64))
+                    counts.append(1)
+                    pos.append(np.asarray([r.n_tokens], dtype=np.int64))
+                    base += 1
                 tok_t = torch.from_numpy(np.concatenate(host_tok)).to(dev)
-                if finishing:  # the last reply tokens come from the device
+                if dev_rows:  # last reply tokens and generating rollouts' tokens come from the device
                     tok_t.index_copy_(0, torch.tensor(dev_at, device=dev),
                                       cur.index_select(0, torch.tensor(dev_rows, device=dev)))
                 pos_t = torch.from_numpy(np.concatenate(pos)).to(dev)
-                order = starting + finishing
-                logits = self.model.forward_cached_batch(tok_t, pos_t, self.cache, [r.seq_id for r in order],
-                                                         counts=counts, last_only=True)
+                order = starting + finishing + merged
+                logits_all = self.model.forward_cached_batch(tok_t, pos_t, self.cache, [r.seq_id for r in order],
+                                                             counts=counts, last_only=True)
+                if merged:
+                    decode_step(logits_all[len(starting) + len(finishing):])
                 if starting:
-                    logits = logits[: len(starting)]
+                    logits = logits_all[: len(starting)]
                     idx = torch.tensor([gen_base[r.idx] + gen_used[r.idx] for r in starting], device=dev)
                     forced = forced_all.index_select(0, idx) if forced_all is not None else None
                     tok, lp = self._sample(logits, forced)
@@ -287,27 +322,21 @@ class BatchedKVStreams:
                 for r in finishing:
                     r.segments.append(Segment(len(r.segments), "turn", r.turn_start, r.n_tokens))
                     r.phase = _PREFILL if r.turn + 1 < r.ep.turns else _DONE
-            # ---- one decode step for every other rollout generating
-            if decoding:
+            # ---- an iteration without chunks: the decode step alone (a replayed graph)
+            elif decoding:
                 rows = torch.tensor([r.idx for r in decoding], device=dev)
                 tok_in = cur.index_select(0, rows)
-                pos_t = torch.tensor([r.n_tokens for r in decoding], dtype=torch.long, device=dev)
-                logits = self.model.forward_cached_batch(tok_in, pos_t, self.cache, [r.seq_id for r in decoding])
-                idx = torch.tensor([gen_base[r.idx] + gen_used[r.idx] for r in decoding], device=dev)
-                forced = forced_all.index_select(0, idx) if forced_all is not None else None
-                tok, lp = self._sample(logits, forced)
-                gen_tok.index_copy_(0, idx, tok)
-                gen_logp.index_copy_(0, idx, lp)
-                cur.index_copy_(0, rows, tok)
-                for r in decoding:
-                    r.n_tokens += 1
-                    r.live += 1
-                    r.step += 1
-                    gen_used[r.idx] += 1
-                    r.stats.decode_tokens += 1
-                    r.stats.tokens_forwarded += 1
-                    r.stats.peak_live_tokens = max(r.stats.peak_live_tokens, r.live)
-                n_dec += len(decoding)
+                if self.cuda_graphs:
+                    if self._graphs is None:
+                        from .graphs import DecodeGraphs
+
+                        self._graphs = DecodeGraphs(self.model, self.cache, len(runs))
+                    logits = self._graphs.step([r.seq_id for r in decoding], tok_in, [r.n_tokens for r in decoding])
+                else:
+                    pos_t = torch.tensor([r.n_tokens for r in decoding], dtype=torch.long, device=dev)
+                    logits = self.model.forward_cached_batch(tok_in, pos_t, self.cache, [r.seq_id for r in decoding])
+                decode_step(logits)
+            n_dec += len(decoding)
             if on_iteration is not None:
                 on_iteration(it, n_dec, n_pre)
         torch.cuda.synchronize(dev)

@@ -222,19 +222,34 @@ class TinyLM(nn.Module):
         dev = self.device
         tokens = tokens.to(dev).reshape(-1)
         positions = positions.to(dev, torch.long).reshape(-1)
-        N = tokens.numel()
         one_each = counts is None or all(c == 1 for c in counts)
         mapping = cache.append_slots_batch(seq_ids, positions, None if one_each else counts)
         slots = [cache.slot(s) for s in seq_ids]
         batch = cache._batch(slots, None if one_each else counts)  # shared by every layer
-        inv = self.rope.table(dev, self.dtype)
+        ends = None
+        if last_only and not one_each:
+            ends = torch.tensor(counts, device=dev).cumsum(0) - 1
+        return self.forward_layers(tokens, positions, cache, batch, mapping, None if one_each else counts, ends)
+
+    @torch.no_grad()
+    def forward_layers(self, tokens: torch.Tensor, positions: torch.Tensor, cache, batch, mapping,
+                       counts: Optional[Sequence[int]] = None, rows: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """The layers and logits of :meth:`forward_cached_batch` once the slots are appended:
+        ``batch`` (kvs_batch, keep-alive) and ``mapping`` describe the new tokens; with ``rows``
+        only those tokens' logits.  Device work only (CUDA-graph capturable with static inputs)."""
+        N = tokens.numel()
+        # trailing one-token sequences of a chunked batch run on the decode kernel
+        tail = 0
+        if counts is not None:
+            while tail < len(counts) and counts[len(counts) - 1 - tail] == 1:
+                tail += 1
+        inv = self.rope.table(self.device, self.dtype)
         x = self.embed(tokens)
         for i, blk in enumerate(self.layers):
             q, k, v = blk.attn.project(blk.attn_norm(x))
-            a = ops.paged_forward(cache, slots, None if one_each else counts, i, q, k, v, positions, mapping, inv,
-                                  blk.attn.scale, batch=batch)
+            a = ops.paged_forward(cache, None, counts, i, q, k, v, positions, mapping, inv, blk.attn.scale,
+                                  batch=batch, tail_singles=tail)
             x = blk.mlp_residual(blk.attn_residual(x, a.reshape(N, -1)))
-        if last_only and not one_each:
-            ends = torch.tensor(counts, device=dev).cumsum(0) - 1
-            x = x.index_select(0, ends)
+        if rows is not None:
+            x = x.index_select(0, rows)
         return self.logits(self.norm(x))

@@ -101,13 +101,15 @@ def replay_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, evicted_
 def paged_forward(cache, slots: Sequence[int], counts: Optional[Sequence[int]], layer: int, q: torch.Tensor,
                   k_new: torch.Tensor, v_new: torch.Tensor, positions: torch.Tensor, mapping,
                   inv_freq: torch.Tensor, scale: float, out: Optional[torch.Tensor] = None,
-                  grid_ctas: int = 0, batch=None) -> torch.Tensor:
+                  grid_ctas: int = 0, batch=None, tail_singles: int = 0) -> torch.Tensor:
     """One layer of the paged incremental forward (model.py:50-75 + hook :182-185) for the
     new tokens of a batch of sequences: RoPE of q/k, append of k/v, paged GQA attention.
 
     q ``[N, Hq, D]``, k_new/v_new ``[N, Hkv, D]`` (not rotated), positions ``[N]``; ``mapping``
     is the SlotMapping returned by append_slots for the same tokens; ``batch`` a descriptor from
-    ``cache._batch(slots, counts)`` that the layers of one forward can share."""
+    ``cache._batch(slots, counts)`` that the layers of one forward can share; ``tail_singles``
+    the number of trailing sequences with exactly one new token (they then run on the decode
+    kernel while the chunks before them run on the prefill path, in one call)."""
     q, k_new, v_new = q.contiguous(), k_new.contiguous(), v_new.contiguous()
     if q.dtype != cache.dtype or k_new.dtype != cache.dtype or v_new.dtype != cache.dtype:
         raise ValueError("activations must have the cache dtype")
@@ -123,7 +125,8 @@ def paged_forward(cache, slots: Sequence[int], counts: Optional[Sequence[int]], 
                         inv_freq=inv_freq.data_ptr(), out=out.data_ptr(),
                         scratch=scratch.data_ptr() if scratch is not None else None,
                         scratch_bytes=scratch.numel() if scratch is not None else 0, scale=float(scale),
-                        layer=int(layer), n_heads=int(q.shape[1]), grid_ctas=int(grid_ctas))
+                        layer=int(layer), n_heads=int(q.shape[1]), grid_ctas=int(grid_ctas),
+                        tail_singles=int(tail_singles) if counts is not None else 0)
     N.check(lib.kvs_paged_decode(C.byref(cache.struct), C.byref(b), C.byref(a), N.stream_ptr(q.device)),
             "kvs_paged_decode")
     return out

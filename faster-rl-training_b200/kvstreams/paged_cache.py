@@ -378,22 +378,38 @@ class PagedKVCache:
         return self._append(slots, counts, positions, one_each=counts is None or all(c == 1 for c in counts))
 
     def _append(self, slots, counts, positions, one_each: bool = False) -> SlotMapping:
-        need = self._check_alloc(slots, counts)
         total = int(sum(counts))
         pos = positions.to(device=self.device, dtype=torch.long).reshape(-1).contiguous()
         if pos.numel() != total:
             raise ValueError("positions do not match the token counts")
+        self._reserve(slots, counts)
         blocks = torch.empty(total, dtype=torch.int32, device=self.device)
         offsets = torch.empty(total, dtype=torch.int32, device=self.device)
         b, keep = self._batch(slots, None if one_each else counts)
-        rc = self._lib.kvs_append_slots(C.byref(self._struct), C.byref(b), pos.data_ptr(), blocks.data_ptr(),
-                                        offsets.data_ptr(), self._stream())
-        N.check(rc, "kvs_append_slots")
+        self.append_slots_device(b, pos, blocks, offsets)
+        return SlotMapping(blocks, offsets)
+
+    def _reserve(self, slots, counts) -> None:
+        """Host half of an append: pool and table checks, then the host mirror's new lengths."""
+        need = self._check_alloc(slots, counts)
         for s, c, k in zip(slots, counts, need):
             self._h_len[s] += c
             self._h_nb[s] += int(k)
         self._h_top -= int(need.sum())
-        return SlotMapping(blocks, offsets)
+
+    def reserve_slots(self, seq_ids: Sequence[int], counts: Optional[Sequence[int]] = None) -> None:
+        """Host half of :meth:`append_slots_batch` for callers that launch the append kernel
+        themselves (:meth:`append_slots_device`, e.g. inside a replayed CUDA graph)."""
+        slots = [self._slot_of[s] for s in seq_ids]
+        self._reserve(slots, [1] * len(slots) if counts is None else list(counts))
+
+    def append_slots_device(self, batch, positions: torch.Tensor, blocks: torch.Tensor,
+                            offsets: torch.Tensor) -> None:
+        """Device half of an append: the append kernel on caller-provided buffers (``batch`` a
+        kvs_batch whose arrays live on the device); no host work, so it can be graph-captured."""
+        rc = self._lib.kvs_append_slots(C.byref(self._struct), C.byref(batch), positions.data_ptr(),
+                                        blocks.data_ptr(), offsets.data_ptr(), self._stream())
+        N.check(rc, "kvs_append_slots")
 
     def write(self, layer: int, slots: SlotMapping, k: torch.Tensor, v: torch.Tensor) -> None:
         """paged_cache.py:167-171: store already-rotated keys/values ``[T, n_kv_heads, head_dim]``."""

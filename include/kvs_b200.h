@@ -218,7 +218,10 @@ int kvs_paged_attention(const kvs_cache* c, const kvs_batch* b, int32_t layer, c
  * slot mapping produced by kvs_append_slots, and paged GQA attention of every new
  * query over the live entries it may see.  One token per sequence (decode,
  * cu_tokens NULL) runs the fused split-K kernel; prefill chunks (cu_tokens set)
- * run rope + append + kvs_paged_attention. */
+ * run rope + append + the tensor-core paged prefill (bf16, head_dim 128, 16-token
+ * blocks, even GQA group) or kvs_paged_attention.  A mixed step (cu_tokens set,
+ * tail_singles > 0: the last tail_singles sequences have one token each) runs the
+ * chunks and the single tokens as two launches of those kernels. */
 typedef struct kvs_decode_args {
   const void* q;            /* [total_tokens][n_heads][head_dim], not yet rotated */
   const void* k_new;        /* [total_tokens][n_kv_heads][head_dim], not yet rotated */
@@ -234,7 +237,8 @@ typedef struct kvs_decode_args {
   int32_t layer;
   int32_t n_heads;
   int32_t grid_ctas;        /* CTAs of the fused decode kernel (0 = one per SM) */
-  int32_t reserved;
+  int32_t tail_singles;     /* with cu_tokens set: the last tail_singles sequences have
+                               exactly one new token each (0: no such promise) */
 } kvs_decode_args;
 /* scratch of kvs_paged_decode: split partials and per-sequence arrival counters of the
  * fused decode kernel, then (bf16, head_dim 128, 16-token blocks, even GQA group) the

@@ -90,3 +90,26 @@ def test_batched_rollouts_bf16_llama_heads():
     rep = measure_mismatch(model, rolls)
     assert rep.max_abs_logprob_diff <= 0.08, rep
     assert rep.mean_abs_logprob_diff <= 0.02, rep
+
+
+def test_decode_cuda_graphs_equal_eager_bf16():
+    """Decode steps replayed as CUDA graphs produce the eager steps' results bit for bit
+    (teacher-forced, so both runs forward the same tokens)."""
+    from kvstreams.config import ModelConfig
+    from kvstreams.engine.batched import synthetic_episodes
+
+    cfg = ModelConfig(vocab_size=512, d_model=4096, n_layers=2, n_heads=32, n_kv_heads=8, d_ff=1024,
+                      rope_theta=5e5)
+    eps = synthetic_episodes(8, turns=3, turn_range=(10, 60), prompt_len=20, vocab=cfg.vocab_size, forced=True,
+                             seed=4)
+    model, eager = _setup(cfg, torch.bfloat16, 8, budget=256, num_blocks=1024)
+    a = eager.run(eps)
+    _, graphed = _setup(cfg, torch.bfloat16, 8, budget=256, num_blocks=1024)
+    graphed.model = model
+    graphed.cuda_graphs = True
+    b = graphed.run(eps)
+    assert graphed._graphs is not None and graphed._graphs.replays > 0
+    for x, y in zip(a, b):
+        assert x.tokens == y.tokens
+        assert [(e.time, e.evicted) for e in x.log] == [(e.time, e.evicted) for e in y.log]
+        assert x.inf_logprobs == y.inf_logprobs
