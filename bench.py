@@ -528,7 +528,7 @@ def replay_bench(dev, args, rank: int) -> dict:
             "ms": ms, "visible_pairs": pairs, "visible_frac_of_causal": pairs / causal,
             "tflops": tf, "tc_frac": tf / peaks["bf16_tflops"], "peak_src": peaks["src"],
             "replay_attn_tok_s": B * T / (ms * 1e-3),
-            "kernel": "replay_pair_kernel (tcgen05/TMEM, two query heads of a GQA group per CTA)"}
+            "kernel": "pair_attn_kernel (tcgen05/TMEM, two query heads of a GQA group per CTA)"}
 
 
 def main() -> int:
