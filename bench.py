@@ -315,6 +315,7 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
         secondary = compaction_bench(dev, args, rank)
         secondary["replay_attention"] = replay_bench(dev, args, rank)
         secondary["rollout"] = rollout_bench(dev, args, rank)
+        secondary["replay_model"] = replay_model_bench(dev, args, rank)
 
     if rank != 0:
         return
@@ -488,6 +489,58 @@ def rollout_bench(dev, args, rank: int) -> dict:
     return out
 
 
+def replay_model_bench(dev, args, rank: int) -> dict:
+    """Config 4 end to end: the trainer's replay of KV-streams rollouts through the whole
+    Llama-3-8B architecture (random init, bf16): token_logprobs = masked full-sequence forward
+    (32 layers; attention in the tcgen05 replay kernel with the evicted_at mask) + lm_head +
+    log-softmax + gather of every next token.  ``--replay-model-b`` streams of
+    ``--replay-model-t`` tokens with 3-8 keep-recent events each; timed by CUDA events."""
+    import torch
+
+    from kvstreams.config import ModelConfig
+    from kvstreams.model import TinyLM
+    from kvstreams.ops import ReplayMask
+    from kvstreams.training.logprobs import token_logprobs
+    from kvstreams.training.replay import Batch
+    from kvstreams.workloads import replay_evicted_at
+    from kvstreams.distributed import reduce_max
+
+    torch.cuda.empty_cache()
+    B, T = args.replay_model_b, args.replay_model_t
+    cfg = ModelConfig(vocab_size=128256, d_model=4096, n_layers=args.rollout_layers, n_heads=32, n_kv_heads=8,
+                      d_ff=14336, rope_theta=5e5)
+    torch.manual_seed(rank)
+    old = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    try:
+        with dev:
+            model = TinyLM(cfg)
+    finally:
+        torch.set_default_dtype(old)
+    model.eval()
+    ev, _ = replay_evicted_at(batch=B, seq_len=T, seed=rank)
+    g = torch.Generator(device=dev).manual_seed(rank)
+    tokens = torch.randint(1, cfg.vocab_size, (B, T), generator=g, device=dev)
+    batch = Batch(tokens, torch.arange(T, device=dev).expand(B, T), torch.from_numpy(ev).to(dev),
+                  torch.ones(B, T, dtype=torch.bool, device=dev), torch.zeros(B, T, device=dev),
+                  torch.full((B,), T, dtype=torch.long, device=dev))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.no_grad():
+        token_logprobs(model, batch)  # warm-up
+        torch.cuda.synchronize(dev)
+        e0.record()
+        lp = token_logprobs(model, batch)
+        e1.record()
+    torch.cuda.synchronize(dev)
+    ms = reduce_max(e0.elapsed_time(e1), dev)
+    finite = bool(torch.isfinite(lp).all())
+    del model, lp, batch, tokens
+    torch.cuda.empty_cache()
+    return {"workload": f"B={B} T={T}, Llama-3-8B arch ({cfg.n_layers} layers) bf16 random init, 3-8 keep-recent "
+                        f"events/stream: token_logprobs (masked forward + lm_head + log-softmax + gather)",
+            "ms": ms, "replay_tok_s_per_gpu": B * T / (ms * 1e-3), "logprobs_finite": finite}
+
+
 def replay_bench(dev, args, rank: int) -> dict:
     """Masked replay attention, one layer of the Llama-3-8B geometry (32 q / 8 kv heads,
     D 128, bf16): B streams x T tokens with 3-8 keep-recent compaction events each.
@@ -554,6 +607,9 @@ def main() -> int:
     ap.add_argument("--rollout-full", action="store_true", help="play the whole episodes (minutes)")
     ap.add_argument("--rollout-eager", action="store_true", help="decode steps without CUDA graphs")
     ap.add_argument("--rollout-only", action="store_true", help="only the batched rollout measurement")
+    ap.add_argument("--replay-model-b", type=int, default=2, help="config 4 uses 16")
+    ap.add_argument("--replay-model-t", type=int, default=32768)
+    ap.add_argument("--replay-model-only", action="store_true", help="only the whole-model replay measurement")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -579,6 +635,11 @@ def main() -> int:
             r = replay_bench(torch.device("cuda", local_rank), args, rank)
             if rank == 0:
                 print(json.dumps({"replay_attention": r}), flush=True)
+        elif args.replay_model_only:
+            torch.cuda.set_device(local_rank)
+            r = replay_model_bench(torch.device("cuda", local_rank), args, rank)
+            if rank == 0:
+                print(json.dumps({"replay_model": r}), flush=True)
         elif args.rollout_only:
             torch.cuda.set_device(local_rank)
             r = rollout_bench(torch.device("cuda", local_rank), args, rank)
