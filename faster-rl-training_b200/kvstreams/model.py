@@ -116,7 +116,10 @@ def causal_mask(T: int, device=None) -> torch.Tensor:
 
 
 class _ReplayAttention(torch.autograd.Function):
-    """RoPE of q/k at ``positions`` plus masked replay attention, as one autograd node."""
+    """RoPE of q/k at ``positions`` plus masked replay attention, as one autograd node.
+
+    Backward: the replay attention backward kernels give the gradients of the rotated q/k
+    and of v; RoPE is a rotation, so its backward rotates back (RoPE at -positions)."""
 
     @staticmethod
     def forward(ctx, q, k, v, positions, evicted_at, lengths, inv_freq, scale):
@@ -124,13 +127,21 @@ class _ReplayAttention(torch.autograd.Function):
         k = k.detach().contiguous().clone()
         ops.rope_(q, positions, inv_freq)
         ops.rope_(k, positions, inv_freq)
-        return ops.replay_attention(q, k, v.detach(), evicted_at, lengths, scale)
+        v = v.detach().contiguous()
+        out = ops.replay_attention(q, k, v, evicted_at, lengths, scale)
+        if any(ctx.needs_input_grad[:3]):
+            ctx.save_for_backward(q, k, v, out, positions, evicted_at, lengths, inv_freq)
+        ctx.scale = scale
+        return out
 
     @staticmethod
     def backward(ctx, grad_out):
-        raise NotImplementedError(
-            "the masked replay backward kernel is not part of this build; run the replay under torch.no_grad()"
-        )
+        q, k, v, out, positions, evicted_at, lengths, inv_freq = ctx.saved_tensors
+        dq, dk, dv = ops.replay_attention_backward(q, k, v, evicted_at, lengths, ctx.scale, out, grad_out)
+        neg = -positions
+        ops.rope_(dq, neg, inv_freq)
+        ops.rope_(dk, neg, inv_freq)
+        return dq, dk, dv, None, None, None, None, None
 
 
 def as_replay_mask(mask, B: int, T: int, device) -> ReplayMask:

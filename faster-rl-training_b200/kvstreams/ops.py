@@ -98,6 +98,31 @@ def replay_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, evicted_
     return out
 
 
+def replay_attention_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, evicted_at: torch.Tensor,
+                              lengths: torch.Tensor, scale: float, out: torch.Tensor, grad_out: torch.Tensor):
+    """Gradients (dq, dk, dv) of :func:`replay_attention` (q and k rotated, ``out`` its
+    output) for the upstream gradient ``grad_out``; exact kernels for every dtype."""
+    _check_cuda(q, k, v, evicted_at, lengths)
+    B, T, Hq, D = q.shape
+    Hkv = k.shape[2]
+    q, k, v, out = q.contiguous(), k.contiguous(), v.contiguous(), out.contiguous()
+    g = grad_out.to(q.dtype).contiguous()
+    ev = evicted_at.to(torch.long).contiguous()
+    ln = lengths.to(torch.int32).contiguous()
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    lib = N.lib()
+    code = N.DTYPE_CODE[q.dtype]
+    nbytes = lib.kvs_replay_backward_scratch_bytes(B, T, Hq, code)
+    scratch = torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=q.device)
+    a = N.KvsReplayArgs(q=q.data_ptr(), k=k.data_ptr(), v=v.data_ptr(), evicted_at=ev.data_ptr(),
+                        lengths=ln.data_ptr(), out=out.data_ptr(), scratch=scratch.data_ptr(),
+                        scratch_bytes=scratch.numel(), batch=B, seq_len=T, n_heads=Hq, n_kv_heads=Hkv, head_dim=D,
+                        dtype=code, scale=float(scale), flags=0)
+    N.check(lib.kvs_replay_attention_backward(C.byref(a), g.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
+                                              N.stream_ptr(q.device)), "kvs_replay_attention_backward")
+    return dq, dk, dv
+
+
 def paged_forward(cache, slots: Sequence[int], counts: Optional[Sequence[int]], layer: int, q: torch.Tensor,
                   k_new: torch.Tensor, v_new: torch.Tensor, positions: torch.Tensor, mapping,
                   inv_freq: torch.Tensor, scale: float, out: Optional[torch.Tensor] = None,

@@ -287,6 +287,16 @@ typedef struct kvs_replay_args {
 size_t kvs_replay_scratch_bytes(int32_t batch, int32_t seq_len);
 int kvs_replay_attention(const kvs_replay_args* a, kvs_stream_t stream);
 
+/* Backward of kvs_replay_attention: what torch autograd computes for the reference's masked
+ * attention (model.py:71-74 under the replay.py:62 mask) when the trainer differentiates
+ * token_logprobs (training/logprobs.py:10-25).  Inputs as the forward (q and k rotated, the
+ * forward's output in a->out) plus dout; writes dq, dk, dv in the layouts and dtype of q, k,
+ * v (dk/dv summed over the query heads of each KV head).  Exact kernels; a->scratch holds
+ * kvs_replay_backward_scratch_bytes (row statistics). */
+size_t kvs_replay_backward_scratch_bytes(int32_t batch, int32_t seq_len, int32_t n_heads, int32_t dtype);
+int kvs_replay_attention_backward(const kvs_replay_args* a, const void* dout, void* dq, void* dk, void* dv,
+                                  kvs_stream_t stream);
+
 /* Self-test of the tcgen05 path (no reference counterpart): c[128][128] f32 =
  * a[128][128] (bf16 row-major) x B, with B given as bt[128 n][128 k] (mode bit 0 = 0,
  * K-major operand) or b[128 k][128 n] (bit 0 = 1, MN-major operand); mode bit 1 = 1

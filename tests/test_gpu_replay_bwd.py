@@ -1,0 +1,133 @@
+"""Replay attention backward: gradients of the masked replay attention against torch
+autograd through a dense masked attention (fp64 1e-10, fp32 1e-4, bf16 on bf16 inputs 5e-2
+absolute on O(1) gradients), and TinyLM parameter gradients through token_logprobs against a
+pure-torch dense-mask model (fp64 1e-9)."""
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _dense_mask(ev, lengths, T):
+    t = torch.arange(T)[:, None]
+    s = torch.arange(T)[None, :]
+    masks = []
+    for b in range(ev.shape[0]):
+        L = int(lengths[b])
+        m = (s <= t) & (t < ev[b][None, :].cpu())
+        pad = (t >= L) & (s == t)
+        masks.append(torch.where(t >= L, pad, m))
+    return torch.stack(masks)  # [B, T, T]
+
+
+def _dense_attention(q, k, v, mask, scale):
+    B, T, Hq, D = q.shape
+    G = Hq // k.shape[2]
+    kk = k.repeat_interleave(G, dim=2)
+    vv = v.repeat_interleave(G, dim=2)
+    sc = torch.einsum("bthd,bshd->bhts", q, kk) * scale
+    sc = sc.masked_fill(~mask[:, None], float("-inf"))
+    p = torch.softmax(sc, dim=-1)
+    return torch.einsum("bhts,bshd->bthd", p, vv)
+
+
+def _case(dtype, D, Hq, Hkv, B=2, T=90, lengths=(90, 61), seed=0):
+    from kvstreams.workloads import replay_evicted_at
+
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    q = torch.randn(B, T, Hq, D, generator=g, device="cuda", dtype=torch.float64)
+    k = torch.randn(B, T, Hkv, D, generator=g, device="cuda", dtype=torch.float64)
+    v = torch.randn(B, T, Hkv, D, generator=g, device="cuda", dtype=torch.float64)
+    go = torch.randn(B, T, Hq, D, generator=g, device="cuda", dtype=torch.float64)
+    ev, _ = replay_evicted_at(batch=B, seq_len=T, events_range=(2, 4), mean_turn=12, seed=seed)
+    ev_t = torch.from_numpy(ev).cuda()
+    ln = torch.tensor(lengths, dtype=torch.int32, device="cuda")
+    return [x.to(dtype) for x in (q, k, v, go)] + [ev_t, ln]
+
+
+@pytest.mark.parametrize("dtype,D,Hq,Hkv,tol", [
+    (torch.float64, 16, 4, 2, 1e-10),
+    (torch.float64, 128, 4, 4, 1e-10),
+    (torch.float32, 128, 8, 2, 1e-4),
+    (torch.bfloat16, 128, 8, 2, 5e-2),
+])
+def test_replay_backward_matches_autograd(dtype, D, Hq, Hkv, tol):
+    from kvstreams import ops
+
+    q, k, v, go, ev, ln = _case(dtype, D, Hq, Hkv, seed=D + Hq)
+    scale = D ** -0.5
+    out = ops.replay_attention(q, k, v, ev, ln, scale)
+    dq, dk, dv = ops.replay_attention_backward(q, k, v, ev, ln, scale, out, go)
+    # reference on the same (possibly rounded) inputs, in float64
+    qr, kr, vr = (x.detach().double().requires_grad_() for x in (q, k, v))
+    mask = _dense_mask(ev, ln.cpu(), q.shape[1]).cuda()
+    ref = _dense_attention(qr, kr, vr, mask, scale)
+    ref.backward(go.double())
+    for got, want, name in ((dq, qr.grad, "dq"), (dk, kr.grad, "dk"), (dv, vr.grad, "dv")):
+        err = (got.double() - want).abs().max().item()
+        assert err <= tol, f"{name}: {err}"
+
+
+def _torch_rope(x, pos, inv):
+    ang = pos.to(inv.dtype)[..., None] * inv  # [B, T, D/2]
+    c, s = torch.cos(ang)[:, :, None, :], torch.sin(ang)[:, :, None, :]
+    h = x.shape[-1] // 2
+    x1, x2 = x[..., :h], x[..., h:]
+    return torch.cat([x1 * c - x2 * s, x2 * c + x1 * s], dim=-1)
+
+
+def _dense_tinylm_logprobs(model, tokens, positions, mask):
+    """TinyLM forward (model.py:132-157) with torch ops only and a dense mask."""
+    import torch.nn.functional as F
+
+    cfg = model.cfg
+    inv = model.rope.table(tokens.device, model.dtype)
+    x = model.embed(tokens)
+    B, T = tokens.shape
+    for blk in model.layers:
+        h = F.rms_norm(x, (x.shape[-1],), blk.attn_norm.weight, blk.attn_norm.eps)
+        a = blk.attn
+        q = a.q_proj(h).view(B, T, a.n_heads, a.head_dim)
+        k = a.k_proj(h).view(B, T, a.n_kv_heads, a.head_dim)
+        v = a.v_proj(h).view(B, T, a.n_kv_heads, a.head_dim)
+        q, k = _torch_rope(q, positions, inv), _torch_rope(k, positions, inv)
+        o = _dense_attention(q, k, v, mask, a.scale)
+        x = x + a.o_proj(o.reshape(B, T, -1))
+        h = F.rms_norm(x, (x.shape[-1],), blk.mlp_norm.weight, blk.mlp_norm.eps)
+        x = x + blk.mlp.down(F.silu(blk.mlp.gate(h)) * blk.mlp.up(h))
+    x = F.rms_norm(x, (x.shape[-1],), model.norm.weight, model.norm.eps)
+    logp = torch.log_softmax(model.lm_head(x), dim=-1)
+    out = torch.zeros(B, T, dtype=logp.dtype, device=logp.device)
+    out[:, 1:] = logp[:, :-1].gather(-1, tokens[:, 1:, None]).squeeze(-1)
+    return out
+
+
+def test_tinylm_gradients_through_token_logprobs_fp64():
+    from kvstreams.config import ModelConfig
+    from kvstreams.model import TinyLM
+    from kvstreams.training.logprobs import token_logprobs
+    from kvstreams.training.replay import Batch
+    from kvstreams.workloads import replay_evicted_at
+
+    torch.manual_seed(0)
+    cfg = ModelConfig()
+    with torch.device("cuda"):
+        model = TinyLM(cfg).double()
+    B, T = 2, 72
+    ev, _ = replay_evicted_at(batch=B, seq_len=T, events_range=(2, 4), mean_turn=10, seed=5)
+    tokens = torch.randint(1, cfg.vocab_size, (B, T), device="cuda")
+    lengths = torch.tensor([T, 50], device="cuda")
+    positions = torch.arange(T, device="cuda").expand(B, T)
+    batch = Batch(tokens, positions, torch.from_numpy(ev).cuda(), torch.ones(B, T, dtype=torch.bool, device="cuda"),
+                  torch.zeros(B, T, dtype=torch.float64, device="cuda"), lengths)
+    w = torch.randn(B, T, dtype=torch.float64, device="cuda")
+    (token_logprobs(model, batch) * w).sum().backward()
+    got = {n: p.grad.clone() for n, p in model.named_parameters()}
+    model.zero_grad()
+    mask = _dense_mask(torch.from_numpy(ev), lengths.cpu(), T).cuda()
+    (_dense_tinylm_logprobs(model, tokens, positions, mask) * w).sum().backward()
+    for n, p in model.named_parameters():
+        err = (got[n] - p.grad).abs().max().item()
+        assert err <= 1e-9, f"{n}: {err}"
