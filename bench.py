@@ -315,6 +315,7 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
         secondary = compaction_bench(dev, args, rank)
         secondary["replay_attention"] = replay_bench(dev, args, rank)
         secondary["rollout"] = rollout_bench(dev, args, rank)
+        secondary["prefill"] = prefill_bench(dev, args, rank)
         secondary["replay_model"] = replay_model_bench(dev, args, rank)
 
     if rank != 0:
@@ -489,6 +490,66 @@ def rollout_bench(dev, args, rank: int) -> dict:
     return out
 
 
+def prefill_bench(dev, args, rank: int) -> dict:
+    """Tensor-core paged prefill, one layer: ``--prefill-streams`` sequences each appending a
+    chunk of ~U[64,512] new tokens (the config-5 observation) onto live contexts ~U[1024,8192]
+    with evicted gaps, 32q/8kv heads, D 128, bs 16, bf16.  Algorithmic work: 4 * Hq * D FLOP per
+    (new token, visible entry) pair; timed by CUDA events around the kvs_paged_decode call
+    (RoPE + append + attention), after warm-up, on fresh appends each step."""
+    import numpy as np
+    import torch
+
+    from kvstreams import ops
+    from kvstreams.distributed import reduce_max
+    from kvstreams.paged_cache import PagedKVCache
+    from kvstreams.rope import RotaryEmbedding
+    from kvstreams.workloads import decode_state
+
+    n, steps = args.prefill_streams, 3
+    rng = np.random.default_rng(7 + rank)
+    chunk = [int(x) for x in rng.integers(64, 513, size=n)]
+    st = decode_state(num_streams=n, ctx_range=(1024, 8192), block_size=16,
+                      num_blocks=n * ((8192 + (steps + 4) * 512) // 16 + 8), evicted_spans_range=(1, 6), seed=3 + rank)
+    cache = PagedKVCache(1, 8, 128, block_size=16, num_blocks=st.num_blocks, dtype=torch.bfloat16, device=dev,
+                         max_seqs=n)
+    cache.load_state(range(n), st.tables, st.positions, st.free_list)
+    g = torch.Generator(device=dev).manual_seed(rank)
+    cache.k.normal_(generator=g)
+    cache.v.normal_(generator=g)
+    inv = RotaryEmbedding(128, 5e5).table(dev, torch.bfloat16)
+    N = sum(chunk)
+    q = torch.randn(N, 32, 128, generator=g, device=dev).bfloat16()
+    kn = torch.randn(N, 8, 128, generator=g, device=dev).bfloat16()
+    vn = torch.randn(N, 8, 128, generator=g, device=dev).bfloat16()
+    nxt = [int(x) for x in st.next_positions]
+    seqs = list(range(n))
+    ms_all, flops_all = [], []
+    for it in range(steps + 2):
+        lens = [cache.num_tokens(s) for s in seqs]
+        pos = torch.from_numpy(np.concatenate([np.arange(p, p + c) for p, c in zip(nxt, chunk)])).to(dev)
+        mapping = cache.append_slots_batch(seqs, pos, chunk)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        ops.paged_forward(cache, seqs, chunk, 0, q, kn, vn, pos, mapping, inv, 128 ** -0.5)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        if it >= 2:
+            ms_all.append(e0.elapsed_time(e1))
+            # visible pairs: token i of a chunk of c over n_old entries sees n_old + i + 1
+            flops_all.append(sum(4 * 32 * 128 * (c * L + c * (c + 1) / 2) for c, L in zip(chunk, lens)))
+        nxt = [p + c for p, c in zip(nxt, chunk)]
+    cache.sync()
+    ms = reduce_max(float(np.mean(ms_all)), dev)
+    tf = float(np.mean(flops_all)) / (ms * 1e-3) / 1e12
+    peaks = _peaks()
+    del cache, q, kn, vn
+    torch.cuda.empty_cache()
+    return {"workload": f"{n} sequences x chunk U[64,512] ({N} new tokens) onto contexts U[1024,8192], 32q/8kv D128 "
+                        "bs16 bf16, one layer", "ms": ms, "tflops": tf, "tc_frac": tf / peaks["bf16_tflops"],
+            "peak_src": peaks["src"], "prefill_tok_s": N / (ms * 1e-3),
+            "kernel": "pair_attn_kernel<true> (tcgen05/TMEM paged prefill)"}
+
+
 def replay_model_bench(dev, args, rank: int) -> dict:
     """Config 4 end to end: the trainer's replay of KV-streams rollouts through the whole
     Llama-3-8B architecture (random init, bf16): token_logprobs = masked full-sequence forward
@@ -610,6 +671,8 @@ def main() -> int:
     ap.add_argument("--replay-model-b", type=int, default=2, help="config 4 uses 16")
     ap.add_argument("--replay-model-t", type=int, default=32768)
     ap.add_argument("--replay-model-only", action="store_true", help="only the whole-model replay measurement")
+    ap.add_argument("--prefill-streams", type=int, default=64)
+    ap.add_argument("--prefill-only", action="store_true", help="only the paged prefill measurement")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -635,6 +698,11 @@ def main() -> int:
             r = replay_bench(torch.device("cuda", local_rank), args, rank)
             if rank == 0:
                 print(json.dumps({"replay_attention": r}), flush=True)
+        elif args.prefill_only:
+            torch.cuda.set_device(local_rank)
+            r = prefill_bench(torch.device("cuda", local_rank), args, rank)
+            if rank == 0:
+                print(json.dumps({"prefill": r}), flush=True)
         elif args.replay_model_only:
             torch.cuda.set_device(local_rank)
             r = replay_model_bench(torch.device("cuda", local_rank), args, rank)
