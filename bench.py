@@ -314,6 +314,7 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
         del hq, hk, hv, hout
         secondary = compaction_bench(dev, args, rank)
         secondary["replay_attention"] = replay_bench(dev, args, rank)
+        secondary["replay_backward"] = replay_backward_bench(dev, args, rank)
         secondary["rollout"] = rollout_bench(dev, args, rank)
         secondary["prefill"] = prefill_bench(dev, args, rank)
         secondary["replay_model"] = replay_model_bench(dev, args, rank)
@@ -645,6 +646,50 @@ def replay_bench(dev, args, rank: int) -> dict:
             "kernel": "pair_attn_kernel (tcgen05/TMEM, two query heads of a GQA group per CTA)"}
 
 
+def replay_backward_bench(dev, args, rank: int) -> dict:
+    """Backward of the masked replay attention, one layer of the Llama-3-8B geometry (bf16):
+    the tcgen05 kernels (row statistics from the forward).  Algorithmic work = 10 * Hq * D
+    FLOP per visible (query, key) pair (dV, dP, dS^T Q, dS K and the S recompute counted
+    once, the standard 2.5x of the forward); the dK/dV kernel's second S/dP product is
+    overhead, not work."""
+    import torch
+
+    from kvstreams import ops
+    from kvstreams.workloads import replay_evicted_at, visible_pairs
+
+    B, T = args.replay_bwd_b, args.replay_t
+    ev, _ = replay_evicted_at(batch=B, seq_len=T, seed=rank)
+    pairs = visible_pairs(ev)
+    g = torch.Generator(device=dev).manual_seed(rank)
+    q = torch.randn(B, T, HQ, D, generator=g, device=dev).bfloat16()
+    k = torch.randn(B, T, HKV, D, generator=g, device=dev).bfloat16()
+    v = torch.randn(B, T, HKV, D, generator=g, device=dev).bfloat16()
+    go = torch.randn(B, T, HQ, D, generator=g, device=dev).bfloat16()
+    ev_t = torch.from_numpy(ev).to(dev)
+    ln_t = torch.full((B,), T, dtype=torch.int32, device=dev)
+    lse = ops.row_lse_buffer(B, HQ, T, dev)
+    out = ops.replay_attention(q, k, v, ev_t, ln_t, D ** -0.5, row_lse=lse)
+    times = []
+    for i in range(2 + args.replay_steps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        grads = ops.replay_attention_backward(q, k, v, ev_t, ln_t, D ** -0.5, out, go, row_lse=lse)
+        b.record()
+        torch.cuda.synchronize()
+        del grads
+        if i >= 2:
+            times.append(a.elapsed_time(b))
+    ms = statistics.median(times)
+    flops = 10.0 * HQ * D * pairs
+    peaks = _peaks()
+    tf = flops / (ms * 1e-3) / 1e12
+    del q, k, v, go, out, lse
+    return {"workload": f"B={B} T={T} 32q/8kv D128 bf16, 3-8 keep-recent events/stream (one layer)",
+            "ms": ms, "visible_pairs": pairs, "tflops": tf, "tc_frac": tf / peaks["bf16_tflops"],
+            "peak_src": peaks["src"], "replay_bwd_tok_s": B * T / (ms * 1e-3),
+            "kernels": "replay_rowdot_kernel + replay_dkdv_kernel + replay_dq_kernel (tcgen05/TMEM)"}
+
+
 def main() -> int:
     global S, NB, CTX
     ap = argparse.ArgumentParser()
@@ -661,6 +706,8 @@ def main() -> int:
     ap.add_argument("--replay-t", type=int, default=32768)
     ap.add_argument("--replay-steps", type=int, default=2)
     ap.add_argument("--replay-only", action="store_true", help="only the replay attention measurement")
+    ap.add_argument("--replay-bwd-b", type=int, default=4)
+    ap.add_argument("--replay-bwd-only", action="store_true", help="only the replay backward measurement")
     ap.add_argument("--rollout-streams", type=int, default=64)
     ap.add_argument("--rollout-layers", type=int, default=32)
     ap.add_argument("--rollout-warmup", type=int, default=20)
@@ -698,6 +745,11 @@ def main() -> int:
             r = replay_bench(torch.device("cuda", local_rank), args, rank)
             if rank == 0:
                 print(json.dumps({"replay_attention": r}), flush=True)
+        elif args.replay_bwd_only:
+            torch.cuda.set_device(local_rank)
+            r = replay_backward_bench(torch.device("cuda", local_rank), args, rank)
+            if rank == 0:
+                print(json.dumps({"replay_backward": r}), flush=True)
         elif args.prefill_only:
             torch.cuda.set_device(local_rank)
             r = prefill_bench(torch.device("cuda", local_rank), args, rank)

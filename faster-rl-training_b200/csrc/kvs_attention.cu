@@ -178,7 +178,7 @@ template <typename T, int DPL>
 __global__ void __launch_bounds__(128)
 replay_generic_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
                       const int64_t* __restrict__ ev, const int32_t* __restrict__ lengths, T* __restrict__ out,
-                      int B, int Tn, int Hq, int Hkv, int D, double scale) {
+                      float* __restrict__ row_lse, int B, int Tn, int Hq, int Hkv, int D, double scale) {
   const int64_t gw = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5);
   if (gw >= (int64_t)B * Tn * Hq) return;
   const int h = (int)(gw % Hq);
@@ -203,6 +203,10 @@ replay_generic_kernel(const T* __restrict__ q, const T* __restrict__ k, const T*
     }
   }
   row.store(out + qo, D);
+  if (row_lse != nullptr && (threadIdx.x & 31) == 0) {  // natural-log sum-exp in log2 units
+    const int T_pad = (Tn + 127) / 128 * 128;
+    row_lse[((int64_t)b * Hq + h) * T_pad + t] = (float)((row.m + log((double)row.l)) * 1.4426950408889634);
+  }
 }
 
 template <typename T>
@@ -230,7 +234,8 @@ int launch_replay_generic(const kvs_replay_args& a, cudaStream_t st) {
   const T* v = static_cast<const T*>(a.v);
   T* o = static_cast<T*>(a.out);
 #define KVS_REPLAY(DPL)                                                                             \
-  replay_generic_kernel<T, DPL><<<(unsigned)grid, 128, 0, st>>>(q, k, v, a.evicted_at, a.lengths, o, a.batch, \
+  replay_generic_kernel<T, DPL><<<(unsigned)grid, 128, 0, st>>>(q, k, v, a.evicted_at, a.lengths, o, a.row_lse, \
+                                                                a.batch, \
                                                                 a.seq_len, a.n_heads, a.n_kv_heads,    \
                                                                 a.head_dim, a.scale)
   if (a.head_dim <= 32) KVS_REPLAY(1);

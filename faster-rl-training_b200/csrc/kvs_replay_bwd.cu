@@ -235,9 +235,15 @@ size_t acc_bytes(int dtype) { return dtype == KVS_F64 ? 8 : 4; }
 
 }  // namespace
 
+size_t kvs_replay_tc_backward_scratch(int B, int T, int Hq);
+int kvs_replay_tc_backward(const kvs_replay_args* a, const void* dout, void* dq, void* dk, void* dv, cudaStream_t st);
+
 KVS_API size_t kvs_replay_backward_scratch_bytes(int32_t batch, int32_t seq_len, int32_t n_heads, int32_t dtype) {
   if (batch <= 0 || seq_len <= 0 || n_heads <= 0) return 0;
-  return align_up((size_t)2 * batch * seq_len * n_heads * acc_bytes(dtype), 256);
+  const size_t exact = align_up((size_t)2 * batch * seq_len * n_heads * acc_bytes(dtype), 256);
+  if (dtype != KVS_BF16) return exact;
+  const size_t tc = kvs_replay_tc_backward_scratch(batch, seq_len, n_heads);
+  return tc > exact ? tc : exact;
 }
 
 KVS_API int kvs_replay_attention_backward(const kvs_replay_args* a, const void* dout, void* dq, void* dk, void* dv,
@@ -251,6 +257,10 @@ KVS_API int kvs_replay_attention_backward(const kvs_replay_args* a, const void* 
       a->scratch_bytes < kvs_replay_backward_scratch_bytes(a->batch, a->seq_len, a->n_heads, a->dtype))
     return KVS_E_SCRATCH;
   const cudaStream_t st = to_cuda(stream);
+  if (a->dtype == KVS_BF16 && a->row_lse != nullptr && !(a->flags & 1)) {
+    const int rc = kvs_replay_tc_backward(a, dout, dq, dk, dv, st);
+    if (rc != KVS_E_UNSUPPORTED) return rc;
+  }
   switch (a->dtype) {
     case KVS_F32: return launch_backward<float>(*a, dout, dq, dk, dv, st);
     case KVS_F64: return launch_backward<double>(*a, dout, dq, dk, dv, st);

@@ -73,6 +73,7 @@ struct ReplayParams {
   const int32_t* tile_max; // [B][n_kt]
   const int32_t* lengths;  // [B]
   __nv_bfloat16* out;      // [B][T][Hq][D]
+  float* lse;              // optional [B][Hq][T_pad]: log2 sum of 2^(scaled score) per row
   int32_t* error;          // [1]
   int B, T, T_pad, Hq, Hkv, n_qt, n_kt;
   float scale_log2;
@@ -379,6 +380,7 @@ replay_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     red[((n & 1) * 2 + half) * BM + r] = l;
     softmax_bar();
     const float lsum = l + red[((n & 1) * 2 + (half ^ 1)) * BM + r];
+    if (ok && half == 0 && p.lse != nullptr && t < p.T) p.lse[((int64_t)b * p.Hq + h) * p.T_pad + t] = m + log2f(lsum);
     if (!ok) {
       *abort_flag = 1;
       atomicExch(p.error, 3);
@@ -823,6 +825,8 @@ pair_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     } else {
       tc_fence_after();
       const float inv = 1.f / l;
+      if (!PAGED && p.lse != nullptr && t < p.T)
+        p.lse[((int64_t)b * p.Hq + h0 + team) * p.T_pad + t] = m + log2f(l);
       const int64_t orow_idx = PAGED ? (int64_t)tok0 + ci : (int64_t)b * p.T + t;
       const bool store = PAGED ? ci < Ti : t < p.T;
       __nv_bfloat16* orow = p.out + (orow_idx * p.Hq + h0 + team) * HD;
@@ -850,6 +854,550 @@ pair_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     tmem_dealloc(tmem, 512);
   }
 }
+
+// ------------------------------------------------------------------ backward (tcgen05)
+// Gradients of the masked replay attention on the tensor cores, bf16, head_dim 128.  With
+// the forward's row statistics lse2[b][h][t] = log2 sum_s 2^(scale*log2(e)*q_t.k_s) (written
+// by the forward kernels) and D[b][h][t] = sum_d dO O (replay_rowdot_kernel):
+//   P = 2^(scale*log2(e)*Q K^T - lse2),  dS = P o (dO V^T - D),
+//   dV = P^T dO,  dK = scale dS^T Q,  dQ = scale dS K.
+// Two kernels, no atomics: replay_dkdv_kernel owns a 128-key tile of one KV head and loops
+// over the query tiles and query heads that see it; replay_dq_kernel owns a 128-query tile
+// of one head and loops over its active key tiles (the forward's list).  P and dS are
+// rounded to bf16 as UMMA operands (as P is in the forward).
+
+// D[b][h][t] = sum_d dO[b][t][h][d] * O[b][t][h][d] (one warp per row and head)
+__global__ void replay_rowdot_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ o,
+                                     float* __restrict__ dvec, int B, int T, int T_pad, int Hq) {
+  const int64_t gw = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (gw >= (int64_t)B * T * Hq) return;
+  const int lane = threadIdx.x & 31;
+  const int h = (int)(gw % Hq), t = (int)((gw / Hq) % T), b = (int)(gw / ((int64_t)Hq * T));
+  const uint2 x = reinterpret_cast<const uint2*>(dout + gw * HD)[lane];
+  const uint2 y = reinterpret_cast<const uint2*>(o + gw * HD)[lane];
+  const __nv_bfloat162* xa = reinterpret_cast<const __nv_bfloat162*>(&x);
+  const __nv_bfloat162* ya = reinterpret_cast<const __nv_bfloat162*>(&y);
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float2 a = __bfloat1622float2(xa[i]), c = __bfloat1622float2(ya[i]);
+    s += a.x * c.x + a.y * c.y;
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  if (lane == 0) dvec[((int64_t)b * Hq + h) * T_pad + t] = s;
+}
+
+constexpr int NTB = 192;  // warp 0 producer, warp 1 UMMA, warps 2-5 one thread per TMEM lane
+constexpr int VEC_BYTES = BM * 4;
+
+struct BwdParams {
+  const int32_t* e32;       // [B][T_pad] evicted_at clamped to int32 (prepass)
+  const int32_t* tile_min;  // [B][n_kt] (prepass)
+  const int32_t* tile_max;
+  const int32_t* lengths;
+  const float* lse;         // [B][Hq][T_pad] log2 units
+  const float* dvec;        // [B][Hq][T_pad]
+  __nv_bfloat16* dq;        // [B][T][Hq][D]
+  __nv_bfloat16* dk;        // [B][T][Hkv][D]
+  __nv_bfloat16* dv;
+  int32_t* error;
+  int B, T, T_pad, Hq, Hkv, n_qt, n_kt;
+  float scale_log2, scale;
+};
+
+// smem of the dK/dV kernel
+constexpr int OFFB_K = 0, OFFB_V = TILE_BYTES;
+constexpr int OFFB_Q = 2 * TILE_BYTES;                // 2 slots
+constexpr int OFFB_DO = OFFB_Q + 2 * TILE_BYTES;      // 2 slots
+constexpr int OFFB_LSE = OFFB_DO + 2 * TILE_BYTES;    // 2 slots of 128 f32
+constexpr int OFFB_D = OFFB_LSE + 2 * VEC_BYTES;      // 2 slots of 128 f32
+constexpr int OFFB_BAR = OFFB_D + 2 * VEC_BYTES;
+enum { D_KVFULL = 0, D_QFULL0, D_QFULL1, D_QEMPTY0, D_QEMPTY1, D_SFULL, D_PFULL, D_FINAL, NBARB };
+constexpr int OFFB_MISC = OFFB_BAR + NBARB * 8;
+constexpr int SMEMB_BYTES = OFFB_MISC + 64 + 1024;
+static_assert(SMEMB_BYTES <= 232448, "dK/dV kernel shared memory");
+
+__host__ __device__ constexpr uint32_t kq_step(int kk) { return (uint32_t)(((kk >> 2) * HALF_BYTES + (kk & 3) * 32) >> 4); }
+__host__ __device__ constexpr uint32_t mn_step(int kk) { return (uint32_t)((kk * 2048) >> 4); }
+
+__global__ void __launch_bounds__(NTB, 1)
+replay_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                   const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+                   const BwdParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + OFFB_BAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFFB_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFFB_MISC + 4);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // CTA order: (stream, KV head) slowest, key tiles ascending (the most-seen first)
+  const int G = p.Hq / p.Hkv;
+  const int kt = (int)(blockIdx.x % p.n_kt);
+  const int bhk = (int)(blockIdx.x / p.n_kt);
+  const int b = bhk / p.Hkv, hk = bhk % p.Hkv;
+  const int k0 = kt * BN;
+  const int L = p.lengths[b];
+  // query tiles that see a key of this tile: from the diagonal to the last row any key's
+  // interval [s, min(evicted_at[s], L)) reaches (padded rows see only themselves, on the diagonal)
+  const int emax = p.tile_max[b * p.n_kt + kt];
+  const int reach = min(emax, L);
+  const int qlast = max(kt, min(p.n_qt - 1, (reach - 1) / BM));
+  const int nsteps = (qlast - kt + 1) * G;
+
+  if (tid == 0) {
+    for (int i = 0; i < NBARB; ++i) mbar_init(&bar[i], 1);
+    mbar_init(&bar[D_PFULL], 128);
+    *abort_flag = 0;
+    mbar_fence_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // TMEM: S^T [0,128) (P^T bf16 over its first 64 columns), dP^T [128,256) (dS^T over its first
+  // 64), dV [256,384), dK [384,512)
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&bar[D_KVFULL], 2 * TILE_BYTES);
+      tma_load_3d(smem + OFFB_K, &tm_k, 0, hk, b * p.T + k0, &bar[D_KVFULL]);
+      tma_load_3d(smem + OFFB_K + HALF_BYTES, &tm_k, 64, hk, b * p.T + k0, &bar[D_KVFULL]);
+      tma_load_3d(smem + OFFB_V, &tm_v, 0, hk, b * p.T + k0, &bar[D_KVFULL]);
+      tma_load_3d(smem + OFFB_V + HALF_BYTES, &tm_v, 64, hk, b * p.T + k0, &bar[D_KVFULL]);
+      for (int i = 0; i < nsteps; ++i) {
+        const int slot = i & 1;
+        if (i >= 2 && !mbar_wait(&bar[D_QEMPTY0 + slot], ((i >> 1) - 1) & 1, abort_flag)) {
+          *abort_flag = 1;
+          atomicExch(p.error, 11);
+          break;
+        }
+        const int qt = kt + i / G, h = hk * G + i % G;
+        const int row = b * p.T + qt * BM;
+        uint64_t* fb = &bar[D_QFULL0 + slot];
+        mbar_arrive_expect_tx(fb, 2 * TILE_BYTES + 2 * VEC_BYTES);
+        uint8_t* qs = smem + OFFB_Q + slot * TILE_BYTES;
+        uint8_t* ds = smem + OFFB_DO + slot * TILE_BYTES;
+        tma_load_3d(qs, &tm_q, 0, h, row, fb);
+        tma_load_3d(qs + HALF_BYTES, &tm_q, 64, h, row, fb);
+        tma_load_3d(ds, &tm_do, 0, h, row, fb);
+        tma_load_3d(ds + HALF_BYTES, &tm_do, 64, h, row, fb);
+        const int64_t vo = ((int64_t)b * p.Hq + h) * p.T_pad + qt * BM;
+        bulk_load(smem + OFFB_LSE + slot * VEC_BYTES, p.lse + vo, VEC_BYTES, fb);
+        bulk_load(smem + OFFB_D + slot * VEC_BYTES, p.dvec + vo, VEC_BYTES, fb);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- UMMA issuer (whole warp)
+    constexpr uint32_t ID_T = idesc_bf16(128, 128, 0);   // S^T, dP^T: both operands K-major
+    constexpr uint32_t ID_MN = idesc_bf16(128, 128, 1);  // dV, dK: B (dO, Q) MN-major
+    const uint64_t dk_ = desc_kmajor_sw128(smem_addr(smem + OFFB_K));
+    const uint64_t dv_ = desc_kmajor_sw128(smem_addr(smem + OFFB_V));
+    auto wait = [&](uint64_t* bb, int parity) {
+      return __all_sync(0xffffffffu, mbar_wait_fast(bb, parity, abort_flag));
+    };
+    bool ok = wait(&bar[D_KVFULL], 0);
+    for (int i = 0; ok && i < nsteps; ++i) {
+      const int slot = i & 1;
+      ok = wait(&bar[D_QFULL0 + slot], (i >> 1) & 1);
+      if (!ok) break;
+      tc_fence_after();
+      const uint64_t dq_k = desc_kmajor_sw128(smem_addr(smem + OFFB_Q + slot * TILE_BYTES));
+      const uint64_t ddo_k = desc_kmajor_sw128(smem_addr(smem + OFFB_DO + slot * TILE_BYTES));
+      const uint64_t dq_mn = desc_mnmajor_sw128(smem_addr(smem + OFFB_Q + slot * TILE_BYTES), HALF_BYTES);
+      const uint64_t ddo_mn = desc_mnmajor_sw128(smem_addr(smem + OFFB_DO + slot * TILE_BYTES), HALF_BYTES);
+      {
+        const uint32_t d = tmem;
+#define KVS_ST(kk) umma_bf16_warp_at<kq_step(kk), kq_step(kk)>(d, dk_, dq_k, ID_T, kk > 0)
+        KVS_ST(0); KVS_ST(1); KVS_ST(2); KVS_ST(3); KVS_ST(4); KVS_ST(5); KVS_ST(6); KVS_ST(7);
+#undef KVS_ST
+      }
+      {
+        const uint32_t d = tmem + 128;
+#define KVS_DPT(kk) umma_bf16_warp_at<kq_step(kk), kq_step(kk)>(d, dv_, ddo_k, ID_T, kk > 0)
+        KVS_DPT(0); KVS_DPT(1); KVS_DPT(2); KVS_DPT(3); KVS_DPT(4); KVS_DPT(5); KVS_DPT(6); KVS_DPT(7);
+#undef KVS_DPT
+      }
+      umma_commit_warp(&bar[D_SFULL]);
+      ok = wait(&bar[D_PFULL], i & 1);
+      if (!ok) break;
+      tc_fence_after();
+      {
+        const uint32_t d = tmem + 256, a = tmem;
+        const uint32_t acc = i > 0;
+#define KVS_DV(kk) umma_bf16_tmem_a_warp_at<kk * 8, mn_step(kk)>(d, a, ddo_mn, ID_MN, (kk > 0) || acc)
+        KVS_DV(0); KVS_DV(1); KVS_DV(2); KVS_DV(3); KVS_DV(4); KVS_DV(5); KVS_DV(6); KVS_DV(7);
+#undef KVS_DV
+      }
+      {
+        const uint32_t d = tmem + 384, a = tmem + 128;
+        const uint32_t acc = i > 0;
+#define KVS_DK(kk) umma_bf16_tmem_a_warp_at<kk * 8, mn_step(kk)>(d, a, dq_mn, ID_MN, (kk > 0) || acc)
+        KVS_DK(0); KVS_DK(1); KVS_DK(2); KVS_DK(3); KVS_DK(4); KVS_DK(5); KVS_DK(6); KVS_DK(7);
+#undef KVS_DK
+      }
+      umma_commit_warp(&bar[D_QEMPTY0 + slot]);
+    }
+    if (!ok && lane == 0) {
+      *abort_flag = 1;
+      atomicExch(p.error, 12);
+    }
+    umma_commit_warp(&bar[D_FINAL]);
+    mbar_wait(&bar[D_FINAL], 0, nullptr);
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ one thread per key row
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const int s = k0 + r;
+    const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16);
+    const float sl2 = p.scale_log2;
+    // the query rows that see key s: [s, min(evicted_at[s], L)) for a real key, s itself for a
+    // padded one, nothing past the stream
+    int rlo = 0, rhi = 0;
+    if (s < L) {
+      rlo = s;
+      rhi = min(p.e32[(int64_t)b * p.T_pad + s], L);
+    } else if (s < p.T) {
+      rlo = s;
+      rhi = s + 1;
+    }
+    bool ok = true;
+    for (int i = 0; i < nsteps; ++i) {
+      const int slot = i & 1;
+      const int t0 = (kt + i / G) * BM;
+      ok = mbar_wait_fast(&bar[D_SFULL], i & 1, abort_flag);
+      if (ok) ok = mbar_wait_fast(&bar[D_QFULL0 + slot], (i >> 1) & 1, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      const int lo = max(rlo - t0, 0), hi = min(rhi - t0, BM);  // visible columns [lo, hi)
+      const float4* lse4 = reinterpret_cast<const float4*>(smem + OFFB_LSE + slot * VEC_BYTES);
+      const float4* d4 = reinterpret_cast<const float4*>(smem + OFFB_D + slot * VEC_BYTES);
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t sv[32], dp[32];
+        tmem_ld32(tl + 32 * c, sv);
+        tmem_ld32(tl + 128 + 32 * c, dp);
+        tmem_wait_ld();
+        uint32_t pk[16], dk[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 4) {
+          const float4 ls = lse4[(32 * c + e) >> 2];
+          const float4 dd = d4[(32 * c + e) >> 2];
+          const float lsv[4] = {ls.x, ls.y, ls.z, ls.w}, ddv[4] = {dd.x, dd.y, dd.z, dd.w};
+          float pv[4], dsv[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int col = 32 * c + e + u;
+            const bool vis = col >= lo && col < hi;
+            const float pr = ex2_approx(fmaf(__uint_as_float(sv[e + u]), sl2, -lsv[u]));
+            pv[u] = vis ? pr : 0.f;
+            dsv[u] = vis ? pr * (__uint_as_float(dp[e + u]) - ddv[u]) : 0.f;
+          }
+          pk[e >> 1] = pack2(pv[0], pv[1]);
+          pk[(e >> 1) + 1] = pack2(pv[2], pv[3]);
+          dk[e >> 1] = pack2(dsv[0], dsv[1]);
+          dk[(e >> 1) + 1] = pack2(dsv[2], dsv[3]);
+        }
+        tmem_st16(tl + 16 * c, pk);
+        tmem_st16(tl + 128 + 16 * c, dk);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&bar[D_PFULL]);
+    }
+    if (ok) ok = mbar_wait(&bar[D_FINAL], 0, abort_flag);
+    ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below is warp-collective
+    if (!ok) {
+      *abort_flag = 1;
+      atomicExch(p.error, 13);
+    } else {
+      tc_fence_after();
+      const int64_t row = ((int64_t)b * p.T + s) * p.Hkv + hk;
+#pragma unroll 1
+      for (int which = 0; which < 2; ++which) {  // dV, then dK (times the softmax scale)
+        __nv_bfloat16* dst = (which == 0 ? p.dv : p.dk) + row * HD;
+        const float mul = which == 0 ? 1.f : p.scale;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          __syncwarp();
+          tmem_ld32(tl + 256 + 128 * which + 32 * c, o);
+          tmem_wait_ld();
+          if (s >= p.T) continue;  // rows past the stream: loaded by the whole warp, not stored
+          uint4* d4o = reinterpret_cast<uint4*>(dst + 32 * c);
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4)
+            d4o[q4] = make_uint4(pack2(__uint_as_float(o[8 * q4]) * mul, __uint_as_float(o[8 * q4 + 1]) * mul),
+                                 pack2(__uint_as_float(o[8 * q4 + 2]) * mul, __uint_as_float(o[8 * q4 + 3]) * mul),
+                                 pack2(__uint_as_float(o[8 * q4 + 4]) * mul, __uint_as_float(o[8 * q4 + 5]) * mul),
+                                 pack2(__uint_as_float(o[8 * q4 + 6]) * mul, __uint_as_float(o[8 * q4 + 7]) * mul));
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// smem of the dQ kernel
+constexpr int OFFQ_Q = 0, OFFQ_DO = TILE_BYTES;
+constexpr int OFFQ_K = 2 * TILE_BYTES;               // 2 slots
+constexpr int OFFQ_V = OFFQ_K + 2 * TILE_BYTES;      // 2 slots
+constexpr int OFFQ_E = OFFQ_V + 2 * TILE_BYTES;      // 2 slots of 128 int32
+constexpr int OFFQ_LIST = OFFQ_E + 2 * E_BYTES;
+constexpr int OFFQ_BAR = OFFQ_LIST + MAX_KT * 2;
+enum { Q_QFULL = 0, Q_KFULL0, Q_KFULL1, Q_KEMPTY0, Q_KEMPTY1, Q_SFULL, Q_PFULL, Q_FINAL, NBARQ };
+constexpr int OFFQ_MISC = OFFQ_BAR + NBARQ * 8;
+constexpr int SMEMQ_BYTES = OFFQ_MISC + 64 + 33 * 4 + 1024;
+static_assert(SMEMQ_BYTES <= 232448, "dQ kernel shared memory");
+
+__global__ void __launch_bounds__(NTB, 1)
+replay_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                 const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+                 const BwdParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint16_t* list = reinterpret_cast<uint16_t*>(smem + OFFQ_LIST);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + OFFQ_BAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFFQ_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFFQ_MISC + 4);
+  int* s_n = reinterpret_cast<int*>(smem + OFFQ_MISC + 8);
+  int* s_scan = reinterpret_cast<int*>(smem + OFFQ_MISC + 64);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // CTA order as the forward: (stream, KV head) slowest, query tiles heaviest first, then heads
+  const int G = p.Hq / p.Hkv;
+  const int g = (int)(blockIdx.x % G);
+  const int rest = (int)(blockIdx.x / G);
+  const int qt = p.n_qt - 1 - rest % p.n_qt;
+  const int bhk = rest / p.n_qt;
+  const int b = bhk / p.Hkv, hk = bhk % p.Hkv;
+  const int h = hk * G + g;
+  const int t0 = qt * BM, t1 = t0 + BM - 1;
+  const int L = p.lengths[b];
+
+  if (tid == 0) {
+    for (int i = 0; i < NBARQ; ++i) mbar_init(&bar[i], 1);
+    mbar_init(&bar[Q_PFULL], 128);
+    *abort_flag = 0;
+    mbar_fence_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  // active key tiles (the forward's list)
+  {
+    const int real_last = min(t1, L - 1);
+    int carry = 0;
+    for (int base = 0; base <= qt; base += NTB) {
+      const int j = base + tid;
+      int flag = 0;
+      if (j <= qt) {
+        const int emin = p.tile_min[b * p.n_kt + j], emax = p.tile_max[b * p.n_kt + j];
+        const bool active = (j == qt) || (j * BN <= real_last && emax > t0);
+        const bool masked = (j == qt) || (emin <= t1) || (t1 >= L);
+        flag = (active ? 1 : 0) | (masked ? 2 : 0);
+      }
+      int tot = 0;
+      const int pre = block_exclusive_scan(flag & 1, s_scan, &tot);
+      if (flag & 1) list[carry + pre] = (uint16_t)(j | ((flag & 2) ? 0x8000 : 0));
+      carry += tot;
+      __syncthreads();
+    }
+    if (tid == 0) *s_n = carry;
+  }
+  __syncthreads();
+  tc_fence_after();
+  const int n = *s_n;
+  const uint32_t tmem = *tmem_slot;
+  // TMEM: S [0,128) (dS bf16 over its first 64 columns), dP [128,256), dQ [256,384)
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&bar[Q_QFULL], 2 * TILE_BYTES);
+      tma_load_3d(smem + OFFQ_Q, &tm_q, 0, h, b * p.T + t0, &bar[Q_QFULL]);
+      tma_load_3d(smem + OFFQ_Q + HALF_BYTES, &tm_q, 64, h, b * p.T + t0, &bar[Q_QFULL]);
+      tma_load_3d(smem + OFFQ_DO, &tm_do, 0, h, b * p.T + t0, &bar[Q_QFULL]);
+      tma_load_3d(smem + OFFQ_DO + HALF_BYTES, &tm_do, 64, h, b * p.T + t0, &bar[Q_QFULL]);
+      for (int k = 0; k < n; ++k) {
+        const int slot = k & 1;
+        if (k >= 2 && !mbar_wait(&bar[Q_KEMPTY0 + slot], ((k >> 1) - 1) & 1, abort_flag)) {
+          *abort_flag = 1;
+          atomicExch(p.error, 21);
+          break;
+        }
+        const int j = list[k] & 0x7fff;
+        const int row = b * p.T + j * BN;
+        uint64_t* fb = &bar[Q_KFULL0 + slot];
+        mbar_arrive_expect_tx(fb, 2 * TILE_BYTES + E_BYTES);
+        uint8_t* ks = smem + OFFQ_K + slot * TILE_BYTES;
+        uint8_t* vs = smem + OFFQ_V + slot * TILE_BYTES;
+        tma_load_3d(ks, &tm_k, 0, hk, row, fb);
+        tma_load_3d(ks + HALF_BYTES, &tm_k, 64, hk, row, fb);
+        tma_load_3d(vs, &tm_v, 0, hk, row, fb);
+        tma_load_3d(vs + HALF_BYTES, &tm_v, 64, hk, row, fb);
+        bulk_load(smem + OFFQ_E + slot * E_BYTES, p.e32 + (int64_t)b * p.T_pad + j * BN, E_BYTES, fb);
+      }
+    }
+  } else if (warp == 1) {
+    constexpr uint32_t ID_K = idesc_bf16(128, 128, 0);   // S, dP: both operands K-major
+    constexpr uint32_t ID_MN = idesc_bf16(128, 128, 1);  // dQ: B (K) MN-major
+    const uint64_t dq_ = desc_kmajor_sw128(smem_addr(smem + OFFQ_Q));
+    const uint64_t ddo_ = desc_kmajor_sw128(smem_addr(smem + OFFQ_DO));
+    auto wait = [&](uint64_t* bb, int parity) {
+      return __all_sync(0xffffffffu, mbar_wait_fast(bb, parity, abort_flag));
+    };
+    bool ok = wait(&bar[Q_QFULL], 0);
+    for (int k = 0; ok && k < n; ++k) {
+      const int slot = k & 1;
+      ok = wait(&bar[Q_KFULL0 + slot], (k >> 1) & 1);
+      if (!ok) break;
+      tc_fence_after();
+      const uint64_t dk_k = desc_kmajor_sw128(smem_addr(smem + OFFQ_K + slot * TILE_BYTES));
+      const uint64_t dv_k = desc_kmajor_sw128(smem_addr(smem + OFFQ_V + slot * TILE_BYTES));
+      const uint64_t dk_mn = desc_mnmajor_sw128(smem_addr(smem + OFFQ_K + slot * TILE_BYTES), HALF_BYTES);
+      {
+        const uint32_t d = tmem;
+#define KVS_S(kk) umma_bf16_warp_at<kq_step(kk), kq_step(kk)>(d, dq_, dk_k, ID_K, kk > 0)
+        KVS_S(0); KVS_S(1); KVS_S(2); KVS_S(3); KVS_S(4); KVS_S(5); KVS_S(6); KVS_S(7);
+#undef KVS_S
+      }
+      {
+        const uint32_t d = tmem + 128;
+#define KVS_DP(kk) umma_bf16_warp_at<kq_step(kk), kq_step(kk)>(d, ddo_, dv_k, ID_K, kk > 0)
+        KVS_DP(0); KVS_DP(1); KVS_DP(2); KVS_DP(3); KVS_DP(4); KVS_DP(5); KVS_DP(6); KVS_DP(7);
+#undef KVS_DP
+      }
+      umma_commit_warp(&bar[Q_SFULL]);
+      ok = wait(&bar[Q_PFULL], k & 1);
+      if (!ok) break;
+      tc_fence_after();
+      {
+        const uint32_t d = tmem + 256, a = tmem;
+        const uint32_t acc = k > 0;
+#define KVS_DQ(kk) umma_bf16_tmem_a_warp_at<kk * 8, mn_step(kk)>(d, a, dk_mn, ID_MN, (kk > 0) || acc)
+        KVS_DQ(0); KVS_DQ(1); KVS_DQ(2); KVS_DQ(3); KVS_DQ(4); KVS_DQ(5); KVS_DQ(6); KVS_DQ(7);
+#undef KVS_DQ
+      }
+      umma_commit_warp(&bar[Q_KEMPTY0 + slot]);
+    }
+    if (!ok && lane == 0) {
+      *abort_flag = 1;
+      atomicExch(p.error, 22);
+    }
+    umma_commit_warp(&bar[Q_FINAL]);
+    mbar_wait(&bar[Q_FINAL], 0, nullptr);
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ one thread per query row
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const int t = t0 + r;
+    const bool real = t < L;
+    const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16);
+    const float sl2 = p.scale_log2;
+    const int64_t vrow = ((int64_t)b * p.Hq + h) * p.T_pad + t;
+    const float lse2 = t < p.T ? p.lse[vrow] : 0.f;
+    const float drow = t < p.T ? p.dvec[vrow] : 0.f;
+    bool ok = true;
+    for (int k = 0; k < n; ++k) {
+      const int slot = k & 1;
+      const int j = list[k] & 0x7fff;
+      const bool masked = (list[k] >> 15) & 1;
+      ok = mbar_wait_fast(&bar[Q_SFULL], k & 1, abort_flag);
+      if (ok) ok = mbar_wait_fast(&bar[Q_KFULL0 + slot], (k >> 1) & 1, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      // visibility bits of the tile's 128 keys for row t (all set for an unmasked tile)
+      uint32_t bits[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu};
+      if (masked) {
+        const int lim = t - j * BN;
+        const int4* E4 = reinterpret_cast<const int4*>(smem + OFFQ_E + slot * E_BYTES);
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          uint32_t bw = 0;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const int4 e = E4[w * 8 + q];
+            const int ev[4] = {e.x, e.y, e.z, e.w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int i = 32 * w + 4 * q + u;
+              const bool vis = (i <= lim) && (real ? (t < ev[u]) : (i >= lim));
+              bw |= (vis ? 1u : 0u) << (4 * q + u);
+            }
+          }
+          bits[w] = (t < p.T) ? bw : 0u;
+        }
+      }
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t sv[32], dp[32];
+        tmem_ld32(tl + 32 * c, sv);
+        tmem_ld32(tl + 128 + 32 * c, dp);
+        tmem_wait_ld();
+        uint32_t dk[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float dsv[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const bool vis = (bits[c] >> (e + u)) & 1;
+            const float pr = ex2_approx(fmaf(__uint_as_float(sv[e + u]), sl2, -lse2));
+            dsv[u] = vis ? pr * (__uint_as_float(dp[e + u]) - drow) : 0.f;
+          }
+          dk[e >> 1] = pack2(dsv[0], dsv[1]);
+        }
+        tmem_st16(tl + 16 * c, dk);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&bar[Q_PFULL]);
+    }
+    if (ok) ok = mbar_wait(&bar[Q_FINAL], 0, abort_flag);
+    ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below is warp-collective
+    if (!ok) {
+      *abort_flag = 1;
+      atomicExch(p.error, 23);
+    } else {
+      tc_fence_after();
+      __nv_bfloat16* dst = p.dq + (((int64_t)b * p.T + t) * p.Hq + h) * HD;
+      const float mul = p.scale;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[32];
+        __syncwarp();
+        tmem_ld32(tl + 256 + 32 * c, o);
+        tmem_wait_ld();
+        if (t >= p.T) continue;  // rows past the stream: loaded by the whole warp, not stored
+        uint4* d4o = reinterpret_cast<uint4*>(dst + 32 * c);
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4)
+          d4o[q4] = make_uint4(pack2(__uint_as_float(o[8 * q4]) * mul, __uint_as_float(o[8 * q4 + 1]) * mul),
+                               pack2(__uint_as_float(o[8 * q4 + 2]) * mul, __uint_as_float(o[8 * q4 + 3]) * mul),
+                               pack2(__uint_as_float(o[8 * q4 + 4]) * mul, __uint_as_float(o[8 * q4 + 5]) * mul),
+                               pack2(__uint_as_float(o[8 * q4 + 6]) * mul, __uint_as_float(o[8 * q4 + 7]) * mul));
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 
 // per-(stream, key tile) min / max of evicted_at and the padded int32 copy
 __global__ void replay_prepass_kernel(const int64_t* __restrict__ ev, int T, int T_pad, int n_kt,
@@ -1094,6 +1642,7 @@ int kvs_replay_tc_launch(const kvs_replay_args* a, cudaStream_t st) {
   p.tile_max = s.tmax;
   p.lengths = a->lengths;
   p.out = static_cast<__nv_bfloat16*>(a->out);
+  p.lse = a->row_lse;
   p.error = s.error;
   p.B = B;
   p.T = T;
@@ -1111,6 +1660,83 @@ int kvs_replay_tc_launch(const kvs_replay_args* a, cudaStream_t st) {
     const int64_t grid = (int64_t)B * a->n_heads * n_kt;
     replay_tc_kernel<<<(unsigned)grid, NT, SMEM_BYTES, st>>>(mq, mk, mv, p);
   }
+  return launch_rc();
+}
+
+
+size_t kvs_replay_tc_backward_scratch(int B, int T, int Hq) {
+  const int T_pad = (T + BN - 1) / BN * BN;
+  return replay_scratch_layout(B, T, nullptr, nullptr) + align_up((size_t)B * Hq * T_pad * 4, 256);
+}
+
+// Tensor-core backward (bf16, head_dim 128, the forward's row_lse given).  Returns
+// KVS_E_UNSUPPORTED when the shape or dtype is not covered (the caller then runs the exact kernels).
+int kvs_replay_tc_backward(const kvs_replay_args* a, const void* dout, void* dq, void* dk, void* dv,
+                           cudaStream_t st) {
+  if (!a->row_lse || !kvs_replay_tc_supported(a) || (reinterpret_cast<uintptr_t>(a->row_lse) & 15))
+    return KVS_E_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(a->scratch) & 15) || (reinterpret_cast<uintptr_t>(dout) & 15) ||
+      (reinterpret_cast<uintptr_t>(dq) & 15) ||
+      (reinterpret_cast<uintptr_t>(dk) & 15) || (reinterpret_cast<uintptr_t>(dv) & 15))
+    return KVS_E_UNSUPPORTED;
+  const int T = a->seq_len, B = a->batch;
+  if (!a->scratch || a->scratch_bytes < kvs_replay_tc_backward_scratch(B, T, a->n_heads)) return KVS_E_SCRATCH;
+  ReplayScratch s;
+  const size_t off = replay_scratch_layout(B, T, a->scratch, &s);
+  float* dvec = reinterpret_cast<float*>(static_cast<uint8_t*>(a->scratch) + off);
+  const int T_pad = (T + BN - 1) / BN * BN, n_kt = T_pad / BN;
+  CUtensorMap mq, mk, mv, mdo;
+  if (!make_map(&mq, a->q, HD, a->n_heads, (uint64_t)B * T) || !make_map(&mk, a->k, HD, a->n_kv_heads, (uint64_t)B * T) ||
+      !make_map(&mv, a->v, HD, a->n_kv_heads, (uint64_t)B * T) || !make_map(&mdo, dout, HD, a->n_heads, (uint64_t)B * T))
+    return KVS_E_UNSUPPORTED;
+  {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    static std::mutex mu;
+    static bool done[64] = {};
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev >= 64) return KVS_E_UNSUPPORTED;
+    if (!done[dev]) {
+      if (cudaFuncSetAttribute(reinterpret_cast<const void*>(replay_dkdv_kernel),
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, SMEMB_BYTES) != cudaSuccess ||
+          cudaFuncSetAttribute(reinterpret_cast<const void*>(replay_dq_kernel),
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, SMEMQ_BYTES) != cudaSuccess)
+        return KVS_E_LAUNCH;
+      done[dev] = true;
+    }
+  }
+  if (cudaMemsetAsync(s.error, 0, 4, st) != cudaSuccess) return KVS_E_LAUNCH;
+  replay_prepass_kernel<<<dim3(n_kt, B), BN, 0, st>>>(a->evicted_at, T, T_pad, n_kt, s.e32, s.tmin, s.tmax);
+  int rc = launch_rc();
+  if (rc) return rc;
+  const int64_t rows = (int64_t)B * T * a->n_heads;
+  replay_rowdot_kernel<<<(unsigned)((rows + 3) / 4), 128, 0, st>>>(static_cast<const __nv_bfloat16*>(dout),
+                                                                    static_cast<const __nv_bfloat16*>(a->out), dvec,
+                                                                    B, T, T_pad, a->n_heads);
+  if ((rc = launch_rc())) return rc;
+  BwdParams p;
+  p.e32 = s.e32;
+  p.tile_min = s.tmin;
+  p.tile_max = s.tmax;
+  p.lengths = a->lengths;
+  p.lse = a->row_lse;
+  p.dvec = dvec;
+  p.dq = static_cast<__nv_bfloat16*>(dq);
+  p.dk = static_cast<__nv_bfloat16*>(dk);
+  p.dv = static_cast<__nv_bfloat16*>(dv);
+  p.error = s.error;
+  p.B = B;
+  p.T = T;
+  p.T_pad = T_pad;
+  p.Hq = a->n_heads;
+  p.Hkv = a->n_kv_heads;
+  p.n_qt = n_kt;
+  p.n_kt = n_kt;
+  p.scale = (float)a->scale;
+  p.scale_log2 = (float)(a->scale * 1.4426950408889634);
+  replay_dkdv_kernel<<<(unsigned)((int64_t)B * a->n_kv_heads * n_kt), NTB, SMEMB_BYTES, st>>>(mq, mk, mv, mdo, p);
+  if ((rc = launch_rc())) return rc;
+  replay_dq_kernel<<<(unsigned)((int64_t)B * a->n_heads * n_kt), NTB, SMEMQ_BYTES, st>>>(mq, mk, mv, mdo, p);
   return launch_rc();
 }
 

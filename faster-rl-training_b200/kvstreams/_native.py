@@ -50,6 +50,7 @@ STAT_FIELDS = (
 )
 STAT_COUNT = 8
 STATUS_WORDS = 4
+ABI_VERSION = 2  # KVS_ABI_VERSION of include/kvs_b200.h
 NEVER = (1 << 63) - 1
 
 
@@ -125,6 +126,7 @@ class KvsReplayArgs(C.Structure):
         ("scale", C.c_double),
         ("flags", C.c_int32),
         ("reserved", C.c_int32),
+        ("row_lse", C.c_void_p),
     ]
 
 
@@ -187,6 +189,8 @@ def load_library(path: Path | str | None = None) -> C.CDLL:
             got = lib.kvs_abi_struct_size(which)
             if got != C.sizeof(st):
                 raise RuntimeError(f"ABI mismatch for {st.__name__}: library {got} B, binding {C.sizeof(st)} B")
+        if lib.kvs_abi_version() != ABI_VERSION:
+            raise RuntimeError(f"library ABI version {lib.kvs_abi_version()}, binding {ABI_VERSION}: rebuild it")
         _lib = lib
         return lib
 

@@ -128,16 +128,19 @@ class _ReplayAttention(torch.autograd.Function):
         ops.rope_(q, positions, inv_freq)
         ops.rope_(k, positions, inv_freq)
         v = v.detach().contiguous()
-        out = ops.replay_attention(q, k, v, evicted_at, lengths, scale)
-        if any(ctx.needs_input_grad[:3]):
-            ctx.save_for_backward(q, k, v, out, positions, evicted_at, lengths, inv_freq)
+        grads = any(ctx.needs_input_grad[:3])
+        B, T, Hq, _ = q.shape
+        lse = ops.row_lse_buffer(B, Hq, T, q.device) if grads else None
+        out = ops.replay_attention(q, k, v, evicted_at, lengths, scale, row_lse=lse)
+        if grads:
+            ctx.save_for_backward(q, k, v, out, positions, evicted_at, lengths, inv_freq, lse)
         ctx.scale = scale
         return out
 
     @staticmethod
     def backward(ctx, grad_out):
-        q, k, v, out, positions, evicted_at, lengths, inv_freq = ctx.saved_tensors
-        dq, dk, dv = ops.replay_attention_backward(q, k, v, evicted_at, lengths, ctx.scale, out, grad_out)
+        q, k, v, out, positions, evicted_at, lengths, inv_freq, lse = ctx.saved_tensors
+        dq, dk, dv = ops.replay_attention_backward(q, k, v, evicted_at, lengths, ctx.scale, out, grad_out, row_lse=lse)
         neg = -positions
         ops.rope_(dq, neg, inv_freq)
         ops.rope_(dk, neg, inv_freq)

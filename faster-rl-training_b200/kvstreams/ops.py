@@ -71,13 +71,16 @@ def evicted_at_from_spans(cu: np.ndarray, triples: np.ndarray, lengths: Sequence
 
 def replay_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, evicted_at: torch.Tensor,
                      lengths: torch.Tensor, scale: float, out: Optional[torch.Tensor] = None,
-                     force_generic: bool = False, one_head_per_cta: bool = False) -> torch.Tensor:
+                     force_generic: bool = False, one_head_per_cta: bool = False,
+                     row_lse: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Masked replay attention (model.py:71-74 with the replay.py:62 mask).
 
     q ``[B, T, Hq, D]``, k/v ``[B, T, Hkv, D]`` already rotated; evicted_at ``[B, T]``
     int64; lengths ``[B]`` int32 (rows past the length attend to themselves only).
     ``force_generic`` selects the exact SIMT kernel; ``one_head_per_cta`` keeps the
-    tensor-core path on its one-query-head-per-CTA kernel for even GQA group sizes."""
+    tensor-core path on its one-query-head-per-CTA kernel for even GQA group sizes.
+    ``row_lse`` (float32 ``[B, Hq, T_pad]``, :func:`row_lse_buffer`) receives each row's
+    log2-sum-exp, which :func:`replay_attention_backward` uses."""
     _check_cuda(q, k, v, evicted_at, lengths)
     B, T, Hq, D = q.shape
     Hkv = k.shape[2]
@@ -93,15 +96,33 @@ def replay_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, evicted_
                         lengths=ln.data_ptr(), out=out.data_ptr(), scratch=scratch.data_ptr(),
                         scratch_bytes=scratch.numel(), batch=B, seq_len=T, n_heads=Hq, n_kv_heads=Hkv, head_dim=D,
                         dtype=N.DTYPE_CODE[q.dtype], scale=float(scale),
-                        flags=(1 if force_generic else 0) | (2 if one_head_per_cta else 0))
+                        flags=(1 if force_generic else 0) | (2 if one_head_per_cta else 0),
+                        row_lse=_lse_ptr(row_lse, B, Hq, T))
     N.check(lib.kvs_replay_attention(C.byref(a), N.stream_ptr(q.device)), "kvs_replay_attention")
     return out
 
 
+def row_lse_buffer(B: int, Hq: int, T: int, device) -> torch.Tensor:
+    """Row statistics buffer of the replay forward: float32 ``[B, Hq, T rounded up to 128]``."""
+    return torch.empty(B, Hq, (T + 127) // 128 * 128, dtype=torch.float32, device=device)
+
+
+def _lse_ptr(row_lse: Optional[torch.Tensor], B: int, Hq: int, T: int):
+    if row_lse is None:
+        return None
+    want = (B, Hq, (T + 127) // 128 * 128)
+    if tuple(row_lse.shape) != want or row_lse.dtype != torch.float32 or not row_lse.is_contiguous():
+        raise ValueError(f"row_lse must be a contiguous float32 tensor of shape {want}")
+    return row_lse.data_ptr()
+
+
 def replay_attention_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, evicted_at: torch.Tensor,
-                              lengths: torch.Tensor, scale: float, out: torch.Tensor, grad_out: torch.Tensor):
+                              lengths: torch.Tensor, scale: float, out: torch.Tensor, grad_out: torch.Tensor,
+                              row_lse: Optional[torch.Tensor] = None, force_exact: bool = False):
     """Gradients (dq, dk, dv) of :func:`replay_attention` (q and k rotated, ``out`` its
-    output) for the upstream gradient ``grad_out``; exact kernels for every dtype."""
+    output) for the upstream gradient ``grad_out``.  With the forward's ``row_lse``, bf16
+    and head_dim 128 run the tcgen05 kernels; otherwise (or ``force_exact``) the exact
+    kernels."""
     _check_cuda(q, k, v, evicted_at, lengths)
     B, T, Hq, D = q.shape
     Hkv = k.shape[2]
@@ -117,7 +138,8 @@ def replay_attention_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     a = N.KvsReplayArgs(q=q.data_ptr(), k=k.data_ptr(), v=v.data_ptr(), evicted_at=ev.data_ptr(),
                         lengths=ln.data_ptr(), out=out.data_ptr(), scratch=scratch.data_ptr(),
                         scratch_bytes=scratch.numel(), batch=B, seq_len=T, n_heads=Hq, n_kv_heads=Hkv, head_dim=D,
-                        dtype=code, scale=float(scale), flags=0)
+                        dtype=code, scale=float(scale), flags=1 if force_exact else 0,
+                        row_lse=_lse_ptr(row_lse, B, Hq, T))
     N.check(lib.kvs_replay_attention_backward(C.byref(a), g.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
                                               N.stream_ptr(q.device)), "kvs_replay_attention_backward")
     return dq, dk, dv

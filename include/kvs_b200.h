@@ -30,7 +30,7 @@ extern "C" {
 
 typedef struct CUstream_st* kvs_stream_t; /* == cudaStream_t */
 
-#define KVS_ABI_VERSION 1
+#define KVS_ABI_VERSION 2
 
 /* element types of K/V pools and activations */
 enum kvs_dtype { KVS_F32 = 0, KVS_F64 = 1, KVS_BF16 = 2, KVS_F16 = 3 };
@@ -283,6 +283,11 @@ typedef struct kvs_replay_args {
                     with one query head per CTA even when the GQA group size is even
                     (default there: two heads of the group share each K/V tile) */
   int32_t reserved;
+  float* row_lse; /* optional [batch][n_heads][seq_len rounded up to 128], 16-byte aligned:
+                     log2 of each query row's sum of 2^(scale*log2(e)*q.k) over its visible
+                     keys.  Written by every forward path when non-NULL; the backward reads it
+                     and, for bf16 with head_dim 128, then runs the tensor-core kernels (NULL
+                     there selects the exact kernels). */
 } kvs_replay_args;
 size_t kvs_replay_scratch_bytes(int32_t batch, int32_t seq_len);
 int kvs_replay_attention(const kvs_replay_args* a, kvs_stream_t stream);
@@ -291,8 +296,10 @@ int kvs_replay_attention(const kvs_replay_args* a, kvs_stream_t stream);
  * attention (model.py:71-74 under the replay.py:62 mask) when the trainer differentiates
  * token_logprobs (training/logprobs.py:10-25).  Inputs as the forward (q and k rotated, the
  * forward's output in a->out) plus dout; writes dq, dk, dv in the layouts and dtype of q, k,
- * v (dk/dv summed over the query heads of each KV head).  Exact kernels; a->scratch holds
- * kvs_replay_backward_scratch_bytes (row statistics). */
+ * v (dk/dv summed over the query heads of each KV head); a->scratch holds
+ * kvs_replay_backward_scratch_bytes.  bf16, head_dim 128 with a->row_lse as the forward left it:
+ * tcgen05 kernels (P and dS rounded to bf16 as UMMA operands, fp32 accumulation, no atomics);
+ * otherwise exact SIMT kernels (fp32 accumulation, fp64 for double). */
 size_t kvs_replay_backward_scratch_bytes(int32_t batch, int32_t seq_len, int32_t n_heads, int32_t dtype);
 int kvs_replay_attention_backward(const kvs_replay_args* a, const void* dout, void* dq, void* dk, void* dv,
                                   kvs_stream_t stream);

@@ -131,3 +131,83 @@ def test_tinylm_gradients_through_token_logprobs_fp64():
     for n, p in model.named_parameters():
         err = (got[n] - p.grad).abs().max().item()
         assert err <= 1e-9, f"{n}: {err}"
+
+
+def _dense_lse2(q, k, mask, scale):
+    B, T, Hq, D = q.shape
+    G = Hq // k.shape[2]
+    kk = k.double().repeat_interleave(G, dim=2)
+    sc = torch.einsum("bthd,bshd->bhts", q.double(), kk) * scale
+    sc = sc.masked_fill(~mask[:, None], float("-inf"))
+    return torch.logsumexp(sc, dim=-1) / np.log(2.0)  # [B, Hq, T]
+
+
+@pytest.mark.parametrize("dtype,generic", [(torch.bfloat16, False), (torch.bfloat16, True), (torch.float32, True)])
+def test_forward_row_lse(dtype, generic):
+    """Every forward path writes the rows' log2-sum-exp (the backward's row statistics):
+    bf16 1e-3 (scores from bf16 inputs accumulated in fp32), fp32 1e-5."""
+    from kvstreams import ops
+
+    q, k, v, _, ev, ln = _case(dtype, 128, 8, 2, B=2, T=300, lengths=(300, 187), seed=7)
+    scale = 128 ** -0.5
+    lse = ops.row_lse_buffer(2, 8, 300, q.device)
+    ops.replay_attention(q, k, v, ev, ln, scale, force_generic=generic, row_lse=lse)
+    mask = _dense_mask(ev, ln.cpu(), 300).cuda()
+    want = _dense_lse2(q, k, mask, scale)
+    err = (lse[:, :, :300].double() - want).abs().max().item()
+    assert err <= (1e-3 if dtype == torch.bfloat16 else 1e-5), err
+
+
+@pytest.mark.parametrize("B,T,Hq,Hkv,lengths,turn", [
+    (2, 300, 8, 2, (300, 211), 24),     # GQA 4, ragged last tile, padded rows
+    (1, 1000, 4, 4, (1000,), 60),       # no GQA, 8 key tiles, unmasked tiles in the interior
+    (3, 257, 6, 2, (257, 129, 5), 16),  # odd group size, a 5-token stream
+    (1, 2048, 8, 1, (1900,), 200),      # MQA, long stream with padding
+])
+def test_tc_backward_matches_dense_autograd(B, T, Hq, Hkv, lengths, turn):
+    """tcgen05 backward (bf16, D 128, the forward's row_lse) against fp64 autograd of the
+    dense masked attention on the same bf16 inputs.  P and dS are bf16 UMMA operands, so
+    the error is bf16 rounding of O(1) terms summed over up to T rows: the bound is 2% of
+    the largest gradient entry, and within 4x the exact kernels' error (which rounds only
+    the outputs) plus 0.5% of it."""
+    from kvstreams import ops
+    from kvstreams.workloads import replay_evicted_at
+
+    g = torch.Generator(device="cuda").manual_seed(T + Hq)
+    q = torch.randn(B, T, Hq, 128, generator=g, device="cuda").to(torch.bfloat16)
+    k = torch.randn(B, T, Hkv, 128, generator=g, device="cuda").to(torch.bfloat16)
+    v = torch.randn(B, T, Hkv, 128, generator=g, device="cuda").to(torch.bfloat16)
+    go = torch.randn(B, T, Hq, 128, generator=g, device="cuda").to(torch.bfloat16)
+    ev_np, _ = replay_evicted_at(batch=B, seq_len=T, events_range=(2, 6), mean_turn=turn, seed=T)
+    ev = torch.from_numpy(ev_np).cuda()
+    ln = torch.tensor(lengths, dtype=torch.int32, device="cuda")
+    scale = 128 ** -0.5
+    lse = ops.row_lse_buffer(B, Hq, T, q.device)
+    out = ops.replay_attention(q, k, v, ev, ln, scale, row_lse=lse)
+    tc = ops.replay_attention_backward(q, k, v, ev, ln, scale, out, go, row_lse=lse)
+    exact = ops.replay_attention_backward(q, k, v, ev, ln, scale, out, go, force_exact=True)
+    qr, kr, vr = (x.detach().double().requires_grad_() for x in (q, k, v))
+    mask = _dense_mask(ev, ln.cpu(), T).cuda()
+    ref = _dense_attention(qr, kr, vr, mask, scale)
+    ref.backward(go.double())
+    for got, ex, want, name in zip(tc, exact, (qr.grad, kr.grad, vr.grad), ("dq", "dk", "dv")):
+        assert torch.isfinite(got).all(), name
+        mag = want.abs().max().item()
+        err = (got.double() - want).abs().max().item()
+        err_exact = (ex.double() - want).abs().max().item()
+        assert err <= 0.02 * mag, f"{name}: {err} (max |grad| {mag})"
+        assert err <= 4 * err_exact + 0.005 * mag, f"{name}: {err} vs exact {err_exact} (max |grad| {mag})"
+
+
+def test_tc_backward_deterministic():
+    """No atomics: two backward passes give the same bits."""
+    from kvstreams import ops
+
+    q, k, v, go, ev, ln = _case(torch.bfloat16, 128, 8, 2, B=2, T=300, lengths=(300, 211), seed=3)
+    scale = 128 ** -0.5
+    lse = ops.row_lse_buffer(2, 8, 300, q.device)
+    out = ops.replay_attention(q, k, v, ev, ln, scale, row_lse=lse)
+    a = ops.replay_attention_backward(q, k, v, ev, ln, scale, out, go, row_lse=lse)
+    b = ops.replay_attention_backward(q, k, v, ev, ln, scale, out, go, row_lse=lse)
+    for x, y in zip(a, b):
+        assert torch.equal(x, y)
