@@ -888,7 +888,7 @@ __global__ void replay_rowdot_kernel(const __nv_bfloat16* __restrict__ dout, con
   if (lane == 0) dvec[((int64_t)b * Hq + h) * T_pad + t] = s;
 }
 
-constexpr int NTB = 192;  // warp 0 producer, warp 1 UMMA, warps 2-5 one thread per TMEM lane
+constexpr int NTB = 320;  // warp 0 producers, warp 1 UMMA, warps 2-9: two groups of four softmax warps
 constexpr int VEC_BYTES = BM * 4;
 
 struct BwdParams {
@@ -906,48 +906,74 @@ struct BwdParams {
   float scale_log2, scale;
 };
 
-// smem of the dK/dV kernel
-constexpr int OFFB_K = 0, OFFB_V = TILE_BYTES;
-constexpr int OFFB_Q = 2 * TILE_BYTES;                // 2 slots
-constexpr int OFFB_DO = OFFB_Q + 2 * TILE_BYTES;      // 2 slots
-constexpr int OFFB_LSE = OFFB_DO + 2 * TILE_BYTES;    // 2 slots of 128 f32
-constexpr int OFFB_D = OFFB_LSE + 2 * VEC_BYTES;      // 2 slots of 128 f32
-constexpr int OFFB_BAR = OFFB_D + 2 * VEC_BYTES;
-enum { D_KVFULL = 0, D_QFULL0, D_QFULL1, D_QEMPTY0, D_QEMPTY1, D_SFULL, D_PFULL, D_FINAL, NBARB };
-constexpr int OFFB_MISC = OFFB_BAR + NBARB * 8;
-constexpr int SMEMB_BYTES = OFFB_MISC + 64 + 1024;
-static_assert(SMEMB_BYTES <= 232448, "dK/dV kernel shared memory");
+// Both kernels: one thread per TMEM lane (a key row in dK/dV, a query row in dQ) in each of
+// two groups of four warps; group g owns columns [64g, 64g + 64) of the 128-wide S and dP
+// tiles.  A step runs in two phases so that the tensor cores work through the next product
+// while the softmax warps compute: phase A turns S into P (kept in fp32 registers) as soon
+// as S lands; phase B forms dS = P (dP - D) when dP lands.
 
 __host__ __device__ constexpr uint32_t kq_step(int kk) { return (uint32_t)(((kk >> 2) * HALF_BYTES + (kk & 3) * 32) >> 4); }
 __host__ __device__ constexpr uint32_t mn_step(int kk) { return (uint32_t)((kk * 2048) >> 4); }
+// TMEM column of K step kk (16 rows of the K dimension = 8 packed columns) when group g packed
+// its 64 bf16 values into columns [64g, 64g + 32) of a 128-column region
+__host__ __device__ constexpr uint32_t split_col(int kk) { return (uint32_t)(kk < 4 ? kk * 8 : 64 + (kk - 4) * 8); }
+
+// smem of the dK/dV kernel (the dynamic shared base is 1024-aligned: no padding; the host
+// checks that once per device before the first launch)
+constexpr int OFFB_K = 0, OFFB_V = TILE_BYTES;
+constexpr int OFFB_Q = 2 * TILE_BYTES;                // 2 slots
+constexpr int OFFB_DO = OFFB_Q + 2 * TILE_BYTES;      // 2 slots
+constexpr int OFFB_P = OFFB_DO + 2 * TILE_BYTES;      // P^T bf16, K-major 128B-swizzled (UMMA A of dV)
+constexpr int OFFB_LSE = OFFB_P + TILE_BYTES;         // 2 slots of 128 f32, loaded with Q
+constexpr int OFFB_D = OFFB_LSE + 2 * VEC_BYTES;      // 2 slots of 128 f32, loaded with Q
+constexpr int OFFB_BAR = OFFB_D + 2 * VEC_BYTES;
+enum {
+  D_KVFULL = 0, D_QFULL0, D_QFULL1, D_OFULL0, D_OFULL1, D_QEMPTY0, D_QEMPTY1, D_OEMPTY0, D_OEMPTY1,
+  D_SFULL, D_SREAD, D_PFULL, D_PEMPTY, D_DPFULL, D_DSFULL, D_FINAL, NBARB
+};
+constexpr int OFFB_MISC = OFFB_BAR + NBARB * 8;
+constexpr int SMEMB_BYTES = OFFB_MISC + 16;
+static_assert(SMEMB_BYTES <= 232448, "dK/dV kernel shared memory");
 
 __global__ void __launch_bounds__(NTB, 1)
 replay_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
                    const BwdParams p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(1024) uint8_t smem_bwd[];
+  uint8_t* smem = smem_bwd;
+  if (smem_addr(smem) & 1023) {  // never expected (the host checked); no work, no TMEM
+    if (threadIdx.x == 0) atomicExch(p.error, 15);
+    return;
+  }
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + OFFB_BAR);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFFB_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFFB_MISC + 4);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  // CTA order: (stream, KV head) slowest, key tiles ascending (the most-seen first)
+  // CTA order: blocks of up to eight (stream, KV head) pairs slowest; inside a block, key tiles
+  // ascending (an early tile is seen by the most query tiles, so the longest CTAs start
+  // first) and the pairs innermost.  The CTAs in flight then cover a few heads and nearby key
+  // tiles, whose query tiles they share in L2.
   const int G = p.Hq / p.Hkv;
-  const int kt = (int)(blockIdx.x % p.n_kt);
-  const int bhk = (int)(blockIdx.x / p.n_kt);
+  const int nbh = p.B * p.Hkv;
+  const int blk = (int)(blockIdx.x / (8 * p.n_kt));
+  const int in_blk = (int)(blockIdx.x % (8 * p.n_kt));
+  const int bw = min(8, nbh - blk * 8);
+  const int kt = in_blk / bw;
+  const int bhk = blk * 8 + in_blk % bw;
   const int b = bhk / p.Hkv, hk = bhk % p.Hkv;
   const int k0 = kt * BN;
   const int L = p.lengths[b];
   // query tiles that see a key of this tile: from the diagonal to the last row any key's
   // interval [s, min(evicted_at[s], L)) reaches (padded rows see only themselves, on the diagonal)
-  const int emax = p.tile_max[b * p.n_kt + kt];
-  const int reach = min(emax, L);
+  const int reach = min(p.tile_max[b * p.n_kt + kt], L);
   const int qlast = max(kt, min(p.n_qt - 1, (reach - 1) / BM));
-  const int nsteps = (qlast - kt + 1) * G;
+  const int nsteps = (qlast - kt + 1) * G;  // step i: query tile kt + i / G, query head hk * G + i % G
 
   if (tid == 0) {
     for (int i = 0; i < NBARB; ++i) mbar_init(&bar[i], 1);
-    mbar_init(&bar[D_PFULL], 128);
+    mbar_init(&bar[D_SREAD], 256);
+    mbar_init(&bar[D_PFULL], 256);
+    mbar_init(&bar[D_DSFULL], 256);
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -958,11 +984,13 @@ replay_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // TMEM: S^T [0,128) (P^T bf16 over its first 64 columns), dP^T [128,256) (dS^T over its first
-  // 64), dV [256,384), dK [384,512)
+  // TMEM: S^T [0,128), dP^T [128,256) (dS^T bf16 of group g over [128+64g, +32)), dV [256,384),
+  // dK [384,512).  P^T goes to shared memory, so S^T(i+1) is computed while the softmax warps
+  // still work on step i.
 
   if (warp == 0) {
     if (lane == 0) {
+      // ---------------------------------------------------------- K, V; the Q ring (+ lse, D)
       mbar_arrive_expect_tx(&bar[D_KVFULL], 2 * TILE_BYTES);
       tma_load_3d(smem + OFFB_K, &tm_k, 0, hk, b * p.T + k0, &bar[D_KVFULL]);
       tma_load_3d(smem + OFFB_K + HALF_BYTES, &tm_k, 64, hk, b * p.T + k0, &bar[D_KVFULL]);
@@ -978,68 +1006,113 @@ replay_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
         const int qt = kt + i / G, h = hk * G + i % G;
         const int row = b * p.T + qt * BM;
         uint64_t* fb = &bar[D_QFULL0 + slot];
-        mbar_arrive_expect_tx(fb, 2 * TILE_BYTES + 2 * VEC_BYTES);
+        mbar_arrive_expect_tx(fb, TILE_BYTES + 2 * VEC_BYTES);
         uint8_t* qs = smem + OFFB_Q + slot * TILE_BYTES;
-        uint8_t* ds = smem + OFFB_DO + slot * TILE_BYTES;
         tma_load_3d(qs, &tm_q, 0, h, row, fb);
         tma_load_3d(qs + HALF_BYTES, &tm_q, 64, h, row, fb);
-        tma_load_3d(ds, &tm_do, 0, h, row, fb);
-        tma_load_3d(ds + HALF_BYTES, &tm_do, 64, h, row, fb);
         const int64_t vo = ((int64_t)b * p.Hq + h) * p.T_pad + qt * BM;
         bulk_load(smem + OFFB_LSE + slot * VEC_BYTES, p.lse + vo, VEC_BYTES, fb);
         bulk_load(smem + OFFB_D + slot * VEC_BYTES, p.dvec + vo, VEC_BYTES, fb);
       }
+    } else if (lane == 1) {
+      // ---------------------------------------------------------- the dO ring
+      for (int i = 0; i < nsteps; ++i) {
+        const int slot = i & 1;
+        if (i >= 2 && !mbar_wait(&bar[D_OEMPTY0 + slot], ((i >> 1) - 1) & 1, abort_flag)) {
+          *abort_flag = 1;
+          atomicExch(p.error, 14);
+          break;
+        }
+        const int qt = kt + i / G, h = hk * G + i % G;
+        const int row = b * p.T + qt * BM;
+        uint64_t* fb = &bar[D_OFULL0 + slot];
+        mbar_arrive_expect_tx(fb, TILE_BYTES);
+        uint8_t* ds = smem + OFFB_DO + slot * TILE_BYTES;
+        tma_load_3d(ds, &tm_do, 0, h, row, fb);
+        tma_load_3d(ds + HALF_BYTES, &tm_do, 64, h, row, fb);
+      }
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------- UMMA issuer (whole warp)
+    // per step i: S^T(i+1) once S^T(i) is read; dV += P^T(i) dO(i); dK += dS^T(i) Q(i); dP^T(i+1)
     constexpr uint32_t ID_T = idesc_bf16(128, 128, 0);   // S^T, dP^T: both operands K-major
     constexpr uint32_t ID_MN = idesc_bf16(128, 128, 1);  // dV, dK: B (dO, Q) MN-major
     const uint64_t dk_ = desc_kmajor_sw128(smem_addr(smem + OFFB_K));
     const uint64_t dv_ = desc_kmajor_sw128(smem_addr(smem + OFFB_V));
+    const uint64_t dp_ = desc_kmajor_sw128(smem_addr(smem + OFFB_P));
     auto wait = [&](uint64_t* bb, int parity) {
       return __all_sync(0xffffffffu, mbar_wait_fast(bb, parity, abort_flag));
     };
+    auto issue_s = [&](int slot) {  // S^T = K Q^T into [0,128)
+      const uint64_t dq_k = desc_kmajor_sw128(smem_addr(smem + OFFB_Q + slot * TILE_BYTES));
+      const uint32_t d = tmem;
+#define KVS_ST(kk) umma_bf16_warp_at<kq_step(kk), kq_step(kk)>(d, dk_, dq_k, ID_T, kk > 0)
+      KVS_ST(0); KVS_ST(1); KVS_ST(2); KVS_ST(3); KVS_ST(4); KVS_ST(5); KVS_ST(6); KVS_ST(7);
+#undef KVS_ST
+    };
+    auto issue_dp = [&](int slot) {  // dP^T = V dO^T into [128,256)
+      const uint64_t ddo_k = desc_kmajor_sw128(smem_addr(smem + OFFB_DO + slot * TILE_BYTES));
+      const uint32_t d = tmem + 128;
+#define KVS_DPT(kk) umma_bf16_warp_at<kq_step(kk), kq_step(kk)>(d, dv_, ddo_k, ID_T, kk > 0)
+      KVS_DPT(0); KVS_DPT(1); KVS_DPT(2); KVS_DPT(3); KVS_DPT(4); KVS_DPT(5); KVS_DPT(6); KVS_DPT(7);
+#undef KVS_DPT
+    };
     bool ok = wait(&bar[D_KVFULL], 0);
+    if (ok) ok = wait(&bar[D_QFULL0], 0);
+    if (ok) {
+      tc_fence_after();
+      issue_s(0);
+      umma_commit_warp(&bar[D_SFULL]);
+      ok = wait(&bar[D_OFULL0], 0);
+    }
+    if (ok) {
+      tc_fence_after();
+      issue_dp(0);
+      umma_commit_warp(&bar[D_DPFULL]);
+    }
     for (int i = 0; ok && i < nsteps; ++i) {
       const int slot = i & 1;
-      ok = wait(&bar[D_QFULL0 + slot], (i >> 1) & 1);
-      if (!ok) break;
-      tc_fence_after();
-      const uint64_t dq_k = desc_kmajor_sw128(smem_addr(smem + OFFB_Q + slot * TILE_BYTES));
-      const uint64_t ddo_k = desc_kmajor_sw128(smem_addr(smem + OFFB_DO + slot * TILE_BYTES));
-      const uint64_t dq_mn = desc_mnmajor_sw128(smem_addr(smem + OFFB_Q + slot * TILE_BYTES), HALF_BYTES);
-      const uint64_t ddo_mn = desc_mnmajor_sw128(smem_addr(smem + OFFB_DO + slot * TILE_BYTES), HALF_BYTES);
-      {
-        const uint32_t d = tmem;
-#define KVS_ST(kk) umma_bf16_warp_at<kq_step(kk), kq_step(kk)>(d, dk_, dq_k, ID_T, kk > 0)
-        KVS_ST(0); KVS_ST(1); KVS_ST(2); KVS_ST(3); KVS_ST(4); KVS_ST(5); KVS_ST(6); KVS_ST(7);
-#undef KVS_ST
+      const bool more = i + 1 < nsteps;
+      if (more) {
+        ok = wait(&bar[D_SREAD], i & 1);
+        if (ok) ok = wait(&bar[D_QFULL0 + (slot ^ 1)], ((i + 1) >> 1) & 1);
+        if (!ok) break;
+        tc_fence_after();
+        issue_s(slot ^ 1);
+        umma_commit_warp(&bar[D_SFULL]);
       }
-      {
-        const uint32_t d = tmem + 128;
-#define KVS_DPT(kk) umma_bf16_warp_at<kq_step(kk), kq_step(kk)>(d, dv_, ddo_k, ID_T, kk > 0)
-        KVS_DPT(0); KVS_DPT(1); KVS_DPT(2); KVS_DPT(3); KVS_DPT(4); KVS_DPT(5); KVS_DPT(6); KVS_DPT(7);
-#undef KVS_DPT
-      }
-      umma_commit_warp(&bar[D_SFULL]);
       ok = wait(&bar[D_PFULL], i & 1);
       if (!ok) break;
       tc_fence_after();
       {
-        const uint32_t d = tmem + 256, a = tmem;
+        const uint64_t ddo_mn = desc_mnmajor_sw128(smem_addr(smem + OFFB_DO + slot * TILE_BYTES), HALF_BYTES);
+        const uint32_t d = tmem + 256;
         const uint32_t acc = i > 0;
-#define KVS_DV(kk) umma_bf16_tmem_a_warp_at<kk * 8, mn_step(kk)>(d, a, ddo_mn, ID_MN, (kk > 0) || acc)
+#define KVS_DV(kk) umma_bf16_warp_at<kq_step(kk), mn_step(kk)>(d, dp_, ddo_mn, ID_MN, (kk > 0) || acc)
         KVS_DV(0); KVS_DV(1); KVS_DV(2); KVS_DV(3); KVS_DV(4); KVS_DV(5); KVS_DV(6); KVS_DV(7);
 #undef KVS_DV
       }
+      umma_commit_warp(&bar[D_OEMPTY0 + slot]);
+      umma_commit_warp(&bar[D_PEMPTY]);
+      ok = wait(&bar[D_DSFULL], i & 1);
+      if (!ok) break;
+      tc_fence_after();
       {
+        const uint64_t dq_mn = desc_mnmajor_sw128(smem_addr(smem + OFFB_Q + slot * TILE_BYTES), HALF_BYTES);
         const uint32_t d = tmem + 384, a = tmem + 128;
         const uint32_t acc = i > 0;
-#define KVS_DK(kk) umma_bf16_tmem_a_warp_at<kk * 8, mn_step(kk)>(d, a, dq_mn, ID_MN, (kk > 0) || acc)
+#define KVS_DK(kk) umma_bf16_tmem_a_warp_at<split_col(kk), mn_step(kk)>(d, a, dq_mn, ID_MN, (kk > 0) || acc)
         KVS_DK(0); KVS_DK(1); KVS_DK(2); KVS_DK(3); KVS_DK(4); KVS_DK(5); KVS_DK(6); KVS_DK(7);
 #undef KVS_DK
       }
       umma_commit_warp(&bar[D_QEMPTY0 + slot]);
+      if (more) {
+        ok = wait(&bar[D_OFULL0 + (slot ^ 1)], ((i + 1) >> 1) & 1);
+        if (!ok) break;
+        tc_fence_after();
+        issue_dp(slot ^ 1);
+        umma_commit_warp(&bar[D_DPFULL]);
+      }
     }
     if (!ok && lane == 0) {
       *abort_flag = 1;
@@ -1049,12 +1122,17 @@ replay_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
     mbar_wait(&bar[D_FINAL], 0, nullptr);
     __syncwarp();
   } else {
-    // ------------------------------------------------------------ one thread per key row
+    // ------------------------------------------------ softmax: key row r, query columns [cb, cb+64)
+    const int grp = (warp - 2) >> 2;
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
     const int s = k0 + r;
+    const int cb = 64 * grp;
     const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16);
     const float sl2 = p.scale_log2;
+    // this thread's row of P^T: half grp of the K-major tile, 16-byte chunks XOR-swizzled by row
+    uint8_t* prow = smem + OFFB_P + grp * HALF_BYTES + r * 128;
+    const int sw = r & 7;
     // the query rows that see key s: [s, min(evicted_at[s], L)) for a real key, s itself for a
     // padded one, nothing past the stream
     int rlo = 0, rhi = 0;
@@ -1068,47 +1146,93 @@ replay_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
     bool ok = true;
     for (int i = 0; i < nsteps; ++i) {
       const int slot = i & 1;
-      const int t0 = (kt + i / G) * BM;
+      const int t0 = (kt + i / G) * BM + cb;  // query row of this thread's first column
       ok = mbar_wait_fast(&bar[D_SFULL], i & 1, abort_flag);
       if (ok) ok = mbar_wait_fast(&bar[D_QFULL0 + slot], (i >> 1) & 1, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      const int lo = max(rlo - t0, 0), hi = min(rhi - t0, BM);  // visible columns [lo, hi)
-      const float4* lse4 = reinterpret_cast<const float4*>(smem + OFFB_LSE + slot * VEC_BYTES);
-      const float4* d4 = reinterpret_cast<const float4*>(smem + OFFB_D + slot * VEC_BYTES);
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t sv[32], dp[32];
-        tmem_ld32(tl + 32 * c, sv);
-        tmem_ld32(tl + 128 + 32 * c, dp);
+      const int lo = max(rlo - t0, 0), hi = min(rhi - t0, 64);  // visible columns [lo, hi) of 64
+      // warp-uniform cases: every key of the warp sees all 64 columns (no masking), or none
+      const bool full = __all_sync(0xffffffffu, lo == 0 && hi == 64);
+      const bool none = __all_sync(0xffffffffu, lo >= hi);
+      const float* lse = reinterpret_cast<const float*>(smem + OFFB_LSE + slot * VEC_BYTES) + cb;
+      const float* dd = reinterpret_cast<const float*>(smem + OFFB_D + slot * VEC_BYTES) + cb;
+      // phase A: P = 2^(S * scale * log2 e - lse) over the visible columns
+      float pf[64];
+      if (!none) {
+        uint32_t sv[64];
+        tmem_ld32(tl + cb, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+        tmem_ld32(tl + cb + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
         tmem_wait_ld();
-        uint32_t pk[16], dk[16];
+        tc_fence_before();
+        mbar_arrive(&bar[D_SREAD]);  // S^T may be overwritten from here on
 #pragma unroll
-        for (int e = 0; e < 32; e += 4) {
-          const float4 ls = lse4[(32 * c + e) >> 2];
-          const float4 dd = d4[(32 * c + e) >> 2];
-          const float lsv[4] = {ls.x, ls.y, ls.z, ls.w}, ddv[4] = {dd.x, dd.y, dd.z, dd.w};
-          float pv[4], dsv[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int col = 32 * c + e + u;
-            const bool vis = col >= lo && col < hi;
-            const float pr = ex2_approx(fmaf(__uint_as_float(sv[e + u]), sl2, -lsv[u]));
-            pv[u] = vis ? pr : 0.f;
-            dsv[u] = vis ? pr * (__uint_as_float(dp[e + u]) - ddv[u]) : 0.f;
-          }
-          pk[e >> 1] = pack2(pv[0], pv[1]);
-          pk[(e >> 1) + 1] = pack2(pv[2], pv[3]);
-          dk[e >> 1] = pack2(dsv[0], dsv[1]);
-          dk[(e >> 1) + 1] = pack2(dsv[2], dsv[3]);
+        for (int e = 0; e < 64; e += 4) {
+          const float4 ls = *reinterpret_cast<const float4*>(lse + e);
+          pf[e] = ex2_approx(fmaf(__uint_as_float(sv[e]), sl2, -ls.x));
+          pf[e + 1] = ex2_approx(fmaf(__uint_as_float(sv[e + 1]), sl2, -ls.y));
+          pf[e + 2] = ex2_approx(fmaf(__uint_as_float(sv[e + 2]), sl2, -ls.z));
+          pf[e + 3] = ex2_approx(fmaf(__uint_as_float(sv[e + 3]), sl2, -ls.w));
         }
-        tmem_st16(tl + 16 * c, pk);
-        tmem_st16(tl + 128 + 16 * c, dk);
+        if (!full) {
+#pragma unroll
+          for (int col = 0; col < 64; ++col) pf[col] = (col >= lo && col < hi) ? pf[col] : 0.f;
+        }
+      } else {
+        mbar_arrive(&bar[D_SREAD]);
+#pragma unroll
+        for (int e = 0; e < 64; ++e) pf[e] = 0.f;
+      }
+      // P^T into shared memory once dV of the previous step has read it
+      if (i > 0) {
+        ok = __all_sync(0xffffffffu, mbar_wait_fast(&bar[D_PEMPTY], (i - 1) & 1, abort_flag));
+        if (!ok) break;
+      }
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        *reinterpret_cast<uint4*>(prow + ((c ^ sw) << 4)) =
+            make_uint4(pack2(pf[8 * c], pf[8 * c + 1]), pack2(pf[8 * c + 2], pf[8 * c + 3]),
+                       pack2(pf[8 * c + 4], pf[8 * c + 5]), pack2(pf[8 * c + 6], pf[8 * c + 7]));
+      fence_proxy_async_smem();
+      mbar_arrive(&bar[D_PFULL]);
+      // phase B: dS = P (dP - D)
+      ok = __all_sync(0xffffffffu, mbar_wait_fast(&bar[D_DPFULL], i & 1, abort_flag));
+      if (!ok) break;
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t dk[16];
+        if (none) {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) dk[e] = 0u;
+        } else {
+          uint32_t dp[32];
+          tmem_ld32(tl + 128 + cb + 32 * c, dp);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; e += 4) {
+            const float4 d4 = *reinterpret_cast<const float4*>(dd + 32 * c + e);
+            const float ddv[4] = {d4.x, d4.y, d4.z, d4.w};
+            float dsv[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) dsv[u] = pf[32 * c + e + u] * (__uint_as_float(dp[e + u]) - ddv[u]);
+            if (!full) {
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                const int col = 32 * c + e + u;
+                dsv[u] = (col >= lo && col < hi) ? dsv[u] : 0.f;  // D past the stream is not defined
+              }
+            }
+            dk[e >> 1] = pack2(dsv[0], dsv[1]);
+            dk[(e >> 1) + 1] = pack2(dsv[2], dsv[3]);
+          }
+        }
+        tmem_st16(tl + 128 + cb + 16 * c, dk);
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&bar[D_PFULL]);
+      mbar_arrive(&bar[D_DSFULL]);
     }
     if (ok) ok = mbar_wait(&bar[D_FINAL], 0, abort_flag);
     ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below is warp-collective
@@ -1120,13 +1244,13 @@ replay_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
       const int64_t row = ((int64_t)b * p.T + s) * p.Hkv + hk;
 #pragma unroll 1
       for (int which = 0; which < 2; ++which) {  // dV, then dK (times the softmax scale)
-        __nv_bfloat16* dst = (which == 0 ? p.dv : p.dk) + row * HD;
+        __nv_bfloat16* dst = (which == 0 ? p.dv : p.dk) + row * HD + cb;
         const float mul = which == 0 ? 1.f : p.scale;
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
           uint32_t o[32];
           __syncwarp();
-          tmem_ld32(tl + 256 + 128 * which + 32 * c, o);
+          tmem_ld32(tl + 256 + 128 * which + cb + 32 * c, o);
           tmem_wait_ld();
           if (s >= p.T) continue;  // rows past the stream: loaded by the whole warp, not stored
           uint4* d4o = reinterpret_cast<uint4*>(dst + 32 * c);
@@ -1148,6 +1272,13 @@ replay_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
   }
 }
 
+// Base address of the dynamic shared memory of a kernel without static shared memory (the
+// dK/dV kernel's layout has no padding for alignment and needs it 1024-aligned)
+__global__ void replay_smem_base_kernel(uint32_t* out) {
+  extern __shared__ __align__(1024) uint8_t smem_bwd[];
+  if (threadIdx.x == 0) *out = smem_addr(smem_bwd);
+}
+
 // smem of the dQ kernel
 constexpr int OFFQ_Q = 0, OFFQ_DO = TILE_BYTES;
 constexpr int OFFQ_K = 2 * TILE_BYTES;               // 2 slots
@@ -1155,7 +1286,8 @@ constexpr int OFFQ_V = OFFQ_K + 2 * TILE_BYTES;      // 2 slots
 constexpr int OFFQ_E = OFFQ_V + 2 * TILE_BYTES;      // 2 slots of 128 int32
 constexpr int OFFQ_LIST = OFFQ_E + 2 * E_BYTES;
 constexpr int OFFQ_BAR = OFFQ_LIST + MAX_KT * 2;
-enum { Q_QFULL = 0, Q_KFULL0, Q_KFULL1, Q_KEMPTY0, Q_KEMPTY1, Q_SFULL, Q_PFULL, Q_FINAL, NBARQ };
+// Q_PFULL: every softmax thread has S of the step in registers (S may be overwritten)
+enum { Q_QFULL = 0, Q_KFULL0, Q_KFULL1, Q_KEMPTY0, Q_KEMPTY1, Q_SFULL, Q_DPFULL, Q_PFULL, Q_DSFULL, Q_FINAL, NBARQ };
 constexpr int OFFQ_MISC = OFFQ_BAR + NBARQ * 8;
 constexpr int SMEMQ_BYTES = OFFQ_MISC + 64 + 33 * 4 + 1024;
 static_assert(SMEMQ_BYTES <= 232448, "dQ kernel shared memory");
@@ -1173,12 +1305,15 @@ replay_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   int* s_n = reinterpret_cast<int*>(smem + OFFQ_MISC + 8);
   int* s_scan = reinterpret_cast<int*>(smem + OFFQ_MISC + 64);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  // CTA order as the forward: (stream, KV head) slowest, query tiles heaviest first, then heads
+  // CTA order: query tiles descending slowest (a late tile has the most key tiles, so the
+  // longest CTAs start first), then (stream, KV head), then the heads of a group (which read
+  // the same K/V tiles)
   const int G = p.Hq / p.Hkv;
+  const int nbh = p.B * p.Hkv;
   const int g = (int)(blockIdx.x % G);
   const int rest = (int)(blockIdx.x / G);
-  const int qt = p.n_qt - 1 - rest % p.n_qt;
-  const int bhk = rest / p.n_qt;
+  const int qt = p.n_qt - 1 - rest / nbh;
+  const int bhk = rest % nbh;
   const int b = bhk / p.Hkv, hk = bhk % p.Hkv;
   const int h = hk * G + g;
   const int t0 = qt * BM, t1 = t0 + BM - 1;
@@ -1186,7 +1321,8 @@ replay_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
 
   if (tid == 0) {
     for (int i = 0; i < NBARQ; ++i) mbar_init(&bar[i], 1);
-    mbar_init(&bar[Q_PFULL], 128);
+    mbar_init(&bar[Q_PFULL], 256);
+    mbar_init(&bar[Q_DSFULL], 256);
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -1219,7 +1355,7 @@ replay_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   tc_fence_after();
   const int n = *s_n;
   const uint32_t tmem = *tmem_slot;
-  // TMEM: S [0,128) (dS bf16 over its first 64 columns), dP [128,256), dQ [256,384)
+  // TMEM: S [0,128), dP [128,256), dQ [256,384), dS bf16 [384,448) (group g over [384+32g, +32))
 
   if (warp == 0) {
     if (lane == 0) {
@@ -1249,6 +1385,8 @@ replay_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       }
     }
   } else if (warp == 1) {
+    // ---------------------------------------------------------- UMMA issuer (whole warp)
+    // per step k: S(k+1); dQ += dS(k) K(k); dP(k+1)
     constexpr uint32_t ID_K = idesc_bf16(128, 128, 0);   // S, dP: both operands K-major
     constexpr uint32_t ID_MN = idesc_bf16(128, 128, 1);  // dQ: B (K) MN-major
     const uint64_t dq_ = desc_kmajor_sw128(smem_addr(smem + OFFQ_Q));
@@ -1256,39 +1394,57 @@ replay_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     auto wait = [&](uint64_t* bb, int parity) {
       return __all_sync(0xffffffffu, mbar_wait_fast(bb, parity, abort_flag));
     };
+    auto issue_s = [&](int slot) {  // S = Q K^T into [0,128)
+      const uint64_t dk_k = desc_kmajor_sw128(smem_addr(smem + OFFQ_K + slot * TILE_BYTES));
+      const uint32_t d = tmem;
+#define KVS_S(kk) umma_bf16_warp_at<kq_step(kk), kq_step(kk)>(d, dq_, dk_k, ID_K, kk > 0)
+      KVS_S(0); KVS_S(1); KVS_S(2); KVS_S(3); KVS_S(4); KVS_S(5); KVS_S(6); KVS_S(7);
+#undef KVS_S
+    };
+    auto issue_dp = [&](int slot) {  // dP = dO V^T into [128,256)
+      const uint64_t dv_k = desc_kmajor_sw128(smem_addr(smem + OFFQ_V + slot * TILE_BYTES));
+      const uint32_t d = tmem + 128;
+#define KVS_DP(kk) umma_bf16_warp_at<kq_step(kk), kq_step(kk)>(d, ddo_, dv_k, ID_K, kk > 0)
+      KVS_DP(0); KVS_DP(1); KVS_DP(2); KVS_DP(3); KVS_DP(4); KVS_DP(5); KVS_DP(6); KVS_DP(7);
+#undef KVS_DP
+    };
     bool ok = wait(&bar[Q_QFULL], 0);
+    if (ok) ok = wait(&bar[Q_KFULL0], 0);
+    if (ok) {
+      tc_fence_after();
+      issue_s(0);
+      umma_commit_warp(&bar[Q_SFULL]);
+      issue_dp(0);
+      umma_commit_warp(&bar[Q_DPFULL]);
+    }
     for (int k = 0; ok && k < n; ++k) {
       const int slot = k & 1;
-      ok = wait(&bar[Q_KFULL0 + slot], (k >> 1) & 1);
-      if (!ok) break;
-      tc_fence_after();
-      const uint64_t dk_k = desc_kmajor_sw128(smem_addr(smem + OFFQ_K + slot * TILE_BYTES));
-      const uint64_t dv_k = desc_kmajor_sw128(smem_addr(smem + OFFQ_V + slot * TILE_BYTES));
-      const uint64_t dk_mn = desc_mnmajor_sw128(smem_addr(smem + OFFQ_K + slot * TILE_BYTES), HALF_BYTES);
-      {
-        const uint32_t d = tmem;
-#define KVS_S(kk) umma_bf16_warp_at<kq_step(kk), kq_step(kk)>(d, dq_, dk_k, ID_K, kk > 0)
-        KVS_S(0); KVS_S(1); KVS_S(2); KVS_S(3); KVS_S(4); KVS_S(5); KVS_S(6); KVS_S(7);
-#undef KVS_S
-      }
-      {
-        const uint32_t d = tmem + 128;
-#define KVS_DP(kk) umma_bf16_warp_at<kq_step(kk), kq_step(kk)>(d, ddo_, dv_k, ID_K, kk > 0)
-        KVS_DP(0); KVS_DP(1); KVS_DP(2); KVS_DP(3); KVS_DP(4); KVS_DP(5); KVS_DP(6); KVS_DP(7);
-#undef KVS_DP
-      }
-      umma_commit_warp(&bar[Q_SFULL]);
+      const bool more = k + 1 < n;
       ok = wait(&bar[Q_PFULL], k & 1);
       if (!ok) break;
+      if (more) {
+        ok = wait(&bar[Q_KFULL0 + (slot ^ 1)], ((k + 1) >> 1) & 1);
+        if (!ok) break;
+        tc_fence_after();
+        issue_s(slot ^ 1);
+        umma_commit_warp(&bar[Q_SFULL]);
+      }
+      ok = wait(&bar[Q_DSFULL], k & 1);
+      if (!ok) break;
       tc_fence_after();
       {
-        const uint32_t d = tmem + 256, a = tmem;
+        const uint64_t dk_mn = desc_mnmajor_sw128(smem_addr(smem + OFFQ_K + slot * TILE_BYTES), HALF_BYTES);
+        const uint32_t d = tmem + 256, a = tmem + 384;
         const uint32_t acc = k > 0;
 #define KVS_DQ(kk) umma_bf16_tmem_a_warp_at<kk * 8, mn_step(kk)>(d, a, dk_mn, ID_MN, (kk > 0) || acc)
         KVS_DQ(0); KVS_DQ(1); KVS_DQ(2); KVS_DQ(3); KVS_DQ(4); KVS_DQ(5); KVS_DQ(6); KVS_DQ(7);
 #undef KVS_DQ
       }
       umma_commit_warp(&bar[Q_KEMPTY0 + slot]);
+      if (more) {
+        issue_dp(slot ^ 1);
+        umma_commit_warp(&bar[Q_DPFULL]);
+      }
     }
     if (!ok && lane == 0) {
       *abort_flag = 1;
@@ -1298,10 +1454,12 @@ replay_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     mbar_wait(&bar[Q_FINAL], 0, nullptr);
     __syncwarp();
   } else {
-    // ------------------------------------------------------------ one thread per query row
+    // ------------------------------------------------ softmax: query row r, key columns [cb, cb+64)
+    const int grp = (warp - 2) >> 2;
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
     const int t = t0 + r;
+    const int cb = 64 * grp;
     const bool real = t < L;
     const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16);
     const float sl2 = p.scale_log2;
@@ -1318,13 +1476,13 @@ replay_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      // visibility bits of the tile's 128 keys for row t (all set for an unmasked tile)
-      uint32_t bits[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu};
+      // visibility bits of this thread's 64 keys (all set for an unmasked tile)
+      uint32_t bits[2] = {0xffffffffu, 0xffffffffu};
       if (masked) {
         const int lim = t - j * BN;
-        const int4* E4 = reinterpret_cast<const int4*>(smem + OFFQ_E + slot * E_BYTES);
+        const int4* E4 = reinterpret_cast<const int4*>(smem + OFFQ_E + slot * E_BYTES) + cb / 4;
 #pragma unroll
-        for (int w = 0; w < 4; ++w) {
+        for (int w = 0; w < 2; ++w) {
           uint32_t bw = 0;
 #pragma unroll
           for (int q = 0; q < 8; ++q) {
@@ -1332,7 +1490,7 @@ replay_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
             const int ev[4] = {e.x, e.y, e.z, e.w};
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
-              const int i = 32 * w + 4 * q + u;
+              const int i = cb + 32 * w + 4 * q + u;
               const bool vis = (i <= lim) && (real ? (t < ev[u]) : (i >= lim));
               bw |= (vis ? 1u : 0u) << (4 * q + u);
             }
@@ -1340,29 +1498,48 @@ replay_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
           bits[w] = (t < p.T) ? bw : 0u;
         }
       }
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t sv[32], dp[32];
-        tmem_ld32(tl + 32 * c, sv);
-        tmem_ld32(tl + 128 + 32 * c, dp);
+      // phase A: P over the visible keys; S may be overwritten as soon as it is in registers
+      float pf[64];
+      {
+        uint32_t sv[64];
+        tmem_ld32(tl + cb, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+        tmem_ld32(tl + cb + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(&bar[Q_PFULL]);
+#pragma unroll
+        for (int e = 0; e < 64; ++e) pf[e] = ex2_approx(fmaf(__uint_as_float(sv[e]), sl2, -lse2));
+      }
+      if (masked) {
+#pragma unroll
+        for (int e = 0; e < 64; ++e) pf[e] = ((bits[e >> 5] >> (e & 31)) & 1) ? pf[e] : 0.f;
+      }
+      // phase B: dS = P (dP - D)
+      ok = __all_sync(0xffffffffu, mbar_wait_fast(&bar[Q_DPFULL], k & 1, abort_flag));
+      if (!ok) break;
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t dp[32];
+        tmem_ld32(tl + 128 + cb + 32 * c, dp);
         tmem_wait_ld();
         uint32_t dk[16];
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
           float dsv[2];
 #pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const bool vis = (bits[c] >> (e + u)) & 1;
-            const float pr = ex2_approx(fmaf(__uint_as_float(sv[e + u]), sl2, -lse2));
-            dsv[u] = vis ? pr * (__uint_as_float(dp[e + u]) - drow) : 0.f;
+          for (int u = 0; u < 2; ++u) dsv[u] = pf[32 * c + e + u] * (__uint_as_float(dp[e + u]) - drow);
+          if (masked) {
+#pragma unroll
+            for (int u = 0; u < 2; ++u) dsv[u] = ((bits[c] >> (e + u)) & 1) ? dsv[u] : 0.f;
           }
           dk[e >> 1] = pack2(dsv[0], dsv[1]);
         }
-        tmem_st16(tl + 16 * c, dk);
+        tmem_st16(tl + 384 + 32 * grp + 16 * c, dk);
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&bar[Q_PFULL]);
+      mbar_arrive(&bar[Q_DSFULL]);
     }
     if (ok) ok = mbar_wait(&bar[Q_FINAL], 0, abort_flag);
     ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below is warp-collective
@@ -1371,13 +1548,13 @@ replay_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       atomicExch(p.error, 23);
     } else {
       tc_fence_after();
-      __nv_bfloat16* dst = p.dq + (((int64_t)b * p.T + t) * p.Hq + h) * HD;
+      __nv_bfloat16* dst = p.dq + (((int64_t)b * p.T + t) * p.Hq + h) * HD + cb;
       const float mul = p.scale;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t o[32];
         __syncwarp();
-        tmem_ld32(tl + 256 + 32 * c, o);
+        tmem_ld32(tl + 256 + cb + 32 * c, o);
         tmem_wait_ld();
         if (t >= p.T) continue;  // rows past the stream: loaded by the whole warp, not stored
         uint4* d4o = reinterpret_cast<uint4*>(dst + 32 * c);
@@ -1690,20 +1867,34 @@ int kvs_replay_tc_backward(const kvs_replay_args* a, const void* dout, void* dq,
       !make_map(&mv, a->v, HD, a->n_kv_heads, (uint64_t)B * T) || !make_map(&mdo, dout, HD, a->n_heads, (uint64_t)B * T))
     return KVS_E_UNSUPPORTED;
   {
+    // once per device: kernel attributes, and a check that the dynamic shared base is
+    // 1024-aligned (the dK/dV layout relies on it; otherwise the exact kernels run)
     int dev = 0;
     cudaGetDevice(&dev);
     static std::mutex mu;
-    static bool done[64] = {};
+    static int state[64] = {};  // 0 unknown, 1 ready, 2 unsupported
     std::lock_guard<std::mutex> lock(mu);
     if (dev >= 64) return KVS_E_UNSUPPORTED;
-    if (!done[dev]) {
+    if (state[dev] == 0) {
       if (cudaFuncSetAttribute(reinterpret_cast<const void*>(replay_dkdv_kernel),
                                cudaFuncAttributeMaxDynamicSharedMemorySize, SMEMB_BYTES) != cudaSuccess ||
           cudaFuncSetAttribute(reinterpret_cast<const void*>(replay_dq_kernel),
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, SMEMQ_BYTES) != cudaSuccess)
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, SMEMQ_BYTES) != cudaSuccess ||
+          cudaFuncSetAttribute(reinterpret_cast<const void*>(replay_smem_base_kernel),
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, SMEMB_BYTES) != cudaSuccess)
         return KVS_E_LAUNCH;
-      done[dev] = true;
+      uint32_t* d_base = nullptr;
+      uint32_t h_base = 1;
+      if (cudaMalloc(&d_base, 4) != cudaSuccess) return KVS_E_LAUNCH;
+      replay_smem_base_kernel<<<1, 32, SMEMB_BYTES, st>>>(d_base);
+      const bool got = cudaGetLastError() == cudaSuccess &&
+                       cudaMemcpyAsync(&h_base, d_base, 4, cudaMemcpyDeviceToHost, st) == cudaSuccess &&
+                       cudaStreamSynchronize(st) == cudaSuccess;
+      cudaFree(d_base);
+      if (!got) return KVS_E_LAUNCH;
+      state[dev] = (h_base & 1023) == 0 ? 1 : 2;
     }
+    if (state[dev] != 1) return KVS_E_UNSUPPORTED;
   }
   if (cudaMemsetAsync(s.error, 0, 4, st) != cudaSuccess) return KVS_E_LAUNCH;
   replay_prepass_kernel<<<dim3(n_kt, B), BN, 0, st>>>(a->evicted_at, T, T_pad, n_kt, s.e32, s.tmin, s.tmax);
