@@ -237,6 +237,15 @@ size_t acc_bytes(int dtype) { return dtype == KVS_F64 ? 8 : 4; }
 
 size_t kvs_replay_tc_backward_scratch(int B, int T, int Hq);
 int kvs_replay_tc_backward(const kvs_replay_args* a, const void* dout, void* dq, void* dk, void* dv, cudaStream_t st);
+int kvs_replay_tc_backward_path(const kvs_replay_args* a, cudaStream_t st);
+
+KVS_API int kvs_replay_backward_path(const kvs_replay_args* a, kvs_stream_t stream) {
+  if (!a || a->batch <= 0 || a->seq_len <= 0 || a->n_heads <= 0 || a->n_kv_heads <= 0 ||
+      a->n_heads % a->n_kv_heads)
+    return KVS_E_ARG;
+  if (a->dtype != KVS_BF16 || (a->flags & 1)) return 0;
+  return kvs_replay_tc_backward_path(a, to_cuda(stream));
+}
 
 KVS_API size_t kvs_replay_backward_scratch_bytes(int32_t batch, int32_t seq_len, int32_t n_heads, int32_t dtype) {
   if (batch <= 0 || seq_len <= 0 || n_heads <= 0) return 0;

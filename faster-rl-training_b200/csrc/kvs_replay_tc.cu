@@ -866,9 +866,10 @@ pair_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
 // of one head and loops over its active key tiles (the forward's list).  P and dS are
 // rounded to bf16 as UMMA operands (as P is in the forward).
 
-// D[b][h][t] = sum_d dO[b][t][h][d] * O[b][t][h][d] (one warp per row and head)
+// -lse2 and -D of each (stream, head, row) (one warp per row and head); both kernels add them
 __global__ void replay_rowdot_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ o,
-                                     float* __restrict__ dvec, int B, int T, int T_pad, int Hq) {
+                                     const float* __restrict__ lse, float* __restrict__ nlse,
+                                     float* __restrict__ nd, int B, int T, int T_pad, int Hq) {
   const int64_t gw = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5);
   if (gw >= (int64_t)B * T * Hq) return;
   const int lane = threadIdx.x & 31;
@@ -885,10 +886,16 @@ __global__ void replay_rowdot_kernel(const __nv_bfloat16* __restrict__ dout, con
   }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-  if (lane == 0) dvec[((int64_t)b * Hq + h) * T_pad + t] = s;
+  if (lane == 0) {
+    const int64_t v = ((int64_t)b * Hq + h) * T_pad + t;
+    nd[v] = -s;
+    nlse[v] = -lse[v];
+  }
 }
 
-constexpr int NTB = 320;  // warp 0 producers, warp 1 UMMA, warps 2-9: two groups of four softmax warps
+constexpr int NGRP = 4;                 // softmax groups of four warps (one per TMEM lane quadrant)
+constexpr int GCOLS = 128 / NGRP;       // columns of S / dP per group
+constexpr int NTB = 64 + NGRP * 128;    // warp 0 producers, warp 1 UMMA, then the softmax groups
 constexpr int VEC_BYTES = BM * 4;
 
 struct BwdParams {
@@ -896,8 +903,8 @@ struct BwdParams {
   const int32_t* tile_min;  // [B][n_kt] (prepass)
   const int32_t* tile_max;
   const int32_t* lengths;
-  const float* lse;         // [B][Hq][T_pad] log2 units
-  const float* dvec;        // [B][Hq][T_pad]
+  const float* nlse;        // [B][Hq][T_pad] -lse2 (log2 units)
+  const float* nd;          // [B][Hq][T_pad] -D
   __nv_bfloat16* dq;        // [B][T][Hq][D]
   __nv_bfloat16* dk;        // [B][T][Hkv][D]
   __nv_bfloat16* dv;
@@ -906,30 +913,46 @@ struct BwdParams {
   float scale_log2, scale;
 };
 
+// One arrival per softmax warp: each thread orders its own TMEM / shared writes (fences), the
+// warp synchronises, and lane 0 arrives (one arrival per warp instead of one per thread).
+__device__ __forceinline__ void warp_arrive(uint64_t* bar) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
+}
+
 // Both kernels: one thread per TMEM lane (a key row in dK/dV, a query row in dQ) in each of
-// two groups of four warps; group g owns columns [64g, 64g + 64) of the 128-wide S and dP
-// tiles.  A step runs in two phases so that the tensor cores work through the next product
-// while the softmax warps compute: phase A turns S into P (kept in fp32 registers) as soon
-// as S lands; phase B forms dS = P (dP - D) when dP lands.
+// NGRP groups of four warps; group g owns columns [32g, 32g + 32) of the 128-wide S and dP
+// tiles (16 softmax warps: four per SM sub-partition hide the TMEM and MUFU latencies).  A
+// step runs in two phases so that the tensor cores work through the next product while the
+// softmax warps compute: phase A turns S into P (kept in fp32 registers) as soon as S lands;
+// phase B forms dS = P (dP - D) when dP lands.
+//
+// Operand tiles of the loop sit in a pool of four 32 KB slots: the tile of step i + 2 takes
+// the slot that step i frees first (in dK/dV, Q(i+2) goes where dO(i) was, released by dV(i)
+// mid-step, and dO(i+2) where Q(i) was, released by dK(i)), so each load has about a step
+// to land; tiles two steps ahead are also prefetched into L2.
+__host__ __device__ constexpr int slot_a(int i) { return (0x3120 >> (4 * (i & 3))) & 0xF; }  // 0 2 1 3
+__host__ __device__ constexpr int slot_b(int i) { return (0x2031 >> (4 * (i & 3))) & 0xF; }  // 1 3 0 2
+static_assert(slot_a(2) == slot_b(0) && slot_a(3) == slot_b(1) && slot_b(2) == slot_a(0) && slot_b(3) == slot_a(1),
+              "slot pool: step i + 2 reuses the slots of step i crosswise");
 
 __host__ __device__ constexpr uint32_t kq_step(int kk) { return (uint32_t)(((kk >> 2) * HALF_BYTES + (kk & 3) * 32) >> 4); }
 __host__ __device__ constexpr uint32_t mn_step(int kk) { return (uint32_t)((kk * 2048) >> 4); }
 // TMEM column of K step kk (16 rows of the K dimension = 8 packed columns) when group g packed
-// its 64 bf16 values into columns [64g, 64g + 32) of a 128-column region
-__host__ __device__ constexpr uint32_t split_col(int kk) { return (uint32_t)(kk < 4 ? kk * 8 : 64 + (kk - 4) * 8); }
+// its 32 bf16 values into columns [32g, 32g + 16) of a 128-column region
+__host__ __device__ constexpr uint32_t split_col(int kk) { return (uint32_t)((kk >> 1) * GCOLS + (kk & 1) * 8); }
 
 // smem of the dK/dV kernel (the dynamic shared base is 1024-aligned: no padding; the host
 // checks that once per device before the first launch)
 constexpr int OFFB_K = 0, OFFB_V = TILE_BYTES;
-constexpr int OFFB_Q = 2 * TILE_BYTES;                // 2 slots
-constexpr int OFFB_DO = OFFB_Q + 2 * TILE_BYTES;      // 2 slots
-constexpr int OFFB_P = OFFB_DO + 2 * TILE_BYTES;      // P^T bf16, K-major 128B-swizzled (UMMA A of dV)
-constexpr int OFFB_LSE = OFFB_P + TILE_BYTES;         // 2 slots of 128 f32, loaded with Q
-constexpr int OFFB_D = OFFB_LSE + 2 * VEC_BYTES;      // 2 slots of 128 f32, loaded with Q
+constexpr int OFFB_SLOT = 2 * TILE_BYTES;             // 4 slots: Q and dO tiles of the loop
+constexpr int OFFB_P = OFFB_SLOT + 4 * TILE_BYTES;    // P^T bf16, K-major 128B-swizzled (UMMA A of dV)
+constexpr int OFFB_LSE = OFFB_P + TILE_BYTES;         // 2 slots of 128 f32 (-lse2), loaded with dO
+constexpr int OFFB_D = OFFB_LSE + 2 * VEC_BYTES;      // 2 slots of 128 f32 (-D), loaded with dO
 constexpr int OFFB_BAR = OFFB_D + 2 * VEC_BYTES;
 enum {
-  D_KVFULL = 0, D_QFULL0, D_QFULL1, D_OFULL0, D_OFULL1, D_QEMPTY0, D_QEMPTY1, D_OEMPTY0, D_OEMPTY1,
-  D_SFULL, D_SREAD, D_PFULL, D_PEMPTY, D_DPFULL, D_DSFULL, D_FINAL, NBARB
+  D_KVFULL = 0, D_FULL0, D_EMPTY0 = D_FULL0 + 4, D_SFULL = D_EMPTY0 + 4, D_SREAD, D_PFULL, D_PEMPTY, D_DPFULL,
+  D_DSFULL, D_FINAL, NBARB
 };
 constexpr int OFFB_MISC = OFFB_BAR + NBARB * 8;
 constexpr int SMEMB_BYTES = OFFB_MISC + 16;
@@ -971,9 +994,9 @@ replay_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
 
   if (tid == 0) {
     for (int i = 0; i < NBARB; ++i) mbar_init(&bar[i], 1);
-    mbar_init(&bar[D_SREAD], 256);
-    mbar_init(&bar[D_PFULL], 256);
-    mbar_init(&bar[D_DSFULL], 256);
+    mbar_init(&bar[D_SREAD], 4 * NGRP);
+    mbar_init(&bar[D_PFULL], 4 * NGRP);
+    mbar_init(&bar[D_DSFULL], 4 * NGRP);
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -984,52 +1007,61 @@ replay_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // TMEM: S^T [0,128), dP^T [128,256) (dS^T bf16 of group g over [128+64g, +32)), dV [256,384),
+  // TMEM: S^T [0,128), dP^T [128,256) (dS^T bf16 of group g over [128+32g, +16)), dV [256,384),
   // dK [384,512).  P^T goes to shared memory, so S^T(i+1) is computed while the softmax warps
   // still work on step i.
 
   if (warp == 0) {
     if (lane == 0) {
-      // ---------------------------------------------------------- K, V; the Q ring (+ lse, D)
+      // ---------------------------------------------------------- K, V; the Q tiles
       mbar_arrive_expect_tx(&bar[D_KVFULL], 2 * TILE_BYTES);
       tma_load_3d(smem + OFFB_K, &tm_k, 0, hk, b * p.T + k0, &bar[D_KVFULL]);
       tma_load_3d(smem + OFFB_K + HALF_BYTES, &tm_k, 64, hk, b * p.T + k0, &bar[D_KVFULL]);
       tma_load_3d(smem + OFFB_V, &tm_v, 0, hk, b * p.T + k0, &bar[D_KVFULL]);
       tma_load_3d(smem + OFFB_V + HALF_BYTES, &tm_v, 64, hk, b * p.T + k0, &bar[D_KVFULL]);
       for (int i = 0; i < nsteps; ++i) {
-        const int slot = i & 1;
-        if (i >= 2 && !mbar_wait(&bar[D_QEMPTY0 + slot], ((i >> 1) - 1) & 1, abort_flag)) {
+        const int sl = slot_a(i);
+        if (i >= 2 && !mbar_wait(&bar[D_EMPTY0 + sl], ((i >> 1) - 1) & 1, abort_flag)) {
           *abort_flag = 1;
           atomicExch(p.error, 11);
           break;
         }
-        const int qt = kt + i / G, h = hk * G + i % G;
-        const int row = b * p.T + qt * BM;
-        uint64_t* fb = &bar[D_QFULL0 + slot];
-        mbar_arrive_expect_tx(fb, TILE_BYTES + 2 * VEC_BYTES);
-        uint8_t* qs = smem + OFFB_Q + slot * TILE_BYTES;
+        const int row = b * p.T + (kt + i / G) * BM, h = hk * G + i % G;
+        uint64_t* fb = &bar[D_FULL0 + sl];
+        mbar_arrive_expect_tx(fb, TILE_BYTES);
+        uint8_t* qs = smem + OFFB_SLOT + sl * TILE_BYTES;
         tma_load_3d(qs, &tm_q, 0, h, row, fb);
         tma_load_3d(qs + HALF_BYTES, &tm_q, 64, h, row, fb);
-        const int64_t vo = ((int64_t)b * p.Hq + h) * p.T_pad + qt * BM;
-        bulk_load(smem + OFFB_LSE + slot * VEC_BYTES, p.lse + vo, VEC_BYTES, fb);
-        bulk_load(smem + OFFB_D + slot * VEC_BYTES, p.dvec + vo, VEC_BYTES, fb);
+        if (i + 2 < nsteps) {
+          const int row2 = b * p.T + (kt + (i + 2) / G) * BM, h2 = hk * G + (i + 2) % G;
+          tma_prefetch_3d(&tm_q, 0, h2, row2);
+          tma_prefetch_3d(&tm_q, 64, h2, row2);
+        }
       }
     } else if (lane == 1) {
-      // ---------------------------------------------------------- the dO ring
+      // ---------------------------------------------------------- the dO tiles (+ -lse2, -D)
       for (int i = 0; i < nsteps; ++i) {
-        const int slot = i & 1;
-        if (i >= 2 && !mbar_wait(&bar[D_OEMPTY0 + slot], ((i >> 1) - 1) & 1, abort_flag)) {
+        const int sl = slot_b(i);
+        if (i >= 2 && !mbar_wait(&bar[D_EMPTY0 + sl], ((i >> 1) - 1) & 1, abort_flag)) {
           *abort_flag = 1;
           atomicExch(p.error, 14);
           break;
         }
         const int qt = kt + i / G, h = hk * G + i % G;
         const int row = b * p.T + qt * BM;
-        uint64_t* fb = &bar[D_OFULL0 + slot];
-        mbar_arrive_expect_tx(fb, TILE_BYTES);
-        uint8_t* ds = smem + OFFB_DO + slot * TILE_BYTES;
+        uint64_t* fb = &bar[D_FULL0 + sl];
+        mbar_arrive_expect_tx(fb, TILE_BYTES + 2 * VEC_BYTES);
+        uint8_t* ds = smem + OFFB_SLOT + sl * TILE_BYTES;
         tma_load_3d(ds, &tm_do, 0, h, row, fb);
         tma_load_3d(ds + HALF_BYTES, &tm_do, 64, h, row, fb);
+        const int64_t vo = ((int64_t)b * p.Hq + h) * p.T_pad + qt * BM;
+        bulk_load(smem + OFFB_LSE + (i & 1) * VEC_BYTES, p.nlse + vo, VEC_BYTES, fb);
+        bulk_load(smem + OFFB_D + (i & 1) * VEC_BYTES, p.nd + vo, VEC_BYTES, fb);
+        if (i + 2 < nsteps) {
+          const int row2 = b * p.T + (kt + (i + 2) / G) * BM, h2 = hk * G + (i + 2) % G;
+          tma_prefetch_3d(&tm_do, 0, h2, row2);
+          tma_prefetch_3d(&tm_do, 64, h2, row2);
+        }
       }
     }
   } else if (warp == 1) {
@@ -1043,74 +1075,76 @@ replay_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
     auto wait = [&](uint64_t* bb, int parity) {
       return __all_sync(0xffffffffu, mbar_wait_fast(bb, parity, abort_flag));
     };
-    auto issue_s = [&](int slot) {  // S^T = K Q^T into [0,128)
-      const uint64_t dq_k = desc_kmajor_sw128(smem_addr(smem + OFFB_Q + slot * TILE_BYTES));
+    auto issue_s = [&](int sl) {  // S^T = K Q^T into [0,128)
+      const uint64_t dq_k = desc_kmajor_sw128(smem_addr(smem + OFFB_SLOT + sl * TILE_BYTES));
       const uint32_t d = tmem;
 #define KVS_ST(kk) umma_bf16_warp_at<kq_step(kk), kq_step(kk)>(d, dk_, dq_k, ID_T, kk > 0)
       KVS_ST(0); KVS_ST(1); KVS_ST(2); KVS_ST(3); KVS_ST(4); KVS_ST(5); KVS_ST(6); KVS_ST(7);
 #undef KVS_ST
     };
-    auto issue_dp = [&](int slot) {  // dP^T = V dO^T into [128,256)
-      const uint64_t ddo_k = desc_kmajor_sw128(smem_addr(smem + OFFB_DO + slot * TILE_BYTES));
+    auto issue_dp = [&](int sl) {  // dP^T = V dO^T into [128,256)
+      const uint64_t ddo_k = desc_kmajor_sw128(smem_addr(smem + OFFB_SLOT + sl * TILE_BYTES));
       const uint32_t d = tmem + 128;
 #define KVS_DPT(kk) umma_bf16_warp_at<kq_step(kk), kq_step(kk)>(d, dv_, ddo_k, ID_T, kk > 0)
       KVS_DPT(0); KVS_DPT(1); KVS_DPT(2); KVS_DPT(3); KVS_DPT(4); KVS_DPT(5); KVS_DPT(6); KVS_DPT(7);
 #undef KVS_DPT
     };
     bool ok = wait(&bar[D_KVFULL], 0);
-    if (ok) ok = wait(&bar[D_QFULL0], 0);
+    if (ok) ok = wait(&bar[D_FULL0 + slot_a(0)], 0);
     if (ok) {
       tc_fence_after();
-      issue_s(0);
+      issue_s(slot_a(0));
       umma_commit_warp(&bar[D_SFULL]);
-      ok = wait(&bar[D_OFULL0], 0);
+      ok = wait(&bar[D_FULL0 + slot_b(0)], 0);
     }
     if (ok) {
       tc_fence_after();
-      issue_dp(0);
+      issue_dp(slot_b(0));
       umma_commit_warp(&bar[D_DPFULL]);
     }
     for (int i = 0; ok && i < nsteps; ++i) {
-      const int slot = i & 1;
       const bool more = i + 1 < nsteps;
+      const int ph1 = ((i + 1) >> 1) & 1;
       if (more) {
         ok = wait(&bar[D_SREAD], i & 1);
-        if (ok) ok = wait(&bar[D_QFULL0 + (slot ^ 1)], ((i + 1) >> 1) & 1);
+        if (ok) ok = wait(&bar[D_FULL0 + slot_a(i + 1)], ph1);
         if (!ok) break;
         tc_fence_after();
-        issue_s(slot ^ 1);
+        issue_s(slot_a(i + 1));
         umma_commit_warp(&bar[D_SFULL]);
       }
       ok = wait(&bar[D_PFULL], i & 1);
       if (!ok) break;
       tc_fence_after();
       {
-        const uint64_t ddo_mn = desc_mnmajor_sw128(smem_addr(smem + OFFB_DO + slot * TILE_BYTES), HALF_BYTES);
+        const uint64_t ddo_mn =
+            desc_mnmajor_sw128(smem_addr(smem + OFFB_SLOT + slot_b(i) * TILE_BYTES), HALF_BYTES);
         const uint32_t d = tmem + 256;
         const uint32_t acc = i > 0;
 #define KVS_DV(kk) umma_bf16_warp_at<kq_step(kk), mn_step(kk)>(d, dp_, ddo_mn, ID_MN, (kk > 0) || acc)
         KVS_DV(0); KVS_DV(1); KVS_DV(2); KVS_DV(3); KVS_DV(4); KVS_DV(5); KVS_DV(6); KVS_DV(7);
 #undef KVS_DV
       }
-      umma_commit_warp(&bar[D_OEMPTY0 + slot]);
+      umma_commit_warp(&bar[D_EMPTY0 + slot_b(i)]);
       umma_commit_warp(&bar[D_PEMPTY]);
       ok = wait(&bar[D_DSFULL], i & 1);
       if (!ok) break;
       tc_fence_after();
       {
-        const uint64_t dq_mn = desc_mnmajor_sw128(smem_addr(smem + OFFB_Q + slot * TILE_BYTES), HALF_BYTES);
+        const uint64_t dq_mn =
+            desc_mnmajor_sw128(smem_addr(smem + OFFB_SLOT + slot_a(i) * TILE_BYTES), HALF_BYTES);
         const uint32_t d = tmem + 384, a = tmem + 128;
         const uint32_t acc = i > 0;
 #define KVS_DK(kk) umma_bf16_tmem_a_warp_at<split_col(kk), mn_step(kk)>(d, a, dq_mn, ID_MN, (kk > 0) || acc)
         KVS_DK(0); KVS_DK(1); KVS_DK(2); KVS_DK(3); KVS_DK(4); KVS_DK(5); KVS_DK(6); KVS_DK(7);
 #undef KVS_DK
       }
-      umma_commit_warp(&bar[D_QEMPTY0 + slot]);
+      umma_commit_warp(&bar[D_EMPTY0 + slot_a(i)]);
       if (more) {
-        ok = wait(&bar[D_OFULL0 + (slot ^ 1)], ((i + 1) >> 1) & 1);
+        ok = wait(&bar[D_FULL0 + slot_b(i + 1)], ph1);
         if (!ok) break;
         tc_fence_after();
-        issue_dp(slot ^ 1);
+        issue_dp(slot_b(i + 1));
         umma_commit_warp(&bar[D_DPFULL]);
       }
     }
@@ -1122,17 +1156,18 @@ replay_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
     mbar_wait(&bar[D_FINAL], 0, nullptr);
     __syncwarp();
   } else {
-    // ------------------------------------------------ softmax: key row r, query columns [cb, cb+64)
+    // ------------------------------------------------ softmax: key row r, query columns [cb, cb+32)
     const int grp = (warp - 2) >> 2;
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
     const int s = k0 + r;
-    const int cb = 64 * grp;
+    const int cb = GCOLS * grp;
     const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16);
     const float sl2 = p.scale_log2;
-    // this thread's row of P^T: half grp of the K-major tile, 16-byte chunks XOR-swizzled by row
-    uint8_t* prow = smem + OFFB_P + grp * HALF_BYTES + r * 128;
-    const int sw = r & 7;
+    // this thread's 32 columns of P^T: half cb / 64 of the K-major tile, 16-byte chunks
+    // (cb % 64) / 8 + c, XOR-swizzled by row
+    uint8_t* prow = smem + OFFB_P + (cb >> 6) * HALF_BYTES + r * 128;
+    const int c0 = (cb & 63) >> 3, sw = r & 7;
     // the query rows that see key s: [s, min(evicted_at[s], L)) for a real key, s itself for a
     // padded one, nothing past the stream
     int rlo = 0, rhi = 0;
@@ -1145,44 +1180,42 @@ replay_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
     }
     bool ok = true;
     for (int i = 0; i < nsteps; ++i) {
-      const int slot = i & 1;
       const int t0 = (kt + i / G) * BM + cb;  // query row of this thread's first column
       ok = mbar_wait_fast(&bar[D_SFULL], i & 1, abort_flag);
-      if (ok) ok = mbar_wait_fast(&bar[D_QFULL0 + slot], (i >> 1) & 1, abort_flag);
+      if (ok) ok = mbar_wait_fast(&bar[D_FULL0 + slot_b(i)], (i >> 1) & 1, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      const int lo = max(rlo - t0, 0), hi = min(rhi - t0, 64);  // visible columns [lo, hi) of 64
-      // warp-uniform cases: every key of the warp sees all 64 columns (no masking), or none
-      const bool full = __all_sync(0xffffffffu, lo == 0 && hi == 64);
+      const int lo = max(rlo - t0, 0), hi = min(rhi - t0, GCOLS);  // visible columns [lo, hi)
+      // warp-uniform cases: every key of the warp sees all the columns (no masking), or none
+      const bool full = __all_sync(0xffffffffu, lo == 0 && hi == GCOLS);
       const bool none = __all_sync(0xffffffffu, lo >= hi);
-      const float* lse = reinterpret_cast<const float*>(smem + OFFB_LSE + slot * VEC_BYTES) + cb;
-      const float* dd = reinterpret_cast<const float*>(smem + OFFB_D + slot * VEC_BYTES) + cb;
+      const float* nl = reinterpret_cast<const float*>(smem + OFFB_LSE + (i & 1) * VEC_BYTES) + cb;
+      const float* nd = reinterpret_cast<const float*>(smem + OFFB_D + (i & 1) * VEC_BYTES) + cb;
       // phase A: P = 2^(S * scale * log2 e - lse) over the visible columns
-      float pf[64];
+      float pf[GCOLS];
       if (!none) {
-        uint32_t sv[64];
-        tmem_ld32(tl + cb, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-        tmem_ld32(tl + cb + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+        uint32_t sv[32];
+        tmem_ld32(tl + cb, sv);
         tmem_wait_ld();
         tc_fence_before();
-        mbar_arrive(&bar[D_SREAD]);  // S^T may be overwritten from here on
+        warp_arrive(&bar[D_SREAD]);  // S^T may be overwritten from here on
 #pragma unroll
-        for (int e = 0; e < 64; e += 4) {
-          const float4 ls = *reinterpret_cast<const float4*>(lse + e);
-          pf[e] = ex2_approx(fmaf(__uint_as_float(sv[e]), sl2, -ls.x));
-          pf[e + 1] = ex2_approx(fmaf(__uint_as_float(sv[e + 1]), sl2, -ls.y));
-          pf[e + 2] = ex2_approx(fmaf(__uint_as_float(sv[e + 2]), sl2, -ls.z));
-          pf[e + 3] = ex2_approx(fmaf(__uint_as_float(sv[e + 3]), sl2, -ls.w));
+        for (int e = 0; e < GCOLS; e += 4) {
+          const float4 n4 = *reinterpret_cast<const float4*>(nl + e);
+          pf[e] = ex2_approx(fmaf(__uint_as_float(sv[e]), sl2, n4.x));
+          pf[e + 1] = ex2_approx(fmaf(__uint_as_float(sv[e + 1]), sl2, n4.y));
+          pf[e + 2] = ex2_approx(fmaf(__uint_as_float(sv[e + 2]), sl2, n4.z));
+          pf[e + 3] = ex2_approx(fmaf(__uint_as_float(sv[e + 3]), sl2, n4.w));
         }
         if (!full) {
 #pragma unroll
-          for (int col = 0; col < 64; ++col) pf[col] = (col >= lo && col < hi) ? pf[col] : 0.f;
+          for (int col = 0; col < GCOLS; ++col) pf[col] = (col >= lo && col < hi) ? pf[col] : 0.f;
         }
       } else {
-        mbar_arrive(&bar[D_SREAD]);
+        warp_arrive(&bar[D_SREAD]);
 #pragma unroll
-        for (int e = 0; e < 64; ++e) pf[e] = 0.f;
+        for (int e = 0; e < GCOLS; ++e) pf[e] = 0.f;
       }
       // P^T into shared memory once dV of the previous step has read it
       if (i > 0) {
@@ -1190,49 +1223,41 @@ replay_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
         if (!ok) break;
       }
 #pragma unroll
-      for (int c = 0; c < 8; ++c)
-        *reinterpret_cast<uint4*>(prow + ((c ^ sw) << 4)) =
+      for (int c = 0; c < GCOLS / 8; ++c)
+        *reinterpret_cast<uint4*>(prow + (((c0 + c) ^ sw) << 4)) =
             make_uint4(pack2(pf[8 * c], pf[8 * c + 1]), pack2(pf[8 * c + 2], pf[8 * c + 3]),
                        pack2(pf[8 * c + 4], pf[8 * c + 5]), pack2(pf[8 * c + 6], pf[8 * c + 7]));
       fence_proxy_async_smem();
-      mbar_arrive(&bar[D_PFULL]);
+      warp_arrive(&bar[D_PFULL]);
       // phase B: dS = P (dP - D)
       ok = __all_sync(0xffffffffu, mbar_wait_fast(&bar[D_DPFULL], i & 1, abort_flag));
       if (!ok) break;
       tc_fence_after();
+      uint32_t dk[GCOLS / 2];
+      if (none) {
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t dk[16];
-        if (none) {
+        for (int e = 0; e < GCOLS / 2; ++e) dk[e] = 0u;
+      } else {
+        uint32_t dp[32];
+        tmem_ld32(tl + 128 + cb, dp);
+        tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 16; ++e) dk[e] = 0u;
-        } else {
-          uint32_t dp[32];
-          tmem_ld32(tl + 128 + cb + 32 * c, dp);
-          tmem_wait_ld();
+        for (int e = 0; e < GCOLS; e += 4) {
+          const float4 n4 = *reinterpret_cast<const float4*>(nd + e);
+          float d[4] = {pf[e] * (__uint_as_float(dp[e]) + n4.x), pf[e + 1] * (__uint_as_float(dp[e + 1]) + n4.y),
+                        pf[e + 2] * (__uint_as_float(dp[e + 2]) + n4.z), pf[e + 3] * (__uint_as_float(dp[e + 3]) + n4.w)};
+          if (!full) {  // D past the stream is not defined: select, do not multiply
 #pragma unroll
-          for (int e = 0; e < 32; e += 4) {
-            const float4 d4 = *reinterpret_cast<const float4*>(dd + 32 * c + e);
-            const float ddv[4] = {d4.x, d4.y, d4.z, d4.w};
-            float dsv[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) dsv[u] = pf[32 * c + e + u] * (__uint_as_float(dp[e + u]) - ddv[u]);
-            if (!full) {
-#pragma unroll
-              for (int u = 0; u < 4; ++u) {
-                const int col = 32 * c + e + u;
-                dsv[u] = (col >= lo && col < hi) ? dsv[u] : 0.f;  // D past the stream is not defined
-              }
-            }
-            dk[e >> 1] = pack2(dsv[0], dsv[1]);
-            dk[(e >> 1) + 1] = pack2(dsv[2], dsv[3]);
+            for (int u = 0; u < 4; ++u) d[u] = (e + u >= lo && e + u < hi) ? d[u] : 0.f;
           }
+          dk[e >> 1] = pack2(d[0], d[1]);
+          dk[(e >> 1) + 1] = pack2(d[2], d[3]);
         }
-        tmem_st16(tl + 128 + cb + 16 * c, dk);
       }
+      tmem_st16(tl + 128 + cb, dk);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&bar[D_DSFULL]);
+      warp_arrive(&bar[D_DSFULL]);
     }
     if (ok) ok = mbar_wait(&bar[D_FINAL], 0, abort_flag);
     ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below is warp-collective
@@ -1247,7 +1272,7 @@ replay_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
         __nv_bfloat16* dst = (which == 0 ? p.dv : p.dk) + row * HD + cb;
         const float mul = which == 0 ? 1.f : p.scale;
 #pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
+        for (int c = 0; c < GCOLS / 32; ++c) {
           uint32_t o[32];
           __syncwarp();
           tmem_ld32(tl + 256 + 128 * which + cb + 32 * c, o);
@@ -1281,23 +1306,26 @@ __global__ void replay_smem_base_kernel(uint32_t* out) {
 
 // smem of the dQ kernel
 constexpr int OFFQ_Q = 0, OFFQ_DO = TILE_BYTES;
-constexpr int OFFQ_K = 2 * TILE_BYTES;               // 2 slots
-constexpr int OFFQ_V = OFFQ_K + 2 * TILE_BYTES;      // 2 slots
-constexpr int OFFQ_E = OFFQ_V + 2 * TILE_BYTES;      // 2 slots of 128 int32
-constexpr int OFFQ_LIST = OFFQ_E + 2 * E_BYTES;
+constexpr int OFFQ_SLOT = 2 * TILE_BYTES;            // 4 slots: K and V tiles of the loop
+constexpr int OFFQ_E = OFFQ_SLOT + 4 * TILE_BYTES;   // 4 slots of 128 int32, loaded with K
+constexpr int OFFQ_LIST = OFFQ_E + 4 * E_BYTES;
 constexpr int OFFQ_BAR = OFFQ_LIST + MAX_KT * 2;
-// Q_PFULL: every softmax thread has S of the step in registers (S may be overwritten)
-enum { Q_QFULL = 0, Q_KFULL0, Q_KFULL1, Q_KEMPTY0, Q_KEMPTY1, Q_SFULL, Q_DPFULL, Q_PFULL, Q_DSFULL, Q_FINAL, NBARQ };
+// Q_SREAD: every softmax warp has S of the step in registers (S may be overwritten)
+enum { Q_QFULL = 0, Q_FULL0, Q_EMPTY0 = Q_FULL0 + 4, Q_SFULL = Q_EMPTY0 + 4, Q_DPFULL, Q_SREAD, Q_DSFULL, Q_FINAL, NBARQ };
 constexpr int OFFQ_MISC = OFFQ_BAR + NBARQ * 8;
-constexpr int SMEMQ_BYTES = OFFQ_MISC + 64 + 33 * 4 + 1024;
+constexpr int SMEMQ_BYTES = OFFQ_MISC + 64 + 33 * 4;
 static_assert(SMEMQ_BYTES <= 232448, "dQ kernel shared memory");
 
 __global__ void __launch_bounds__(NTB, 1)
 replay_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                  const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
                  const BwdParams p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(1024) uint8_t smem_bwd[];
+  uint8_t* smem = smem_bwd;
+  if (smem_addr(smem) & 1023) {  // never expected (the host checked); no work, no TMEM
+    if (threadIdx.x == 0) atomicExch(p.error, 25);
+    return;
+  }
   uint16_t* list = reinterpret_cast<uint16_t*>(smem + OFFQ_LIST);
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + OFFQ_BAR);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFFQ_MISC);
@@ -1321,8 +1349,8 @@ replay_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
 
   if (tid == 0) {
     for (int i = 0; i < NBARQ; ++i) mbar_init(&bar[i], 1);
-    mbar_init(&bar[Q_PFULL], 256);
-    mbar_init(&bar[Q_DSFULL], 256);
+    mbar_init(&bar[Q_SREAD], 4 * NGRP);
+    mbar_init(&bar[Q_DSFULL], 4 * NGRP);
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -1355,38 +1383,62 @@ replay_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   tc_fence_after();
   const int n = *s_n;
   const uint32_t tmem = *tmem_slot;
-  // TMEM: S [0,128), dP [128,256), dQ [256,384), dS bf16 [384,448) (group g over [384+32g, +32))
+  // TMEM: S [0,128), dP [128,256), dQ [256,384), dS bf16 [384,448) (group g over [384+16g, +16))
 
   if (warp == 0) {
     if (lane == 0) {
+      // ---------------------------------------------------------- Q, dO; the K tiles (+ evicted_at)
       mbar_arrive_expect_tx(&bar[Q_QFULL], 2 * TILE_BYTES);
       tma_load_3d(smem + OFFQ_Q, &tm_q, 0, h, b * p.T + t0, &bar[Q_QFULL]);
       tma_load_3d(smem + OFFQ_Q + HALF_BYTES, &tm_q, 64, h, b * p.T + t0, &bar[Q_QFULL]);
       tma_load_3d(smem + OFFQ_DO, &tm_do, 0, h, b * p.T + t0, &bar[Q_QFULL]);
       tma_load_3d(smem + OFFQ_DO + HALF_BYTES, &tm_do, 64, h, b * p.T + t0, &bar[Q_QFULL]);
       for (int k = 0; k < n; ++k) {
-        const int slot = k & 1;
-        if (k >= 2 && !mbar_wait(&bar[Q_KEMPTY0 + slot], ((k >> 1) - 1) & 1, abort_flag)) {
+        const int sl = slot_a(k);
+        if (k >= 2 && !mbar_wait(&bar[Q_EMPTY0 + sl], ((k >> 1) - 1) & 1, abort_flag)) {
           *abort_flag = 1;
           atomicExch(p.error, 21);
           break;
         }
         const int j = list[k] & 0x7fff;
-        const int row = b * p.T + j * BN;
-        uint64_t* fb = &bar[Q_KFULL0 + slot];
-        mbar_arrive_expect_tx(fb, 2 * TILE_BYTES + E_BYTES);
-        uint8_t* ks = smem + OFFQ_K + slot * TILE_BYTES;
-        uint8_t* vs = smem + OFFQ_V + slot * TILE_BYTES;
-        tma_load_3d(ks, &tm_k, 0, hk, row, fb);
-        tma_load_3d(ks + HALF_BYTES, &tm_k, 64, hk, row, fb);
-        tma_load_3d(vs, &tm_v, 0, hk, row, fb);
-        tma_load_3d(vs + HALF_BYTES, &tm_v, 64, hk, row, fb);
-        bulk_load(smem + OFFQ_E + slot * E_BYTES, p.e32 + (int64_t)b * p.T_pad + j * BN, E_BYTES, fb);
+        uint64_t* fb = &bar[Q_FULL0 + sl];
+        mbar_arrive_expect_tx(fb, TILE_BYTES + E_BYTES);
+        uint8_t* ks = smem + OFFQ_SLOT + sl * TILE_BYTES;
+        tma_load_3d(ks, &tm_k, 0, hk, b * p.T + j * BN, fb);
+        tma_load_3d(ks + HALF_BYTES, &tm_k, 64, hk, b * p.T + j * BN, fb);
+        bulk_load(smem + OFFQ_E + (k & 3) * E_BYTES, p.e32 + (int64_t)b * p.T_pad + j * BN, E_BYTES, fb);
+        if (k + 2 < n) {
+          const int j2 = list[k + 2] & 0x7fff;
+          tma_prefetch_3d(&tm_k, 0, hk, b * p.T + j2 * BN);
+          tma_prefetch_3d(&tm_k, 64, hk, b * p.T + j2 * BN);
+        }
+      }
+    } else if (lane == 1) {
+      // ---------------------------------------------------------- the V tiles
+      for (int k = 0; k < n; ++k) {
+        const int sl = slot_b(k);
+        if (k >= 2 && !mbar_wait(&bar[Q_EMPTY0 + sl], ((k >> 1) - 1) & 1, abort_flag)) {
+          *abort_flag = 1;
+          atomicExch(p.error, 24);
+          break;
+        }
+        const int j = list[k] & 0x7fff;
+        uint64_t* fb = &bar[Q_FULL0 + sl];
+        mbar_arrive_expect_tx(fb, TILE_BYTES);
+        uint8_t* vs = smem + OFFQ_SLOT + sl * TILE_BYTES;
+        tma_load_3d(vs, &tm_v, 0, hk, b * p.T + j * BN, fb);
+        tma_load_3d(vs + HALF_BYTES, &tm_v, 64, hk, b * p.T + j * BN, fb);
+        if (k + 2 < n) {
+          const int j2 = list[k + 2] & 0x7fff;
+          tma_prefetch_3d(&tm_v, 0, hk, b * p.T + j2 * BN);
+          tma_prefetch_3d(&tm_v, 64, hk, b * p.T + j2 * BN);
+        }
       }
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------- UMMA issuer (whole warp)
-    // per step k: S(k+1); dQ += dS(k) K(k); dP(k+1)
+    // per step k: S(k+1) once S(k) is read; dQ += dS(k) K(k); dP(k+1).  K(k) is released by
+    // dQ(k), V(k) by dP(k): K(k+2) takes V(k)'s slot and V(k+2) K(k)'s.
     constexpr uint32_t ID_K = idesc_bf16(128, 128, 0);   // S, dP: both operands K-major
     constexpr uint32_t ID_MN = idesc_bf16(128, 128, 1);  // dQ: B (K) MN-major
     const uint64_t dq_ = desc_kmajor_sw128(smem_addr(smem + OFFQ_Q));
@@ -1394,55 +1446,64 @@ replay_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     auto wait = [&](uint64_t* bb, int parity) {
       return __all_sync(0xffffffffu, mbar_wait_fast(bb, parity, abort_flag));
     };
-    auto issue_s = [&](int slot) {  // S = Q K^T into [0,128)
-      const uint64_t dk_k = desc_kmajor_sw128(smem_addr(smem + OFFQ_K + slot * TILE_BYTES));
+    auto issue_s = [&](int sl) {  // S = Q K^T into [0,128)
+      const uint64_t dk_k = desc_kmajor_sw128(smem_addr(smem + OFFQ_SLOT + sl * TILE_BYTES));
       const uint32_t d = tmem;
 #define KVS_S(kk) umma_bf16_warp_at<kq_step(kk), kq_step(kk)>(d, dq_, dk_k, ID_K, kk > 0)
       KVS_S(0); KVS_S(1); KVS_S(2); KVS_S(3); KVS_S(4); KVS_S(5); KVS_S(6); KVS_S(7);
 #undef KVS_S
     };
-    auto issue_dp = [&](int slot) {  // dP = dO V^T into [128,256)
-      const uint64_t dv_k = desc_kmajor_sw128(smem_addr(smem + OFFQ_V + slot * TILE_BYTES));
+    auto issue_dp = [&](int sl) {  // dP = dO V^T into [128,256)
+      const uint64_t dv_k = desc_kmajor_sw128(smem_addr(smem + OFFQ_SLOT + sl * TILE_BYTES));
       const uint32_t d = tmem + 128;
 #define KVS_DP(kk) umma_bf16_warp_at<kq_step(kk), kq_step(kk)>(d, ddo_, dv_k, ID_K, kk > 0)
       KVS_DP(0); KVS_DP(1); KVS_DP(2); KVS_DP(3); KVS_DP(4); KVS_DP(5); KVS_DP(6); KVS_DP(7);
 #undef KVS_DP
     };
     bool ok = wait(&bar[Q_QFULL], 0);
-    if (ok) ok = wait(&bar[Q_KFULL0], 0);
+    if (ok) ok = wait(&bar[Q_FULL0 + slot_a(0)], 0);
     if (ok) {
       tc_fence_after();
-      issue_s(0);
+      issue_s(slot_a(0));
       umma_commit_warp(&bar[Q_SFULL]);
-      issue_dp(0);
+      ok = wait(&bar[Q_FULL0 + slot_b(0)], 0);
+    }
+    if (ok) {
+      tc_fence_after();
+      issue_dp(slot_b(0));
+      umma_commit_warp(&bar[Q_EMPTY0 + slot_b(0)]);
       umma_commit_warp(&bar[Q_DPFULL]);
     }
     for (int k = 0; ok && k < n; ++k) {
-      const int slot = k & 1;
       const bool more = k + 1 < n;
-      ok = wait(&bar[Q_PFULL], k & 1);
-      if (!ok) break;
+      const int ph1 = ((k + 1) >> 1) & 1;
       if (more) {
-        ok = wait(&bar[Q_KFULL0 + (slot ^ 1)], ((k + 1) >> 1) & 1);
+        ok = wait(&bar[Q_SREAD], k & 1);
+        if (ok) ok = wait(&bar[Q_FULL0 + slot_a(k + 1)], ph1);
         if (!ok) break;
         tc_fence_after();
-        issue_s(slot ^ 1);
+        issue_s(slot_a(k + 1));
         umma_commit_warp(&bar[Q_SFULL]);
       }
       ok = wait(&bar[Q_DSFULL], k & 1);
       if (!ok) break;
       tc_fence_after();
       {
-        const uint64_t dk_mn = desc_mnmajor_sw128(smem_addr(smem + OFFQ_K + slot * TILE_BYTES), HALF_BYTES);
+        const uint64_t dk_mn =
+            desc_mnmajor_sw128(smem_addr(smem + OFFQ_SLOT + slot_a(k) * TILE_BYTES), HALF_BYTES);
         const uint32_t d = tmem + 256, a = tmem + 384;
         const uint32_t acc = k > 0;
 #define KVS_DQ(kk) umma_bf16_tmem_a_warp_at<kk * 8, mn_step(kk)>(d, a, dk_mn, ID_MN, (kk > 0) || acc)
         KVS_DQ(0); KVS_DQ(1); KVS_DQ(2); KVS_DQ(3); KVS_DQ(4); KVS_DQ(5); KVS_DQ(6); KVS_DQ(7);
 #undef KVS_DQ
       }
-      umma_commit_warp(&bar[Q_KEMPTY0 + slot]);
+      umma_commit_warp(&bar[Q_EMPTY0 + slot_a(k)]);
       if (more) {
-        issue_dp(slot ^ 1);
+        ok = wait(&bar[Q_FULL0 + slot_b(k + 1)], ph1);
+        if (!ok) break;
+        tc_fence_after();
+        issue_dp(slot_b(k + 1));
+        umma_commit_warp(&bar[Q_EMPTY0 + slot_b(k + 1)]);
         umma_commit_warp(&bar[Q_DPFULL]);
       }
     }
@@ -1454,92 +1515,82 @@ replay_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     mbar_wait(&bar[Q_FINAL], 0, nullptr);
     __syncwarp();
   } else {
-    // ------------------------------------------------ softmax: query row r, key columns [cb, cb+64)
+    // ------------------------------------------------ softmax: query row r, key columns [cb, cb+32)
     const int grp = (warp - 2) >> 2;
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
     const int t = t0 + r;
-    const int cb = 64 * grp;
+    const int cb = GCOLS * grp;
     const bool real = t < L;
     const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16);
     const float sl2 = p.scale_log2;
     const int64_t vrow = ((int64_t)b * p.Hq + h) * p.T_pad + t;
-    const float lse2 = t < p.T ? p.lse[vrow] : 0.f;
-    const float drow = t < p.T ? p.dvec[vrow] : 0.f;
+    const float nlse = t < p.T ? p.nlse[vrow] : 0.f;
+    const float nd = t < p.T ? p.nd[vrow] : 0.f;
     bool ok = true;
     for (int k = 0; k < n; ++k) {
-      const int slot = k & 1;
       const int j = list[k] & 0x7fff;
       const bool masked = (list[k] >> 15) & 1;
       ok = mbar_wait_fast(&bar[Q_SFULL], k & 1, abort_flag);
-      if (ok) ok = mbar_wait_fast(&bar[Q_KFULL0 + slot], (k >> 1) & 1, abort_flag);
+      if (ok) ok = mbar_wait_fast(&bar[Q_FULL0 + slot_a(k)], (k >> 1) & 1, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      // visibility bits of this thread's 64 keys (all set for an unmasked tile)
-      uint32_t bits[2] = {0xffffffffu, 0xffffffffu};
-      if (masked) {
-        const int lim = t - j * BN;
-        const int4* E4 = reinterpret_cast<const int4*>(smem + OFFQ_E + slot * E_BYTES) + cb / 4;
-#pragma unroll
-        for (int w = 0; w < 2; ++w) {
-          uint32_t bw = 0;
-#pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const int4 e = E4[w * 8 + q];
-            const int ev[4] = {e.x, e.y, e.z, e.w};
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const int i = cb + 32 * w + 4 * q + u;
-              const bool vis = (i <= lim) && (real ? (t < ev[u]) : (i >= lim));
-              bw |= (vis ? 1u : 0u) << (4 * q + u);
-            }
-          }
-          bits[w] = (t < p.T) ? bw : 0u;
-        }
-      }
       // phase A: P over the visible keys; S may be overwritten as soon as it is in registers
-      float pf[64];
+      float pf[GCOLS];
       {
-        uint32_t sv[64];
-        tmem_ld32(tl + cb, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-        tmem_ld32(tl + cb + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+        uint32_t sv[32];
+        tmem_ld32(tl + cb, sv);
         tmem_wait_ld();
         tc_fence_before();
-        mbar_arrive(&bar[Q_PFULL]);
+        warp_arrive(&bar[Q_SREAD]);
 #pragma unroll
-        for (int e = 0; e < 64; ++e) pf[e] = ex2_approx(fmaf(__uint_as_float(sv[e]), sl2, -lse2));
+        for (int e = 0; e < GCOLS; ++e) pf[e] = ex2_approx(fmaf(__uint_as_float(sv[e]), sl2, nlse));
       }
+      // visibility bits of this thread's 32 keys (all set for an unmasked tile)
+      uint32_t bits = 0xffffffffu;
       if (masked) {
+        const int lim = t - j * BN;
+        const int4* E4 = reinterpret_cast<const int4*>(smem + OFFQ_E + (k & 3) * E_BYTES) + cb / 4;
+        uint32_t bw = 0;
 #pragma unroll
-        for (int e = 0; e < 64; ++e) pf[e] = ((bits[e >> 5] >> (e & 31)) & 1) ? pf[e] : 0.f;
+        for (int q = 0; q < 8; ++q) {
+          const int4 e = E4[q];
+          const int ev[4] = {e.x, e.y, e.z, e.w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int i = cb + 4 * q + u;
+            const bool vis = (i <= lim) && (real ? (t < ev[u]) : (i >= lim));
+            bw |= (vis ? 1u : 0u) << (4 * q + u);
+          }
+        }
+        bits = (t < p.T) ? bw : 0u;
+#pragma unroll
+        for (int e = 0; e < GCOLS; ++e) pf[e] = ((bits >> e) & 1) ? pf[e] : 0.f;
       }
       // phase B: dS = P (dP - D)
       ok = __all_sync(0xffffffffu, mbar_wait_fast(&bar[Q_DPFULL], k & 1, abort_flag));
       if (!ok) break;
       tc_fence_after();
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
+      uint32_t dk[GCOLS / 2];
+      {
         uint32_t dp[32];
-        tmem_ld32(tl + 128 + cb + 32 * c, dp);
+        tmem_ld32(tl + 128 + cb, dp);
         tmem_wait_ld();
-        uint32_t dk[16];
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          float dsv[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) dsv[u] = pf[32 * c + e + u] * (__uint_as_float(dp[e + u]) - drow);
+        for (int e = 0; e < GCOLS; e += 2) {
+          float d0 = pf[e] * (__uint_as_float(dp[e]) + nd), d1 = pf[e + 1] * (__uint_as_float(dp[e + 1]) + nd);
           if (masked) {
-#pragma unroll
-            for (int u = 0; u < 2; ++u) dsv[u] = ((bits[c] >> (e + u)) & 1) ? dsv[u] : 0.f;
+            d0 = ((bits >> e) & 1) ? d0 : 0.f;
+            d1 = ((bits >> (e + 1)) & 1) ? d1 : 0.f;
           }
-          dk[e >> 1] = pack2(dsv[0], dsv[1]);
+          dk[e >> 1] = pack2(d0, d1);
         }
-        tmem_st16(tl + 384 + 32 * grp + 16 * c, dk);
       }
+      tmem_st16(tl + 384 + (GCOLS / 2) * grp, dk);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&bar[Q_DSFULL]);
+      warp_arrive(&bar[Q_DSFULL]);
     }
     if (ok) ok = mbar_wait(&bar[Q_FINAL], 0, abort_flag);
     ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below is warp-collective
@@ -1551,7 +1602,7 @@ replay_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       __nv_bfloat16* dst = p.dq + (((int64_t)b * p.T + t) * p.Hq + h) * HD + cb;
       const float mul = p.scale;
 #pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
+      for (int c = 0; c < GCOLS / 32; ++c) {
         uint32_t o[32];
         __syncwarp();
         tmem_ld32(tl + 256 + cb + 32 * c, o);
@@ -1574,7 +1625,6 @@ replay_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     tmem_dealloc(tmem, 512);
   }
 }
-
 
 // per-(stream, key tile) min / max of evicted_at and the padded int32 copy
 __global__ void replay_prepass_kernel(const int64_t* __restrict__ ev, int T, int T_pad, int n_kt,
@@ -1843,75 +1893,98 @@ int kvs_replay_tc_launch(const kvs_replay_args* a, cudaStream_t st) {
 
 size_t kvs_replay_tc_backward_scratch(int B, int T, int Hq) {
   const int T_pad = (T + BN - 1) / BN * BN;
-  return replay_scratch_layout(B, T, nullptr, nullptr) + align_up((size_t)B * Hq * T_pad * 4, 256);
+  return replay_scratch_layout(B, T, nullptr, nullptr) + 2 * align_up((size_t)B * Hq * T_pad * 4, 256);
+}
+
+namespace {
+// Once per device: kernel attributes, a check that the dynamic shared base is 1024-aligned
+// (the backward layouts rely on it) and that one CTA of each kernel fits on an SM.
+// 1 ready, 0 not available (the exact kernels run), < 0 a CUDA error.
+int bwd_device_ready(cudaStream_t st) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return KVS_E_LAUNCH;
+  static std::mutex mu;
+  static int state[64] = {};  // 0 unknown, 1 ready, 2 unsupported
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev >= 64) return 0;
+  if (state[dev] == 0) {
+    if (cudaFuncSetAttribute(reinterpret_cast<const void*>(replay_dkdv_kernel),
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, SMEMB_BYTES) != cudaSuccess ||
+        cudaFuncSetAttribute(reinterpret_cast<const void*>(replay_dq_kernel),
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, SMEMQ_BYTES) != cudaSuccess ||
+        cudaFuncSetAttribute(reinterpret_cast<const void*>(replay_smem_base_kernel),
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, SMEMB_BYTES) != cudaSuccess)
+      return KVS_E_LAUNCH;
+    int nb_dkdv = 0, nb_dq = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb_dkdv, replay_dkdv_kernel, NTB, SMEMB_BYTES) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb_dq, replay_dq_kernel, NTB, SMEMQ_BYTES) != cudaSuccess)
+      return KVS_E_LAUNCH;
+    uint32_t* d_base = nullptr;
+    uint32_t h_base = 1;
+    if (cudaMalloc(&d_base, 4) != cudaSuccess) return KVS_E_LAUNCH;
+    replay_smem_base_kernel<<<1, 32, SMEMB_BYTES, st>>>(d_base);
+    const bool got = cudaGetLastError() == cudaSuccess &&
+                     cudaMemcpyAsync(&h_base, d_base, 4, cudaMemcpyDeviceToHost, st) == cudaSuccess &&
+                     cudaStreamSynchronize(st) == cudaSuccess;
+    cudaFree(d_base);
+    if (!got) return KVS_E_LAUNCH;
+    state[dev] = ((h_base & 1023) == 0 && nb_dkdv >= 1 && nb_dq >= 1) ? 1 : 2;
+  }
+  return state[dev] == 1 ? 1 : 0;
+}
+
+bool bwd_args_covered(const kvs_replay_args* a, const void* dout, const void* dq, const void* dk, const void* dv) {
+  auto al = [](const void* x) { return (reinterpret_cast<uintptr_t>(x) & 15) == 0; };
+  return a->row_lse != nullptr && kvs_replay_tc_supported(a) && al(a->row_lse) && al(a->scratch) && al(dout) &&
+         al(dq) && al(dk) && al(dv);
+}
+}  // namespace
+
+// 1 when kvs_replay_attention_backward would run the tensor-core kernels for these arguments
+// (the gradient pointers are not known here and assumed 16-byte aligned), 0 for the exact ones.
+int kvs_replay_tc_backward_path(const kvs_replay_args* a, cudaStream_t st) {
+  if (!bwd_args_covered(a, a->q, a->q, a->k, a->v)) return 0;
+  const int ready = bwd_device_ready(st);
+  return ready;
 }
 
 // Tensor-core backward (bf16, head_dim 128, the forward's row_lse given).  Returns
-// KVS_E_UNSUPPORTED when the shape or dtype is not covered (the caller then runs the exact kernels).
+// KVS_E_UNSUPPORTED when the shape, alignment or device is not covered (the caller then runs
+// the exact kernels).
 int kvs_replay_tc_backward(const kvs_replay_args* a, const void* dout, void* dq, void* dk, void* dv,
                            cudaStream_t st) {
-  if (!a->row_lse || !kvs_replay_tc_supported(a) || (reinterpret_cast<uintptr_t>(a->row_lse) & 15))
-    return KVS_E_UNSUPPORTED;
-  if ((reinterpret_cast<uintptr_t>(a->scratch) & 15) || (reinterpret_cast<uintptr_t>(dout) & 15) ||
-      (reinterpret_cast<uintptr_t>(dq) & 15) ||
-      (reinterpret_cast<uintptr_t>(dk) & 15) || (reinterpret_cast<uintptr_t>(dv) & 15))
-    return KVS_E_UNSUPPORTED;
+  if (!bwd_args_covered(a, dout, dq, dk, dv)) return KVS_E_UNSUPPORTED;
   const int T = a->seq_len, B = a->batch;
   if (!a->scratch || a->scratch_bytes < kvs_replay_tc_backward_scratch(B, T, a->n_heads)) return KVS_E_SCRATCH;
   ReplayScratch s;
   const size_t off = replay_scratch_layout(B, T, a->scratch, &s);
-  float* dvec = reinterpret_cast<float*>(static_cast<uint8_t*>(a->scratch) + off);
   const int T_pad = (T + BN - 1) / BN * BN, n_kt = T_pad / BN;
+  float* nlse = reinterpret_cast<float*>(static_cast<uint8_t*>(a->scratch) + off);
+  float* nd = reinterpret_cast<float*>(static_cast<uint8_t*>(a->scratch) + off +
+                                       align_up((size_t)B * a->n_heads * T_pad * 4, 256));
   CUtensorMap mq, mk, mv, mdo;
   if (!make_map(&mq, a->q, HD, a->n_heads, (uint64_t)B * T) || !make_map(&mk, a->k, HD, a->n_kv_heads, (uint64_t)B * T) ||
       !make_map(&mv, a->v, HD, a->n_kv_heads, (uint64_t)B * T) || !make_map(&mdo, dout, HD, a->n_heads, (uint64_t)B * T))
     return KVS_E_UNSUPPORTED;
-  {
-    // once per device: kernel attributes, and a check that the dynamic shared base is
-    // 1024-aligned (the dK/dV layout relies on it; otherwise the exact kernels run)
-    int dev = 0;
-    cudaGetDevice(&dev);
-    static std::mutex mu;
-    static int state[64] = {};  // 0 unknown, 1 ready, 2 unsupported
-    std::lock_guard<std::mutex> lock(mu);
-    if (dev >= 64) return KVS_E_UNSUPPORTED;
-    if (state[dev] == 0) {
-      if (cudaFuncSetAttribute(reinterpret_cast<const void*>(replay_dkdv_kernel),
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, SMEMB_BYTES) != cudaSuccess ||
-          cudaFuncSetAttribute(reinterpret_cast<const void*>(replay_dq_kernel),
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, SMEMQ_BYTES) != cudaSuccess ||
-          cudaFuncSetAttribute(reinterpret_cast<const void*>(replay_smem_base_kernel),
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, SMEMB_BYTES) != cudaSuccess)
-        return KVS_E_LAUNCH;
-      uint32_t* d_base = nullptr;
-      uint32_t h_base = 1;
-      if (cudaMalloc(&d_base, 4) != cudaSuccess) return KVS_E_LAUNCH;
-      replay_smem_base_kernel<<<1, 32, SMEMB_BYTES, st>>>(d_base);
-      const bool got = cudaGetLastError() == cudaSuccess &&
-                       cudaMemcpyAsync(&h_base, d_base, 4, cudaMemcpyDeviceToHost, st) == cudaSuccess &&
-                       cudaStreamSynchronize(st) == cudaSuccess;
-      cudaFree(d_base);
-      if (!got) return KVS_E_LAUNCH;
-      state[dev] = (h_base & 1023) == 0 ? 1 : 2;
-    }
-    if (state[dev] != 1) return KVS_E_UNSUPPORTED;
-  }
+  const int ready = bwd_device_ready(st);
+  if (ready < 0) return ready;
+  if (ready == 0) return KVS_E_UNSUPPORTED;
   if (cudaMemsetAsync(s.error, 0, 4, st) != cudaSuccess) return KVS_E_LAUNCH;
   replay_prepass_kernel<<<dim3(n_kt, B), BN, 0, st>>>(a->evicted_at, T, T_pad, n_kt, s.e32, s.tmin, s.tmax);
   int rc = launch_rc();
   if (rc) return rc;
   const int64_t rows = (int64_t)B * T * a->n_heads;
   replay_rowdot_kernel<<<(unsigned)((rows + 3) / 4), 128, 0, st>>>(static_cast<const __nv_bfloat16*>(dout),
-                                                                    static_cast<const __nv_bfloat16*>(a->out), dvec,
-                                                                    B, T, T_pad, a->n_heads);
+                                                                    static_cast<const __nv_bfloat16*>(a->out),
+                                                                    a->row_lse, nlse, nd, B, T, T_pad, a->n_heads);
   if ((rc = launch_rc())) return rc;
   BwdParams p;
   p.e32 = s.e32;
   p.tile_min = s.tmin;
   p.tile_max = s.tmax;
   p.lengths = a->lengths;
-  p.lse = a->row_lse;
-  p.dvec = dvec;
+  p.nlse = nlse;
+  p.nd = nd;
   p.dq = static_cast<__nv_bfloat16*>(dq);
   p.dk = static_cast<__nv_bfloat16*>(dk);
   p.dv = static_cast<__nv_bfloat16*>(dv);

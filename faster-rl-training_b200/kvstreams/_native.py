@@ -159,6 +159,7 @@ SIGNATURES = {
     "kvs_replay_attention": (C.c_int, [_P, _P]),
     "kvs_replay_backward_scratch_bytes": (_Z, [_I, _I, _I, _I]),
     "kvs_replay_attention_backward": (C.c_int, [_P, _P, _P, _P, _P, _P]),
+    "kvs_replay_backward_path": (C.c_int, [_P, _P]),
     "kvs_selftest_umma": (C.c_int, [_P, _P, _P, _I, _P, _P]),
 }
 

@@ -118,11 +118,12 @@ def _lse_ptr(row_lse: Optional[torch.Tensor], B: int, Hq: int, T: int):
 
 def replay_attention_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, evicted_at: torch.Tensor,
                               lengths: torch.Tensor, scale: float, out: torch.Tensor, grad_out: torch.Tensor,
-                              row_lse: Optional[torch.Tensor] = None, force_exact: bool = False):
+                              row_lse: Optional[torch.Tensor] = None, force_exact: bool = False,
+                              report_path: Optional[list] = None):
     """Gradients (dq, dk, dv) of :func:`replay_attention` (q and k rotated, ``out`` its
     output) for the upstream gradient ``grad_out``.  With the forward's ``row_lse``, bf16
     and head_dim 128 run the tcgen05 kernels; otherwise (or ``force_exact``) the exact
-    kernels."""
+    kernels.  ``report_path`` (a list) receives 1 when the tcgen05 kernels ran, 0 otherwise."""
     _check_cuda(q, k, v, evicted_at, lengths)
     B, T, Hq, D = q.shape
     Hkv = k.shape[2]
@@ -140,6 +141,8 @@ def replay_attention_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                         scratch_bytes=scratch.numel(), batch=B, seq_len=T, n_heads=Hq, n_kv_heads=Hkv, head_dim=D,
                         dtype=code, scale=float(scale), flags=1 if force_exact else 0,
                         row_lse=_lse_ptr(row_lse, B, Hq, T))
+    if report_path is not None:
+        report_path.append(int(lib.kvs_replay_backward_path(C.byref(a), N.stream_ptr(q.device))))
     N.check(lib.kvs_replay_attention_backward(C.byref(a), g.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
                                               N.stream_ptr(q.device)), "kvs_replay_attention_backward")
     return dq, dk, dv

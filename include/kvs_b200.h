@@ -303,6 +303,10 @@ int kvs_replay_attention(const kvs_replay_args* a, kvs_stream_t stream);
 size_t kvs_replay_backward_scratch_bytes(int32_t batch, int32_t seq_len, int32_t n_heads, int32_t dtype);
 int kvs_replay_attention_backward(const kvs_replay_args* a, const void* dout, void* dq, void* dk, void* dv,
                                   kvs_stream_t stream);
+/* Which kernels kvs_replay_attention_backward runs for these arguments: 1 the tensor-core
+ * ones, 0 the exact ones, negative a CUDA error (the first call on a device checks, once and
+ * synchronously, that the tensor-core kernels fit it; no reference counterpart). */
+int kvs_replay_backward_path(const kvs_replay_args* a, kvs_stream_t stream);
 
 /* Self-test of the tcgen05 path (no reference counterpart): c[128][128] f32 =
  * a[128][128] (bf16 row-major) x B, with B given as bt[128 n][128 k] (mode bit 0 = 0,

@@ -184,8 +184,10 @@ def test_tc_backward_matches_dense_autograd(B, T, Hq, Hkv, lengths, turn):
     scale = 128 ** -0.5
     lse = ops.row_lse_buffer(B, Hq, T, q.device)
     out = ops.replay_attention(q, k, v, ev, ln, scale, row_lse=lse)
-    tc = ops.replay_attention_backward(q, k, v, ev, ln, scale, out, go, row_lse=lse)
-    exact = ops.replay_attention_backward(q, k, v, ev, ln, scale, out, go, force_exact=True)
+    path = []
+    tc = ops.replay_attention_backward(q, k, v, ev, ln, scale, out, go, row_lse=lse, report_path=path)
+    exact = ops.replay_attention_backward(q, k, v, ev, ln, scale, out, go, force_exact=True, report_path=path)
+    assert path == [1, 0], path  # the tensor-core kernels ran, then the exact ones
     qr, kr, vr = (x.detach().double().requires_grad_() for x in (q, k, v))
     mask = _dense_mask(ev, ln.cpu(), T).cuda()
     ref = _dense_attention(qr, kr, vr, mask, scale)
