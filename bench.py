@@ -315,6 +315,7 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
         secondary = compaction_bench(dev, args, rank)
         secondary["replay_attention"] = replay_bench(dev, args, rank)
         secondary["replay_backward"] = replay_backward_bench(dev, args, rank)
+        secondary["compaction_policy"] = compaction_policy_bench(dev, args, rank)
         secondary["rollout"] = rollout_bench(dev, args, rank)
         secondary["prefill"] = prefill_bench(dev, args, rank)
         secondary["replay_model"] = replay_model_bench(dev, args, rank)
@@ -410,6 +411,89 @@ def compaction_bench(dev, args, rank: int) -> dict:
                                      "streams_per_s": len(ev.evict_seqs) / (ms * 1e-3),
                                      "live_tokens": int(blocks * bs * 256)}
     return out
+
+
+def compaction_policy_bench(dev, args, rank: int) -> dict:
+    """One compaction round of config 5 (64 rollouts over the 8192-token budget, Markovian
+    keep_last=1, 16-token blocks): decide and evict for every rollout.  Host path as the
+    engine's default (the reference policy in Python per rollout, one batched eviction, the
+    evicted spans read back, events and segment marks updated): wall time per round.  Device
+    path (kvs_compact: plan, eviction and bookkeeping kernels, no round trip): host time to
+    launch and GPU time by CUDA events.  Cache state restored between rounds."""
+    import torch
+
+    from kvstreams.compaction.device import DeviceCompaction
+    from kvstreams.compaction.policies import MarkovianPolicy
+    from kvstreams.compaction.segments import Segment
+    from kvstreams.paged_cache import PagedKVCache
+
+    rng = np.random.default_rng(rank)
+    n, budget, bs = 64, 8192, 16
+    cache = PagedKVCache(1, 1, 2, block_size=bs, num_blocks=n * 1024, dtype=torch.bfloat16, device=dev,
+                         max_seqs=n, max_blocks_per_seq=1024)
+    policy = MarkovianPolicy(keep_last=1)
+    segs, lens, needs = [], [], []
+    for s in range(n):
+        cache.add_sequence(s)
+        seg = [Segment(0, "prompt", 0, 64, protected=True)]
+        pos = 64
+        while pos < budget - 256:
+            ln = int(rng.integers(128, 1024)) // bs * bs
+            seg.append(Segment(len(seg), "turn", pos, pos + ln))
+            pos += ln
+        cache.append_slots_batch([s], torch.arange(pos, dtype=torch.long), [pos])
+        segs.append(seg)
+        lens.append(pos)
+        needs.append(int(rng.integers(512, 1024)))
+    dc = DeviceCompaction(cache, policy, budget)
+    snap = cache.snapshot_state()
+    host_ms, launch_ms, gpu_ms, evicted = [], [], [], 0
+    for i in range(args.warmup + args.steps):
+        # host path
+        cache.restore_state(snap)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        todo, plans = [], []
+        for s in range(n):
+            required = lens[s] + needs[s]
+            if required > budget:
+                plan = policy.plan(segs[s], lens[s], budget, required)
+                if plan.spans:
+                    todo.append(s)
+                    plans.append(plan)
+        ev = cache.evict_positions_batch(todo, [pl.spans for pl in plans])
+        for s, e in zip(todo, ev):  # the engine's per-rollout bookkeeping
+            for seg in segs[s]:
+                covered = sum(max(0, min(seg.end, b) - max(seg.start, a)) for a, b in e)
+                _ = covered >= seg.length
+        t1 = time.perf_counter()
+        evicted = sum(b - a for e in ev for a, b in e)
+        # device path (segment tables uploaded before the timed call)
+        cache.restore_state(snap)
+        for s in range(n):
+            dc.reset_slot(cache.slot(s))
+            for seg in segs[s]:
+                dc.add_segment(cache.slot(s), seg)
+        dc._flush()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t2 = time.perf_counter()
+        a.record()
+        dc.compact([cache.slot(s) for s in range(n)], [0] * n, needs, lens)
+        b.record()
+        t3 = time.perf_counter()
+        torch.cuda.synchronize()
+        if i >= args.warmup:
+            host_ms.append((t1 - t0) * 1e3)
+            launch_ms.append((t3 - t2) * 1e3)
+            gpu_ms.append(a.elapsed_time(b))
+    dev_evicted = sum(sum(e.num_evicted for e in d["events"]) for d in dc.read([cache.slot(s) for s in range(n)]))
+    return {"workload": "64 rollouts over an 8192-token budget, ~12 turns each, Markovian keep_last=1, bs 16",
+            "host_policy_ms_per_round": statistics.median(host_ms),
+            "device_policy_launch_ms_per_round": statistics.median(launch_ms),
+            "device_policy_gpu_ms_per_round": statistics.median(gpu_ms),
+            "evicted_tokens_per_round": evicted, "device_evicted_tokens_per_round": dev_evicted,
+            "kernels": "compact_live + compact_plan + evict_mark + evict_apply + compact_commit"}
 
 
 def rollout_bench(dev, args, rank: int) -> dict:
@@ -708,6 +792,8 @@ def main() -> int:
     ap.add_argument("--replay-only", action="store_true", help="only the replay attention measurement")
     ap.add_argument("--replay-bwd-b", type=int, default=4)
     ap.add_argument("--replay-bwd-only", action="store_true", help="only the replay backward measurement")
+    ap.add_argument("--compaction-policy-only", action="store_true",
+                    help="only the host vs device compaction-round measurement")
     ap.add_argument("--rollout-streams", type=int, default=64)
     ap.add_argument("--rollout-layers", type=int, default=32)
     ap.add_argument("--rollout-warmup", type=int, default=20)
@@ -745,6 +831,11 @@ def main() -> int:
             r = replay_bench(torch.device("cuda", local_rank), args, rank)
             if rank == 0:
                 print(json.dumps({"replay_attention": r}), flush=True)
+        elif args.compaction_policy_only:
+            torch.cuda.set_device(local_rank)
+            r = compaction_policy_bench(torch.device("cuda", local_rank), args, rank)
+            if rank == 0:
+                print(json.dumps({"compaction_policy": r}), flush=True)
         elif args.replay_bwd_only:
             torch.cuda.set_device(local_rank)
             r = replay_backward_bench(torch.device("cuda", local_rank), args, rank)

@@ -324,6 +324,7 @@ KVS_API size_t kvs_abi_struct_size(int which) {
     case 1: return sizeof(kvs_batch);
     case 2: return sizeof(kvs_decode_args);
     case 3: return sizeof(kvs_replay_args);
+    case 4: return sizeof(kvs_segments);
   }
   return 0;
 }

@@ -35,6 +35,11 @@ ST_SPAN_CAPACITY = 10
 ST_OWNER = 11
 ST_KERNEL_TIMEOUT = 12
 ST_SEQ_TOO_LONG = 13
+ST_LOG_CAPACITY = 14
+
+# device compaction (kvs_segments / kvs_compact)
+POLICY_CODES = {"keep_recent": 0, "markovian": 1, "summary": 2, "token_window": 3}
+EV_FIELDS = 9  # KVS_EV_TIME .. KVS_EV_SEG_OFFSET
 
 RC_NAMES = {-1: "bad argument", -2: "unsupported shape/dtype", -3: "CUDA launch error", -4: "scratch too small",
             -5: "request exceeds the built-in scratch of a no-alloc entry point"}
@@ -135,6 +140,28 @@ _I = C.c_int32
 _Z = C.c_size_t
 
 # name -> (restype, argtypes); every symbol of include/kvs_b200.h
+class KvsSegments(C.Structure):
+    _fields_ = [
+        ("start", C.c_void_p),
+        ("end", C.c_void_p),
+        ("evicted_at", C.c_void_p),
+        ("flags", C.c_void_p),
+        ("count", C.c_void_p),
+        ("ev_count", C.c_void_p),
+        ("ev_meta", C.c_void_p),
+        ("ev_spans", C.c_void_p),
+        ("ev_segs", C.c_void_p),
+        ("ev_fill", C.c_void_p),
+        ("stats", C.c_void_p),
+        ("max_seqs", C.c_int32),
+        ("max_segs", C.c_int32),
+        ("max_events", C.c_int32),
+        ("span_pool", C.c_int32),
+        ("seg_pool", C.c_int32),
+        ("reserved", C.c_int32),
+    ]
+
+
 SIGNATURES = {
     "kvs_abi_struct_size": (_Z, [C.c_int]),
     "kvs_abi_version": (C.c_int, []),
@@ -160,10 +187,13 @@ SIGNATURES = {
     "kvs_replay_backward_scratch_bytes": (_Z, [_I, _I, _I, _I]),
     "kvs_replay_attention_backward": (C.c_int, [_P, _P, _P, _P, _P, _P]),
     "kvs_replay_backward_path": (C.c_int, [_P, _P]),
+    "kvs_compact_plan": (C.c_int, [_P, _P, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "kvs_compact_scratch_bytes": (_Z, [_P, _P, _I]),
+    "kvs_compact": (C.c_int, [_P, _P, _P, _I, _I, _I, _P, _P, _Z, _P]),
     "kvs_selftest_umma": (C.c_int, [_P, _P, _P, _I, _P, _P]),
 }
 
-STRUCTS = {0: KvsCache, 1: KvsBatch, 2: KvsDecodeArgs, 3: KvsReplayArgs}
+STRUCTS = {0: KvsCache, 1: KvsBatch, 2: KvsDecodeArgs, 3: KvsReplayArgs, 4: KvsSegments}
 
 _lock = threading.Lock()
 _lib: C.CDLL | None = None

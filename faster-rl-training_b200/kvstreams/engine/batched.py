@@ -13,7 +13,10 @@ whole batch of rollouts sharing one :class:`~kvstreams.paged_cache.PagedKVCache`
   check, as in the reference);
 * compaction decisions are the reference policies' (``policy.plan`` on the rollout's segments,
   same ``required = live + incoming + reserve`` test), executed for all rollouts that need one
-  in a single batched in-place eviction (``evict_positions_batch``);
+  in a single batched in-place eviction (``evict_positions_batch``, one device round trip for
+  its result); with ``device_policy=True`` the decision, the eviction and the bookkeeping all
+  run on the device (:class:`~kvstreams.compaction.device.DeviceCompaction`, no round trip)
+  and segments, compaction log and stats are read back once, when the rollouts end;
 * sampling, sampled tokens and their log-probs stay on the device; the host only tracks
   lengths, positions and segments, so a step needs no device round trip.
 
@@ -98,7 +101,7 @@ class BatchedKVStreams:
 
     def __init__(self, model, cache, policy: CompactionPolicy, context_budget: int = 8192, pad_to_block: bool = True,
                  pad_id: int = 0, temperature: float = 1.0, greedy: bool = False, seed: int = 0,
-                 cuda_graphs: bool = False) -> None:
+                 cuda_graphs: bool = False, device_policy: bool = False) -> None:
         self.model = model
         self.cache = cache
         self.policy = policy
@@ -113,6 +116,9 @@ class BatchedKVStreams:
         # decode steps replayed as CUDA graphs (one per batch size), see engine/graphs.py
         self.cuda_graphs = cuda_graphs
         self._graphs = None
+        # compaction planned and applied on the device (compaction/device.py)
+        self.device_policy = device_policy
+        self._dev = None
 
     # ------------------------------------------------------------------ helpers
     def _reserve(self, run: _Run) -> int:
@@ -122,6 +128,11 @@ class BatchedKVStreams:
 
     def _maybe_compact(self, runs: Sequence[_Run]) -> None:
         """engine/base.py:260-285 for every rollout about to start a turn, one batched eviction."""
+        if self.device_policy:
+            self._dev.compact([self.cache.slot(r.seq_id) for r in runs], [len(r.pending) for r in runs],
+                              [len(r.ep.observations[r.turn + 1]) + self._reserve(r) for r in runs],
+                              [r.n_tokens for r in runs])
+            return
         todo, plans = [], []
         for run in runs:
             incoming = len(run.ep.observations[run.turn + 1])
@@ -133,9 +144,9 @@ class BatchedKVStreams:
             if plan.spans:
                 todo.append(run)
                 plans.append(plan)
-        if not todo:
-            return
-        evicted = self.cache.evict_positions_batch([r.seq_id for r in todo], [p.spans for p in plans])
+        # (no early return when nothing is evicted: the overflow count below still applies,
+        # engine/base.py:274-275)
+        evicted = self.cache.evict_positions_batch([r.seq_id for r in todo], [p.spans for p in plans]) if todo else []
         for run, plan, ev in zip(todo, plans, evicted):
             if not ev:
                 continue
@@ -162,6 +173,22 @@ class BatchedKVStreams:
             live = run.live + len(run.pending)
             if live + len(run.ep.observations[run.turn + 1]) + self._reserve(run) > self.budget:
                 run.stats.budget_overflows += 1
+
+    def _collect_device_compaction(self, runs: Sequence[_Run]) -> None:
+        """Segments' eviction marks, compaction log and stats from the device (one read)."""
+        res = self._dev.read([self.cache.slot(r.seq_id) for r in runs])
+        for r, d in zip(runs, res):
+            for seg, ev_at, part in zip(r.segments, d["evicted_at"], d["partial"]):
+                seg.evicted_at = None if ev_at < 0 else ev_at
+                seg.partially_evicted = part
+            for ev in d["events"]:
+                r.log.append(ev)
+            r.stats.compactions = d["stats"]["compactions"]
+            r.stats.evicted_tokens = d["stats"]["evicted_tokens"]
+            r.stats.budget_overflows = d["stats"]["budget_overflows"]
+            # the live count only drops at compactions: its peak is before one of them or at the end
+            r.stats.peak_live_tokens = max(d["peak_cached"], self.cache.num_tokens(r.seq_id))
+            r.live = self.cache.num_tokens(r.seq_id)
 
     def _sample(self, logits: torch.Tensor, forced: Optional[torch.Tensor]):
         """Next token and its log-prob under temperature (engine/base.py:176-193), on the device."""
@@ -198,6 +225,14 @@ class BatchedKVStreams:
                 run.stats.padding_tokens += len(pads)
                 run.n_tokens += len(pads)
             run.segments.append(Segment(0, "prompt", 0, run.n_tokens, protected=True))
+            if self.device_policy:
+                if self._dev is None:
+                    from ..compaction.device import DeviceCompaction
+
+                    self._dev = DeviceCompaction(self.cache, self.policy, self.budget)
+                slot = self.cache.slot(seq)
+                self._dev.reset_slot(slot)
+                self._dev.add_segment(slot, run.segments[0])
             runs.append(run)
         total_gen = sum(sum(ep.reply_lens) for ep in episodes)
         gen_tok = torch.zeros(max(total_gen, 1), dtype=torch.long, device=dev)
@@ -321,6 +356,8 @@ class BatchedKVStreams:
                     gen_used[r.idx] += 1
                 for r in finishing:
                     r.segments.append(Segment(len(r.segments), "turn", r.turn_start, r.n_tokens))
+                    if self.device_policy:
+                        self._dev.add_segment(self.cache.slot(r.seq_id), r.segments[-1])
                     r.phase = _PREFILL if r.turn + 1 < r.ep.turns else _DONE
             # ---- an iteration without chunks: the decode step alone (a replayed graph)
             elif decoding:
@@ -344,6 +381,8 @@ class BatchedKVStreams:
         # ---- assemble the rollouts (one device-to-host copy)
         toks_h = gen_tok.cpu().numpy()
         logp_h = gen_logp.cpu().numpy()
+        if self.device_policy:
+            self._collect_device_compaction(runs)
         out = []
         for r in runs:
             n = r.n_tokens

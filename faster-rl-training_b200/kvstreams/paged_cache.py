@@ -144,6 +144,7 @@ class PagedKVCache:
         self._alloc_seq_storage(int(max_seqs))
         self._h_top = self.num_blocks
         self._slot_of: dict[int, int] = {}
+        self._stale: set[int] = set()  # slots whose host mirror is a bound (device-side eviction)
         self._scratch = torch.empty(0, dtype=torch.uint8, device=dev)
         self.allocator = BlockAllocator(self)
         with torch.cuda.device(dev):
@@ -255,6 +256,9 @@ class PagedKVCache:
         if code == N.ST_SEQ_TOO_LONG:
             raise RuntimeError(f"sequence in slot {a} has {b} live entries, more than the 32768 the "
                                "tensor-core prefill attends over")
+        if code == N.ST_LOG_CAPACITY:
+            raise RuntimeError(f"device compaction log of slot {a} is full ({b} events, {c} spans): "
+                               "raise DeviceCompaction's max_events / span_pool")
         if code == N.ST_KERNEL_TIMEOUT:
             raise RuntimeError(f"a tensor-core attention kernel timed out waiting (site {a}, CTA {b}); "
                                "its outputs are invalid")
@@ -264,6 +268,12 @@ class PagedKVCache:
         """Wait for queued cache kernels and raise any device-side error they reported."""
         torch.cuda.current_stream(self.device).synchronize()
         self._raise_status()
+
+    def mark_mirror_stale(self, slots: Sequence[int]) -> None:
+        """A device-side eviction ran for these slots without a round trip: their host-mirror
+        lengths and table sizes (and the free count) are now upper / lower bounds.  Allocation
+        checks that fail on the bounds re-read the device state before raising."""
+        self._stale.update(int(s) for s in slots)
 
     def _refresh(self, slots: Sequence[int]) -> None:
         """Re-read lengths / table sizes / free count after a data-dependent kernel."""
@@ -276,6 +286,7 @@ class PagedKVCache:
         self._h_len[list(slots)] = vals[:n]
         self._h_nb[list(slots)] = vals[n : 2 * n]
         self._h_top = int(vals[2 * n])
+        self._stale.difference_update(int(s) for s in slots)
         if vals[2 * n + 1] != 0:
             self._raise_status()
 
@@ -301,6 +312,9 @@ class PagedKVCache:
     def free_sequences_slots(self, slots: Sequence[int]) -> None:
         if not slots:
             return
+        stale = [s for s in slots if s in self._stale]
+        if stale:  # the free count must not be credited with an upper bound of their blocks
+            self._refresh(stale)
         b, keep = self._batch(slots)
         N.check(self._lib.kvs_release(C.byref(self._struct), C.byref(b), None, 1, self._stream()), "kvs_release")
         for s in slots:
@@ -312,7 +326,10 @@ class PagedKVCache:
         return seq_id in self._slot_of
 
     def num_tokens(self, seq_id: int) -> int:
-        return int(self._h_len[self._slot_of[seq_id]])
+        slot = self._slot_of[seq_id]
+        if slot in self._stale:
+            self._refresh([slot])
+        return int(self._h_len[slot])
 
     def slot(self, seq_id: int) -> int:
         return self._slot_of[seq_id]
@@ -351,6 +368,17 @@ class PagedKVCache:
 
     # ------------------------------------------------------------------ writes
     def _check_alloc(self, slots: Sequence[int], counts: Sequence[int]) -> np.ndarray:
+        try:
+            return self._check_alloc_mirror(slots, counts)
+        except OutOfBlocksError:
+            if not self._stale:
+                raise
+            # the mirror is conservative after device-side evictions: re-read, then decide
+            self._refresh(sorted(self._slot_of.values()))
+            self._stale.clear()
+            return self._check_alloc_mirror(slots, counts)
+
+    def _check_alloc_mirror(self, slots: Sequence[int], counts: Sequence[int]) -> np.ndarray:
         bs = self.block_size
         s = np.asarray(slots, dtype=np.int64)
         n = self._h_len[s]
@@ -620,12 +648,13 @@ class PagedKVCache:
         """Device copies of every mutable tensor (restore with :meth:`restore_state`)."""
         names = ("slot_pos", "_tables", "_n_blocks", "_lengths", "_free_stack", "_free_top", "_owner", "_stats")
         return {"dev": {n: getattr(self, n).clone() for n in names},
-                "host": (self._h_len.copy(), self._h_nb.copy(), self._h_top)}
+                "host": (self._h_len.copy(), self._h_nb.copy(), self._h_top, set(self._stale))}
 
     def restore_state(self, snap: dict) -> None:
         for n, t in snap["dev"].items():
             getattr(self, n).copy_(t)
         self._h_len[:], self._h_nb[:], self._h_top = snap["host"][0], snap["host"][1], snap["host"][2]
+        self._stale = set(snap["host"][3])
 
     # ------------------------------------------------------------------ stats
     @property

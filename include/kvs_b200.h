@@ -61,8 +61,9 @@ enum kvs_status {
   KVS_ST_OWNER = 11,           /* block freed by a sequence that does not own it */
   KVS_ST_KERNEL_TIMEOUT = 12,  /* a bounded wait inside a tensor-core kernel expired; its outputs
                                   are invalid (no reference counterpart) */
-  KVS_ST_SEQ_TOO_LONG = 13     /* a sequence is longer than the 32768 entries the tensor-core
+  KVS_ST_SEQ_TOO_LONG = 13,     /* a sequence is longer than the 32768 entries the tensor-core
                                   prefill attends over (no reference counterpart) */
+  KVS_ST_LOG_CAPACITY = 14     /* a device compaction event did not fit the sequence's event log */
 };
 
 /* CacheStats counters (paged_cache.py:70-78), int64 each */
@@ -119,7 +120,7 @@ typedef struct kvs_batch {
 } kvs_batch;
 
 /* size of each public struct as compiled into the library (ABI check):
- * which = 0 kvs_cache, 1 kvs_batch, 2 kvs_decode_args, 3 kvs_replay_args */
+ * which = 0 kvs_cache, 1 kvs_batch, 2 kvs_decode_args, 3 kvs_replay_args, 4 kvs_segments */
 size_t kvs_abi_struct_size(int which);
 int kvs_abi_version(void);
 /* number of SMs of the current device, cached per device (grid sizing) */
@@ -307,6 +308,84 @@ int kvs_replay_attention_backward(const kvs_replay_args* a, const void* dout, vo
  * ones, 0 the exact ones, negative a CUDA error (the first call on a device checks, once and
  * synchronously, that the tensor-core kernels fit it; no reference counterpart). */
 int kvs_replay_backward_path(const kvs_replay_args* a, kvs_stream_t stream);
+
+/* ---------------------------------------------------------------- device-side compaction
+ * The reference decides compaction on the host, per rollout, before each turn
+ * (engine/base.py:260-308 with compaction/policies.py:34-170 over compaction/segments.py).
+ * kvs_compact runs that decision, the in-place eviction and its bookkeeping for a batch of
+ * rollouts on the device, so a rollout loop needs no device round trip per compaction; the
+ * segments, events and stats are read back once, when the rollouts end.  State per sequence
+ * slot, all device arrays (zero-initialised; the caller appends segments as turns end):
+ *   start, end        [max_seqs][max_segs] stream span of each segment
+ *   evicted_at        [max_seqs][max_segs] stream length at the compaction that removed the
+ *                     whole segment, -1 while (at least partly) alive
+ *   flags             [max_seqs][max_segs] bit 0 protected (the prompt), bit 1 partially evicted
+ *   count             [max_seqs] segments in use
+ *   ev_count          [max_seqs] events logged
+ *   ev_meta           [max_seqs][max_events][KVS_EV_FIELDS] (CompactionEvent, events.py:20-40)
+ *   ev_spans          [max_seqs][span_pool][2] requested spans of each event, then evicted ones
+ *   ev_segs           [max_seqs][seg_pool] segment indices chosen by each event
+ *   ev_fill           [max_seqs][2] entries used in ev_spans / ev_segs
+ *   stats             [max_seqs][4] compactions, evicted tokens, budget overflows, 0 */
+typedef struct kvs_segments {
+  int32_t* start;
+  int32_t* end;
+  int32_t* evicted_at;
+  int32_t* flags;
+  int32_t* count;
+  int32_t* ev_count;
+  int32_t* ev_meta;
+  int64_t* ev_spans;
+  int32_t* ev_segs;
+  int32_t* ev_fill;
+  int32_t* stats;
+  int32_t max_seqs;
+  int32_t max_segs;
+  int32_t max_events;
+  int32_t span_pool;
+  int32_t seg_pool;
+  int32_t reserved;
+} kvs_segments;
+
+enum kvs_event_field {
+  KVS_EV_TIME = 0,          /* stream length when the compaction ran */
+  KVS_EV_LIVE_BEFORE = 1,   /* live entries incl. pending tokens (engine/base.py:284) */
+  KVS_EV_LIVE_AFTER = 2,
+  KVS_EV_CACHED_BEFORE = 3, /* cache entries before the eviction (live_before without pending) */
+  KVS_EV_N_REQUESTED = 4,
+  KVS_EV_N_EVICTED = 5,
+  KVS_EV_N_SEGMENTS = 6,
+  KVS_EV_SPAN_OFFSET = 7,   /* first requested span in ev_spans; the evicted ones follow them */
+  KVS_EV_SEG_OFFSET = 8,
+  KVS_EV_FIELDS = 9
+};
+
+enum kvs_policy_code {
+  KVS_POLICY_KEEP_RECENT = 0,  /* KeepRecentTurns(keep_last = param) */
+  KVS_POLICY_MARKOVIAN = 1,    /* MarkovianPolicy(keep_last = param) */
+  KVS_POLICY_SUMMARY = 2,      /* SummaryPolicy's spans (the summary turn itself is the caller's) */
+  KVS_POLICY_TOKEN_WINDOW = 3  /* TokenSlidingWindow(window = param) */
+};
+
+/* CompactionPolicy.plan for every sequence of the batch whose live[i] + need[i] > budget
+ * (engine/base.py:262-267; live incl. pending tokens, need = incoming + reserve), others get no
+ * spans.  Per sequence i: spans[i][max_segs][2] merged sorted spans (merge_spans), n_spans[i];
+ * chosen[i][max_segs] segment indices, n_chosen[i]; cu_spans[num_seqs+1] and span_start /
+ * span_end [num_seqs*max_segs] in kvs_evict_positions' input form. */
+int kvs_compact_plan(const kvs_segments* s, const kvs_batch* b, int32_t policy, int32_t param, int32_t budget,
+                     const int32_t* live, const int32_t* need, int64_t* spans, int32_t* n_spans, int32_t* chosen,
+                     int32_t* n_chosen, int32_t* cu_spans, int64_t* span_start, int64_t* span_end,
+                     kvs_stream_t stream);
+
+/* _maybe_compact + _compact (engine/base.py:260-308) for a batch: step [num_seqs][3] device
+ * int32 = pending tokens, need (incoming + reserve), stream length.  Plans with live = the
+ * cache's live entries + pending, evicts the planned spans (kvs_evict_positions), then for each
+ * sequence whose eviction removed something appends the event, adds to its stats and marks its
+ * segments (evicted_at = stream length when wholly covered, else partially evicted); a sequence
+ * that was over budget and still is counts a budget overflow. */
+size_t kvs_compact_scratch_bytes(const kvs_cache* c, const kvs_segments* s, int32_t num_seqs);
+int kvs_compact(const kvs_cache* c, const kvs_batch* b, const kvs_segments* s, int32_t policy, int32_t param,
+                int32_t budget, const int32_t* step, void* scratch, size_t scratch_bytes, kvs_stream_t stream);
 
 /* Self-test of the tcgen05 path (no reference counterpart): c[128][128] f32 =
  * a[128][128] (bf16 row-major) x B, with B given as bt[128 n][128 k] (mode bit 0 = 0,

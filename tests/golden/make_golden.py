@@ -14,7 +14,9 @@ only) in a process of its own and records, for seeded inputs:
                           KV-streams mask (state dict included);
 * rollouts.npz/json    -- teacher-forced KV-streams rollouts (fp64 test model and
                           the fp32 default model at the repo's CPU bench config),
-                          with their inference and replay log-probs.
+                          with their inference and replay log-probs;
+* policy_plans.json    -- CompactionPolicy.plan (keep_recent, markovian, summary,
+                          token_window) on random segment lists: spans and segments.
 
 The fixtures are committed; this script is only needed to regenerate them.
 """
@@ -307,19 +309,56 @@ def make_rollouts():
     (HERE / "rollouts.json").write_text(json.dumps(meta))
 
 
+def make_policies():
+    from kvstreams.compaction.policies import build_policy
+    from kvstreams.compaction.segments import Segment
+
+    rng = random.Random(11)
+    cases = []
+    for c in range(400):
+        n = rng.randint(1, 40)
+        segs, pos = [], 0
+        for i in range(n):
+            prompt = i == 0 and rng.random() < 0.9
+            length = rng.choice([0, 16, 32]) if rng.random() < 0.1 else rng.randint(1, 400)
+            seg = Segment(i, "prompt" if prompt else "turn", pos, pos + length, protected=prompt)
+            pos += length
+            r = rng.random()
+            if not prompt and i < n - 1 and r < 0.25:
+                seg.evicted_at = pos + rng.randint(0, 500)
+            elif not prompt and i < n - 1 and r < 0.35:
+                seg.partially_evicted = True
+            segs.append(seg)
+        live = sum(s.length for s in segs if s.alive) + rng.randint(0, 64)
+        incoming, reserve = rng.randint(0, 600), rng.randint(1, 400)
+        required = live + incoming + reserve
+        budget = rng.randint(max(1, required // 4), required + 200)
+        name = ["keep_recent", "markovian", "summary", "token_window"][c % 4]
+        param = rng.randint(16, 1024) if name == "token_window" else rng.randint(1, 4)
+        pol = build_policy(name, **({"window": param} if name == "token_window" else {"keep_last": param}))
+        plan = pol.plan(segs, live, budget, required)
+        cases.append({
+            "policy": name, "param": param, "live": live, "budget": budget, "required": required,
+            "segments": [[s.start, s.end, int(s.protected), int(s.alive), int(s.partially_evicted)] for s in segs],
+            "spans": [list(x) for x in plan.spans], "chosen": list(plan.segments),
+        })
+    (HERE / "policy_plans.json").write_text(json.dumps(cases))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--only", default="", help="comma-separated subset: traces,evicted_at,rope,tinylm,rollouts,policies")
     a = ap.parse_args()
     sys.path.insert(0, a.ref)
     import kvstreams  # noqa: F401  (the reference package)
 
     assert Path(kvstreams.__file__).resolve().is_relative_to(Path(a.ref).resolve()), kvstreams.__file__
-    make_traces()
-    make_evicted_at()
-    make_rope()
-    make_tinylm()
-    make_rollouts()
+    steps = {"traces": make_traces, "evicted_at": make_evicted_at, "rope": make_rope, "tinylm": make_tinylm,
+             "rollouts": make_rollouts, "policies": make_policies}
+    for name, fn in steps.items():
+        if not a.only or name in a.only.split(","):
+            fn()
     for p in sorted(HERE.glob("*.*")):
         print(f"{p.name:28s} {p.stat().st_size:>9d} B")
 
