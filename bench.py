@@ -316,6 +316,7 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
         secondary["replay_attention"] = replay_bench(dev, args, rank)
         secondary["replay_backward"] = replay_backward_bench(dev, args, rank)
         secondary["compaction_policy"] = compaction_policy_bench(dev, args, rank)
+        secondary["lm_head_logprobs"] = lm_head_logprobs_bench(dev, args, rank)
         secondary["rollout"] = rollout_bench(dev, args, rank)
         secondary["prefill"] = prefill_bench(dev, args, rank)
         secondary["replay_model"] = replay_model_bench(dev, args, rank)
@@ -494,6 +495,95 @@ def compaction_policy_bench(dev, args, rank: int) -> dict:
             "device_policy_gpu_ms_per_round": statistics.median(gpu_ms),
             "evicted_tokens_per_round": evicted, "device_evicted_tokens_per_round": dev_evicted,
             "kernels": "compact_live + compact_plan + evict_mark + evict_apply + compact_commit"}
+
+
+def lm_head_logprobs_bench(dev, args, rank: int) -> dict:
+    """token_logprobs' lm_head stage for one chunk of config 4 (8192 tokens, d 4096, vocab
+    128256, bf16 weight, float32 logits): forward and forward + backward, the torch chunk
+    (GEMM, logits / T, log_softmax, gather; autograd keeps the log-softmax rows) against the
+    fused chunk (GEMM + kvs_lse_gather; backward recomputes the logits, kvs_lse_gather_backward,
+    two GEMMs).  The torch forward + backward uses bf16 logits cast to float32 (the float32-result
+    GEMM has no autograd derivative).  The kvs_lse_gather kernel alone against the measured HBM bandwidth: it reads
+    each float32 logit once (algorithmic bytes = rows x vocab x 4 + 16 B per row)."""
+    import torch
+
+    from kvstreams import ops
+    from kvstreams.training.logprobs import _LmHeadLogprob
+
+    n, d, V, temp = 8192, 4096, 128256, 1.0
+    g = torch.Generator(device=dev).manual_seed(rank)
+    w = (torch.randn(V, d, generator=g, device=dev) * 0.02).bfloat16()
+    h = torch.randn(n, d, generator=g, device=dev).bfloat16()
+    tgt = torch.randint(0, V, (n,), generator=g, device=dev)
+
+    class _Head:  # the model's lm_head.logits for a standalone weight
+        def logits(self, x):
+            return torch.mm(x, w.t(), out_dtype=torch.float32)
+
+    head = _Head()
+
+    def ev_time(fn, reps=3):
+        ts = []
+        for i in range(2 + reps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            if i >= 2:
+                ts.append(a.elapsed_time(b))
+        return statistics.median(ts)
+
+    def torch_fwd():
+        with torch.no_grad():
+            lp = torch.log_softmax(head.logits(h) / temp, dim=-1)
+            return lp.gather(-1, tgt[:, None]).squeeze(-1)
+
+    def fused_fwd():
+        with torch.no_grad():
+            return ops.lse_gather(head.logits(h), tgt, temp)[0]
+
+    def torch_fb():  # differentiable torch form: bf16 GEMM, float32 log-softmax
+        hh = h.detach().requires_grad_()
+        ww = w.detach().requires_grad_()
+        lp = torch.log_softmax(torch.nn.functional.linear(hh, ww).float() / temp, dim=-1)
+        lp.gather(-1, tgt[:, None]).sum().backward()
+
+    class _HeadW:
+        def __init__(self, ww):
+            self.ww = ww
+
+        def logits(self, x):
+            return torch.mm(x, self.ww.t(), out_dtype=torch.float32)
+
+    def fused_fb():
+        hh = h.detach().requires_grad_()
+        ww = w.detach().requires_grad_()
+        _LmHeadLogprob.apply(hh, ww, tgt, temp, _HeadW(ww)).sum().backward()
+
+    logits = head.logits(h)
+    k_ms = ev_time(lambda: ops.lse_gather(logits, tgt, temp))
+    peaks = _peaks()
+    gbs = (n * V * 4 + n * 16) / (k_ms * 1e-3) / 1e9
+    out = {"workload": "8192 tokens x d 4096 x vocab 128256, bf16 weight, float32 logits",
+           "torch_fwd_ms": ev_time(torch_fwd), "fused_fwd_ms": ev_time(fused_fwd),
+           "lse_gather_kernel_ms": k_ms, "lse_gather_gbs": gbs, "lse_gather_hbm_frac": gbs / peaks["hbm_gbs"],
+           "peak_src": peaks["src"]}
+    del logits
+    torch.cuda.empty_cache()
+    torch.cuda.reset_peak_memory_stats(dev)
+    out["torch_fwd_bwd_ms"] = ev_time(torch_fb, reps=2)
+    out["torch_fwd_bwd_peak_gb"] = torch.cuda.max_memory_allocated(dev) / 1e9
+    torch.cuda.empty_cache()
+    torch.cuda.reset_peak_memory_stats(dev)
+    out["fused_fwd_bwd_ms"] = ev_time(fused_fb, reps=2)
+    out["fused_fwd_bwd_peak_gb"] = torch.cuda.max_memory_allocated(dev) / 1e9
+    # the same outputs
+    a, b = torch_fwd(), fused_fwd()
+    out["max_abs_diff_vs_torch"] = float((a - b).abs().max())
+    del w, h
+    torch.cuda.empty_cache()
+    return out
 
 
 def rollout_bench(dev, args, rank: int) -> dict:
@@ -794,6 +884,7 @@ def main() -> int:
     ap.add_argument("--replay-bwd-only", action="store_true", help="only the replay backward measurement")
     ap.add_argument("--compaction-policy-only", action="store_true",
                     help="only the host vs device compaction-round measurement")
+    ap.add_argument("--logprobs-only", action="store_true", help="only the lm_head log-prob stage measurement")
     ap.add_argument("--rollout-streams", type=int, default=64)
     ap.add_argument("--rollout-layers", type=int, default=32)
     ap.add_argument("--rollout-warmup", type=int, default=20)
@@ -831,6 +922,11 @@ def main() -> int:
             r = replay_bench(torch.device("cuda", local_rank), args, rank)
             if rank == 0:
                 print(json.dumps({"replay_attention": r}), flush=True)
+        elif args.logprobs_only:
+            torch.cuda.set_device(local_rank)
+            r = lm_head_logprobs_bench(torch.device("cuda", local_rank), args, rank)
+            if rank == 0:
+                print(json.dumps({"lm_head_logprobs": r}), flush=True)
         elif args.compaction_policy_only:
             torch.cuda.set_device(local_rank)
             r = compaction_policy_bench(torch.device("cuda", local_rank), args, rank)

@@ -190,6 +190,8 @@ SIGNATURES = {
     "kvs_compact_plan": (C.c_int, [_P, _P, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "kvs_compact_scratch_bytes": (_Z, [_P, _P, _I]),
     "kvs_compact": (C.c_int, [_P, _P, _P, _I, _I, _I, _P, _P, _Z, _P]),
+    "kvs_lse_gather": (C.c_int, [_P, C.c_int64, _I, _I, _P, C.c_double, _I, _P, _P, _P]),
+    "kvs_lse_gather_backward": (C.c_int, [_P, C.c_int64, _I, _I, _P, _P, _P, C.c_double, _I, _P, C.c_int64, _I, _P]),
     "kvs_selftest_umma": (C.c_int, [_P, _P, _P, _I, _P, _P]),
 }
 

@@ -237,3 +237,37 @@ class ReplayMask:
                 "pass a ReplayMask for padded batches"
             )
         return rm
+
+
+def lse_gather(logits: torch.Tensor, targets: torch.Tensor, temperature: float = 1.0):
+    """``(logp, lse)``: ``log_softmax(logits / T)[r, targets[r]]`` and ``logsumexp(logits[r] / T)``
+    for a 2-D float32/float64 CUDA tensor (training/logprobs.py:17-20), one pass per row."""
+    _check_cuda(logits, targets)
+    if logits.dim() != 2 or logits.stride(1) != 1:
+        raise ValueError("logits must be a 2-D tensor with contiguous rows")
+    n, vocab = logits.shape
+    t = targets.to(torch.long).contiguous().reshape(-1)
+    logp = torch.empty(n, dtype=logits.dtype, device=logits.device)
+    lse = torch.empty(n, dtype=logits.dtype, device=logits.device)
+    rc = N.lib().kvs_lse_gather(logits.data_ptr(), logits.stride(0), n, vocab, t.data_ptr(), float(temperature),
+                                N.DTYPE_CODE[logits.dtype], logp.data_ptr(), lse.data_ptr(), N.stream_ptr(logits.device))
+    N.check(rc, "kvs_lse_gather")
+    return logp, lse
+
+
+def lse_gather_backward(logits: torch.Tensor, targets: torch.Tensor, lse: torch.Tensor, grad: torch.Tensor,
+                        temperature: float = 1.0, out_dtype: Optional[torch.dtype] = None,
+                        out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Gradient of :func:`lse_gather`'s logp with respect to the logits for upstream ``grad``,
+    in ``out_dtype`` (default the logits' dtype); ``out`` may be ``logits`` itself."""
+    n, vocab = logits.shape
+    out_dtype = out_dtype or logits.dtype
+    if out is None:
+        out = torch.empty(n, vocab, dtype=out_dtype, device=logits.device)
+    t = targets.to(torch.long).contiguous().reshape(-1)
+    g = grad.to(logits.dtype).contiguous()
+    rc = N.lib().kvs_lse_gather_backward(logits.data_ptr(), logits.stride(0), n, vocab, t.data_ptr(), lse.data_ptr(),
+                                         g.data_ptr(), float(temperature), N.DTYPE_CODE[logits.dtype], out.data_ptr(),
+                                         out.stride(0), N.DTYPE_CODE[out.dtype], N.stream_ptr(logits.device))
+    N.check(rc, "kvs_lse_gather_backward")
+    return out

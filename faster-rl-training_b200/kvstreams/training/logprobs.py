@@ -4,10 +4,46 @@ from __future__ import annotations
 
 import torch
 
+from .. import ops
 from .replay import Batch
 
 # tokens per lm_head chunk: bounds the [chunk, vocab] logits held at once
 _CHUNK_TOKENS = 8192
+
+
+class _LmHeadLogprob(torch.autograd.Function):
+    """One chunk of lm_head -> log_softmax(logits / T) -> gather (logprobs.py:17-20).
+
+    Forward: the lm_head GEMM (cuBLAS; float32 result for half-precision models), then one
+    pass over each logits row (``kvs_lse_gather``).  Only the hidden states and each row's
+    log-sum-exp are kept; backward recomputes the chunk's logits, turns them into
+    dlogits = g (onehot - softmax) / T in place (``kvs_lse_gather_backward``, in the weight's
+    dtype) and runs the two GEMMs of dh and dW."""
+
+    @staticmethod
+    def forward(ctx, h, weight, targets, temperature, model):
+        logits = model.logits(h)
+        if logits.dtype in (torch.bfloat16, torch.float16):
+            logits = logits.float()
+        logp, lse = ops.lse_gather(logits, targets, temperature)
+        ctx.save_for_backward(h, weight, targets, lse)
+        ctx.temperature, ctx.model = temperature, model
+        return logp
+
+    @staticmethod
+    def backward(ctx, g):
+        h, weight, targets, lse = ctx.saved_tensors
+        logits = ctx.model.logits(h)
+        if logits.dtype in (torch.bfloat16, torch.float16):
+            logits = logits.float()
+        if weight.dtype == logits.dtype:
+            dlog = ops.lse_gather_backward(logits, targets, lse, g, ctx.temperature, out=logits)
+        else:
+            dlog = ops.lse_gather_backward(logits, targets, lse, g, ctx.temperature, out_dtype=weight.dtype)
+        del logits
+        dh = dlog @ weight if ctx.needs_input_grad[0] else None
+        dw = dlog.t() @ h.to(weight.dtype) if ctx.needs_input_grad[1] else None
+        return dh, dw, None, None, None
 
 
 def token_logprobs(model, batch: Batch, temperature: float = 1.0, return_full: bool = False):
@@ -28,6 +64,14 @@ def token_logprobs(model, batch: Batch, temperature: float = 1.0, return_full: b
     full = torch.zeros((B, T, model.cfg.vocab_size), dtype=want, device=dev) if return_full else None
     flat_h = hidden[:, :-1].reshape(-1, hidden.shape[-1])
     flat_next = tokens[:, 1:].reshape(-1)
+    if full is None and flat_h.is_cuda:
+        # fused path: lm_head GEMM + one pass per row, recomputed in backward
+        parts = [_LmHeadLogprob.apply(flat_h[a:a + _CHUNK_TOKENS], model.lm_head.weight,
+                                      flat_next[a:a + _CHUNK_TOKENS], float(temperature), model)
+                 for a in range(0, flat_h.shape[0], _CHUNK_TOKENS)]
+        res = torch.cat(parts) if parts else torch.empty(0, dtype=want, device=dev)
+        out = torch.cat([torch.zeros(B, 1, dtype=res.dtype, device=dev), res.view(B, T - 1)], dim=1)
+        return out
     res = torch.empty(flat_next.numel(), dtype=want, device=dev)
     for a in range(0, flat_h.shape[0], _CHUNK_TOKENS):
         z = slice(a, a + _CHUNK_TOKENS)

@@ -387,6 +387,20 @@ size_t kvs_compact_scratch_bytes(const kvs_cache* c, const kvs_segments* s, int3
 int kvs_compact(const kvs_cache* c, const kvs_batch* b, const kvs_segments* s, int32_t policy, int32_t param,
                 int32_t budget, const int32_t* step, void* scratch, size_t scratch_bytes, kvs_stream_t stream);
 
+/* token_logprobs' log-softmax + gather (training/logprobs.py:17-20) on lm_head logits
+ * [n_rows][ld] (dtype KVS_F32 or KVS_F64, row stride ld >= vocab): logp[r] = x[r][t_r]/T -
+ * log sum_v exp(x[r][v]/T) in one pass over each row (a target outside [0, vocab) gives NaN);
+ * lse[r] (optional, same dtype) receives the log-sum-exp for the backward. */
+int kvs_lse_gather(const void* logits, int64_t ld, int32_t n_rows, int32_t vocab, const int64_t* targets,
+                   double temperature, int32_t dtype, void* logp, void* lse, kvs_stream_t stream);
+/* Its gradient with respect to the logits for upstream grad[r] (same dtype as logits):
+ * dlogits[r][v] = grad[r] * (onehot(t_r)[v] - exp(x[r][v]/T - lse[r])) / T, written in
+ * out_dtype (KVS_F32 / KVS_BF16 / KVS_F16 from float logits, KVS_F64 from double ones) with row
+ * stride ld_out; dlogits may be the logits buffer itself when the dtypes match. */
+int kvs_lse_gather_backward(const void* logits, int64_t ld, int32_t n_rows, int32_t vocab, const int64_t* targets,
+                            const void* lse, const void* grad, double temperature, int32_t dtype, void* dlogits,
+                            int64_t ld_out, int32_t out_dtype, kvs_stream_t stream);
+
 /* Self-test of the tcgen05 path (no reference counterpart): c[128][128] f32 =
  * a[128][128] (bf16 row-major) x B, with B given as bt[128 n][128 k] (mode bit 0 = 0,
  * K-major operand) or b[128 k][128 n] (bit 0 = 1, MN-major operand); mode bit 1 = 1
