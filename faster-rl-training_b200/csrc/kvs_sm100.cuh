@@ -91,24 +91,6 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
-// 2^x on the FMA/ALU pipes, for x <= 64 (arguments below -125 give +0): x = j + f with
-// j = round(x) taken from the low mantissa bits of x + 1.5*2^23 and f in [-0.5, 0.5];
-// 2^f ~ 1 + f*(c1 + f*(c2 + f*c3)), a cubic fitted here by relative least squares on
-// Chebyshev nodes (max relative error 1.14e-4, below bf16 rounding); 2^j is added to
-// the exponent field.  Used for part of the softmax exponentials so that they do not
-// all queue on the MUFU unit.
-__device__ __forceinline__ float exp2_poly(float x) {
-  const float magic = 12582912.0f;  // 1.5 * 2^23
-  const float xc = fmaxf(x, -125.0f);
-  const float t = xc + magic;
-  const float f = xc - (t - magic);
-  float p = fmaf(0.05459282547235489f, f, 0.24221783876419067f);
-  p = fmaf(p, f, 0.6933686137199402f);
-  p = fmaf(p, f, 1.0f);
-  const float r = __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
-  return x < -125.0f ? 0.0f : r;
-}
-
 // Packed fp32 pairs (sm_100 .f32x2 forms): one instruction for two lanes of work.
 // (d0, d1) = (a0, a1) * b + c
 __device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b, float c) {
@@ -120,38 +102,6 @@ __device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, 
       "mov.b64 {%0, %1}, d;\n}\n"
       : "=f"(d0), "=f"(d1)
       : "f"(a0), "f"(a1), "f"(b), "f"(c));
-}
-// (d0, d1) = (a0, a1) * (b0, b1) + (c0, c1)
-__device__ __forceinline__ void ffma2v(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0,
-                                       float c1) {
-  asm("{\n.reg .b64 a, b, c, d;\n"
-      "mov.b64 a, {%2, %3};\n"
-      "mov.b64 b, {%4, %5};\n"
-      "mov.b64 c, {%6, %7};\n"
-      "fma.rn.f32x2 d, a, b, c;\n"
-      "mov.b64 {%0, %1}, d;\n}\n"
-      : "=f"(d0), "=f"(d1)
-      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
-}
-// (d0, d1) = (a0, a1) + (b0, b1)
-__device__ __forceinline__ void fadd2v(float& d0, float& d1, float a0, float a1, float b0, float b1) {
-  asm("{\n.reg .b64 a, b, d;\n"
-      "mov.b64 a, {%2, %3};\n"
-      "mov.b64 b, {%4, %5};\n"
-      "add.rn.f32x2 d, a, b;\n"
-      "mov.b64 {%0, %1}, d;\n}\n"
-      : "=f"(d0), "=f"(d1)
-      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
-}
-// (d0, d1) = (a0, a1) * (b0, b1)
-__device__ __forceinline__ void fmul2v(float& d0, float& d1, float a0, float a1, float b0, float b1) {
-  asm("{\n.reg .b64 a, b, d;\n"
-      "mov.b64 a, {%2, %3};\n"
-      "mov.b64 b, {%4, %5};\n"
-      "mul.rn.f32x2 d, a, b;\n"
-      "mov.b64 {%0, %1}, d;\n}\n"
-      : "=f"(d0), "=f"(d1)
-      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
 }
 // (s0, s1) += (a0, a1)
 __device__ __forceinline__ void fadd2(float& s0, float& s1, float a0, float a1) {
@@ -247,27 +197,10 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 // operands and one elected lane issues the instruction.  Keeping the issuing code
 // warp-uniform lets the compiler hold descriptors in uniform registers, so an UMMA
 // costs a few issue cycles instead of a register-to-uniform transfer each.
-__device__ __forceinline__ void umma_bf16_warp(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                               uint32_t accumulate) {
-  asm volatile(
-      "{\n.reg .pred p, e;\n"
-      "elect.sync _|e, 0xffffffff;\n"
-      "setp.ne.b32 p, %4, 0;\n"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
-}
-__device__ __forceinline__ void umma_bf16_tmem_a_warp(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                                      uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n.reg .pred p, e;\n"
-      "elect.sync _|e, 0xffffffff;\n"
-      "setp.ne.b32 p, %4, 0;\n"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
-}
-// The same with the K-step offsets added inside the instruction block: `a_off`/`b_off` are
-// added to the descriptors' start-address fields (byte offset >> 4), so the compiler cannot
-// hoist one 64-bit descriptor per step out of the tile loop and run short of registers.
+// The K-step offsets are added inside the instruction block: A_OFF / B_OFF (compile-time)
+// go to the descriptors' start-address fields (byte offset >> 4; a TMEM column for an A
+// operand in TMEM), so the compiler cannot hoist one 64-bit descriptor per step out of the
+// tile loop and run short of registers.
 template <uint32_t A_OFF, uint32_t B_OFF>
 __device__ __forceinline__ void umma_bf16_warp_at(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                                   uint32_t accumulate) {
@@ -318,20 +251,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
       : KVS_R32(r)
       : "r"(taddr));
-}
-// 64 consecutive 32-bit TMEM columns of this thread's lane (warp-collective)
-__device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&r)[64]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];\n"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
-      : "r"(taddr));
-}
-// 16 consecutive 32-bit TMEM columns of this thread's lane (warp-collective)
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n" : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]) : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};\n" ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]) : "memory");
 }
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
