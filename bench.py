@@ -346,6 +346,7 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
         secondary["rollout"] = rollout_bench(dev, args, rank)
         secondary["prefill"] = prefill_bench(dev, args, rank)
         secondary["replay_model"] = replay_model_bench(dev, args, rank)
+        secondary["replay_train"] = replay_train_bench(dev, args, rank)
 
     if rank != 0:
         return
@@ -755,6 +756,73 @@ def prefill_bench(dev, args, rank: int) -> dict:
             "kernel": "pair_attn_kernel<true> (tcgen05/TMEM paged prefill)"}
 
 
+def replay_train_bench(dev, args, rank: int) -> dict:
+    """A replay training step of config 4's model (Llama-3-8B architecture, random init, bf16):
+    loss = sum(advantage * token_logprobs) and its backward through the whole model -- the
+    masked replay forward and backward kernels in every layer, the lm_head chunks with their
+    fused log-softmax + gather and its recomputing backward.  One stream of
+    ``--replay-train-t`` tokens (3-8 keep-recent events); one untimed step, then one timed
+    by CUDA events.  Model FLOP: 6 per parameter per token for the dense layers (forward +
+    backward) + 14·Hq·D per visible pair per layer for attention (4 forward, 10 backward)."""
+    import torch
+
+    from kvstreams.config import ModelConfig
+    from kvstreams.distributed import reduce_max
+    from kvstreams.model import TinyLM
+    from kvstreams.training.logprobs import token_logprobs
+    from kvstreams.training.replay import Batch
+    from kvstreams.workloads import replay_evicted_at, visible_pairs
+
+    torch.cuda.empty_cache()
+    B, T = 1, args.replay_train_t
+    cfg = ModelConfig(vocab_size=128256, d_model=4096, n_layers=args.rollout_layers, n_heads=32, n_kv_heads=8,
+                      d_ff=14336, rope_theta=5e5)
+    torch.manual_seed(rank)
+    old = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    try:
+        with dev:
+            model = TinyLM(cfg)
+    finally:
+        torch.set_default_dtype(old)
+    model.train()
+    ev, _ = replay_evicted_at(batch=B, seq_len=T, seed=rank)
+    pairs = visible_pairs(ev)
+    g = torch.Generator(device=dev).manual_seed(rank)
+    tokens = torch.randint(1, cfg.vocab_size, (B, T), generator=g, device=dev)
+    adv = torch.randn(B, T, generator=g, device=dev)
+    batch = Batch(tokens, torch.arange(T, device=dev).expand(B, T), torch.from_numpy(ev).to(dev),
+                  torch.ones(B, T, dtype=torch.bool, device=dev), torch.zeros(B, T, device=dev),
+                  torch.full((B,), T, dtype=torch.long, device=dev))
+
+    def step():
+        model.zero_grad(set_to_none=True)
+        (token_logprobs(model, batch) * adv).sum().backward()
+
+    step()
+    torch.cuda.synchronize(dev)
+    torch.cuda.reset_peak_memory_stats(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    step()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    ms = reduce_max(e0.elapsed_time(e1), dev)
+    finite = all(bool(torch.isfinite(p.grad).all()) for p in model.parameters() if p.grad is not None)
+    n_dense = sum(p.numel() for n, p in model.named_parameters() if "embed" not in n and p.dim() == 2)
+    flops = 6.0 * n_dense * B * T + 14.0 * cfg.n_heads * (cfg.d_model // cfg.n_heads) * pairs * cfg.n_layers
+    peaks = _peaks()
+    tf = flops / (ms * 1e-3) / 1e12
+    peak_gb = torch.cuda.max_memory_allocated(dev) / 1e9
+    del model, batch, tokens, adv
+    torch.cuda.empty_cache()
+    return {"workload": f"B={B} T={T}, Llama-3-8B arch ({cfg.n_layers} layers) bf16 random init, 3-8 keep-recent "
+                        "events: forward + backward of sum(advantage * token_logprobs)",
+            "ms": ms, "train_tok_s_per_gpu": B * T / (ms * 1e-3), "model_tflops": tf,
+            "model_flop_frac": tf / peaks["bf16_tflops"], "peak_src": peaks["src"], "peak_mem_gb": peak_gb,
+            "grads_finite": finite}
+
+
 def replay_model_bench(dev, args, rank: int) -> dict:
     """Config 4 end to end: the trainer's replay of KV-streams rollouts through the whole
     Llama-3-8B architecture (random init, bf16): token_logprobs = masked full-sequence forward
@@ -925,6 +993,8 @@ def main() -> int:
     ap.add_argument("--replay-model-b", type=int, default=2, help="config 4 uses 16")
     ap.add_argument("--replay-model-t", type=int, default=32768)
     ap.add_argument("--replay-model-only", action="store_true", help="only the whole-model replay measurement")
+    ap.add_argument("--replay-train-t", type=int, default=16384)
+    ap.add_argument("--replay-train-only", action="store_true", help="only the replay training step measurement")
     ap.add_argument("--prefill-streams", type=int, default=64)
     ap.add_argument("--prefill-only", action="store_true", help="only the paged prefill measurement")
     args = ap.parse_args()
@@ -972,6 +1042,11 @@ def main() -> int:
             r = prefill_bench(torch.device("cuda", local_rank), args, rank)
             if rank == 0:
                 print(json.dumps({"prefill": r}), flush=True)
+        elif args.replay_train_only:
+            torch.cuda.set_device(local_rank)
+            r = replay_train_bench(torch.device("cuda", local_rank), args, rank)
+            if rank == 0:
+                print(json.dumps({"replay_train": r}), flush=True)
         elif args.replay_model_only:
             torch.cuda.set_device(local_rank)
             r = replay_model_bench(torch.device("cuda", local_rank), args, rank)
