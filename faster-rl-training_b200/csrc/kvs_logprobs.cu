@@ -64,17 +64,18 @@ __device__ Lse<A> block_lse(Lse<A> v) {
   return r;
 }
 
-// one CTA per row: lse of x / T over the row, logp of the target
+// one CTA per row: lse of x / T over the row, logp of the target.  x / T is x * (1 / T)
+// (within one ulp of the reference's division; exact for the usual T = 1, where it is x).
 template <typename T>
 __global__ void __launch_bounds__(kRowThreads)
 lse_gather_kernel(const T* __restrict__ logits, int64_t ld, int vocab, const int64_t* __restrict__ targets,
-                  T temp, T* __restrict__ logp, T* __restrict__ lse_out) {
+                  T inv_temp, T* __restrict__ logp, T* __restrict__ lse_out) {
   using V = typename Vec<T>::type;
   constexpr int NV = Vec<T>::n;
   const int64_t row = blockIdx.x;
   const T* x = logits + row * ld;
   Lse<T> acc{-INFINITY, T(0)};
-  // x / T as the reference divides (logits / temperature); aligned vector loads when possible
+  // aligned vector loads when the row allows them
   const bool vec = (reinterpret_cast<uintptr_t>(x) % sizeof(V)) == 0;
   const int nvec = vec ? vocab / NV : 0;
   const V* xv = reinterpret_cast<const V*>(x);
@@ -95,7 +96,7 @@ lse_gather_kernel(const T* __restrict__ logits, int64_t ld, int vocab, const int
       T vm = -INFINITY;
 #pragma unroll
       for (int k = 0; k < NV; ++k) {
-        e[k] = qe[k] / temp;
+        e[k] = qe[k] * inv_temp;
         vm = vm > e[k] ? vm : e[k];
       }
       if (vm > acc.m) {
@@ -108,12 +109,12 @@ lse_gather_kernel(const T* __restrict__ logits, int64_t ld, int vocab, const int
       acc.s += part;
     }
   }
-  for (int i = nvec * NV + threadIdx.x; i < vocab; i += kRowThreads) acc.add(x[i] / temp);
+  for (int i = nvec * NV + threadIdx.x; i < vocab; i += kRowThreads) acc.add(x[i] * inv_temp);
   const Lse<T> r = block_lse(acc);
   if (threadIdx.x == 0) {
     const T lse = r.m + log_of(r.s);
     const int64_t t = targets[row];
-    logp[row] = (t >= 0 && t < vocab) ? x[t] / temp - lse : T(NAN);
+    logp[row] = (t >= 0 && t < vocab) ? x[t] * inv_temp - lse : T(NAN);
     if (lse_out) lse_out[row] = lse;
   }
 }
@@ -122,15 +123,15 @@ lse_gather_kernel(const T* __restrict__ logits, int64_t ld, int vocab, const int
 template <typename T, typename OutT>
 __global__ void __launch_bounds__(kRowThreads)
 lse_gather_bwd_kernel(const T* __restrict__ logits, int64_t ld, int vocab, const int64_t* __restrict__ targets,
-                      const T* __restrict__ lse, const T* __restrict__ grad, T temp, OutT* __restrict__ dlogits,
+                      const T* __restrict__ lse, const T* __restrict__ grad, T inv_temp, OutT* __restrict__ dlogits,
                       int64_t ld_out) {
   const int64_t row = blockIdx.x;
   const T* x = logits + row * ld;
   OutT* d = dlogits + row * ld_out;
-  const T l = lse[row], g = grad[row] / temp;
+  const T l = lse[row], g = grad[row] * inv_temp;
   const int64_t t = targets[row];
   for (int i = threadIdx.x; i < vocab; i += kRowThreads) {
-    const T p = exp_of(x[i] / temp - l);
+    const T p = exp_of(x[i] * inv_temp - l);
     const T v = g * ((i == t ? T(1) : T(0)) - p);
     if constexpr (sizeof(OutT) == 2) {
       if constexpr (std::is_same<OutT, __nv_bfloat16>::value) d[i] = __float2bfloat16_rn((float)v);
@@ -150,11 +151,11 @@ KVS_API int kvs_lse_gather(const void* logits, int64_t ld, int32_t n_rows, int32
   const cudaStream_t st = to_cuda(stream);
   if (dtype == KVS_F32)
     lse_gather_kernel<float><<<n_rows, kRowThreads, 0, st>>>(static_cast<const float*>(logits), ld, vocab, targets,
-                                                           (float)temperature, static_cast<float*>(logp),
+                                                           (float)(1.0 / temperature), static_cast<float*>(logp),
                                                            static_cast<float*>(lse));
   else if (dtype == KVS_F64)
     lse_gather_kernel<double><<<n_rows, kRowThreads, 0, st>>>(static_cast<const double*>(logits), ld, vocab, targets,
-                                                            temperature, static_cast<double*>(logp),
+                                                            1.0 / temperature, static_cast<double*>(logp),
                                                             static_cast<double*>(lse));
   else
     return KVS_E_UNSUPPORTED;
@@ -174,7 +175,7 @@ KVS_API int kvs_lse_gather_backward(const void* logits, int64_t ld, int32_t n_ro
     const float* x = static_cast<const float*>(logits);
     const float* l = static_cast<const float*>(lse);
     const float* g = static_cast<const float*>(grad);
-    const float tf = (float)temperature;
+    const float tf = (float)(1.0 / temperature);
     if (out_dtype == KVS_F32)
       lse_gather_bwd_kernel<float, float><<<n_rows, kRowThreads, 0, st>>>(x, ld, vocab, targets, l, g, tf,
                                                                          static_cast<float*>(dlogits), ld_out);
@@ -189,7 +190,7 @@ KVS_API int kvs_lse_gather_backward(const void* logits, int64_t ld, int32_t n_ro
   } else if (dtype == KVS_F64 && out_dtype == KVS_F64) {
     lse_gather_bwd_kernel<double, double><<<n_rows, kRowThreads, 0, st>>>(
         static_cast<const double*>(logits), ld, vocab, targets, static_cast<const double*>(lse),
-        static_cast<const double*>(grad), temperature, static_cast<double*>(dlogits), ld_out);
+        static_cast<const double*>(grad), 1.0 / temperature, static_cast<double*>(dlogits), ld_out);
   } else {
     return KVS_E_UNSUPPORTED;
   }
