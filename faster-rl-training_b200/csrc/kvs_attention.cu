@@ -18,10 +18,11 @@ using namespace kvs;
 namespace {
 
 // ------------------------------------------------------------------ RoPE
-// in place (src == dst) or copying; one thread per rotated pair (i, i + D/2).
+// in place (src == dst) or copying; one thread per rotated pair (i, i + D/2).  src rows
+// (tokens) are src_stride elements apart, dst rows packed.
 template <typename T, typename F>
 __global__ void rope_kernel(const T* __restrict__ src, T* __restrict__ dst, const int64_t* __restrict__ pos,
-                            int n_tokens, int n_heads, int D, const F* __restrict__ inv_freq) {
+                            int n_tokens, int n_heads, int D, const F* __restrict__ inv_freq, int64_t src_stride) {
   const int half = D >> 1;
   const int64_t total = (int64_t)n_tokens * n_heads * half;
   for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
@@ -30,8 +31,9 @@ __global__ void rope_kernel(const T* __restrict__ src, T* __restrict__ dst, cons
     const int64_t th = idx / half;
     const int t = (int)(th / n_heads);
     const int64_t base = th * D;
+    const int64_t sbase = (int64_t)t * src_stride + (th - (int64_t)t * n_heads) * D;
     using A = typename Acc<T>::type;
-    A a = to_acc(src[base + i]), b = to_acc(src[base + i + half]);
+    A a = to_acc(src[sbase + i]), b = to_acc(src[sbase + i + half]);
     A r0, r1;
     rope_rotate<A, F>(a, b, pos[t], inv_freq[i], r0, r1);
     dst[base + i] = from_acc<T>(r0);
@@ -45,7 +47,7 @@ template <typename T, typename F>
 __global__ void rope_write_kv_kernel(kvs_cache c, int layer, const int32_t* __restrict__ blocks,
                                      const int32_t* __restrict__ offsets, const T* __restrict__ k,
                                      const T* __restrict__ v, const int64_t* __restrict__ pos, int n_tokens,
-                                     const F* __restrict__ inv_freq) {
+                                     const F* __restrict__ inv_freq, int64_t kv_stride) {
   const int D = c.head_dim, half = D >> 1, H = c.n_kv_heads;
   const int64_t total = (int64_t)n_tokens * H * half;
   T* K = static_cast<T*>(c.k);
@@ -58,7 +60,7 @@ __global__ void rope_write_kv_kernel(kvs_cache c, int layer, const int32_t* __re
     const int t = (int)(th / H);
     const int64_t row = ((int64_t)layer * c.num_blocks + blocks[t]) * c.block_size + offsets[t];
     const int64_t dst = (row * H + h) * D;
-    const int64_t src = th * D;
+    const int64_t src = (int64_t)t * kv_stride + (int64_t)h * D;
     using A = typename Acc<T>::type;
     A a = to_acc(k[src + i]), b = to_acc(k[src + i + half]);
     A r0, r1;
@@ -249,35 +251,37 @@ int launch_replay_generic(const kvs_replay_args& a, cudaStream_t st) {
 
 template <typename T, typename F>
 int launch_rope(const void* src, void* dst, const int64_t* pos, int n_tokens, int n_heads, int D,
-                const void* inv_freq, cudaStream_t st) {
+                const void* inv_freq, cudaStream_t st, int64_t src_stride) {
   const int64_t total = (int64_t)n_tokens * n_heads * (D / 2);
   if (total == 0) return KVS_OK;
   const int grid = (int)std::min<int64_t>((total + 255) / 256, 148 * 32);
   rope_kernel<T, F><<<grid, 256, 0, st>>>(static_cast<const T*>(src), static_cast<T*>(dst), pos, n_tokens,
-                                          n_heads, D, static_cast<const F*>(inv_freq));
+                                          n_heads, D, static_cast<const F*>(inv_freq),
+                                          src_stride ? src_stride : (int64_t)n_heads * D);
   return launch_rc();
 }
 
 template <typename T, typename F>
 int launch_rope_write(const kvs_cache& c, int layer, const int32_t* blocks, const int32_t* offsets,
                       const void* k, const void* v, const int64_t* pos, int n_tokens, const void* inv_freq,
-                      cudaStream_t st) {
+                      cudaStream_t st, int64_t kv_stride) {
   const int64_t total = (int64_t)n_tokens * c.n_kv_heads * (c.head_dim / 2);
   if (total == 0) return KVS_OK;
   const int grid = (int)std::min<int64_t>((total + 255) / 256, 148 * 32);
   rope_write_kv_kernel<T, F><<<grid, 256, 0, st>>>(c, layer, blocks, offsets, static_cast<const T*>(k),
                                                    static_cast<const T*>(v), pos, n_tokens,
-                                                   static_cast<const F*>(inv_freq));
+                                                   static_cast<const F*>(inv_freq),
+                                                   kv_stride ? kv_stride : (int64_t)c.n_kv_heads * c.head_dim);
   return launch_rc();
 }
 
 int rope_dispatch(const void* src, void* dst, int dtype, const int64_t* pos, int n_tokens, int n_heads, int D,
-                  const void* inv_freq, cudaStream_t st) {
+                  const void* inv_freq, cudaStream_t st, int64_t src_stride = 0) {
   switch (dtype) {
-    case KVS_F32: return launch_rope<float, float>(src, dst, pos, n_tokens, n_heads, D, inv_freq, st);
-    case KVS_F64: return launch_rope<double, double>(src, dst, pos, n_tokens, n_heads, D, inv_freq, st);
-    case KVS_BF16: return launch_rope<__nv_bfloat16, float>(src, dst, pos, n_tokens, n_heads, D, inv_freq, st);
-    case KVS_F16: return launch_rope<__half, float>(src, dst, pos, n_tokens, n_heads, D, inv_freq, st);
+    case KVS_F32: return launch_rope<float, float>(src, dst, pos, n_tokens, n_heads, D, inv_freq, st, src_stride);
+    case KVS_F64: return launch_rope<double, double>(src, dst, pos, n_tokens, n_heads, D, inv_freq, st, src_stride);
+    case KVS_BF16: return launch_rope<__nv_bfloat16, float>(src, dst, pos, n_tokens, n_heads, D, inv_freq, st, src_stride);
+    case KVS_F16: return launch_rope<__half, float>(src, dst, pos, n_tokens, n_heads, D, inv_freq, st, src_stride);
   }
   return KVS_E_UNSUPPORTED;
 }
@@ -289,13 +293,15 @@ int rope_dispatch(const void* src, void* dst, int dtype, const int64_t* pos, int
 // RoPE of q (into a->out) and of the new k, and the append of k/v to their slots
 int kvs_rope_append(const kvs_cache* c, const kvs_batch* b, const kvs_decode_args* a, cudaStream_t st) {
   const int n = b->total_tokens;
-  int rc = rope_dispatch(a->q, a->out, c->dtype, a->positions, n, a->n_heads, c->head_dim, a->inv_freq, st);
+  int rc = rope_dispatch(a->q, a->out, c->dtype, a->positions, n, a->n_heads, c->head_dim, a->inv_freq, st,
+                         a->q_stride);
   if (rc) return rc;
+  const int64_t ks = a->kv_stride;
   switch (c->dtype) {
-    case KVS_F32: return launch_rope_write<float, float>(*c, a->layer, a->slot_blocks, a->slot_offsets, a->k_new, a->v_new, a->positions, n, a->inv_freq, st);
-    case KVS_F64: return launch_rope_write<double, double>(*c, a->layer, a->slot_blocks, a->slot_offsets, a->k_new, a->v_new, a->positions, n, a->inv_freq, st);
-    case KVS_BF16: return launch_rope_write<__nv_bfloat16, float>(*c, a->layer, a->slot_blocks, a->slot_offsets, a->k_new, a->v_new, a->positions, n, a->inv_freq, st);
-    case KVS_F16: return launch_rope_write<__half, float>(*c, a->layer, a->slot_blocks, a->slot_offsets, a->k_new, a->v_new, a->positions, n, a->inv_freq, st);
+    case KVS_F32: return launch_rope_write<float, float>(*c, a->layer, a->slot_blocks, a->slot_offsets, a->k_new, a->v_new, a->positions, n, a->inv_freq, st, ks);
+    case KVS_F64: return launch_rope_write<double, double>(*c, a->layer, a->slot_blocks, a->slot_offsets, a->k_new, a->v_new, a->positions, n, a->inv_freq, st, ks);
+    case KVS_BF16: return launch_rope_write<__nv_bfloat16, float>(*c, a->layer, a->slot_blocks, a->slot_offsets, a->k_new, a->v_new, a->positions, n, a->inv_freq, st, ks);
+    case KVS_F16: return launch_rope_write<__half, float>(*c, a->layer, a->slot_blocks, a->slot_offsets, a->k_new, a->v_new, a->positions, n, a->inv_freq, st, ks);
   }
   return KVS_E_UNSUPPORTED;
 }

@@ -59,9 +59,10 @@ struct DecodeParams {
   const int32_t* seq_slots;
   int num_seqs;
   int layer;
-  const __nv_bfloat16* q;      // [S][HQ][D]
-  const __nv_bfloat16* k_new;  // [S][HKV][D]
+  const __nv_bfloat16* q;      // [S] rows of [HQ][D], q_stride elements apart
+  const __nv_bfloat16* k_new;  // [S] rows of [HKV][D], kv_stride elements apart
   const __nv_bfloat16* v_new;
+  int64_t q_stride, kv_stride;
   const int64_t* positions;    // [S]
   const int32_t* slot_blocks;  // [S]
   const int32_t* slot_offsets; // [S]
@@ -352,7 +353,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
     // RoPE of q into shared memory (same rotation as every other kernel of the library)
     for (int e = tid; e < HQ * (D / 2); e += NTHREADS) {
       const int h = e / (D / 2), d = e % (D / 2);
-      const __nv_bfloat16* qr = p.q + ((int64_t)i * HQ + h) * D;
+      const __nv_bfloat16* qr = p.q + (int64_t)i * p.q_stride + h * D;
       float r0, r1;
       rope_rotate<float, float>(__bfloat162float(qr[d]), __bfloat162float(qr[d + D / 2]), pos, p.inv_freq[d], r0, r1);
       q_s[h * D + d] = __float2bfloat16_rn(r0);
@@ -366,7 +367,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
       __nv_bfloat16* V = static_cast<__nv_bfloat16*>(c.v);
       for (int e = tid; e < HKV * (D / 2); e += NTHREADS) {
         const int h = e / (D / 2), d = e % (D / 2);
-        const __nv_bfloat16* kr = p.k_new + ((int64_t)i * HKV + h) * D;
+        const __nv_bfloat16* kr = p.k_new + (int64_t)i * p.kv_stride + h * D;
         float r0, r1;
         rope_rotate<float, float>(__bfloat162float(kr[d]), __bfloat162float(kr[d + D / 2]), pos, p.inv_freq[d], r0, r1);
         const __nv_bfloat16 b0 = __float2bfloat16_rn(r0), b1 = __float2bfloat16_rn(r1);
@@ -376,7 +377,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
         K[(row + h) * D + d + D / 2] = b1;
       }
       for (int e = tid; e < HKV * D; e += NTHREADS) {
-        const __nv_bfloat16 x = p.v_new[(int64_t)i * HKV * D + e];
+        const __nv_bfloat16 x = p.v_new[(int64_t)i * p.kv_stride + e];
         vnew_s[e] = x;
         V[row * D + e] = x;
       }
@@ -534,6 +535,8 @@ int kvs_decode_bf16_launch(const kvs_cache* c, const kvs_batch* b, const kvs_dec
   p.q = static_cast<const __nv_bfloat16*>(a->q);
   p.k_new = static_cast<const __nv_bfloat16*>(a->k_new);
   p.v_new = static_cast<const __nv_bfloat16*>(a->v_new);
+  p.q_stride = a->q_stride ? a->q_stride : (int64_t)HQ * D;
+  p.kv_stride = a->kv_stride ? a->kv_stride : (int64_t)HKV * D;
   p.positions = a->positions;
   p.slot_blocks = a->slot_blocks;
   p.slot_offsets = a->slot_offsets;

@@ -59,7 +59,9 @@ KVS_API int kvs_paged_decode(const kvs_cache* c, const kvs_batch* b, const kvs_d
     // mixed step: chunks first, then tail_singles one-token sequences (a decode sub-batch)
     const int ns = a->tail_singles, nc = b->num_seqs - ns, tok1 = b->total_tokens - ns;
     if (ns > b->num_seqs || tok1 < nc) return KVS_E_ARG;
-    const size_t qrow = (size_t)a->n_heads * c->head_dim, kvrow = (size_t)c->n_kv_heads * c->head_dim;
+    const size_t qrow = a->q_stride ? (size_t)a->q_stride : (size_t)a->n_heads * c->head_dim;
+    const size_t kvrow = a->kv_stride ? (size_t)a->kv_stride : (size_t)c->n_kv_heads * c->head_dim;
+    const size_t orow = (size_t)a->n_heads * c->head_dim;  // out is packed
     const size_t esz = c->dtype == KVS_F64 ? 8 : (c->dtype == KVS_F32 ? 4 : 2);
     kvs_batch bs_ = {b->seq_slots + nc, nullptr, ns, ns};
     kvs_decode_args as_ = *a;
@@ -69,7 +71,7 @@ KVS_API int kvs_paged_decode(const kvs_cache* c, const kvs_batch* b, const kvs_d
     as_.positions = a->positions + tok1;
     as_.slot_blocks = a->slot_blocks + tok1;
     as_.slot_offsets = a->slot_offsets + tok1;
-    as_.out = static_cast<uint8_t*>(a->out) + tok1 * qrow * esz;
+    as_.out = static_cast<uint8_t*>(a->out) + tok1 * orow * esz;
     as_.tail_singles = 0;
     int rc = KVS_OK;
     if (nc > 0) {

@@ -1,0 +1,191 @@
+// The two elementwise steps of each decoder layer (model.py:29-36, 78-86) as single passes for
+// half-precision models: RMSNorm of a row (fp32 sum of squares, one rounding of x * rstd * w)
+// and the SwiGLU product silu(gate) * up read from the fused gate|up projection output
+// (fp32 arithmetic, one rounding).  PyTorch runs each of them as two or more kernels, and the
+// decode step of a rollout batch (64 rows) is dominated by their fixed costs.
+
+#include <algorithm>
+#include <cmath>
+
+#include "kvs_common.cuh"
+
+using namespace kvs;
+
+namespace {
+
+template <typename T> __device__ __forceinline__ float tof(T x);
+template <> __device__ __forceinline__ float tof<__nv_bfloat16>(__nv_bfloat16 x) { return __bfloat162float(x); }
+template <> __device__ __forceinline__ float tof<__half>(__half x) { return __half2float(x); }
+template <typename T> __device__ __forceinline__ T fromf(float x);
+template <> __device__ __forceinline__ __nv_bfloat16 fromf<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+template <> __device__ __forceinline__ __half fromf<__half>(float x) { return __float2half_rn(x); }
+
+constexpr int kNormThreads = 256;
+
+// one CTA per row; 8 elements (16 bytes) per thread and step
+template <typename T>
+__global__ void __launch_bounds__(kNormThreads)
+rms_norm_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict__ y, float* __restrict__ rstd_out,
+                int dim, int64_t ld_x, int64_t ld_y, float eps) {
+  const int64_t row = blockIdx.x;
+  const T* xr = x + row * ld_x;
+  T* yr = y + row * ld_y;
+  float ss = 0.f;
+  const int nvec = dim / 8;
+  for (int i = threadIdx.x; i < nvec; i += kNormThreads) {
+    const uint4 q = reinterpret_cast<const uint4*>(xr)[i];
+    const T* e = reinterpret_cast<const T*>(&q);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float f = tof(e[k]);
+      ss += f * f;
+    }
+  }
+  for (int i = nvec * 8 + threadIdx.x; i < dim; i += kNormThreads) {
+    const float f = tof(xr[i]);
+    ss += f * f;
+  }
+  __shared__ float red[kNormThreads / 32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < kNormThreads / 32; ++i) tot += red[i];
+  const float r = rsqrtf(tot / (float)dim + eps);
+  if (threadIdx.x == 0 && rstd_out) rstd_out[row] = r;
+  for (int i = threadIdx.x; i < nvec; i += kNormThreads) {
+    const uint4 q = reinterpret_cast<const uint4*>(xr)[i];
+    const uint4 wq = reinterpret_cast<const uint4*>(w)[i];
+    const T* e = reinterpret_cast<const T*>(&q);
+    const T* we = reinterpret_cast<const T*>(&wq);
+    uint4 o;
+    T* oe = reinterpret_cast<T*>(&o);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) oe[k] = fromf<T>(tof(e[k]) * r * tof(we[k]));
+    reinterpret_cast<uint4*>(yr)[i] = o;
+  }
+  for (int i = nvec * 8 + threadIdx.x; i < dim; i += kNormThreads) yr[i] = fromf<T>(tof(xr[i]) * r * tof(w[i]));
+}
+
+__device__ __forceinline__ float silu_f(float g) { return g / (1.f + __expf(-g)); }
+
+// out[r][j] = silu(gu[r][j]) * gu[r][F + j]; 8 outputs per thread
+template <typename T>
+__global__ void silu_mul_kernel(const T* __restrict__ gu, T* __restrict__ out, int64_t rows, int F, int64_t ld_gu,
+                                int64_t ld_out) {
+  const int nvec = F / 8;
+  const int64_t total = rows * nvec;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = idx / nvec;
+    const int j = (int)(idx % nvec);
+    const uint4 gq = reinterpret_cast<const uint4*>(gu + r * ld_gu)[j];
+    const uint4 uq = reinterpret_cast<const uint4*>(gu + r * ld_gu + F)[j];
+    const T* g = reinterpret_cast<const T*>(&gq);
+    const T* u = reinterpret_cast<const T*>(&uq);
+    uint4 o;
+    T* oe = reinterpret_cast<T*>(&o);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) oe[k] = fromf<T>(silu_f(tof(g[k])) * tof(u[k]));
+    reinterpret_cast<uint4*>(out + r * ld_out)[j] = o;
+  }
+}
+
+// d gate = grad * up * s (1 + gate (1 - s)), d up = grad * silu(gate), s = sigmoid(gate)
+template <typename T>
+__global__ void silu_mul_bwd_kernel(const T* __restrict__ gu, const T* __restrict__ grad, T* __restrict__ dgu,
+                                    int64_t rows, int F, int64_t ld_gu, int64_t ld_grad, int64_t ld_dgu) {
+  const int nvec = F / 8;
+  const int64_t total = rows * nvec;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = idx / nvec;
+    const int j = (int)(idx % nvec);
+    const uint4 gq = reinterpret_cast<const uint4*>(gu + r * ld_gu)[j];
+    const uint4 uq = reinterpret_cast<const uint4*>(gu + r * ld_gu + F)[j];
+    const uint4 dq = reinterpret_cast<const uint4*>(grad + r * ld_grad)[j];
+    const T* g = reinterpret_cast<const T*>(&gq);
+    const T* u = reinterpret_cast<const T*>(&uq);
+    const T* d = reinterpret_cast<const T*>(&dq);
+    uint4 og, ou;
+    T* oge = reinterpret_cast<T*>(&og);
+    T* oue = reinterpret_cast<T*>(&ou);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float gf = tof(g[k]), uf = tof(u[k]), df = tof(d[k]);
+      const float s = 1.f / (1.f + __expf(-gf));
+      oge[k] = fromf<T>(df * uf * s * (1.f + gf * (1.f - s)));
+      oue[k] = fromf<T>(df * gf * s);
+    }
+    reinterpret_cast<uint4*>(dgu + r * ld_dgu)[j] = og;
+    reinterpret_cast<uint4*>(dgu + r * ld_dgu + F)[j] = ou;
+  }
+}
+
+int grid_for(int64_t work) { return (int)std::max<int64_t>(1, std::min<int64_t>((work + 255) / 256, 148 * 16)); }
+
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+
+KVS_API int kvs_rms_norm(const void* x, const void* weight, void* y, float* rstd, int64_t n_rows, int32_t dim,
+                         int64_t ld_x, int64_t ld_y, double eps, int32_t dtype, kvs_stream_t stream) {
+  if (!x || !weight || !y || n_rows < 0 || dim <= 0 || ld_x < dim || ld_y < dim) return KVS_E_ARG;
+  if (dim % 8 || ld_x % 8 || ld_y % 8 || !al16(x) || !al16(weight) || !al16(y)) return KVS_E_UNSUPPORTED;
+  if (n_rows == 0) return KVS_OK;
+  const cudaStream_t st = to_cuda(stream);
+  if (dtype == KVS_BF16)
+    rms_norm_kernel<__nv_bfloat16><<<(unsigned)n_rows, kNormThreads, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(weight),
+        static_cast<__nv_bfloat16*>(y), rstd, dim, ld_x, ld_y, (float)eps);
+  else if (dtype == KVS_F16)
+    rms_norm_kernel<__half><<<(unsigned)n_rows, kNormThreads, 0, st>>>(
+        static_cast<const __half*>(x), static_cast<const __half*>(weight), static_cast<__half*>(y), rstd, dim, ld_x,
+        ld_y, (float)eps);
+  else
+    return KVS_E_UNSUPPORTED;
+  return launch_rc();
+}
+
+KVS_API int kvs_silu_mul(const void* gu, void* out, int64_t n_rows, int32_t f, int64_t ld_gu, int64_t ld_out,
+                         int32_t dtype, kvs_stream_t stream) {
+  if (!gu || !out || n_rows < 0 || f <= 0 || ld_gu < 2 * (int64_t)f || ld_out < f) return KVS_E_ARG;
+  if (f % 8 || ld_gu % 8 || ld_out % 8 || !al16(gu) || !al16(out)) return KVS_E_UNSUPPORTED;
+  if (n_rows == 0) return KVS_OK;
+  const cudaStream_t st = to_cuda(stream);
+  const int grid = grid_for(n_rows * (f / 8));
+  if (dtype == KVS_BF16)
+    silu_mul_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(gu),
+                                                       static_cast<__nv_bfloat16*>(out), n_rows, f, ld_gu, ld_out);
+  else if (dtype == KVS_F16)
+    silu_mul_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(gu), static_cast<__half*>(out), n_rows,
+                                                 f, ld_gu, ld_out);
+  else
+    return KVS_E_UNSUPPORTED;
+  return launch_rc();
+}
+
+KVS_API int kvs_silu_mul_backward(const void* gu, const void* grad, void* dgu, int64_t n_rows, int32_t f,
+                                  int64_t ld_gu, int64_t ld_grad, int64_t ld_dgu, int32_t dtype,
+                                  kvs_stream_t stream) {
+  if (!gu || !grad || !dgu || n_rows < 0 || f <= 0 || ld_gu < 2 * (int64_t)f || ld_grad < f ||
+      ld_dgu < 2 * (int64_t)f)
+    return KVS_E_ARG;
+  if (f % 8 || ld_gu % 8 || ld_grad % 8 || ld_dgu % 8 || !al16(gu) || !al16(grad) || !al16(dgu))
+    return KVS_E_UNSUPPORTED;
+  if (n_rows == 0) return KVS_OK;
+  const cudaStream_t st = to_cuda(stream);
+  const int grid = grid_for(n_rows * (f / 8));
+  if (dtype == KVS_BF16)
+    silu_mul_bwd_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(gu), static_cast<const __nv_bfloat16*>(grad),
+        static_cast<__nv_bfloat16*>(dgu), n_rows, f, ld_gu, ld_grad, ld_dgu);
+  else if (dtype == KVS_F16)
+    silu_mul_bwd_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(gu), static_cast<const __half*>(grad),
+                                                    static_cast<__half*>(dgu), n_rows, f, ld_gu, ld_grad, ld_dgu);
+  else
+    return KVS_E_UNSUPPORTED;
+  return launch_rc();
+}

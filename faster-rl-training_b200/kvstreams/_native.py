@@ -55,7 +55,7 @@ STAT_FIELDS = (
 )
 STAT_COUNT = 8
 STATUS_WORDS = 4
-ABI_VERSION = 2  # KVS_ABI_VERSION of include/kvs_b200.h
+ABI_VERSION = 3  # KVS_ABI_VERSION of include/kvs_b200.h
 NEVER = (1 << 63) - 1
 
 
@@ -109,6 +109,8 @@ class KvsDecodeArgs(C.Structure):
         ("n_heads", C.c_int32),
         ("grid_ctas", C.c_int32),
         ("tail_singles", C.c_int32),
+        ("q_stride", C.c_int64),
+        ("kv_stride", C.c_int64),
     ]
 
 
@@ -191,6 +193,9 @@ SIGNATURES = {
     "kvs_compact_scratch_bytes": (_Z, [_P, _P, _I]),
     "kvs_compact": (C.c_int, [_P, _P, _P, _I, _I, _I, _P, _P, _Z, _P]),
     "kvs_lse_gather": (C.c_int, [_P, C.c_int64, _I, _I, _P, C.c_double, _I, _P, _P, _P]),
+    "kvs_rms_norm": (C.c_int, [_P, _P, _P, _P, C.c_int64, _I, C.c_int64, C.c_int64, C.c_double, _I, _P]),
+    "kvs_silu_mul": (C.c_int, [_P, _P, C.c_int64, _I, C.c_int64, C.c_int64, _I, _P]),
+    "kvs_silu_mul_backward": (C.c_int, [_P, _P, _P, C.c_int64, _I, C.c_int64, C.c_int64, C.c_int64, _I, _P]),
     "kvs_lse_gather_backward": (C.c_int, [_P, C.c_int64, _I, _I, _P, _P, _P, C.c_double, _I, _P, C.c_int64, _I, _P]),
     "kvs_selftest_umma": (C.c_int, [_P, _P, _P, _I, _P, _P]),
 }

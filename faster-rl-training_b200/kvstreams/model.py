@@ -10,8 +10,8 @@
   for many sequences at once.
 
 Module and parameter names equal the reference's, so state dicts load unchanged.
-Dense projections, norms and the MLP stay in PyTorch (cuBLAS); attention, RoPE and
-every cache operation are this library's kernels.
+Dense projections stay in PyTorch (cuBLAS); attention, RoPE, every cache operation and, for
+half-precision models, RMSNorm and the MLP's silu(gate) * up are this library's kernels.
 """
 
 from __future__ import annotations
@@ -28,6 +28,53 @@ from .ops import ReplayMask
 from .rope import RotaryEmbedding
 
 
+def _half_kernels(x: torch.Tensor, width: int) -> bool:
+    """bf16/fp16 CUDA rows of a width the library's elementwise kernels take (fp32/fp64 models
+    keep PyTorch's ops, whose rounding the reference shares)."""
+    return x.is_cuda and x.dtype in (torch.bfloat16, torch.float16) and width % 8 == 0
+
+
+class _RMSNormFn(torch.autograd.Function):
+    """RMSNorm (model.py:29-36) as one kernel pass; backward from the saved per-row rstd."""
+
+    @staticmethod
+    def forward(ctx, x, w, eps):
+        y, rstd = ops.rms_norm(x, w, eps)
+        ctx.save_for_backward(x, w, rstd)
+        return y
+
+    @staticmethod
+    def backward(ctx, gy):
+        x, w, rstd = ctx.saved_tensors
+        r = rstd.unsqueeze(-1)
+        xn = x.float() * r
+        gxn = gy.float() * w.float()
+        gx = r * (gxn - xn * (gxn * xn).mean(-1, keepdim=True))
+        gw = (gy.float() * xn).reshape(-1, x.shape[-1]).sum(0)
+        return gx.to(x.dtype), gw.to(w.dtype), None
+
+
+class _SiluMulFn(torch.autograd.Function):
+    """silu(gate) * up of the fused gate|up output (model.py:78-86) in one pass, and its backward."""
+
+    @staticmethod
+    def forward(ctx, gu):
+        ctx.save_for_backward(gu)
+        return ops.silu_mul(gu)
+
+    @staticmethod
+    def backward(ctx, go):
+        (gu,) = ctx.saved_tensors
+        return ops.silu_mul_backward(gu, go)
+
+
+def _silu_mul(gu: torch.Tensor) -> torch.Tensor:
+    if _half_kernels(gu, gu.shape[-1] // 2):
+        return _SiluMulFn.apply(gu)
+    g, u = gu.chunk(2, dim=-1)
+    return F.silu(g) * u
+
+
 class RMSNorm(nn.Module):
     def __init__(self, dim: int, eps: float = 1e-6) -> None:
         super().__init__()
@@ -35,7 +82,10 @@ class RMSNorm(nn.Module):
         self.weight = nn.Parameter(torch.ones(dim))
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        # x * rsqrt(mean(x^2) + eps) * weight as one kernel (half precision reduces in float32)
+        # x * rsqrt(mean(x^2) + eps) * weight: one pass of the library's kernel for half precision
+        # (fp32 reduction and arithmetic), PyTorch's fused op otherwise
+        if _half_kernels(x, x.shape[-1]) and self.weight.dtype == x.dtype:
+            return _RMSNormFn.apply(x, self.weight, self.eps)
         return F.rms_norm(x, (x.shape[-1],), self.weight, self.eps)
 
 
@@ -87,8 +137,7 @@ class MLP(nn.Module):
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         # gate and up as one GEMM over the concatenated weights
         gu = F.linear(x, _fused_weight(self, "_gate_up", (self.gate.weight, self.up.weight)))
-        g, u = gu.chunk(2, dim=-1)
-        return self.down(F.silu(g) * u)
+        return self.down(_silu_mul(gu))
 
 
 class Block(nn.Module):
@@ -107,8 +156,7 @@ class Block(nn.Module):
     def mlp_residual(self, x: torch.Tensor) -> torch.Tensor:
         h = self.mlp_norm(x)
         gu = F.linear(h, _fused_weight(self.mlp, "_gate_up", (self.mlp.gate.weight, self.mlp.up.weight)))
-        g, u = gu.chunk(2, dim=-1)
-        return torch.addmm(x, F.silu(g) * u, self.mlp.down.weight.t())
+        return torch.addmm(x, _silu_mul(gu), self.mlp.down.weight.t())
 
 
 def causal_mask(T: int, device=None) -> torch.Tensor:

@@ -148,6 +148,14 @@ def replay_attention_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     return dq, dk, dv
 
 
+def _token_rows(x: torch.Tensor):
+    """``(x, row stride)`` when each token's ``[heads][head_dim]`` block of ``x`` is dense (the
+    stride between tokens is then passed to the kernels), else ``(contiguous copy, 0)``."""
+    if x.dim() == 3 and x.stride(2) == 1 and x.stride(1) == x.shape[2] and x.stride(0) >= x.shape[1] * x.shape[2]:
+        return x, (0 if x.is_contiguous() else int(x.stride(0)))
+    return x.contiguous(), 0
+
+
 def paged_forward(cache, slots: Sequence[int], counts: Optional[Sequence[int]], layer: int, q: torch.Tensor,
                   k_new: torch.Tensor, v_new: torch.Tensor, positions: torch.Tensor, mapping,
                   inv_freq: torch.Tensor, scale: float, out: Optional[torch.Tensor] = None,
@@ -160,12 +168,18 @@ def paged_forward(cache, slots: Sequence[int], counts: Optional[Sequence[int]], 
     ``cache._batch(slots, counts)`` that the layers of one forward can share; ``tail_singles``
     the number of trailing sequences with exactly one new token (they then run on the decode
     kernel while the chunks before them run on the prefill path, in one call)."""
-    q, k_new, v_new = q.contiguous(), k_new.contiguous(), v_new.contiguous()
+    # q, k_new, v_new may be row-strided views (the column blocks of a fused q|k|v projection
+    # output): each token's [heads][head_dim] block dense, rows any distance apart
+    q, q_stride = _token_rows(q)
+    k_new, kv_stride = _token_rows(k_new)
+    v_new, v_stride = _token_rows(v_new)
+    if v_stride != kv_stride:
+        k_new, v_new, kv_stride = k_new.contiguous(), v_new.contiguous(), 0
     if q.dtype != cache.dtype or k_new.dtype != cache.dtype or v_new.dtype != cache.dtype:
         raise ValueError("activations must have the cache dtype")
     pos = positions.to(device=q.device, dtype=torch.long).contiguous()
     if out is None:
-        out = torch.empty_like(q)
+        out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
     b, keep = batch if batch is not None else cache._batch(slots, counts)
     lib = N.lib()
     nbytes = int(lib.kvs_decode_scratch_bytes(C.byref(cache.struct), b.num_seqs, q.shape[1], grid_ctas))
@@ -176,7 +190,8 @@ def paged_forward(cache, slots: Sequence[int], counts: Optional[Sequence[int]], 
                         scratch=scratch.data_ptr() if scratch is not None else None,
                         scratch_bytes=scratch.numel() if scratch is not None else 0, scale=float(scale),
                         layer=int(layer), n_heads=int(q.shape[1]), grid_ctas=int(grid_ctas),
-                        tail_singles=int(tail_singles) if counts is not None else 0)
+                        tail_singles=int(tail_singles) if counts is not None else 0,
+                        q_stride=q_stride, kv_stride=kv_stride)
     N.check(lib.kvs_paged_decode(C.byref(cache.struct), C.byref(b), C.byref(a), N.stream_ptr(q.device)),
             "kvs_paged_decode")
     return out
@@ -271,3 +286,51 @@ def lse_gather_backward(logits: torch.Tensor, targets: torch.Tensor, lse: torch.
                                          out.stride(0), N.DTYPE_CODE[out.dtype], N.stream_ptr(logits.device))
     N.check(rc, "kvs_lse_gather_backward")
     return out
+
+
+def _rows2d(x: torch.Tensor) -> torch.Tensor:
+    """``x`` as a 2-D ``[rows, last]`` tensor with contiguous rows (a view when possible)."""
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    try:
+        return x.view(-1, x.shape[-1])
+    except RuntimeError:
+        return x.contiguous().view(-1, x.shape[-1])
+
+
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float):
+    """``(y, rstd)``: RMSNorm of the last dimension (model.py:29-36) for bf16/fp16 CUDA tensors,
+    fp32 arithmetic with one rounding; ``rstd`` float32 per row."""
+    _check_cuda(x, weight)
+    x2 = _rows2d(x)
+    y = torch.empty(x2.shape, dtype=x.dtype, device=x.device)
+    rstd = torch.empty(x2.shape[0], dtype=torch.float32, device=x.device)
+    rc = N.lib().kvs_rms_norm(x2.data_ptr(), weight.contiguous().data_ptr(), y.data_ptr(), rstd.data_ptr(),
+                              x2.shape[0], x2.shape[1], x2.stride(0), y.stride(0), float(eps), N.DTYPE_CODE[x.dtype],
+                              N.stream_ptr(x.device))
+    N.check(rc, "kvs_rms_norm")
+    return y.view(x.shape), rstd.view(x.shape[:-1])
+
+
+def silu_mul(gu: torch.Tensor) -> torch.Tensor:
+    """``silu(gate) * up`` of a fused ``[..., 2F]`` gate|up tensor (model.py:78-86), one pass."""
+    _check_cuda(gu)
+    g2 = _rows2d(gu)
+    f = g2.shape[1] // 2
+    out = torch.empty(g2.shape[0], f, dtype=gu.dtype, device=gu.device)
+    rc = N.lib().kvs_silu_mul(g2.data_ptr(), out.data_ptr(), g2.shape[0], f, g2.stride(0), out.stride(0),
+                              N.DTYPE_CODE[gu.dtype], N.stream_ptr(gu.device))
+    N.check(rc, "kvs_silu_mul")
+    return out.view(*gu.shape[:-1], f)
+
+
+def silu_mul_backward(gu: torch.Tensor, grad: torch.Tensor) -> torch.Tensor:
+    """Gradient of :func:`silu_mul` with respect to ``gu`` (``[..., 2F]``)."""
+    g2 = _rows2d(gu)
+    d2 = _rows2d(grad.to(gu.dtype))
+    dgu = torch.empty(g2.shape, dtype=gu.dtype, device=gu.device)
+    rc = N.lib().kvs_silu_mul_backward(g2.data_ptr(), d2.data_ptr(), dgu.data_ptr(), g2.shape[0], g2.shape[1] // 2,
+                                       g2.stride(0), d2.stride(0), dgu.stride(0), N.DTYPE_CODE[gu.dtype],
+                                       N.stream_ptr(gu.device))
+    N.check(rc, "kvs_silu_mul_backward")
+    return dgu.view(gu.shape)

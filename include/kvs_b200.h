@@ -30,7 +30,7 @@ extern "C" {
 
 typedef struct CUstream_st* kvs_stream_t; /* == cudaStream_t */
 
-#define KVS_ABI_VERSION 2
+#define KVS_ABI_VERSION 3
 
 /* element types of K/V pools and activations */
 enum kvs_dtype { KVS_F32 = 0, KVS_F64 = 1, KVS_BF16 = 2, KVS_F16 = 3 };
@@ -224,9 +224,9 @@ int kvs_paged_attention(const kvs_cache* c, const kvs_batch* b, int32_t layer, c
  * tail_singles > 0: the last tail_singles sequences have one token each) runs the
  * chunks and the single tokens as two launches of those kernels. */
 typedef struct kvs_decode_args {
-  const void* q;            /* [total_tokens][n_heads][head_dim], not yet rotated */
-  const void* k_new;        /* [total_tokens][n_kv_heads][head_dim], not yet rotated */
-  const void* v_new;        /* [total_tokens][n_kv_heads][head_dim] */
+  const void* q;            /* [total_tokens] rows of [n_heads][head_dim], not yet rotated */
+  const void* k_new;        /* [total_tokens] rows of [n_kv_heads][head_dim], not yet rotated */
+  const void* v_new;        /* [total_tokens] rows of [n_kv_heads][head_dim] */
   const int64_t* positions; /* [total_tokens] */
   const int32_t* slot_blocks;  /* [total_tokens] from kvs_append_slots */
   const int32_t* slot_offsets; /* [total_tokens] */
@@ -240,6 +240,9 @@ typedef struct kvs_decode_args {
   int32_t grid_ctas;        /* CTAs of the fused decode kernel (0 = one per SM) */
   int32_t tail_singles;     /* with cu_tokens set: the last tail_singles sequences have
                                exactly one new token each (0: no such promise) */
+  int64_t q_stride;         /* elements from one token's q row to the next (0: packed, n_heads*head_dim);
+                               e.g. the q columns of a fused [tokens][q|k|v] projection output */
+  int64_t kv_stride;        /* the same for k_new and v_new (0: packed, n_kv_heads*head_dim) */
 } kvs_decode_args;
 /* scratch of kvs_paged_decode: split partials and per-sequence arrival counters of the
  * fused decode kernel, then (bf16, head_dim 128, 16-token blocks, even GQA group) the
@@ -400,6 +403,20 @@ int kvs_lse_gather(const void* logits, int64_t ld, int32_t n_rows, int32_t vocab
 int kvs_lse_gather_backward(const void* logits, int64_t ld, int32_t n_rows, int32_t vocab, const int64_t* targets,
                             const void* lse, const void* grad, double temperature, int32_t dtype, void* dlogits,
                             int64_t ld_out, int32_t out_dtype, kvs_stream_t stream);
+
+/* The decoder layer's elementwise steps for half-precision models (KVS_BF16 / KVS_F16), one
+ * pass each (model.py:29-36 RMSNorm, model.py:78-86 the MLP's silu(gate) * up):
+ * y[r] = x[r] * rsqrt(mean(x[r]^2) + eps) * weight in fp32 with one rounding (rstd[r], optional
+ * float32, receives the row's rsqrt for a backward); out[r][j] = silu(gu[r][j]) * gu[r][f + j]
+ * from the fused gate|up output, and its gradient dgu[r] = (d gate | d up).  Rows are ld_*
+ * elements apart; dim / f and the row strides multiples of 8, pointers 16-byte aligned
+ * (KVS_E_UNSUPPORTED otherwise). */
+int kvs_rms_norm(const void* x, const void* weight, void* y, float* rstd, int64_t n_rows, int32_t dim, int64_t ld_x,
+                 int64_t ld_y, double eps, int32_t dtype, kvs_stream_t stream);
+int kvs_silu_mul(const void* gu, void* out, int64_t n_rows, int32_t f, int64_t ld_gu, int64_t ld_out, int32_t dtype,
+                 kvs_stream_t stream);
+int kvs_silu_mul_backward(const void* gu, const void* grad, void* dgu, int64_t n_rows, int32_t f, int64_t ld_gu,
+                          int64_t ld_grad, int64_t ld_dgu, int32_t dtype, kvs_stream_t stream);
 
 /* Self-test of the tcgen05 path (no reference counterpart): c[128][128] f32 =
  * a[128][128] (bf16 row-major) x B, with B given as bt[128 n][128 k] (mode bit 0 = 0,

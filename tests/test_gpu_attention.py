@@ -259,3 +259,48 @@ def test_prefill_then_decode_share_scratch_any_slot_order():
             np.testing.assert_allclose(got[sl], want, rtol=0, atol=TOL[dtype], err_msg=f"sequence {s}")
             start += n
             nxt[s] += n
+
+
+@pytest.mark.parametrize("dtype,D,Hq,Hkv,counts", [
+    (torch.bfloat16, 128, 32, 8, [1] * 9),               # fused decode kernel
+    (torch.bfloat16, 128, 32, 8, [40, 17, 1, 1, 1]),     # mixed step: prefill chunks + decode tail
+    (torch.float32, 32, 8, 2, [3, 1, 5]),                # generic path (RoPE kernels + exact attention)
+])
+def test_paged_forward_strided_qkv_equals_packed(dtype, D, Hq, Hkv, counts):
+    """q, k_new, v_new given as the column blocks of one fused [tokens, q|k|v] projection output
+    (rows q_stride / kv_stride apart, no copies) give the same bits as packed tensors: the
+    output and the keys/values appended to the pool."""
+    from kvstreams import ops
+    from kvstreams.rope import RotaryEmbedding
+
+    S = len(counts)
+    cache, st = _setup_cache(dtype, D, Hkv, 16, S, (30, 600), seed=9, extra_tokens=max(counts))
+    rope = RotaryEmbedding(D, 5e5)
+    inv = rope.table("cuda", dtype)
+    g = torch.Generator(device="cuda").manual_seed(4)
+    n = sum(counts)
+    nq, nk = Hq * D, Hkv * D
+    qkv = torch.randn(n, nq + 2 * nk, generator=g, device="cuda").to(dtype)
+    q = qkv[:, :nq].reshape(n, Hq, D)
+    k = qkv[:, nq:nq + nk].reshape(n, Hkv, D)
+    v = qkv[:, nq + nk:].reshape(n, Hkv, D)
+    assert not q.is_contiguous() and q.stride(0) == nq + 2 * nk
+    pos = torch.cat([torch.arange(int(p), int(p) + c) for p, c in zip(st.next_positions, counts)]).cuda()
+    tail = 0  # one-token sequences at the end, after at least one chunk
+    while tail < len(counts) and counts[-1 - tail] == 1:
+        tail += 1
+    if tail == len(counts):
+        tail = 0
+    snap = cache.snapshot_state()
+    outs, pools = [], []
+    for packed in (False, True):
+        cache.restore_state(snap)
+        mapping = cache.append_slots_batch(list(range(S)), pos, counts)
+        args = (q.contiguous(), k.contiguous(), v.contiguous()) if packed else (q, k, v)
+        out = ops.paged_forward(cache, list(range(S)), counts, 0, *args, pos, mapping, inv, D ** -0.5,
+                                tail_singles=tail)
+        cache.sync()
+        outs.append(out.clone())
+        pools.append((cache.k.clone(), cache.v.clone()))
+    assert torch.equal(outs[0], outs[1])
+    assert torch.equal(pools[0][0], pools[1][0]) and torch.equal(pools[0][1], pools[1][1])
