@@ -651,7 +651,7 @@ def rollout_bench(dev, args, rank: int) -> dict:
     cache = PagedKVCache(cfg.n_layers, cfg.n_kv_heads, cfg.head_dim, block_size=16, num_blocks=blocks,
                          dtype=torch.bfloat16, device=dev, max_seqs=n)
     eng = BatchedKVStreams(model, cache, MarkovianPolicy(keep_last=1), context_budget=budget, seed=rank,
-                           cuda_graphs=not args.rollout_eager)
+                           cuda_graphs=not args.rollout_eager, device_policy=args.rollout_device_policy)
     eps = synthetic_episodes(n, turns=turns, turn_range=(64, 512), prompt_len=64, vocab=cfg.vocab_size,
                              seed=1000 + rank)
     W, K = args.rollout_warmup, args.rollout_iters
@@ -685,6 +685,7 @@ def rollout_bench(dev, args, rank: int) -> dict:
         "library_launches": N.lib().kvs_launch_count() - launches0,
         "engine_iterations": eng.last_iterations,
         "cuda_graphs": not args.rollout_eager,
+        "device_policy": bool(args.rollout_device_policy),
     }
     if args.rollout_full:
         out["compactions"] = sum(r.stats.compactions for r in rolls)
@@ -989,6 +990,8 @@ def main() -> int:
     ap.add_argument("--rollout-iters", type=int, default=100)
     ap.add_argument("--rollout-full", action="store_true", help="play the whole episodes (minutes)")
     ap.add_argument("--rollout-eager", action="store_true", help="decode steps without CUDA graphs")
+    ap.add_argument("--rollout-device-policy", action="store_true",
+                    help="compaction decided and applied on the device (kvs_compact)")
     ap.add_argument("--rollout-only", action="store_true", help="only the batched rollout measurement")
     ap.add_argument("--replay-model-b", type=int, default=2, help="config 4 uses 16")
     ap.add_argument("--replay-model-t", type=int, default=32768)
