@@ -658,7 +658,17 @@ def rollout_bench(dev, args, rank: int) -> dict:
     ev = [torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
     tally = {"decode": 0, "prefill": 0}
 
+    prof = args.rollout_profile_iter
+
     def hook(i, n_dec, n_pre):
+        # iterations [prof, prof + 3) inside cudaProfilerStart/Stop, for an ncu launch list
+        # taken with --profile-from-start off (no work is skipped)
+        if prof > 0 and i == prof - 1:
+            torch.cuda.synchronize(dev)
+            torch.cuda.profiler.start()
+        elif prof > 0 and i == prof + 2:
+            torch.cuda.synchronize(dev)
+            torch.cuda.profiler.stop()
         if i == W:
             ev[0].record()
         elif W < i <= W + K:
@@ -990,6 +1000,8 @@ def main() -> int:
     ap.add_argument("--rollout-iters", type=int, default=100)
     ap.add_argument("--rollout-full", action="store_true", help="play the whole episodes (minutes)")
     ap.add_argument("--rollout-eager", action="store_true", help="decode steps without CUDA graphs")
+    ap.add_argument("--rollout-profile-iter", type=int, default=0,
+                    help="bracket engine iterations [N, N+3) with cudaProfilerStart/Stop")
     ap.add_argument("--rollout-device-policy", action="store_true",
                     help="compaction decided and applied on the device (kvs_compact)")
     ap.add_argument("--rollout-only", action="store_true", help="only the batched rollout measurement")
