@@ -32,7 +32,25 @@ rms_norm_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict_
   T* yr = y + row * ld_y;
   float ss = 0.f;
   const int nvec = dim / 8;
-  for (int i = threadIdx.x; i < nvec; i += kNormThreads) {
+  // the first kKeep vectors of each thread stay in registers for the second pass
+  constexpr int kKeep = 4;
+  uint4 keep[kKeep];
+#pragma unroll
+  for (int u = 0; u < kKeep; ++u) {
+    const int i = threadIdx.x + u * kNormThreads;
+    if (i < nvec) keep[u] = reinterpret_cast<const uint4*>(xr)[i];
+  }
+#pragma unroll
+  for (int u = 0; u < kKeep; ++u) {
+    if (threadIdx.x + u * kNormThreads >= nvec) break;
+    const T* e = reinterpret_cast<const T*>(&keep[u]);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float f = tof(e[k]);
+      ss += f * f;
+    }
+  }
+  for (int i = threadIdx.x + kKeep * kNormThreads; i < nvec; i += kNormThreads) {
     const uint4 q = reinterpret_cast<const uint4*>(xr)[i];
     const T* e = reinterpret_cast<const T*>(&q);
 #pragma unroll
@@ -55,8 +73,7 @@ rms_norm_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict_
   for (int i = 0; i < kNormThreads / 32; ++i) tot += red[i];
   const float r = rsqrtf(tot / (float)dim + eps);
   if (threadIdx.x == 0 && rstd_out) rstd_out[row] = r;
-  for (int i = threadIdx.x; i < nvec; i += kNormThreads) {
-    const uint4 q = reinterpret_cast<const uint4*>(xr)[i];
+  auto emit = [&](int i, const uint4& q) {
     const uint4 wq = reinterpret_cast<const uint4*>(w)[i];
     const T* e = reinterpret_cast<const T*>(&q);
     const T* we = reinterpret_cast<const T*>(&wq);
@@ -65,7 +82,14 @@ rms_norm_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict_
 #pragma unroll
     for (int k = 0; k < 8; ++k) oe[k] = fromf<T>(tof(e[k]) * r * tof(we[k]));
     reinterpret_cast<uint4*>(yr)[i] = o;
+  };
+#pragma unroll
+  for (int u = 0; u < kKeep; ++u) {
+    const int i = threadIdx.x + u * kNormThreads;
+    if (i < nvec) emit(i, keep[u]);
   }
+  for (int i = threadIdx.x + kKeep * kNormThreads; i < nvec; i += kNormThreads)
+    emit(i, reinterpret_cast<const uint4*>(xr)[i]);
   for (int i = nvec * 8 + threadIdx.x; i < dim; i += kNormThreads) yr[i] = fromf<T>(tof(xr[i]) * r * tof(w[i]));
 }
 
