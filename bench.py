@@ -614,6 +614,39 @@ def lm_head_logprobs_bench(dev, args, rank: int) -> dict:
     out["max_abs_diff_vs_torch"] = float((a - b).abs().max())
     del w, h
     torch.cuda.empty_cache()
+    # the rollout's next-token step for 64 rollouts (engine/base.py:180-193): torch's
+    # log_softmax + exp + multinomial + gather against one kvs_sample launch
+    rows = 64
+    x = torch.randn(rows, V, generator=g, device=dev) * 4
+    tgen = torch.Generator(device=dev).manual_seed(rank)
+
+    def torch_sample():
+        lp = torch.log_softmax(x / temp, dim=-1)
+        tok = torch.multinomial(lp.exp(), 1, generator=tgen).squeeze(1)
+        return tok, lp.gather(1, tok[:, None]).squeeze(1)
+
+    draws = iter(range(1 << 30))
+
+    def graphed_ms(greedy, n=20):  # kernel time: n launches replayed as one CUDA graph
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            ops.sample(x, temp, greedy, seed=rank, offset=0)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for i in range(n):
+                ops.sample(x, temp, greedy, seed=rank, offset=i)
+        return ev_time(graph.replay, reps=5) / n
+
+    s_ms = graphed_ms(False)
+    sgbs = rows * V * 4 / (s_ms * 1e-3) / 1e9
+    out["sampling"] = {"workload": "64 rows x vocab 128256 float32 logits, temperature 1",
+                       "torch_call_ms": ev_time(torch_sample, reps=20),
+                       "kvs_sample_call_ms": ev_time(lambda: ops.sample(x, temp, False, seed=rank,
+                                                                        offset=next(draws)), reps=20),
+                       "kvs_sample_kernel_ms": s_ms, "kvs_sample_gbs": sgbs,
+                       "kvs_sample_hbm_frac": sgbs / peaks["hbm_gbs"], "greedy_kernel_ms": graphed_ms(True)}
     return out
 
 

@@ -112,6 +112,8 @@ class BatchedKVStreams:
         self.temperature = float(temperature)
         self.greedy = greedy
         self.gen = torch.Generator(device=model.device).manual_seed(seed)
+        self.seed = int(seed)
+        self._draws = 0  # sampling calls so far: the Philox offset of the next one (ops.sample)
         self._next_seq = 0
         # decode steps replayed as CUDA graphs (one per batch size), see engine/graphs.py
         self.cuda_graphs = cuda_graphs
@@ -191,7 +193,17 @@ class BatchedKVStreams:
             r.live = self.cache.num_tokens(r.seq_id)
 
     def _sample(self, logits: torch.Tensor, forced: Optional[torch.Tensor]):
-        """Next token and its log-prob under temperature (engine/base.py:176-193), on the device."""
+        """Next token and its log-prob under temperature (engine/base.py:176-193), on the device:
+        on CUDA one pass per logits row (``kvs_sample``; ``kvs_lse_gather`` for forced tokens)."""
+        if logits.is_cuda:
+            from .. import ops
+
+            x = logits.float()  # log-probs are kept in float32 (as the torch path below)
+            if forced is not None:
+                return forced, ops.lse_gather(x, forced, self.temperature)[0]
+            tok, lp = ops.sample(x, self.temperature, self.greedy, seed=self.seed, offset=self._draws)
+            self._draws += 1
+            return tok, lp
         logp = torch.log_softmax(logits.float() / self.temperature, dim=-1)
         if forced is not None:
             tok = forced

@@ -270,6 +270,25 @@ def lse_gather(logits: torch.Tensor, targets: torch.Tensor, temperature: float =
     return logp, lse
 
 
+def sample(logits: torch.Tensor, temperature: float = 1.0, greedy: bool = False, seed: int = 0, offset: int = 0):
+    """``(tokens, logp)``: one next token per row of 2-D float32/float64 CUDA logits and its
+    ``log_softmax(logits / T)`` value (engine/base.py:180-193), in one launch.  Greedy takes the
+    row's argmax (first maximum); otherwise a draw from ``softmax(logits / T)`` by the Gumbel-max
+    rule over a Philox4x32-10 stream keyed by ``seed`` and ``offset`` (same pair, same tokens)."""
+    _check_cuda(logits)
+    if logits.dim() != 2 or logits.stride(1) != 1:
+        raise ValueError("logits must be a 2-D tensor with contiguous rows")
+    n, vocab = logits.shape
+    tokens = torch.empty(n, dtype=torch.long, device=logits.device)
+    logp = torch.empty(n, dtype=logits.dtype, device=logits.device)
+    mask = (1 << 64) - 1
+    rc = N.lib().kvs_sample(logits.data_ptr(), logits.stride(0), n, vocab, float(temperature),
+                            N.DTYPE_CODE[logits.dtype], int(bool(greedy)), int(seed) & mask, int(offset) & mask,
+                            tokens.data_ptr(), logp.data_ptr(), N.stream_ptr(logits.device))
+    N.check(rc, "kvs_sample")
+    return tokens, logp
+
+
 def lse_gather_backward(logits: torch.Tensor, targets: torch.Tensor, lse: torch.Tensor, grad: torch.Tensor,
                         temperature: float = 1.0, out_dtype: Optional[torch.dtype] = None,
                         out: Optional[torch.Tensor] = None) -> torch.Tensor:

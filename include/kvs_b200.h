@@ -404,6 +404,19 @@ int kvs_lse_gather_backward(const void* logits, int64_t ld, int32_t n_rows, int3
                             const void* lse, const void* grad, double temperature, int32_t dtype, void* dlogits,
                             int64_t ld_out, int32_t out_dtype, kvs_stream_t stream);
 
+/* The rollout's next-token step (engine/base.py:180-193: log_softmax(logits / T), then
+ * multinomial or argmax, and the token's log-prob) for a batch of logits rows [n_rows][ld]
+ * (KVS_F32 or KVS_F64) in one pass over each row.  greedy != 0: tokens[r] = the row's argmax
+ * (lowest index among equal maxima).  Otherwise a sample of softmax(x[r] / T) by the Gumbel-max
+ * rule, argmax_v x[r][v]/T - log(-log U_v), with U_v from a Philox4x32-10 stream (key = seed,
+ * counter = (v / 4, r, offset low word, offset high word), word v % 4; U = ((bits >> 9) + 0.5)
+ * * 2^-23): the same seed and offset give the same tokens, a new offset a new draw.
+ * logp[r] (logits dtype) = log_softmax(x[r] / T)[tokens[r]].  A row of -inf / NaN only gives
+ * tokens[r] = -1 and a NaN log-prob.  Replaces the per-row log_softmax + multinomial/argmax +
+ * gather (about 17 launches per batch) with one launch of 4-CTA clusters per row. */
+int kvs_sample(const void* logits, int64_t ld, int32_t n_rows, int32_t vocab, double temperature, int32_t dtype,
+               int32_t greedy, uint64_t seed, uint64_t offset, int64_t* tokens, void* logp, kvs_stream_t stream);
+
 /* The decoder layer's elementwise steps for half-precision models (KVS_BF16 / KVS_F16), one
  * pass each (model.py:29-36 RMSNorm, model.py:78-86 the MLP's silu(gate) * up):
  * y[r] = x[r] * rsqrt(mean(x[r]^2) + eps) * weight in fp32 with one rounding (rstd[r], optional
