@@ -53,6 +53,7 @@ constexpr int SMEM_NEW = 2 * HKV * D * 2;
 constexpr int SMEM_PREF = (MAX_SEQS + 1) * 4;
 constexpr int SMEM_TAB = TAB_CAP * 4;
 constexpr int SMEM_TOTAL = SMEM_STAGES + SMEM_Q + SMEM_NEW + SMEM_PREF + SMEM_TAB + 256;
+static_assert(HQ * 8 == NTHREADS, "start(): one thread per (query head, 16-byte chunk)");
 
 struct DecodeParams {
   kvs_cache c;
@@ -110,6 +111,11 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
 }
+__device__ __forceinline__ float2 unpack_bf16(uint32_t w) {
+  __nv_bfloat162 v;
+  memcpy(&v, &w, sizeof(w));
+  return __bfloat1622float2(v);
+}
 
 // byte offset of 16-byte chunk `c` (0..15) of row `r` (= token*HKV + head) inside a K or V stage
 __device__ __forceinline__ uint32_t swz(int r, int c) {
@@ -128,6 +134,15 @@ __device__ __forceinline__ float warp_sum_rows(float v) {
   v += __shfl_xor_sync(0xffffffffu, v, 16);
   return v;
 }
+
+// the global inputs of one sequence's start: its q chunk, new k / v chunks, inv_freq slice,
+// logical position and append row (owner = this CTA holds the sequence's last block)
+struct SeqIn {
+  uint4 q_lo, q_hi, k_lo, k_hi, v_c;
+  float4 f_lo, f_hi;
+  int64_t pos, row;
+  bool owner;
+};
 
 __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodeParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -184,6 +199,37 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
     }
     return lo;
   };
+
+  // A sequence's start inputs in one round of 16-byte loads: thread -> head h = tid / 8 and
+  // chunk d0 = 8 (tid % 8), i.e. elements d0 .. d0+7 of each half of the head.  Threads 0..63
+  // also load the new k (8 heads), threads 0..127 the new v, when this CTA appends the token.
+  auto load_seq = [&](int i) {
+    SeqIn s;
+    const int h = tid >> 3, d0 = (tid & 7) * 8;
+    s.pos = p.positions[i];
+    const int last = s_pref[i + 1] - 1;
+    s.owner = last >= g0 && last < g1;
+    const uint4* qsrc = reinterpret_cast<const uint4*>(p.q + (int64_t)i * p.q_stride + h * D + d0);
+    s.q_lo = qsrc[0];
+    s.q_hi = qsrc[D / 16];
+    s.f_lo = *reinterpret_cast<const float4*>(p.inv_freq + d0);
+    s.f_hi = *reinterpret_cast<const float4*>(p.inv_freq + d0 + 4);
+    s.k_lo = s.k_hi = s.v_c = make_uint4(0, 0, 0, 0);
+    s.row = 0;
+    if (s.owner) {
+      s.row = ((layer_rows + p.slot_blocks[i]) * BS + p.slot_offsets[i]) * HKV;
+      if (tid < HKV * 8) {
+        const uint4* ksrc = reinterpret_cast<const uint4*>(p.k_new + (int64_t)i * p.kv_stride + h * D + d0);
+        s.k_lo = ksrc[0];
+        s.k_hi = ksrc[D / 16];
+      }
+      if (tid < HKV * D / 8) s.v_c = reinterpret_cast<const uint4*>(p.v_new + (int64_t)i * p.kv_stride)[tid];
+    }
+    return s;
+  };
+  // the first sequence's loads overlap the table gather and the prologue's KV copies
+  const int first = seq_of(g0);
+  const SeqIn first_in = load_seq(first);
 
   // block ids of this CTA's range, gathered once (the copies below then need no global lookups)
   const bool tab_in_smem = (g1 - g0) <= TAB_CAP;
@@ -279,110 +325,109 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
     __syncthreads();
     if (*s_flag) {
       __threadfence();
-      // weights w[h][k] = 2^(m_k - M_h) / sum_k 2^(m_k - M_h) l_k, kept in q_s (its q is already in
-      // registers; start() rewrites it); partials beyond COMBINE_CAP fall back to direct loops
-      constexpr int COMBINE_CAP = SMEM_Q / 4 / HQ;  // 64 partials
-      float* w_s = reinterpret_cast<float*>(q_s);
-      if (expected <= COMBINE_CAP) {
-        for (int e = tid; e < HQ * expected; e += NTHREADS) {
-          const int h = e / expected, k = e % expected;
-          w_s[h * COMBINE_CAP + k] = __ldcg(p.part_ml + ((int64_t)(c0 + k + i) * HQ + h) * 2);
-        }
-        __syncthreads();
-        if (tid < HQ) {
-          float M = -INFINITY, den = 0.f;
-          for (int k = 0; k < expected; ++k) M = fmaxf(M, w_s[tid * COMBINE_CAP + k]);
-          for (int k = 0; k < expected; ++k) {
-            const float wk = exp2f(w_s[tid * COMBINE_CAP + k] - M);
-            den += wk * __ldcg(p.part_ml + ((int64_t)(c0 + k + i) * HQ + tid) * 2 + 1);
-            w_s[tid * COMBINE_CAP + k] = wk;
+      // thread -> head h = tid / 8, dims d0 = 16 (tid % 8) .. +16.  The partials are read four at
+      // a time with all their loads in flight and combined under a running maximum:
+      // out = sum_k 2^(m_k - M) o_k / sum_k 2^(m_k - M) l_k
+      const int h = tid >> 3, d0 = (tid & 7) * 16;
+      float M = -INFINITY, den = 0.f;
+      float4 o[4];
+#pragma unroll
+      for (int v = 0; v < 4; ++v) o[v] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int k0 = 0; k0 < expected; k0 += 4) {
+        float mk[4], lk[4];
+        float4 xk[4][4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          mk[u] = -INFINITY;
+          lk[u] = 0.f;
+#pragma unroll
+          for (int v = 0; v < 4; ++v) xk[u][v] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (k0 + u < expected) {
+            const int64_t slot = c0 + k0 + u + i;
+            const float* ml = p.part_ml + (slot * HQ + h) * 2;
+            mk[u] = __ldcg(ml);
+            lk[u] = __ldcg(ml + 1);
+            const float4* src = reinterpret_cast<const float4*>(p.part_o + (slot * HQ + h) * D + d0);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) xk[u][v] = __ldcg(src + v);
           }
-          const float inv = 1.f / den;
-          for (int k = 0; k < expected; ++k) w_s[tid * COMBINE_CAP + k] *= inv;
         }
-        __syncthreads();
-        // thread -> head tid/8, dims 16*(tid%8) .. +16: four independent float4 loads per partial
-        const int h = tid >> 3, d0 = (tid & 7) * 16;
-        float4 o[4] = {};
-#pragma unroll 4
-        for (int k = 0; k < expected; ++k) {
-          const float wk = w_s[h * COMBINE_CAP + k];
-          const float4* src = reinterpret_cast<const float4*>(p.part_o + ((int64_t)(c0 + k + i) * HQ + h) * D + d0);
+        float Mn = M;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) Mn = fmaxf(Mn, mk[u]);
+        const float sc = exp2f(M - Mn);  // 0 on the first group (M = -inf)
+        den *= sc;
+#pragma unroll
+        for (int v = 0; v < 4; ++v) o[v] = make_float4(o[v].x * sc, o[v].y * sc, o[v].z * sc, o[v].w * sc);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float w = exp2f(mk[u] - Mn);  // 0 for the slots beyond `expected`
+          den += w * lk[u];
 #pragma unroll
           for (int v = 0; v < 4; ++v) {
-            const float4 x = __ldcg(src + v);
-            o[v].x += wk * x.x;
-            o[v].y += wk * x.y;
-            o[v].z += wk * x.z;
-            o[v].w += wk * x.w;
+            o[v].x += w * xk[u][v].x;
+            o[v].y += w * xk[u][v].y;
+            o[v].z += w * xk[u][v].z;
+            o[v].w += w * xk[u][v].w;
           }
         }
-        uint32_t packed[8];
-#pragma unroll
-        for (int v = 0; v < 4; ++v) {
-          packed[2 * v] = pack_bf16(o[v].x, o[v].y);
-          packed[2 * v + 1] = pack_bf16(o[v].z, o[v].w);
-        }
-        int4* dst = reinterpret_cast<int4*>(p.out + ((int64_t)i * HQ + h) * D + d0);
-        dst[0] = make_int4(packed[0], packed[1], packed[2], packed[3]);
-        dst[1] = make_int4(packed[4], packed[5], packed[6], packed[7]);
-      } else {
-        for (int e = tid; e < HQ * D; e += NTHREADS) {
-          const int h = e / D;
-          float M = -INFINITY;
-          for (int cc = c0; cc <= c1; ++cc)
-            M = fmaxf(M, __ldcg(p.part_ml + ((int64_t)(cc + i) * HQ + h) * 2));
-          float num = 0.f, den = 0.f;
-          for (int cc = c0; cc <= c1; ++cc) {
-            const float* ml = p.part_ml + ((int64_t)(cc + i) * HQ + h) * 2;
-            const float w = exp2f(__ldcg(ml) - M);
-            den += w * __ldcg(ml + 1);
-            num += w * __ldcg(p.part_o + (int64_t)(cc + i) * HQ * D + e);
-          }
-          p.out[(int64_t)i * HQ * D + e] = __float2bfloat16_rn(num / den);
-        }
+        M = Mn;
       }
+      const float inv = 1.f / den;
+      uint32_t packed[8];
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        packed[2 * v] = pack_bf16(o[v].x * inv, o[v].y * inv);
+        packed[2 * v + 1] = pack_bf16(o[v].z * inv, o[v].w * inv);
+      }
+      int4* dst = reinterpret_cast<int4*>(p.out + ((int64_t)i * HQ + h) * D + d0);
+      dst[0] = make_int4(packed[0], packed[1], packed[2], packed[3]);
+      dst[1] = make_int4(packed[4], packed[5], packed[6], packed[7]);
       if (tid == 0) p.counters[i] = 0;  // ready for the next launch
     }
     __syncthreads();
   };
 
-  auto start = [&](int i) {
-    const int slot = p.seq_slots[i];
-    const int64_t pos = p.positions[i];
-    // RoPE of q into shared memory (same rotation as every other kernel of the library)
-    for (int e = tid; e < HQ * (D / 2); e += NTHREADS) {
-      const int h = e / (D / 2), d = e % (D / 2);
-      const __nv_bfloat16* qr = p.q + (int64_t)i * p.q_stride + h * D;
-      float r0, r1;
-      rope_rotate<float, float>(__bfloat162float(qr[d]), __bfloat162float(qr[d + D / 2]), pos, p.inv_freq[d], r0, r1);
-      q_s[h * D + d] = __float2bfloat16_rn(r0);
-      q_s[h * D + d + D / 2] = __float2bfloat16_rn(r1);
-    }
-    const int last = s_pref[i + 1] - 1;
-    if (last >= g0 && last < g1) {
-      // this CTA owns the sequence's last block: rotate + append the new token
-      const int64_t row = ((layer_rows + p.slot_blocks[i]) * BS + p.slot_offsets[i]) * HKV;
+  // RoPE of q into shared memory, and the append of the rotated new k and of v (same rotation
+  // as every other kernel of the library); pairs (d, d + D/2) of each head
+  auto apply_seq = [&](const SeqIn& in) {
+    const int h = tid >> 3, d0 = (tid & 7) * 8;
+    const int64_t pos = in.pos, row = in.row;
+    const float fr[8] = {in.f_lo.x, in.f_lo.y, in.f_lo.z, in.f_lo.w, in.f_hi.x, in.f_hi.y, in.f_hi.z, in.f_hi.w};
+    // words w of lo / hi hold elements (d0 + 2w, d0 + 2w + 1) and (d0 + D/2 + 2w, ...)
+    auto rot2 = [&](uint32_t lo, uint32_t hi, int w, uint32_t& out_lo, uint32_t& out_hi) {
+      const float2 a = unpack_bf16(lo), b = unpack_bf16(hi);
+      float r0, r1, r2, r3;
+      rope_rotate<float, float>(a.x, b.x, pos, fr[2 * w], r0, r1);
+      rope_rotate<float, float>(a.y, b.y, pos, fr[2 * w + 1], r2, r3);
+      out_lo = pack_bf16(r0, r2);
+      out_hi = pack_bf16(r1, r3);
+    };
+    auto rotate = [&](const uint4 lo, const uint4 hi, uint4& out_lo, uint4& out_hi) {
+      rot2(lo.x, hi.x, 0, out_lo.x, out_hi.x);
+      rot2(lo.y, hi.y, 1, out_lo.y, out_hi.y);
+      rot2(lo.z, hi.z, 2, out_lo.z, out_hi.z);
+      rot2(lo.w, hi.w, 3, out_lo.w, out_hi.w);
+    };
+    uint4 o_lo, o_hi;
+    rotate(in.q_lo, in.q_hi, o_lo, o_hi);
+    *reinterpret_cast<uint4*>(q_s + h * D + d0) = o_lo;
+    *reinterpret_cast<uint4*>(q_s + h * D + d0 + D / 2) = o_hi;
+    if (in.owner) {
       __nv_bfloat16* K = static_cast<__nv_bfloat16*>(c.k);
       __nv_bfloat16* V = static_cast<__nv_bfloat16*>(c.v);
-      for (int e = tid; e < HKV * (D / 2); e += NTHREADS) {
-        const int h = e / (D / 2), d = e % (D / 2);
-        const __nv_bfloat16* kr = p.k_new + (int64_t)i * p.kv_stride + h * D;
-        float r0, r1;
-        rope_rotate<float, float>(__bfloat162float(kr[d]), __bfloat162float(kr[d + D / 2]), pos, p.inv_freq[d], r0, r1);
-        const __nv_bfloat16 b0 = __float2bfloat16_rn(r0), b1 = __float2bfloat16_rn(r1);
-        knew_s[h * D + d] = b0;
-        knew_s[h * D + d + D / 2] = b1;
-        K[(row + h) * D + d] = b0;
-        K[(row + h) * D + d + D / 2] = b1;
+      if (tid < HKV * 8) {
+        rotate(in.k_lo, in.k_hi, o_lo, o_hi);
+        *reinterpret_cast<uint4*>(knew_s + h * D + d0) = o_lo;
+        *reinterpret_cast<uint4*>(knew_s + h * D + d0 + D / 2) = o_hi;
+        *reinterpret_cast<uint4*>(K + (row + h) * D + d0) = o_lo;
+        *reinterpret_cast<uint4*>(K + (row + h) * D + d0 + D / 2) = o_hi;
       }
-      for (int e = tid; e < HKV * D; e += NTHREADS) {
-        const __nv_bfloat16 x = p.v_new[(int64_t)i * p.kv_stride + e];
-        vnew_s[e] = x;
-        V[row * D + e] = x;
+      if (tid < HKV * D / 8) {
+        *reinterpret_cast<uint4*>(vnew_s + tid * 8) = in.v_c;
+        *reinterpret_cast<uint4*>(V + row * D + tid * 8) = in.v_c;
       }
     }
-    (void)slot;
     __syncthreads();
     const __nv_bfloat16* qh = q_s + (warp * G + g) * D;
 #pragma unroll
@@ -395,6 +440,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
     m0 = m1 = -INFINITY;
     l0 = l1 = 0.f;
   };
+  auto start = [&](int i) { apply_seq(load_seq(i)); };
+
+  cur = first;
+  apply_seq(first_in);
 
   for (int gb = g0; gb < g1; ++gb) {
     const int it = gb - g0;

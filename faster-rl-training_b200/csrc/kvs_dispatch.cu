@@ -83,7 +83,12 @@ KVS_API int kvs_paged_decode(const kvs_cache* c, const kvs_batch* b, const kvs_d
     }
     return kvs_paged_decode(c, &bs_, &as_, stream);
   }
-  if (out_aligned && kvs_decode_bf16_supported(c, b, a->n_heads))
+  // the fused bf16 decode kernel also reads q / k_new / v_new / inv_freq with 16-byte loads
+  const bool in_aligned = ((reinterpret_cast<uintptr_t>(a->q) | reinterpret_cast<uintptr_t>(a->k_new) |
+                            reinterpret_cast<uintptr_t>(a->v_new) | reinterpret_cast<uintptr_t>(a->inv_freq)) &
+                           15) == 0 &&
+                          a->q_stride % 8 == 0 && a->kv_stride % 8 == 0;
+  if (out_aligned && in_aligned && kvs_decode_bf16_supported(c, b, a->n_heads))
     return kvs_decode_bf16_launch(c, b, a, kvs_decode_bf16_grid(a->grid_ctas), st);
   if (b->cu_tokens != nullptr && out_aligned && kvs_prefill_tc_capable(c, a->n_heads)) {
     // chunks (prefill): RoPE + append, then the tensor-core paged attention in place on `out`
