@@ -11,8 +11,9 @@
 //     softmax, weighted V).
 //
 // Work split ("stream-K"): the blocks of all sequences, concatenated in batch order,
-// are cut into gridDim.x equal contiguous ranges, one per CTA (one CTA per SM), so
-// every SM streams the same number of KV bytes whatever the context lengths.  A
+// are cut into gridDim.x contiguous ranges of equal cost, one per CTA (one CTA per SM):
+// a block costs one unit and each sequence two more (its start and finish), so every SM
+// streams about the same number of KV bytes whatever the context lengths.  A
 // sequence cut by range boundaries yields one partial (m, l, O) per CTA; the last
 // CTA to finish a sequence (per-sequence arrival counter) merges its partials.
 //
@@ -52,6 +53,7 @@ constexpr int SMEM_Q = HQ * D * 2;
 constexpr int SMEM_NEW = 2 * HKV * D * 2;
 constexpr int SMEM_PREF = (MAX_SEQS + 1) * 4;
 constexpr int SMEM_TAB = TAB_CAP * 4;
+constexpr int SEQ_COST = 2;  // a stream's start + finish, in blocks of streaming time (work split)
 constexpr int SMEM_TOTAL = SMEM_STAGES + SMEM_Q + SMEM_NEW + SMEM_PREF + SMEM_TAB + 256;
 static_assert(HQ * 8 == NTHREADS, "start(): one thread per (query head, 16-byte chunk)");
 
@@ -181,10 +183,25 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
     if (tid == 0) s_pref[S] = total_nb;
   }
   __syncthreads();
+  // Cost units: every block is one, and every stream adds SEQ_COST in front of its first block
+  // (the start and finish work of a stream, ~2 blocks of streaming time), so a CTA that carries
+  // a stream boundary gets fewer blocks.  Global block gb of stream i sits at unit
+  // gb + SEQ_COST (i + 1); CTA c takes the units [c RU, (c + 1) RU).
   const int total = s_pref[S];
-  const int R = (total + gridDim.x - 1) / gridDim.x;
-  const int g0 = blockIdx.x * R;
-  const int g1 = min(total, g0 + R);
+  const int total_units = total + SEQ_COST * S;
+  const int RU = (total_units + gridDim.x - 1) / gridDim.x;
+  auto first_block = [&](int u) {  // the first block at unit >= u
+    if (u >= total_units) return total;
+    int lo = 0, hi = S - 1;  // last stream i with s_pref[i] + SEQ_COST i <= u
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (s_pref[mid] + SEQ_COST * mid <= u) lo = mid; else hi = mid - 1;
+    }
+    const int j = u - (s_pref[lo] + SEQ_COST * (lo + 1));
+    return j <= 0 ? s_pref[lo] : min(s_pref[lo] + j, s_pref[lo + 1]);
+  };
+  const int g0 = first_block(blockIdx.x * RU);
+  const int g1 = first_block(blockIdx.x * RU + RU);
   if (g0 >= g1) return;
 
   const uint8_t* Kpool = static_cast<const uint8_t*>(c.k);
@@ -278,7 +295,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
   auto finish = [&](int i) {
     // sequence i: this CTA's part is done; write it (or the final output) and merge if last
     const int P0 = s_pref[i], nb = s_pref[i + 1] - P0;
-    const int c0 = P0 / R, c1 = (P0 + nb - 1) / R;
+    const int c0 = (P0 + SEQ_COST * (i + 1)) / RU, c1 = (P0 + nb - 1 + SEQ_COST * (i + 1)) / RU;
     const int expected = c1 - c0 + 1;
     const float lt0 = warp_sum_rows(l0), lt1 = warp_sum_rows(l1);
     const int hq0 = warp * G + 2 * t;  // query heads hq0, hq0+1 (valid for t < 2)
