@@ -58,6 +58,8 @@ def _setup_cache(dtype, D, Hkv, bs, S, ctx, seed, extra_tokens=0):
     # fused kernel with CTA ranges spanning several sequences and sequences spanning several CTAs
     (torch.bfloat16, 128, 32, 8, 16, 1, 12, (500, 3000)),
     (torch.bfloat16, 128, 32, 8, 16, 1, 40, (16, 40)),
+    (torch.bfloat16, 128, 32, 8, 16, 1, 2, (12000, 16000)),   # ~74 partials per stream to combine
+    (torch.bfloat16, 128, 32, 8, 16, 1, 300, (1, 40)),        # several whole streams per CTA
     (torch.bfloat16, 128, 32, 8, 16, 7, 5, (3, 200)),
     (torch.bfloat16, 64, 8, 8, 1, 1, 5, (3, 200)),
 ])
