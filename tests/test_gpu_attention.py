@@ -306,3 +306,39 @@ def test_paged_forward_strided_qkv_equals_packed(dtype, D, Hq, Hkv, counts):
         pools.append((cache.k.clone(), cache.v.clone()))
     assert torch.equal(outs[0], outs[1])
     assert torch.equal(pools[0][0], pools[1][0]) and torch.equal(pools[0][1], pools[1][1])
+
+
+def test_paged_decode_unaligned_inputs_take_the_exact_path():
+    """q / k_new / v_new that are not 16-byte aligned (views one element into a buffer) run the
+    exact kernels instead of the fused decode kernel, which reads them with 16-byte loads: the
+    appended keys and values are bit-identical and the outputs agree within bf16 tolerance."""
+    from kvstreams import ops
+    from kvstreams.rope import RotaryEmbedding
+
+    dtype, D, Hq, Hkv, S = torch.bfloat16, 128, 32, 8, 9
+    cache, st = _setup_cache(dtype, D, Hkv, 16, S, (30, 600), seed=21)
+    inv = RotaryEmbedding(D, 5e5).table("cuda", dtype)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    q = torch.randn(S, Hq, D, generator=g, device="cuda").to(dtype)
+    k = torch.randn(S, Hkv, D, generator=g, device="cuda").to(dtype)
+    v = torch.randn(S, Hkv, D, generator=g, device="cuda").to(dtype)
+
+    def shifted(t):  # same values, one element past a 16-byte boundary
+        buf = torch.empty(t.numel() + 1, dtype=t.dtype, device=t.device)
+        view = buf[1:].view(t.shape)
+        view.copy_(t)
+        assert view.data_ptr() % 16 != 0
+        return view
+
+    pos = torch.as_tensor(st.next_positions, device="cuda")
+    snap = cache.snapshot_state()
+    outs, pools = [], []
+    for args in ((q, k, v), (shifted(q), shifted(k), shifted(v))):
+        cache.restore_state(snap)
+        mapping = cache.append_slots_batch(list(range(S)), pos)
+        out = ops.paged_forward(cache, list(range(S)), None, 0, *args, pos, mapping, inv, D ** -0.5)
+        cache.sync()
+        outs.append(out.float().clone())
+        pools.append((cache.k.clone(), cache.v.clone()))
+    assert torch.equal(pools[0][0], pools[1][0]) and torch.equal(pools[0][1], pools[1][1])
+    assert (outs[0] - outs[1]).abs().max().item() <= TOL[dtype]
