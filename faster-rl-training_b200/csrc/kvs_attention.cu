@@ -6,6 +6,8 @@
 // kvstreams/model.py:50-75 (Attention.forward): GQA by repeat_interleave
 // (head h reads kv head h // (n_heads / n_kv_heads)), scores * head_dim**-0.5,
 // masked softmax over keys, probabilities times values.
+#include <initializer_list>
+
 #include "kvs_common.cuh"
 #include "kvs_rope.cuh"
 
@@ -70,6 +72,151 @@ __global__ void rope_write_kv_kernel(kvs_cache c, int layer, const int32_t* __re
     V[dst + i] = v[src + i];
     V[dst + i + half] = v[src + i + half];
   }
+}
+
+// 16 bytes of T as accumulator values (and back, rounded as from_acc rounds)
+template <typename T> struct Pack16;
+template <> struct Pack16<float> {
+  static constexpr int n = 4;
+  static __device__ void unpack(const uint4& u, float (&x)[4]) {
+    x[0] = __uint_as_float(u.x), x[1] = __uint_as_float(u.y), x[2] = __uint_as_float(u.z), x[3] = __uint_as_float(u.w);
+  }
+  static __device__ uint4 pack(const float (&x)[4]) {
+    return make_uint4(__float_as_uint(x[0]), __float_as_uint(x[1]), __float_as_uint(x[2]), __float_as_uint(x[3]));
+  }
+};
+template <> struct Pack16<double> {
+  static constexpr int n = 2;
+  static __device__ void unpack(const uint4& u, double (&x)[2]) {
+    x[0] = __hiloint2double((int)u.y, (int)u.x), x[1] = __hiloint2double((int)u.w, (int)u.z);
+  }
+  static __device__ uint4 pack(const double (&x)[2]) {
+    return make_uint4((unsigned)__double2loint(x[0]), (unsigned)__double2hiint(x[0]), (unsigned)__double2loint(x[1]),
+                      (unsigned)__double2hiint(x[1]));
+  }
+};
+template <typename H, typename H2>
+struct PackHalf16 {
+  static constexpr int n = 8;
+  static __device__ float2 to2(uint32_t w) {
+    H2 v;
+    memcpy(&v, &w, 4);
+    return make_float2(to_acc<H>(v.x), to_acc<H>(v.y));
+  }
+  static __device__ uint32_t from2(float a, float b) {
+    H2 v;
+    v.x = from_acc<H>(a);
+    v.y = from_acc<H>(b);
+    uint32_t w;
+    memcpy(&w, &v, 4);
+    return w;
+  }
+  static __device__ void unpack(const uint4& u, float (&x)[8]) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 f = to2(w[k]);
+      x[2 * k] = f.x, x[2 * k + 1] = f.y;
+    }
+  }
+  static __device__ uint4 pack(const float (&x)[8]) {
+    return make_uint4(from2(x[0], x[1]), from2(x[2], x[3]), from2(x[4], x[5]), from2(x[6], x[7]));
+  }
+};
+template <> struct Pack16<__nv_bfloat16> : PackHalf16<__nv_bfloat16, __nv_bfloat162> {};
+template <> struct Pack16<__half> : PackHalf16<__half, __half2> {};
+
+// The same rotations with one angle per (token, frequency) shared by every head: thread ->
+// (token, chunk of V = 16 / sizeof(T) consecutive frequencies), sin / cos computed once, then
+// 16-byte loads of the chunk from both halves of each head.  Rows and heads 16-byte aligned.
+template <typename T, typename F>
+__global__ void rope_heads_kernel(const T* __restrict__ src, T* __restrict__ dst, const int64_t* __restrict__ pos,
+                                  int n_tokens, int n_heads, int D, const F* __restrict__ inv_freq,
+                                  int64_t src_stride) {
+  using A = typename Acc<T>::type;
+  using P = Pack16<T>;
+  constexpr int V = P::n;
+  const int half = D >> 1, chunks = half / V;
+  const int64_t total = (int64_t)n_tokens * chunks;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int t = (int)(idx / chunks);
+    const int i0 = (int)(idx - (int64_t)t * chunks) * V;
+    const int64_t p = pos[t];
+    A sn[V], cs[V];
+#pragma unroll
+    for (int k = 0; k < V; ++k) rope_sincos<A, F>(p, inv_freq[i0 + k], sn[k], cs[k]);
+    const T* srow = src + (int64_t)t * src_stride + i0;
+    T* drow = dst + (int64_t)t * n_heads * D + i0;
+#pragma unroll 4
+    for (int h = 0; h < n_heads; ++h) {
+      const uint4 ulo = *reinterpret_cast<const uint4*>(srow + (int64_t)h * D);
+      const uint4 uhi = *reinterpret_cast<const uint4*>(srow + (int64_t)h * D + half);
+      A a[V], b[V], r0[V], r1[V];
+      P::unpack(ulo, a);
+      P::unpack(uhi, b);
+#pragma unroll
+      for (int k = 0; k < V; ++k) rope_apply(a[k], b[k], sn[k], cs[k], r0[k], r1[k]);
+      *reinterpret_cast<uint4*>(drow + (int64_t)h * D) = P::pack(r0);
+      *reinterpret_cast<uint4*>(drow + (int64_t)h * D + half) = P::pack(r1);
+    }
+  }
+}
+
+// rope_write_kv_kernel with the same thread layout
+template <typename T, typename F>
+__global__ void rope_heads_write_kv_kernel(kvs_cache c, int layer, const int32_t* __restrict__ blocks,
+                                           const int32_t* __restrict__ offsets, const T* __restrict__ k,
+                                           const T* __restrict__ v, const int64_t* __restrict__ pos, int n_tokens,
+                                           const F* __restrict__ inv_freq, int64_t kv_stride) {
+  using A = typename Acc<T>::type;
+  using P = Pack16<T>;
+  constexpr int V = P::n;
+  const int D = c.head_dim, half = D >> 1, H = c.n_kv_heads, chunks = half / V;
+  T* K = static_cast<T*>(c.k);
+  T* Vp = static_cast<T*>(c.v);
+  const int64_t total = (int64_t)n_tokens * chunks;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int t = (int)(idx / chunks);
+    const int i0 = (int)(idx - (int64_t)t * chunks) * V;
+    const int64_t p = pos[t];
+    A sn[V], cs[V];
+#pragma unroll
+    for (int q = 0; q < V; ++q) rope_sincos<A, F>(p, inv_freq[i0 + q], sn[q], cs[q]);
+    const int64_t row = ((int64_t)layer * c.num_blocks + blocks[t]) * c.block_size + offsets[t];
+    const T* krow = k + (int64_t)t * kv_stride + i0;
+    const T* vrow = v + (int64_t)t * kv_stride + i0;
+    T* kdst = K + row * H * D + i0;
+    T* vdst = Vp + row * H * D + i0;
+#pragma unroll 2
+    for (int h = 0; h < H; ++h) {
+      const int64_t o = (int64_t)h * D;
+      const uint4 ulo = *reinterpret_cast<const uint4*>(krow + o);
+      const uint4 uhi = *reinterpret_cast<const uint4*>(krow + o + half);
+      const uint4 vlo = *reinterpret_cast<const uint4*>(vrow + o);
+      const uint4 vhi = *reinterpret_cast<const uint4*>(vrow + o + half);
+      A a[V], b[V], r0[V], r1[V];
+      P::unpack(ulo, a);
+      P::unpack(uhi, b);
+#pragma unroll
+      for (int q = 0; q < V; ++q) rope_apply(a[q], b[q], sn[q], cs[q], r0[q], r1[q]);
+      *reinterpret_cast<uint4*>(kdst + o) = P::pack(r0);
+      *reinterpret_cast<uint4*>(kdst + o + half) = P::pack(r1);
+      *reinterpret_cast<uint4*>(vdst + o) = vlo;
+      *reinterpret_cast<uint4*>(vdst + o + half) = vhi;
+    }
+  }
+}
+
+// whether the 16-byte-chunk kernels apply: every head row and half-row starts on 16 bytes
+template <typename T>
+bool rope_vec_ok(int D, int64_t stride, std::initializer_list<const void*> ptrs) {
+  constexpr int V = 16 / (int)sizeof(T);
+  if ((D / 2) % V != 0 || (stride * (int64_t)sizeof(T)) % 16 != 0) return false;
+  for (const void* q : ptrs)
+    if (reinterpret_cast<uintptr_t>(q) % 16 != 0) return false;
+  return true;
 }
 
 template <typename A>
@@ -254,6 +401,14 @@ int launch_rope(const void* src, void* dst, const int64_t* pos, int n_tokens, in
                 const void* inv_freq, cudaStream_t st, int64_t src_stride) {
   const int64_t total = (int64_t)n_tokens * n_heads * (D / 2);
   if (total == 0) return KVS_OK;
+  const int64_t sstride = src_stride ? src_stride : (int64_t)n_heads * D;
+  if (rope_vec_ok<T>(D, sstride, {src, dst})) {
+    const int64_t units = (int64_t)n_tokens * (D / 2 / Pack16<T>::n);
+    const int grid = (int)std::min<int64_t>((units + 255) / 256, 148 * 64);
+    rope_heads_kernel<T, F><<<grid, 256, 0, st>>>(static_cast<const T*>(src), static_cast<T*>(dst), pos, n_tokens,
+                                                  n_heads, D, static_cast<const F*>(inv_freq), sstride);
+    return launch_rc();
+  }
   const int grid = (int)std::min<int64_t>((total + 255) / 256, 148 * 32);
   rope_kernel<T, F><<<grid, 256, 0, st>>>(static_cast<const T*>(src), static_cast<T*>(dst), pos, n_tokens,
                                           n_heads, D, static_cast<const F*>(inv_freq),
@@ -267,6 +422,15 @@ int launch_rope_write(const kvs_cache& c, int layer, const int32_t* blocks, cons
                       cudaStream_t st, int64_t kv_stride) {
   const int64_t total = (int64_t)n_tokens * c.n_kv_heads * (c.head_dim / 2);
   if (total == 0) return KVS_OK;
+  const int64_t kstride = kv_stride ? kv_stride : (int64_t)c.n_kv_heads * c.head_dim;
+  if (rope_vec_ok<T>(c.head_dim, kstride, {k, v, c.k, c.v})) {
+    const int64_t units = (int64_t)n_tokens * (c.head_dim / 2 / Pack16<T>::n);
+    const int grid = (int)std::min<int64_t>((units + 255) / 256, 148 * 64);
+    rope_heads_write_kv_kernel<T, F><<<grid, 256, 0, st>>>(c, layer, blocks, offsets, static_cast<const T*>(k),
+                                                           static_cast<const T*>(v), pos, n_tokens,
+                                                           static_cast<const F*>(inv_freq), kstride);
+    return launch_rc();
+  }
   const int grid = (int)std::min<int64_t>((total + 255) / 256, 148 * 32);
   rope_write_kv_kernel<T, F><<<grid, 256, 0, st>>>(c, layer, blocks, offsets, static_cast<const T*>(k),
                                                    static_cast<const T*>(v), pos, n_tokens,

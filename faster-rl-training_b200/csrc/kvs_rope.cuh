@@ -15,27 +15,36 @@
 
 namespace kvs {
 
+// sin and cos of the angle float(position) * inv_freq[i], the product rounded once
 template <typename A, typename F>
-__device__ __forceinline__ void rope_rotate(A a, A b, int64_t pos, F inv_freq, A& r0, A& r1);
+__device__ __forceinline__ void rope_sincos(int64_t pos, F inv_freq, A& s, A& c);
 
 template <>
-__device__ __forceinline__ void rope_rotate<float, float>(float a, float b, int64_t pos, float inv_freq,
-                                                          float& r0, float& r1) {
-  const float ang = __fmul_rn((float)pos, inv_freq);
-  float s, c;
-  sincosf(ang, &s, &c);
+__device__ __forceinline__ void rope_sincos<float, float>(int64_t pos, float inv_freq, float& s, float& c) {
+  sincosf(__fmul_rn((float)pos, inv_freq), &s, &c);
+}
+
+template <>
+__device__ __forceinline__ void rope_sincos<double, double>(int64_t pos, double inv_freq, double& s, double& c) {
+  sincos(__dmul_rn((double)pos, inv_freq), &s, &c);
+}
+
+// the rotation of one pair by a precomputed angle, each product and sum rounded separately
+__device__ __forceinline__ void rope_apply(float a, float b, float s, float c, float& r0, float& r1) {
   r0 = __fadd_rn(__fmul_rn(a, c), __fmul_rn(-b, s));
   r1 = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));
 }
 
-template <>
-__device__ __forceinline__ void rope_rotate<double, double>(double a, double b, int64_t pos, double inv_freq,
-                                                            double& r0, double& r1) {
-  const double ang = __dmul_rn((double)pos, inv_freq);
-  double s, c;
-  sincos(ang, &s, &c);
+__device__ __forceinline__ void rope_apply(double a, double b, double s, double c, double& r0, double& r1) {
   r0 = __dadd_rn(__dmul_rn(a, c), __dmul_rn(-b, s));
   r1 = __dadd_rn(__dmul_rn(b, c), __dmul_rn(a, s));
+}
+
+template <typename A, typename F>
+__device__ __forceinline__ void rope_rotate(A a, A b, int64_t pos, F inv_freq, A& r0, A& r1) {
+  A s, c;
+  rope_sincos<A, F>(pos, inv_freq, s, c);
+  rope_apply(a, b, s, c, r0, r1);
 }
 
 }  // namespace kvs

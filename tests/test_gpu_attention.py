@@ -342,3 +342,25 @@ def test_paged_decode_unaligned_inputs_take_the_exact_path():
         pools.append((cache.k.clone(), cache.v.clone()))
     assert torch.equal(pools[0][0], pools[1][0]) and torch.equal(pools[0][1], pools[1][1])
     assert (outs[0] - outs[1]).abs().max().item() <= TOL[dtype]
+
+
+@pytest.mark.parametrize("dtype,D,H", [(torch.bfloat16, 128, 32), (torch.float16, 64, 8), (torch.float32, 128, 8),
+                                       (torch.float64, 16, 4)])
+def test_rope_vector_path_equals_scalar_path(dtype, D, H):
+    """The 16-byte-chunk RoPE kernel (one angle per token and frequency, shared by the heads)
+    gives the same bits as the per-pair kernel, which unaligned rows still take."""
+    from kvstreams import ops
+    from kvstreams.rope import RotaryEmbedding
+
+    n = 1000
+    g = torch.Generator(device="cuda").manual_seed(D + H)
+    x = torch.randn(n, H, D, generator=g, device="cuda", dtype=torch.float64).to(dtype)
+    pos = torch.randint(0, 200_000, (n,), generator=g, device="cuda")
+    inv = RotaryEmbedding(D, 5e5).table("cuda", dtype)
+    a = ops.rope_(x.clone(), pos, inv)
+    buf = torch.empty(x.numel() + 1, dtype=dtype, device="cuda")
+    xs = buf[1:].view(x.shape)
+    xs.copy_(x)
+    assert xs.data_ptr() % 16 != 0
+    b = ops.rope_(xs, pos, inv)
+    assert torch.equal(a, b)
