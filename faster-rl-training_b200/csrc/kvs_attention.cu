@@ -519,6 +519,16 @@ KVS_API int kvs_rope(void* x, int32_t dtype, const int64_t* positions, int32_t n
   return rope_dispatch(x, x, dtype, positions, n_tokens, n_heads, head_dim, inv_freq, to_cuda(stream));
 }
 
+KVS_API int kvs_rope_copy(const void* src, int64_t src_stride, void* dst, int32_t dtype, const int64_t* positions,
+                          int32_t n_tokens, int32_t n_heads, int32_t head_dim, const void* inv_freq,
+                          kvs_stream_t stream) {
+  if (!src || !dst || !positions || !inv_freq || n_tokens < 0 || n_heads <= 0 || head_dim <= 0 || head_dim % 2 ||
+      src_stride < 0 || (src_stride != 0 && src_stride < (int64_t)n_heads * head_dim))
+    return KVS_E_ARG;
+  return rope_dispatch(src, dst, dtype, positions, n_tokens, n_heads, head_dim, inv_freq, to_cuda(stream),
+                       src_stride);
+}
+
 KVS_API int kvs_paged_attention(const kvs_cache* c, const kvs_batch* b, int32_t layer, const void* q, void* out,
                                 int32_t n_heads, double scale, kvs_stream_t stream) {
   if (!c || !b || !q || !out || layer < 0 || layer >= c->n_layers || n_heads <= 0 ||

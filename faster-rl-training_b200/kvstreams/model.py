@@ -171,10 +171,9 @@ class _ReplayAttention(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, q, k, v, positions, evicted_at, lengths, inv_freq, scale):
-        q = q.detach().contiguous().clone()
-        k = k.detach().contiguous().clone()
-        ops.rope_(q, positions, inv_freq)
-        ops.rope_(k, positions, inv_freq)
+        # rotated copies straight out of the (possibly strided) projection output, one pass each
+        q = ops.rope(q.detach(), positions, inv_freq)
+        k = ops.rope(k.detach(), positions, inv_freq)
         v = v.detach().contiguous()
         grads = any(ctx.needs_input_grad[:3])
         B, T, Hq, _ = q.shape

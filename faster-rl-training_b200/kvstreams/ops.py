@@ -148,6 +148,25 @@ def replay_attention_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     return dq, dk, dv
 
 
+def rope(x: torch.Tensor, positions: torch.Tensor, inv_freq: torch.Tensor) -> torch.Tensor:
+    """RoPE of ``x [..., H, D]`` at ``positions [...]`` into a new contiguous tensor (rope.py:42-46),
+    in one pass that reads ``x`` where it lies when each token's ``[H][D]`` block is dense (the q or
+    k column block of a fused projection output)."""
+    _check_cuda(x)
+    H, D = x.shape[-2], x.shape[-1]
+    lead = tuple(x.shape[:-2])
+    n = int(np.prod(lead)) if lead else 1
+    rows, stride = _token_rows(x.reshape(n, H, D))
+    pos = positions.reshape(-1).to(device=x.device, dtype=torch.long).contiguous()
+    if pos.numel() != n:
+        raise ValueError("positions do not match x")
+    out = torch.empty(*lead, H, D, dtype=x.dtype, device=x.device)
+    rc = N.lib().kvs_rope_copy(rows.data_ptr(), stride, out.data_ptr(), N.DTYPE_CODE[x.dtype], pos.data_ptr(), n, H,
+                               D, inv_freq.data_ptr(), N.stream_ptr(x.device))
+    N.check(rc, "kvs_rope_copy")
+    return out
+
+
 def _token_rows(x: torch.Tensor):
     """``(x, row stride)`` when each token's ``[heads][head_dim]`` block of ``x`` is dense (the
     stride between tokens is then passed to the kernels), else ``(contiguous copy, 0)``."""

@@ -364,3 +364,22 @@ def test_rope_vector_path_equals_scalar_path(dtype, D, H):
     assert xs.data_ptr() % 16 != 0
     b = ops.rope_(xs, pos, inv)
     assert torch.equal(a, b)
+
+
+def test_rope_copy_from_fused_projection_equals_in_place():
+    """ops.rope on the q / k column blocks of a fused [tokens, q|k|v] output (one pass, strided
+    rows) gives the same bits as copying them out and rotating in place."""
+    from kvstreams import ops
+    from kvstreams.rope import RotaryEmbedding
+
+    B, T, Hq, Hkv, D = 2, 300, 32, 8, 128
+    g = torch.Generator(device="cuda").manual_seed(11)
+    qkv = torch.randn(B, T, (Hq + 2 * Hkv) * D, generator=g, device="cuda").bfloat16()
+    q = qkv[..., : Hq * D].view(B, T, Hq, D)
+    k = qkv[..., Hq * D: (Hq + Hkv) * D].view(B, T, Hkv, D)
+    pos = torch.randint(0, 40_000, (B, T), generator=g, device="cuda")
+    inv = RotaryEmbedding(D, 5e5).table("cuda", torch.bfloat16)
+    for x in (q, k):
+        got = ops.rope(x, pos, inv)
+        assert got.is_contiguous() and got.shape == x.shape
+        assert torch.equal(got, ops.rope_(x.contiguous().clone(), pos, inv))
