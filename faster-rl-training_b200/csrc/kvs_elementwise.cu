@@ -93,6 +93,102 @@ rms_norm_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict_
   for (int i = nvec * 8 + threadIdx.x; i < dim; i += kNormThreads) yr[i] = fromf<T>(tof(xr[i]) * r * tof(w[i]));
 }
 
+// RMSNorm backward with the forward's per-row rstd (model.py:29-36 differentiated):
+//   gx[r] = rstd_r (gxn - xn mean_j(gxn xn)),  xn = x[r] rstd_r,  gxn = gy[r] w   (fp32, one rounding)
+//   gw    = sum_r gy[r] xn[r]
+// A CTA takes rows blockIdx.x, blockIdx.x + gridDim.x, ...; thread t owns the 16-byte chunks
+// t and t + 512 (dim <= 8192) and keeps w and its gw sums in registers;
+// each CTA writes its gw sums to its own row of `part`, summed in CTA order by rms_norm_gw_kernel
+// (no float atomics: the result does not depend on scheduling).
+constexpr int kBwdThreads = 512, kBwdChunks = 2;
+
+template <typename T>
+__global__ void __launch_bounds__(kBwdThreads, 1)
+rms_norm_bwd_kernel(const T* __restrict__ x, const T* __restrict__ w, const float* __restrict__ rstd,
+                    const T* __restrict__ gy, T* __restrict__ gx, float* __restrict__ part, int64_t n_rows, int dim,
+                    int64_t ld_x, int64_t ld_gy, int64_t ld_gx) {
+  const int nvec = dim / 8;
+  float wf[kBwdChunks][8], acc[kBwdChunks][8];
+#pragma unroll
+  for (int u = 0; u < kBwdChunks; ++u) {
+    const int i = threadIdx.x + u * kBwdThreads;
+    uint4 wq = make_uint4(0, 0, 0, 0);
+    if (i < nvec) wq = reinterpret_cast<const uint4*>(w)[i];
+    const T* we = reinterpret_cast<const T*>(&wq);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      wf[u][k] = tof(we[k]);
+      acc[u][k] = 0.f;
+    }
+  }
+  __shared__ float red[kBwdThreads / 32];
+  for (int64_t row = blockIdx.x; row < n_rows; row += gridDim.x) {
+    const float r = rstd[row];
+    uint4 xq[kBwdChunks], gq[kBwdChunks];
+#pragma unroll
+    for (int u = 0; u < kBwdChunks; ++u) {
+      const int i = threadIdx.x + u * kBwdThreads;
+      xq[u] = gq[u] = make_uint4(0, 0, 0, 0);
+      if (i < nvec) {
+        xq[u] = reinterpret_cast<const uint4*>(x + row * ld_x)[i];
+        gq[u] = reinterpret_cast<const uint4*>(gy + row * ld_gy)[i];
+      }
+    }
+    float dot = 0.f;
+#pragma unroll
+    for (int u = 0; u < kBwdChunks; ++u) {
+      const T* xe = reinterpret_cast<const T*>(&xq[u]);
+      const T* ge = reinterpret_cast<const T*>(&gq[u]);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) dot += (tof(ge[k]) * wf[u][k]) * (tof(xe[k]) * r);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = dot;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < kBwdThreads / 32; ++i) tot += red[i];
+    __syncthreads();  // red is rewritten for the next row
+    const float mean = tot / (float)dim;
+#pragma unroll
+    for (int u = 0; u < kBwdChunks; ++u) {
+      const int i = threadIdx.x + u * kBwdThreads;
+      if (i >= nvec) break;
+      const T* xe = reinterpret_cast<const T*>(&xq[u]);
+      const T* ge = reinterpret_cast<const T*>(&gq[u]);
+      uint4 o;
+      T* oe = reinterpret_cast<T*>(&o);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float xn = tof(xe[k]) * r, g = tof(ge[k]);
+        oe[k] = fromf<T>(r * (g * wf[u][k] - xn * mean));
+        acc[u][k] += g * xn;
+      }
+      reinterpret_cast<uint4*>(gx + row * ld_gx)[i] = o;
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < kBwdChunks; ++u) {
+    const int i = threadIdx.x + u * kBwdThreads;
+    if (i >= nvec) break;
+    float4* dst = reinterpret_cast<float4*>(part + (int64_t)blockIdx.x * dim + i * 8);
+    dst[0] = make_float4(acc[u][0], acc[u][1], acc[u][2], acc[u][3]);
+    dst[1] = make_float4(acc[u][4], acc[u][5], acc[u][6], acc[u][7]);
+  }
+}
+
+// gw[j] = sum over the CTAs' partial rows, in CTA order
+__global__ void rms_norm_gw_kernel(const float* __restrict__ part, float* __restrict__ gw, int n_parts, int dim) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= dim) return;
+  float s = 0.f;
+  for (int c = 0; c < n_parts; ++c) s += part[(int64_t)c * dim + j];
+  gw[j] = s;
+}
+
+int norm_bwd_ctas(int64_t n_rows) { return (int)std::max<int64_t>(1, std::min<int64_t>(n_rows, 148)); }
+
 __device__ __forceinline__ float silu_f(float g) { return g / (1.f + __expf(-g)); }
 
 // out[r][j] = silu(gu[r][j]) * gu[r][F + j]; 8 outputs per thread
@@ -211,5 +307,41 @@ KVS_API int kvs_silu_mul_backward(const void* gu, const void* grad, void* dgu, i
                                                     static_cast<__half*>(dgu), n_rows, f, ld_gu, ld_grad, ld_dgu);
   else
     return KVS_E_UNSUPPORTED;
+  return launch_rc();
+}
+
+KVS_API size_t kvs_rms_norm_backward_scratch_bytes(int64_t n_rows, int32_t dim) {
+  if (n_rows <= 0 || dim <= 0) return 0;
+  return (size_t)norm_bwd_ctas(n_rows) * (size_t)dim * sizeof(float);
+}
+
+KVS_API int kvs_rms_norm_backward(const void* x, const void* weight, const float* rstd, const void* gy, void* gx,
+                                  float* gw, int64_t n_rows, int32_t dim, int64_t ld_x, int64_t ld_gy, int64_t ld_gx,
+                                  int32_t dtype, void* scratch, size_t scratch_bytes, kvs_stream_t stream) {
+  if (!x || !weight || !rstd || !gy || !gx || !gw || n_rows < 0 || dim <= 0 || ld_x < dim || ld_gy < dim ||
+      ld_gx < dim)
+    return KVS_E_ARG;
+  if (dim % 8 || dim > 8 * kBwdThreads * kBwdChunks || ld_x % 8 || ld_gy % 8 || ld_gx % 8 || !al16(x) ||
+      !al16(weight) || !al16(gy) || !al16(gx))
+    return KVS_E_UNSUPPORTED;
+  const cudaStream_t st = to_cuda(stream);
+  if (n_rows == 0) return cudaMemsetAsync(gw, 0, (size_t)dim * sizeof(float), st) == cudaSuccess ? KVS_OK : KVS_E_LAUNCH;
+  if (!scratch || scratch_bytes < kvs_rms_norm_backward_scratch_bytes(n_rows, dim) || !al16(scratch))
+    return KVS_E_SCRATCH;
+  const int grid = norm_bwd_ctas(n_rows);
+  float* part = static_cast<float*>(scratch);
+  if (dtype == KVS_BF16)
+    rms_norm_bwd_kernel<__nv_bfloat16><<<grid, kBwdThreads, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(weight), rstd,
+        static_cast<const __nv_bfloat16*>(gy), static_cast<__nv_bfloat16*>(gx), part, n_rows, dim, ld_x, ld_gy, ld_gx);
+  else if (dtype == KVS_F16)
+    rms_norm_bwd_kernel<__half><<<grid, kBwdThreads, 0, st>>>(
+        static_cast<const __half*>(x), static_cast<const __half*>(weight), rstd, static_cast<const __half*>(gy),
+        static_cast<__half*>(gx), part, n_rows, dim, ld_x, ld_gy, ld_gx);
+  else
+    return KVS_E_UNSUPPORTED;
+  int rc = launch_rc();
+  if (rc) return rc;
+  rms_norm_gw_kernel<<<(dim + 255) / 256, 256, 0, st>>>(part, gw, grid, dim);
   return launch_rc();
 }

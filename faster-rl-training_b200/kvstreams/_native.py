@@ -196,6 +196,9 @@ SIGNATURES = {
     "kvs_lse_gather": (C.c_int, [_P, C.c_int64, _I, _I, _P, C.c_double, _I, _P, _P, _P]),
     "kvs_sample": (C.c_int, [_P, C.c_int64, _I, _I, C.c_double, _I, _I, C.c_uint64, C.c_uint64, _P, _P, _P]),
     "kvs_rms_norm": (C.c_int, [_P, _P, _P, _P, C.c_int64, _I, C.c_int64, C.c_int64, C.c_double, _I, _P]),
+    "kvs_rms_norm_backward_scratch_bytes": (C.c_size_t, [C.c_int64, _I]),
+    "kvs_rms_norm_backward": (C.c_int, [_P, _P, _P, _P, _P, _P, C.c_int64, _I, C.c_int64, C.c_int64, C.c_int64, _I, _P,
+                                        C.c_size_t, _P]),
     "kvs_silu_mul": (C.c_int, [_P, _P, C.c_int64, _I, C.c_int64, C.c_int64, _I, _P]),
     "kvs_silu_mul_backward": (C.c_int, [_P, _P, _P, C.c_int64, _I, C.c_int64, C.c_int64, C.c_int64, _I, _P]),
     "kvs_lse_gather_backward": (C.c_int, [_P, C.c_int64, _I, _I, _P, _P, _P, C.c_double, _I, _P, C.c_int64, _I, _P]),

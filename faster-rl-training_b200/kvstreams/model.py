@@ -35,7 +35,8 @@ def _half_kernels(x: torch.Tensor, width: int) -> bool:
 
 
 class _RMSNormFn(torch.autograd.Function):
-    """RMSNorm (model.py:29-36) as one kernel pass; backward from the saved per-row rstd."""
+    """RMSNorm (model.py:29-36) as one kernel pass; backward (one pass, deterministic weight
+    gradient) from the saved per-row rstd."""
 
     @staticmethod
     def forward(ctx, x, w, eps):
@@ -46,12 +47,8 @@ class _RMSNormFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, gy):
         x, w, rstd = ctx.saved_tensors
-        r = rstd.unsqueeze(-1)
-        xn = x.float() * r
-        gxn = gy.float() * w.float()
-        gx = r * (gxn - xn * (gxn * xn).mean(-1, keepdim=True))
-        gw = (gy.float() * xn).reshape(-1, x.shape[-1]).sum(0)
-        return gx.to(x.dtype), gw.to(w.dtype), None
+        gx, gw = ops.rms_norm_backward(x, w, rstd, gy)
+        return gx, gw.to(w.dtype), None
 
 
 class _SiluMulFn(torch.autograd.Function):

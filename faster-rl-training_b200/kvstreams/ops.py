@@ -350,6 +350,26 @@ def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float):
     return y.view(x.shape), rstd.view(x.shape[:-1])
 
 
+def rms_norm_backward(x: torch.Tensor, weight: torch.Tensor, rstd: torch.Tensor, gy: torch.Tensor):
+    """``(gx, gw)``: gradients of :func:`rms_norm` for the upstream ``gy`` with the forward's
+    ``rstd``, one pass over the rows; ``gw`` float32, summed in a fixed order (deterministic)."""
+    _check_cuda(x, weight, rstd, gy)
+    x2, g2 = _rows2d(x), _rows2d(gy.to(x.dtype))
+    n, dim = x2.shape
+    gx = torch.empty(n, dim, dtype=x.dtype, device=x.device)
+    gw = torch.empty(dim, dtype=torch.float32, device=x.device)
+    r = rstd.reshape(-1).to(torch.float32).contiguous()
+    lib = N.lib()
+    scratch = torch.empty(max(int(lib.kvs_rms_norm_backward_scratch_bytes(n, dim)) // 4, 1), dtype=torch.float32,
+                          device=x.device)
+    rc = lib.kvs_rms_norm_backward(x2.data_ptr(), weight.contiguous().data_ptr(), r.data_ptr(), g2.data_ptr(),
+                                   gx.data_ptr(), gw.data_ptr(), n, dim, x2.stride(0), g2.stride(0), gx.stride(0),
+                                   N.DTYPE_CODE[x.dtype], scratch.data_ptr(), scratch.numel() * 4,
+                                   N.stream_ptr(x.device))
+    N.check(rc, "kvs_rms_norm_backward")
+    return gx.view(x.shape), gw
+
+
 def silu_mul(gu: torch.Tensor) -> torch.Tensor:
     """``silu(gate) * up`` of a fused ``[..., 2F]`` gate|up tensor (model.py:78-86), one pass."""
     _check_cuda(gu)

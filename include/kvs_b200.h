@@ -432,6 +432,14 @@ int kvs_sample(const void* logits, int64_t ld, int32_t n_rows, int32_t vocab, do
  * (KVS_E_UNSUPPORTED otherwise). */
 int kvs_rms_norm(const void* x, const void* weight, void* y, float* rstd, int64_t n_rows, int32_t dim, int64_t ld_x,
                  int64_t ld_y, double eps, int32_t dtype, kvs_stream_t stream);
+/* Its backward with the forward's rstd: gx[r] = rstd[r] (gxn - xn mean_j(gxn xn)), xn = x[r] rstd[r],
+ * gxn = gy[r] weight (fp32, one rounding of gx); gw (float32 [dim]) = sum_r gy[r] xn[r], summed per
+ * CTA and then across CTAs in a fixed order (the bits do not depend on scheduling).  dim <= 8192;
+ * scratch: kvs_rms_norm_backward_scratch_bytes(n_rows, dim) bytes, 16-byte aligned. */
+size_t kvs_rms_norm_backward_scratch_bytes(int64_t n_rows, int32_t dim);
+int kvs_rms_norm_backward(const void* x, const void* weight, const float* rstd, const void* gy, void* gx, float* gw,
+                          int64_t n_rows, int32_t dim, int64_t ld_x, int64_t ld_gy, int64_t ld_gx, int32_t dtype,
+                          void* scratch, size_t scratch_bytes, kvs_stream_t stream);
 int kvs_silu_mul(const void* gu, void* out, int64_t n_rows, int32_t f, int64_t ld_gu, int64_t ld_out, int32_t dtype,
                  kvs_stream_t stream);
 int kvs_silu_mul_backward(const void* gu, const void* grad, void* dgu, int64_t n_rows, int32_t f, int64_t ld_gu,

@@ -27,6 +27,29 @@ def test_rms_norm_matches_torch(rows, dim):
     assert (w.grad.float() - wr.grad).abs().max().item() <= 2e-2 * wr.grad.abs().max().item()
 
 
+@pytest.mark.parametrize("rows,dim", [(16384, 4096), (1, 8192), (777, 64)])
+def test_rms_norm_backward_kernel_matches_float64(rows, dim):
+    """kvs_rms_norm_backward against the float64 formula on the same bf16 inputs (gx within bf16
+    rounding, gw float32 to 1e-4 relative), and the same bits on a second call (gw is summed
+    per CTA and then in CTA order, without float atomics)."""
+    from kvstreams import ops
+
+    g = torch.Generator(device="cuda").manual_seed(rows + dim)
+    x = (torch.randn(rows, dim, generator=g, device="cuda") * 2).bfloat16()
+    w = (torch.rand(dim, generator=g, device="cuda") + 0.5).bfloat16()
+    gy = torch.randn(rows, dim, generator=g, device="cuda").bfloat16()
+    _, rstd = ops.rms_norm(x, w, 1e-5)
+    gx, gw = ops.rms_norm_backward(x, w, rstd, gy)
+    xd, wd, gd, rd = x.double(), w.double(), gy.double(), rstd.double()[:, None]
+    xn, gxn = xd * rd, gd * wd
+    want_gx = rd * (gxn - xn * (gxn * xn).mean(-1, keepdim=True))
+    want_gw = (gd * xn).sum(0)
+    assert ((gx.double() - want_gx).abs() / want_gx.abs().clamp_min(1e-2)).max().item() <= 2 ** -7
+    assert ((gw.double() - want_gw).abs().max() / want_gw.abs().max()).item() <= 1e-4
+    gx2, gw2 = ops.rms_norm_backward(x, w, rstd, gy)
+    assert torch.equal(gx, gx2) and torch.equal(gw, gw2)
+
+
 @pytest.mark.parametrize("rows,f", [(64, 14336), (5, 24), (300, 512)])
 def test_silu_mul_matches_torch(rows, f):
     from kvstreams.model import _SiluMulFn
