@@ -24,7 +24,8 @@ namespace {
 // (tokens) are src_stride elements apart, dst rows packed.
 template <typename T, typename F>
 __global__ void rope_kernel(const T* __restrict__ src, T* __restrict__ dst, const int64_t* __restrict__ pos,
-                            int n_tokens, int n_heads, int D, const F* __restrict__ inv_freq, int64_t src_stride) {
+                            int n_tokens, int n_heads, int D, const F* __restrict__ inv_freq, int64_t src_stride,
+                            int64_t dst_stride) {
   const int half = D >> 1;
   const int64_t total = (int64_t)n_tokens * n_heads * half;
   for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
@@ -32,7 +33,7 @@ __global__ void rope_kernel(const T* __restrict__ src, T* __restrict__ dst, cons
     const int i = (int)(idx % half);
     const int64_t th = idx / half;
     const int t = (int)(th / n_heads);
-    const int64_t base = th * D;
+    const int64_t base = (int64_t)t * dst_stride + (th - (int64_t)t * n_heads) * D;
     const int64_t sbase = (int64_t)t * src_stride + (th - (int64_t)t * n_heads) * D;
     using A = typename Acc<T>::type;
     A a = to_acc(src[sbase + i]), b = to_acc(src[sbase + i + half]);
@@ -132,7 +133,7 @@ template <> struct Pack16<__half> : PackHalf16<__half, __half2> {};
 template <typename T, typename F>
 __global__ void rope_heads_kernel(const T* __restrict__ src, T* __restrict__ dst, const int64_t* __restrict__ pos,
                                   int n_tokens, int n_heads, int D, const F* __restrict__ inv_freq,
-                                  int64_t src_stride) {
+                                  int64_t src_stride, int64_t dst_stride) {
   using A = typename Acc<T>::type;
   using P = Pack16<T>;
   constexpr int V = P::n;
@@ -147,7 +148,7 @@ __global__ void rope_heads_kernel(const T* __restrict__ src, T* __restrict__ dst
 #pragma unroll
     for (int k = 0; k < V; ++k) rope_sincos<A, F>(p, inv_freq[i0 + k], sn[k], cs[k]);
     const T* srow = src + (int64_t)t * src_stride + i0;
-    T* drow = dst + (int64_t)t * n_heads * D + i0;
+    T* drow = dst + (int64_t)t * dst_stride + i0;
 #pragma unroll 4
     for (int h = 0; h < n_heads; ++h) {
       const uint4 ulo = *reinterpret_cast<const uint4*>(srow + (int64_t)h * D);
@@ -211,9 +212,11 @@ __global__ void rope_heads_write_kv_kernel(kvs_cache c, int layer, const int32_t
 
 // whether the 16-byte-chunk kernels apply: every head row and half-row starts on 16 bytes
 template <typename T>
-bool rope_vec_ok(int D, int64_t stride, std::initializer_list<const void*> ptrs) {
+bool rope_vec_ok(int D, std::initializer_list<int64_t> strides, std::initializer_list<const void*> ptrs) {
   constexpr int V = 16 / (int)sizeof(T);
-  if ((D / 2) % V != 0 || (stride * (int64_t)sizeof(T)) % 16 != 0) return false;
+  if ((D / 2) % V != 0) return false;
+  for (int64_t stride : strides)
+    if ((stride * (int64_t)sizeof(T)) % 16 != 0) return false;
   for (const void* q : ptrs)
     if (reinterpret_cast<uintptr_t>(q) % 16 != 0) return false;
   return true;
@@ -398,21 +401,21 @@ int launch_replay_generic(const kvs_replay_args& a, cudaStream_t st) {
 
 template <typename T, typename F>
 int launch_rope(const void* src, void* dst, const int64_t* pos, int n_tokens, int n_heads, int D,
-                const void* inv_freq, cudaStream_t st, int64_t src_stride) {
+                const void* inv_freq, cudaStream_t st, int64_t src_stride, int64_t dst_stride) {
   const int64_t total = (int64_t)n_tokens * n_heads * (D / 2);
   if (total == 0) return KVS_OK;
   const int64_t sstride = src_stride ? src_stride : (int64_t)n_heads * D;
-  if (rope_vec_ok<T>(D, sstride, {src, dst})) {
+  const int64_t dstride = dst_stride ? dst_stride : (int64_t)n_heads * D;
+  if (rope_vec_ok<T>(D, {sstride, dstride}, {src, dst})) {
     const int64_t units = (int64_t)n_tokens * (D / 2 / Pack16<T>::n);
     const int grid = (int)std::min<int64_t>((units + 255) / 256, 148 * 64);
     rope_heads_kernel<T, F><<<grid, 256, 0, st>>>(static_cast<const T*>(src), static_cast<T*>(dst), pos, n_tokens,
-                                                  n_heads, D, static_cast<const F*>(inv_freq), sstride);
+                                                  n_heads, D, static_cast<const F*>(inv_freq), sstride, dstride);
     return launch_rc();
   }
   const int grid = (int)std::min<int64_t>((total + 255) / 256, 148 * 32);
   rope_kernel<T, F><<<grid, 256, 0, st>>>(static_cast<const T*>(src), static_cast<T*>(dst), pos, n_tokens,
-                                          n_heads, D, static_cast<const F*>(inv_freq),
-                                          src_stride ? src_stride : (int64_t)n_heads * D);
+                                          n_heads, D, static_cast<const F*>(inv_freq), sstride, dstride);
   return launch_rc();
 }
 
@@ -423,7 +426,7 @@ int launch_rope_write(const kvs_cache& c, int layer, const int32_t* blocks, cons
   const int64_t total = (int64_t)n_tokens * c.n_kv_heads * (c.head_dim / 2);
   if (total == 0) return KVS_OK;
   const int64_t kstride = kv_stride ? kv_stride : (int64_t)c.n_kv_heads * c.head_dim;
-  if (rope_vec_ok<T>(c.head_dim, kstride, {k, v, c.k, c.v})) {
+  if (rope_vec_ok<T>(c.head_dim, {kstride}, {k, v, c.k, c.v})) {
     const int64_t units = (int64_t)n_tokens * (c.head_dim / 2 / Pack16<T>::n);
     const int grid = (int)std::min<int64_t>((units + 255) / 256, 148 * 64);
     rope_heads_write_kv_kernel<T, F><<<grid, 256, 0, st>>>(c, layer, blocks, offsets, static_cast<const T*>(k),
@@ -440,12 +443,17 @@ int launch_rope_write(const kvs_cache& c, int layer, const int32_t* blocks, cons
 }
 
 int rope_dispatch(const void* src, void* dst, int dtype, const int64_t* pos, int n_tokens, int n_heads, int D,
-                  const void* inv_freq, cudaStream_t st, int64_t src_stride = 0) {
+                  const void* inv_freq, cudaStream_t st, int64_t src_stride = 0, int64_t dst_stride = 0) {
   switch (dtype) {
-    case KVS_F32: return launch_rope<float, float>(src, dst, pos, n_tokens, n_heads, D, inv_freq, st, src_stride);
-    case KVS_F64: return launch_rope<double, double>(src, dst, pos, n_tokens, n_heads, D, inv_freq, st, src_stride);
-    case KVS_BF16: return launch_rope<__nv_bfloat16, float>(src, dst, pos, n_tokens, n_heads, D, inv_freq, st, src_stride);
-    case KVS_F16: return launch_rope<__half, float>(src, dst, pos, n_tokens, n_heads, D, inv_freq, st, src_stride);
+    case KVS_F32:
+      return launch_rope<float, float>(src, dst, pos, n_tokens, n_heads, D, inv_freq, st, src_stride, dst_stride);
+    case KVS_F64:
+      return launch_rope<double, double>(src, dst, pos, n_tokens, n_heads, D, inv_freq, st, src_stride, dst_stride);
+    case KVS_BF16:
+      return launch_rope<__nv_bfloat16, float>(src, dst, pos, n_tokens, n_heads, D, inv_freq, st, src_stride,
+                                               dst_stride);
+    case KVS_F16:
+      return launch_rope<__half, float>(src, dst, pos, n_tokens, n_heads, D, inv_freq, st, src_stride, dst_stride);
   }
   return KVS_E_UNSUPPORTED;
 }
@@ -519,14 +527,15 @@ KVS_API int kvs_rope(void* x, int32_t dtype, const int64_t* positions, int32_t n
   return rope_dispatch(x, x, dtype, positions, n_tokens, n_heads, head_dim, inv_freq, to_cuda(stream));
 }
 
-KVS_API int kvs_rope_copy(const void* src, int64_t src_stride, void* dst, int32_t dtype, const int64_t* positions,
-                          int32_t n_tokens, int32_t n_heads, int32_t head_dim, const void* inv_freq,
-                          kvs_stream_t stream) {
+KVS_API int kvs_rope_copy(const void* src, int64_t src_stride, void* dst, int64_t dst_stride, int32_t dtype,
+                          const int64_t* positions, int32_t n_tokens, int32_t n_heads, int32_t head_dim,
+                          const void* inv_freq, kvs_stream_t stream) {
+  const int64_t row = (int64_t)n_heads * head_dim;
   if (!src || !dst || !positions || !inv_freq || n_tokens < 0 || n_heads <= 0 || head_dim <= 0 || head_dim % 2 ||
-      src_stride < 0 || (src_stride != 0 && src_stride < (int64_t)n_heads * head_dim))
+      src_stride < 0 || (src_stride != 0 && src_stride < row) || dst_stride < 0 || (dst_stride != 0 && dst_stride < row))
     return KVS_E_ARG;
   return rope_dispatch(src, dst, dtype, positions, n_tokens, n_heads, head_dim, inv_freq, to_cuda(stream),
-                       src_stride);
+                       src_stride, dst_stride);
 }
 
 KVS_API int kvs_paged_attention(const kvs_cache* c, const kvs_batch* b, int32_t layer, const void* q, void* out,

@@ -180,7 +180,7 @@ SIGNATURES = {
     "kvs_check_scratch_bytes": (_Z, [_I]),
     "kvs_check_invariants": (C.c_int, [_P, _P, _P, _P, _Z, _P]),
     "kvs_rope": (C.c_int, [_P, _I, _P, _I, _I, _I, _P, _P]),
-    "kvs_rope_copy": (C.c_int, [_P, C.c_int64, _P, _I, _P, _I, _I, _I, _P, _P]),
+    "kvs_rope_copy": (C.c_int, [_P, C.c_int64, _P, C.c_int64, _I, _P, _I, _I, _I, _P, _P]),
     "kvs_paged_attention": (C.c_int, [_P, _P, _I, _P, _P, _I, C.c_double, _P]),
     "kvs_decode_scratch_bytes": (_Z, [_P, _I, _I, _I]),
     "kvs_paged_decode": (C.c_int, [_P, _P, _P, _P]),

@@ -112,11 +112,16 @@ class Attention(nn.Module):
         self.v_proj = nn.Linear(cfg.d_model, cfg.n_kv_heads * cfg.head_dim, bias=False)
         self.o_proj = nn.Linear(cfg.n_heads * cfg.head_dim, cfg.d_model, bias=False)
 
-    def project(self, x: torch.Tensor):
-        """q, k, v of ``x`` (one GEMM over the concatenated projection weights)."""
-        lead = x.shape[:-1]
+    def project_qkv(self, x: torch.Tensor) -> torch.Tensor:
+        """The fused ``[..., (Hq + 2 Hkv) D]`` q|k|v projection of ``x`` (one GEMM over the
+        concatenated projection weights)."""
         w = _fused_weight(self, "_qkv", (self.q_proj.weight, self.k_proj.weight, self.v_proj.weight))
-        qkv = F.linear(x, w)
+        return F.linear(x, w)
+
+    def project(self, x: torch.Tensor):
+        """q, k, v of ``x``: views of :meth:`project_qkv`'s output."""
+        lead = x.shape[:-1]
+        qkv = self.project_qkv(x)
         nq, nk = self.n_heads * self.head_dim, self.n_kv_heads * self.head_dim
         q = qkv[..., :nq].reshape(*lead, self.n_heads, self.head_dim)
         k = qkv[..., nq:nq + nk].reshape(*lead, self.n_kv_heads, self.head_dim)
@@ -161,34 +166,44 @@ def causal_mask(T: int, device=None) -> torch.Tensor:
 
 
 class _ReplayAttention(torch.autograd.Function):
-    """RoPE of q/k at ``positions`` plus masked replay attention, as one autograd node.
+    """RoPE of q/k at ``positions`` plus masked replay attention, as one autograd node over the
+    fused q|k|v projection output ``qkv [B, T, (Hq + 2 Hkv) D]``; ``heads`` = (Hq, Hkv, D).
 
-    Backward: the replay attention backward kernels give the gradients of the rotated q/k
-    and of v; RoPE is a rotation, so its backward rotates back (RoPE at -positions)."""
+    Backward: the replay attention backward kernels give the gradients of the rotated q/k and of
+    v; RoPE is a rotation, so its backward rotates back (RoPE at -positions), written straight
+    into the column blocks of the fused gradient (no zero-filled slice gradients to add up)."""
 
     @staticmethod
-    def forward(ctx, q, k, v, positions, evicted_at, lengths, inv_freq, scale):
-        # rotated copies straight out of the (possibly strided) projection output, one pass each
-        q = ops.rope(q.detach(), positions, inv_freq)
-        k = ops.rope(k.detach(), positions, inv_freq)
-        v = v.detach().contiguous()
-        grads = any(ctx.needs_input_grad[:3])
-        B, T, Hq, _ = q.shape
+    def forward(ctx, qkv, heads, positions, evicted_at, lengths, inv_freq, scale):
+        Hq, Hkv, D = heads
+        B, T, _ = qkv.shape
+        nq, nk = Hq * D, Hkv * D
+        qkv = qkv.detach()
+        # rotated copies straight out of the projection output, one pass each
+        q = ops.rope(qkv[..., :nq].view(B, T, Hq, D), positions, inv_freq)
+        k = ops.rope(qkv[..., nq:nq + nk].view(B, T, Hkv, D), positions, inv_freq)
+        v = qkv[..., nq + nk:].reshape(B, T, Hkv, D).contiguous()
+        grads = ctx.needs_input_grad[0]
         lse = ops.row_lse_buffer(B, Hq, T, q.device) if grads else None
         out = ops.replay_attention(q, k, v, evicted_at, lengths, scale, row_lse=lse)
         if grads:
             ctx.save_for_backward(q, k, v, out, positions, evicted_at, lengths, inv_freq, lse)
-        ctx.scale = scale
+        ctx.scale, ctx.heads = scale, heads
         return out
 
     @staticmethod
     def backward(ctx, grad_out):
         q, k, v, out, positions, evicted_at, lengths, inv_freq, lse = ctx.saved_tensors
         dq, dk, dv = ops.replay_attention_backward(q, k, v, evicted_at, lengths, ctx.scale, out, grad_out, row_lse=lse)
+        Hq, Hkv, D = ctx.heads
+        B, T = dq.shape[:2]
+        nq, nk = Hq * D, Hkv * D
+        dqkv = torch.empty(B, T, nq + 2 * nk, dtype=dq.dtype, device=dq.device)
         neg = -positions
-        ops.rope_(dq, neg, inv_freq)
-        ops.rope_(dk, neg, inv_freq)
-        return dq, dk, dv, None, None, None, None, None
+        ops.rope(dq, neg, inv_freq, out=dqkv[..., :nq].view(B, T, Hq, D))
+        ops.rope(dk, neg, inv_freq, out=dqkv[..., nq:nq + nk].view(B, T, Hkv, D))
+        dqkv[..., nq + nk:].copy_(dv.view(B, T, nk))
+        return dqkv, None, None, None, None, None, None
 
 
 def as_replay_mask(mask, B: int, T: int, device) -> ReplayMask:
@@ -251,8 +266,10 @@ class TinyLM(nn.Module):
         inv = self.rope.table(dev, self.dtype)
         x = self.embed(tokens)
         for blk in self.layers:
-            q, k, v = blk.attn.project(blk.attn_norm(x))
-            a = _ReplayAttention.apply(q, k, v, positions, rm.evicted_at, rm.lengths, inv, blk.attn.scale)
+            at = blk.attn
+            qkv = at.project_qkv(blk.attn_norm(x))
+            a = _ReplayAttention.apply(qkv, (at.n_heads, at.n_kv_heads, at.head_dim), positions, rm.evicted_at,
+                                       rm.lengths, inv, at.scale)
             x2 = blk.attn_residual(x.reshape(B * T, -1), a.reshape(B * T, -1))
             x = blk.mlp_residual(x2).view(B, T, -1)
         return self.norm(x)

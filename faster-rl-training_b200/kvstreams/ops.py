@@ -148,10 +148,12 @@ def replay_attention_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     return dq, dk, dv
 
 
-def rope(x: torch.Tensor, positions: torch.Tensor, inv_freq: torch.Tensor) -> torch.Tensor:
-    """RoPE of ``x [..., H, D]`` at ``positions [...]`` into a new contiguous tensor (rope.py:42-46),
-    in one pass that reads ``x`` where it lies when each token's ``[H][D]`` block is dense (the q or
-    k column block of a fused projection output)."""
+def rope(x: torch.Tensor, positions: torch.Tensor, inv_freq: torch.Tensor,
+         out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """RoPE of ``x [..., H, D]`` at ``positions [...]`` (rope.py:42-46) in one pass, out of place:
+    ``x`` is read where it lies when each token's ``[H][D]`` block is dense (the q or k column
+    block of a fused projection output); the result goes to a new contiguous tensor, or to
+    ``out`` (same shape, dense token blocks, e.g. a column block of a fused gradient)."""
     _check_cuda(x)
     H, D = x.shape[-2], x.shape[-1]
     lead = tuple(x.shape[:-2])
@@ -160,9 +162,18 @@ def rope(x: torch.Tensor, positions: torch.Tensor, inv_freq: torch.Tensor) -> to
     pos = positions.reshape(-1).to(device=x.device, dtype=torch.long).contiguous()
     if pos.numel() != n:
         raise ValueError("positions do not match x")
-    out = torch.empty(*lead, H, D, dtype=x.dtype, device=x.device)
-    rc = N.lib().kvs_rope_copy(rows.data_ptr(), stride, out.data_ptr(), N.DTYPE_CODE[x.dtype], pos.data_ptr(), n, H,
-                               D, inv_freq.data_ptr(), N.stream_ptr(x.device))
+    if out is None:
+        out = torch.empty(*lead, H, D, dtype=x.dtype, device=x.device)
+        dst, dstride = out, 0
+    else:
+        if out.shape != x.shape or out.dtype != x.dtype or out.device != x.device:
+            raise ValueError("out must match x in shape, dtype and device")
+        dst = out.reshape(n, H, D)
+        if dst.data_ptr() != out.data_ptr() or dst.stride(2) != 1 or dst.stride(1) != D or dst.stride(0) < H * D:
+            raise ValueError("out needs dense [H][D] token blocks")
+        dstride = int(dst.stride(0))
+    rc = N.lib().kvs_rope_copy(rows.data_ptr(), stride, dst.data_ptr(), dstride, N.DTYPE_CODE[x.dtype],
+                               pos.data_ptr(), n, H, D, inv_freq.data_ptr(), N.stream_ptr(x.device))
     N.check(rc, "kvs_rope_copy")
     return out
 

@@ -205,12 +205,14 @@ int kvs_check_invariants(const kvs_cache* c, const kvs_batch* b, int32_t* out_co
  * inv_freq: [head_dim/2] float (f32/bf16/f16 activations) or double (f64). */
 int kvs_rope(void* x, int32_t dtype, const int64_t* positions, int32_t n_tokens, int32_t n_heads,
              int32_t head_dim, const void* inv_freq, kvs_stream_t stream);
-/* The same rotation out of place, in one pass: src token rows src_stride elements apart (each
- * row's [n_heads][head_dim] block dense, e.g. the q or k column block of a fused q|k|v projection
- * output; 0 = packed) into packed dst [n_tokens][n_heads][head_dim].  Replaces the copy of q / k
- * out of the projection output followed by the in-place rotation (model.py:62-63). */
-int kvs_rope_copy(const void* src, int64_t src_stride, void* dst, int32_t dtype, const int64_t* positions,
-                  int32_t n_tokens, int32_t n_heads, int32_t head_dim, const void* inv_freq, kvs_stream_t stream);
+/* The same rotation out of place, in one pass: src token rows src_stride elements apart, dst token
+ * rows dst_stride apart (each row's [n_heads][head_dim] block dense; 0 = packed rows), e.g. q or k
+ * read from / written to their column block of a fused q|k|v tensor.  Replaces the copy of q / k
+ * out of the projection output followed by the in-place rotation (model.py:62-63), and in the
+ * backward the assembly of the fused gradient from the rotated-back dq / dk. */
+int kvs_rope_copy(const void* src, int64_t src_stride, void* dst, int64_t dst_stride, int32_t dtype,
+                  const int64_t* positions, int32_t n_tokens, int32_t n_heads, int32_t head_dim, const void* inv_freq,
+                  kvs_stream_t stream);
 
 /* Paged attention of the new tokens of each sequence over its live cache entries
  * (Attention.forward in cached mode, model.py:50-75 with the kv_hook of

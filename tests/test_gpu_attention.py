@@ -383,3 +383,8 @@ def test_rope_copy_from_fused_projection_equals_in_place():
         got = ops.rope(x, pos, inv)
         assert got.is_contiguous() and got.shape == x.shape
         assert torch.equal(got, ops.rope_(x.contiguous().clone(), pos, inv))
+    # and back: packed rows rotated into a column block of a fused tensor
+    dst = torch.zeros_like(qkv)
+    ops.rope(q.contiguous(), -pos, inv, out=dst[..., : Hq * D].view(B, T, Hq, D))
+    assert torch.equal(dst[..., : Hq * D].reshape(B, T, Hq, D), ops.rope_(q.contiguous().clone(), -pos, inv))
+    assert not dst[..., Hq * D:].any()
