@@ -250,6 +250,17 @@ def check(rc: int, what: str) -> None:
         raise RuntimeError(f"{what} failed: {RC_NAMES.get(rc, rc)} (rc={rc})")
 
 
+def to_device(values, dtype: torch.dtype, device) -> torch.Tensor:
+    """A host list or array as a tensor on ``device`` without waiting for the GPU: staged in pinned
+    memory and copied on the current stream (a copy from pageable memory, as
+    ``torch.tensor(values, device="cuda")`` makes, first waits for the stream's queued work)."""
+    t = torch.as_tensor(values, dtype=dtype)
+    dev = torch.device(device)
+    if dev.type != "cuda":
+        return t.to(dev)
+    return t.pin_memory().to(dev, non_blocking=True)
+
+
 def stream_ptr(device: torch.device | None = None) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 

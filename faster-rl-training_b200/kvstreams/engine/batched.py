@@ -34,6 +34,7 @@ from typing import Optional, Sequence
 import numpy as np
 import torch
 
+from .. import _native as N
 from ..compaction.events import CompactionEvent, CompactionLog
 from ..compaction.policies import CompactionPolicy
 from ..compaction.segments import Segment
@@ -259,6 +260,10 @@ class BatchedKVStreams:
         # the token each decoding rollout forwards next: device slot per rollout
         cur = torch.zeros(len(runs), dtype=torch.long, device=dev)
         t0 = time.perf_counter()
+        # host index lists reach the device through pinned memory: the loop never waits on the GPU
+        def _to_dev(values):
+            return N.to_device(values, torch.long, dev)
+
         it = 0
         while True:
             active = [r for r in runs if r.phase != _DONE]
@@ -270,8 +275,8 @@ class BatchedKVStreams:
 
             def decode_step(logits: torch.Tensor) -> None:
                 """Sample the next token of every generating rollout from its logits row."""
-                rows = torch.tensor([r.idx for r in decoding], device=dev)
-                idx = torch.tensor([gen_base[r.idx] + gen_used[r.idx] for r in decoding], device=dev)
+                rows = _to_dev([r.idx for r in decoding])
+                idx = _to_dev([gen_base[r.idx] + gen_used[r.idx] for r in decoding])
                 forced = forced_all.index_select(0, idx) if forced_all is not None else None
                 tok, lp = self._sample(logits, forced)
                 gen_tok.index_copy_(0, idx, tok)
@@ -342,11 +347,10 @@ class BatchedKVStreams:
                     counts.append(1)
                     pos.append(np.asarray([r.n_tokens], dtype=np.int64))
                     base += 1
-                tok_t = torch.from_numpy(np.concatenate(host_tok)).to(dev)
+                tok_t = _to_dev(np.concatenate(host_tok))
                 if dev_rows:  # last reply tokens and generating rollouts' tokens come from the device
-                    tok_t.index_copy_(0, torch.tensor(dev_at, device=dev),
-                                      cur.index_select(0, torch.tensor(dev_rows, device=dev)))
-                pos_t = torch.from_numpy(np.concatenate(pos)).to(dev)
+                    tok_t.index_copy_(0, _to_dev(dev_at), cur.index_select(0, _to_dev(dev_rows)))
+                pos_t = _to_dev(np.concatenate(pos))
                 order = starting + finishing + merged
                 logits_all = self.model.forward_cached_batch(tok_t, pos_t, self.cache, [r.seq_id for r in order],
                                                              counts=counts, last_only=True)
@@ -354,12 +358,12 @@ class BatchedKVStreams:
                     decode_step(logits_all[len(starting) + len(finishing):])
                 if starting:
                     logits = logits_all[: len(starting)]
-                    idx = torch.tensor([gen_base[r.idx] + gen_used[r.idx] for r in starting], device=dev)
+                    idx = _to_dev([gen_base[r.idx] + gen_used[r.idx] for r in starting])
                     forced = forced_all.index_select(0, idx) if forced_all is not None else None
                     tok, lp = self._sample(logits, forced)
                     gen_tok.index_copy_(0, idx, tok)
                     gen_logp.index_copy_(0, idx, lp)
-                    cur.index_copy_(0, torch.tensor([r.idx for r in starting], device=dev), tok)
+                    cur.index_copy_(0, _to_dev([r.idx for r in starting]), tok)
                 for r in starting:
                     r.turn += 1
                     r.phase = _DECODE
@@ -373,7 +377,7 @@ class BatchedKVStreams:
                     r.phase = _PREFILL if r.turn + 1 < r.ep.turns else _DONE
             # ---- an iteration without chunks: the decode step alone (a replayed graph)
             elif decoding:
-                rows = torch.tensor([r.idx for r in decoding], device=dev)
+                rows = _to_dev([r.idx for r in decoding])
                 tok_in = cur.index_select(0, rows)
                 if self.cuda_graphs:
                     if self._graphs is None:
@@ -382,7 +386,7 @@ class BatchedKVStreams:
                         self._graphs = DecodeGraphs(self.model, self.cache, len(runs))
                     logits = self._graphs.step([r.seq_id for r in decoding], tok_in, [r.n_tokens for r in decoding])
                 else:
-                    pos_t = torch.tensor([r.n_tokens for r in decoding], dtype=torch.long, device=dev)
+                    pos_t = _to_dev([r.n_tokens for r in decoding])
                     logits = self.model.forward_cached_batch(tok_in, pos_t, self.cache, [r.seq_id for r in decoding])
                 decode_step(logits)
             n_dec += len(decoding)

@@ -22,6 +22,7 @@ import torch
 import torch.nn.functional as F
 from torch import nn
 
+from . import _native as N
 from . import ops
 from .config import ModelConfig
 from .ops import ReplayMask
@@ -303,7 +304,7 @@ class TinyLM(nn.Module):
         batch = cache._batch(slots, None if one_each else counts)  # shared by every layer
         ends = None
         if last_only and not one_each:
-            ends = torch.tensor(counts, device=dev).cumsum(0) - 1
+            ends = N.to_device(counts, torch.long, dev).cumsum(0) - 1
         return self.forward_layers(tokens, positions, cache, batch, mapping, None if one_each else counts, ends)
 
     @torch.no_grad()

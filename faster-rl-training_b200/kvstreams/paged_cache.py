@@ -352,7 +352,7 @@ class PagedKVCache:
         if contiguous:
             slot_t = self._slot_ids[slots[0] : slots[0] + len(slots)] if slots else self._slot_ids[:0]
         else:
-            slot_t = torch.tensor(slots, dtype=torch.int32).to(self.device, non_blocking=True)
+            slot_t = N.to_device(slots, torch.int32, self.device)
         keep = [slot_t]
         cu_ptr = None
         total = len(slots)
@@ -360,7 +360,7 @@ class PagedKVCache:
             cu = np.zeros(len(slots) + 1, dtype=np.int32)
             cu[1:] = np.cumsum(np.asarray(counts, dtype=np.int64))
             total = int(cu[-1])
-            cu_t = torch.from_numpy(cu).to(self.device, non_blocking=True)
+            cu_t = N.to_device(cu, torch.int32, self.device)
             keep.append(cu_t)
             cu_ptr = cu_t.data_ptr()
         b = N.KvsBatch(seq_slots=slot_t.data_ptr(), cu_tokens=cu_ptr, num_seqs=len(slots), total_tokens=total)
