@@ -39,7 +39,7 @@ enum kvs_dtype { KVS_F32 = 0, KVS_F64 = 1, KVS_BF16 = 2, KVS_F16 = 3 };
 enum kvs_rc {
   KVS_OK = 0,
   KVS_E_ARG = -1,         /* null pointer / size out of range */
-  KVS_E_UNSUPPORTED = -2, /* shape or dtype this build has no kernel for */
+  KVS_E_UNSUPPORTED = -2, /* shape or dtype the library has no kernel for */
   KVS_E_LAUNCH = -3,      /* cudaGetLastError() after the launch */
   KVS_E_SCRATCH = -4,     /* caller's scratch buffer too small */
   KVS_E_NOALLOC_LIMIT = -5 /* request larger than the built-in scratch of a *_noalloc entry point */
