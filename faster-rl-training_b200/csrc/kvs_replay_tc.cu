@@ -6,8 +6,9 @@
 //   visible(t, s) = s == t                             (padded rows, collate replay.py:221-222)
 //
 // Two kernels share the tile skipping, the TMA/UMMA plumbing and the mask:
-//   replay_pair_kernel (GQA group size even, the default there): a CTA takes two query
-//     heads of one KV head at the same 128 positions, so every staged K/V tile feeds four
+//   pair_attn_kernel<false> (GQA group size even, the default there): a CTA takes two query
+//     heads of one KV head at the same 128 positions (pair_attn_kernel<true> is the same
+//     pipeline over paged K/V for prefill chunks), so every staged K/V tile feeds four
 //     UMMA tiles and two softmax warpgroups (one full row per thread) alternate with the
 //     tensor pipe; described at the kernel.
 //   replay_tc_kernel (any group size): CTA = (stream b, query head h, 128-query tile),
