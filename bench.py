@@ -120,18 +120,20 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------- workload
-def build_decode(dev, seed: int, value_seed: int):
+def build_decode(dev, seed: int, value_seed: int, bs: int = BS):
     """Same stream shapes on every rank (weak scaling: identical work per GPU); the K/V,
-    q, k, v values are drawn with a per-rank seed."""
+    q, k, v values are drawn with a per-rank seed.  ``bs`` = 1 keeps the pool's bytes
+    (NB * 16 one-token blocks)."""
     import torch
 
     from kvstreams.paged_cache import PagedKVCache
     from kvstreams.rope import RotaryEmbedding
     from kvstreams.workloads import decode_state
 
-    st = decode_state(num_streams=S, ctx_range=CTX, block_size=BS, num_blocks=NB, seed=seed)
-    cache = PagedKVCache(1, HKV, D, block_size=BS, num_blocks=NB, dtype=torch.bfloat16, device=dev, max_seqs=S,
-                         max_blocks_per_seq=CTX[1] // BS + 256)
+    nb = NB * (BS // bs)
+    st = decode_state(num_streams=S, ctx_range=CTX, block_size=bs, num_blocks=nb, seed=seed)
+    cache = PagedKVCache(1, HKV, D, block_size=bs, num_blocks=nb, dtype=torch.bfloat16, device=dev, max_seqs=S,
+                         max_blocks_per_seq=(CTX[1] + 4096) // bs)
     cache.load_state(range(S), st.tables, st.positions, st.free_list)
     g = torch.Generator(device=dev).manual_seed(value_seed)
     for t in (cache.k, cache.v):
@@ -143,13 +145,50 @@ def build_decode(dev, seed: int, value_seed: int):
     return st, cache, q, k, v, rope
 
 
-def decode_bytes(lengths: np.ndarray) -> int:
+def decode_bytes(lengths: np.ndarray, bs: int = BS) -> int:
     """Algorithmic HBM bytes of one decode launch: every live K and V row read once
     (4096 B per context token), the new K/V read + written, Q read, O written, tables."""
     kv_read = int(lengths.sum()) * HKV * D * 2 * 2
     per_stream = HQ * D * 2 * 2 + HKV * D * 2 * 2 * 2
-    tables = int(sum(-(-int(n) // BS) for n in lengths)) * 4
+    tables = int(sum(-(-int(n) // bs) for n in lengths)) * 4
     return kv_read + S * per_stream + tables
+
+
+def decode_bs1_bench(dev, args, rank: int) -> dict:
+    """The headline decode step with one-token blocks (SGLang-style): same streams, contexts,
+    evicted spans and pool bytes (NB * 16 blocks of one token), one layer of fused RoPE /
+    append / split-K paged attention per step, CUDA events around each kvs_paged_decode."""
+    import torch
+
+    from kvstreams import ops
+    from kvstreams.distributed import reduce_max
+
+    st, cache, q, k, v, rope = build_decode(dev, seed=1000, value_seed=1000 + rank, bs=1)
+    inv = rope.table(dev, torch.bfloat16)
+    seqs = list(range(S))
+    pos = torch.as_tensor(st.next_positions, device=dev)
+    out = torch.empty_like(q)
+    path = []
+    times = []
+    for i in range(args.warmup + args.steps):
+        p = pos + i
+        mapping = cache.append_slots_batch(seqs, p)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        ops.paged_forward(cache, seqs, None, 0, q, k, v, p, mapping, inv, D ** -0.5, out=out,
+                          report_path=path if i == 0 else None)
+        b.record()
+        if i >= args.warmup:
+            times.append((a, b))
+    torch.cuda.synchronize(dev)
+    ms = reduce_max(statistics.mean(x.elapsed_time(y) for x, y in times), dev)
+    alg = decode_bytes(st.lengths + args.warmup + args.steps // 2 + 1, bs=1)
+    gbs = alg / (ms * 1e-3) / 1e9
+    peaks = _peaks()
+    del cache, q, k, v, out
+    torch.cuda.empty_cache()
+    return {"ms": ms, "gbs": gbs, "hbm_frac": gbs / peaks["hbm_gbs"], "kv_bytes": int(alg),
+            "decode_tok_s": S / (ms * 1e-3), "fused_kernel": path == [1]}
 
 
 # ---------------------------------------------------------------------- cpu baseline
@@ -339,6 +378,7 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     if not args.skip_secondary:
         del hq, hk, hv, hout
         secondary = compaction_bench(dev, args, rank)
+        secondary["decode_bs1"] = decode_bs1_bench(dev, args, rank)
         secondary["replay_attention"] = replay_bench(dev, args, rank)
         secondary["replay_backward"] = replay_backward_bench(dev, args, rank)
         secondary["compaction_policy"] = compaction_policy_bench(dev, args, rank)
@@ -1045,6 +1085,7 @@ def main() -> int:
     ap.add_argument("--replay-train-only", action="store_true", help="only the replay training step measurement")
     ap.add_argument("--prefill-streams", type=int, default=64)
     ap.add_argument("--prefill-only", action="store_true", help="only the paged prefill measurement")
+    ap.add_argument("--decode-bs1-only", action="store_true", help="only the one-token-block decode measurement")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -1085,6 +1126,11 @@ def main() -> int:
             r = replay_backward_bench(torch.device("cuda", local_rank), args, rank)
             if rank == 0:
                 print(json.dumps({"replay_backward": r}), flush=True)
+        elif args.decode_bs1_only:
+            torch.cuda.set_device(local_rank)
+            r = decode_bs1_bench(torch.device("cuda", local_rank), args, rank)
+            if rank == 0:
+                print(json.dumps({"decode_bs1": r}), flush=True)
         elif args.prefill_only:
             torch.cuda.set_device(local_rank)
             r = prefill_bench(torch.device("cuda", local_rank), args, rank)

@@ -1,5 +1,6 @@
-// Fused paged decode for bf16, head_dim 128, block_size 16, 8 KV heads, GQA group 4
-// (the Llama-3-8B attention geometry): one new token per sequence.
+// Fused paged decode for bf16, head_dim 128, 8 KV heads, GQA group 4 (the Llama-3-8B
+// attention geometry), block_size 16 or 1 (the SGLang-style one-token block): one new token
+// per sequence.
 //
 // One launch does, for every sequence of the batch (TinyLM.forward_cached,
 // model.py:160-188, decode step, one layer):
@@ -10,20 +11,30 @@
 //     (Attention.forward, model.py:67-74: head h reads KV head h / 4, scores * D^-0.5,
 //     softmax, weighted V).
 //
-// Work split ("stream-K"): the blocks of all sequences, concatenated in batch order,
+// The unit of work is a group of 16 consecutive live entries of a sequence: one table entry
+// when block_size is 16, sixteen table entries when it is 1.  Either way a group is 64 KiB of
+// K and V (16 tokens x 8 heads x 128 x 2 B, twice), staged as one pipeline stage.
+//
+// Work split ("stream-K"): the groups of all sequences, concatenated in batch order,
 // are cut into gridDim.x contiguous ranges of equal cost, one per CTA (one CTA per SM):
-// a block costs one unit and each sequence two more (its start and finish), so every SM
+// a group costs one unit and each sequence two more (its start and finish), so every SM
 // streams about the same number of KV bytes whatever the context lengths.  A
 // sequence cut by range boundaries yields one partial (m, l, O) per CTA; the last
 // CTA to finish a sequence (per-sequence arrival counter) merges its partials.
 //
 // Per CTA: 8 warps, warp w <-> KV head w (4 query heads).  A 3-stage cp.async
-// pipeline stages whole 16-token blocks (K and V of all heads, 64 KiB) in shared
+// pipeline stages whole 16-token groups (K and V of all heads, 64 KiB) in shared
 // memory with a 16-byte-chunk XOR swizzle (chunk ^ token%8), so ldmatrix reads are
 // conflict free.  Per block and warp: S^T[16 tokens x 8] = K[16x128] . Q^T (4 real
 // heads + 4 zero columns) with 8 mma.m16n8k16 (bf16 in, fp32 accumulate), online
 // softmax in fp32 (base 2), P^T brought into B-fragment layout with movmatrix, and
 // O^T[128 x 8] += V^T . P^T with 8 more mma.
+//
+// One-token blocks: each token's K (or V) row of all heads is 2 KiB contiguous in the pool,
+// so a group is gathered as 16 rows of 2 KiB through the block table (a warp copies 512
+// contiguous bytes of one row per instruction).  The table entries of the CTA's range are read
+// into shared memory through a rolling window of TAB_CAP entries; entries past a sequence's
+// end are zero-filled instead of read (cp.async with a source size of 0).
 #include "kvs_common.cuh"
 #include "kvs_rope.cuh"
 
@@ -34,7 +45,7 @@ using namespace kvs;
 namespace {
 
 constexpr int D = 128;
-constexpr int BS = 16;
+constexpr int BS = 16;  // tokens of one work group (= one stage), whatever the block size
 constexpr int HKV = 8;
 constexpr int G = 4;
 constexpr int HQ = HKV * G;
@@ -47,6 +58,7 @@ constexpr int MAX_SEQS = 1024;
 constexpr int CHUNKS = KV_BLOCK_BYTES / 16;            // 2048 16-byte chunks per K (or V) block
 
 constexpr int TAB_CAP = 2048;  // table entries of one CTA's range staged in shared memory
+constexpr int TAB_GROUPS1 = TAB_CAP / BS;  // groups of one-token blocks per table window
 
 constexpr int SMEM_STAGES = STAGES * STAGE_BYTES;
 constexpr int SMEM_Q = HQ * D * 2;
@@ -85,6 +97,10 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src));
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+// 16-byte copy that reads `src_bytes` (16 or 0) bytes and zero-fills the rest
+__device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(src_bytes));
+}
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
 
@@ -146,7 +162,11 @@ struct SeqIn {
   bool owner;
 };
 
+// BSZ: the pool's block_size (16 or 1)
+template <int BSZ>
 __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodeParams p) {
+  static_assert(BSZ == BS || BSZ == 1, "block_size 16 or 1");
+  constexpr int ENTRY_BYTES = BSZ * HKV * ROW_BYTES;  // one table entry of K (or V), all heads
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* stages = smem;
   __nv_bfloat16* q_s = reinterpret_cast<__nv_bfloat16*>(smem + SMEM_STAGES);
@@ -234,7 +254,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
     s.k_lo = s.k_hi = s.v_c = make_uint4(0, 0, 0, 0);
     s.row = 0;
     if (s.owner) {
-      s.row = ((layer_rows + p.slot_blocks[i]) * BS + p.slot_offsets[i]) * HKV;
+      s.row = ((layer_rows + p.slot_blocks[i]) * BSZ + p.slot_offsets[i]) * HKV;
       if (tid < HKV * 8) {
         const uint4* ksrc = reinterpret_cast<const uint4*>(p.k_new + (int64_t)i * p.kv_stride + h * D + d0);
         s.k_lo = ksrc[0];
@@ -248,9 +268,25 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
   const int first = seq_of(g0);
   const SeqIn first_in = load_seq(first);
 
-  // block ids of this CTA's range, gathered once (the copies below then need no global lookups)
-  const bool tab_in_smem = (g1 - g0) <= TAB_CAP;
-  if (tab_in_smem) {
+  // block ids of this CTA's range, gathered once (the copies below then need no global lookups).
+  // One-token blocks: a window of TAB_GROUPS1 groups (16 entries each, -1 past a sequence's
+  // end), starting at group w0 and moved forward by the main loop when the prefetch leaves it.
+  const bool tab_in_smem = BSZ == 1 || (g1 - g0) <= TAB_CAP;
+  int w0 = g0;
+  auto gather1 = [&](int w) {
+    const int n = min(TAB_GROUPS1, g1 - w) * BS;
+    for (int e = tid; e < n; e += NTHREADS) {
+      const int gb = w + (e >> 4);
+      const int i = seq_of(gb);
+      const int slot = p.seq_slots[i];
+      const int idx = (gb - s_pref[i]) * BS + (e & 15);
+      s_tab[e] = idx < c.lengths[slot] ? c.tables[(int64_t)slot * c.max_blocks + idx] : -1;
+    }
+  };
+  if constexpr (BSZ == 1) {
+    gather1(g0);
+    __syncthreads();
+  } else if (tab_in_smem) {
     for (int gb = g0 + tid; gb < g1; gb += NTHREADS) {
       const int i = seq_of(gb);
       s_tab[gb - g0] = c.tables[(int64_t)p.seq_slots[i] * c.max_blocks + (gb - s_pref[i])];
@@ -259,23 +295,37 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
   }
 
   auto issue = [&](int gb, int st) {
-    int64_t blk;
-    if (tab_in_smem) {
-      blk = s_tab[gb - g0];
-    } else {
-      const int i = seq_of(gb);
-      blk = c.tables[(int64_t)p.seq_slots[i] * c.max_blocks + (gb - s_pref[i])];
-    }
-    const uint8_t* ks = Kpool + (layer_rows + blk) * KV_BLOCK_BYTES;
-    const uint8_t* vs = Vpool + (layer_rows + blk) * KV_BLOCK_BYTES;
     const uint32_t kd = smem_u32(stages + st * STAGE_BYTES);
     const uint32_t vd = kd + KV_BLOCK_BYTES;
+    if constexpr (BSZ == 1) {
+      // chunk q = tid + k NTHREADS is 16-byte chunk (q & 127) of token q >> 7 (row q >> 4)
+      const int* ent = s_tab + (gb - w0) * BS;
 #pragma unroll
-    for (int k = 0; k < CHUNKS / NTHREADS; ++k) {
-      const int q = tid + k * NTHREADS;
-      const int r = q >> 4, ch = q & 15;
-      cp_async16(kd + swz(r, ch), ks + (q << 4));
-      cp_async16(vd + swz(r, ch), vs + (q << 4));
+      for (int k = 0; k < CHUNKS / NTHREADS; ++k) {
+        const int q = tid + k * NTHREADS;
+        const int r = q >> 4, ch = q & 15;
+        const int blk = ent[q >> 7];
+        const int64_t off = (layer_rows + (blk < 0 ? 0 : blk)) * ENTRY_BYTES + ((q & 127) << 4);
+        cp_async16_zfill(kd + swz(r, ch), Kpool + off, blk < 0 ? 0 : 16);
+        cp_async16_zfill(vd + swz(r, ch), Vpool + off, blk < 0 ? 0 : 16);
+      }
+    } else {
+      int64_t blk;
+      if (tab_in_smem) {
+        blk = s_tab[gb - g0];
+      } else {
+        const int i = seq_of(gb);
+        blk = c.tables[(int64_t)p.seq_slots[i] * c.max_blocks + (gb - s_pref[i])];
+      }
+      const uint8_t* ks = Kpool + (layer_rows + blk) * KV_BLOCK_BYTES;
+      const uint8_t* vs = Vpool + (layer_rows + blk) * KV_BLOCK_BYTES;
+#pragma unroll
+      for (int k = 0; k < CHUNKS / NTHREADS; ++k) {
+        const int q = tid + k * NTHREADS;
+        const int r = q >> 4, ch = q & 15;
+        cp_async16(kd + swz(r, ch), ks + (q << 4));
+        cp_async16(vd + swz(r, ch), vs + (q << 4));
+      }
     }
   };
 
@@ -465,6 +515,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
   for (int gb = g0; gb < g1; ++gb) {
     const int it = gb - g0;
     const int st = it % STAGES;
+    if constexpr (BSZ == 1) {
+      // every thread finished last iteration's issue before the trailing barrier, so the
+      // window may be refilled here; groups gb .. gb + STAGES - 2 are in flight already
+      if (gb + STAGES - 1 < g1 && gb + STAGES - 1 >= w0 + TAB_GROUPS1) {
+        w0 = gb;
+        gather1(w0);
+        __syncthreads();
+      }
+    }
     if (gb + STAGES - 1 < g1) issue(gb + STAGES - 1, (it + STAGES - 1) % STAGES);
     cp_async_commit();
     cp_async_wait<STAGES - 1>();
@@ -478,13 +537,17 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
     }
     const int j = gb - s_pref[i];
     const int nb = s_pref[i + 1] - s_pref[i];
-    // the new token is the last live entry, at offset slot_offsets[i] of the last block
-    const int valid = (j == nb - 1) ? p.slot_offsets[i] + 1 : BS;
+    // the new token is the last live entry: at offset slot_offsets[i] of the last block
+    // (block_size 16), or the (length - 1) % 16-th token of the last group (one-token blocks)
+    const int tail = (j == nb - 1) ? (BSZ == BS ? p.slot_offsets[i] + 1
+                                                : ((c.lengths[p.seq_slots[i]] - 1) & (BS - 1)) + 1)
+                                   : BS;
+    const int valid = tail;
     uint8_t* kst = stages + st * STAGE_BYTES;
     uint8_t* vst = kst + KV_BLOCK_BYTES;
     if (j == nb - 1) {
       // the prefetch may predate the append: patch the new token's rows in shared memory
-      const int off = p.slot_offsets[i];
+      const int off = tail - 1;
       const int r = off * HKV + (tid >> 4) % HKV, ch = tid & 15;  // 256 threads = 8 heads x 16 chunks
       const __nv_bfloat16* srck = (tid < HKV * 16) ? knew_s + ((tid >> 4)) * D + ch * 8 : nullptr;
       if (tid < HKV * 16) {
@@ -552,7 +615,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
 }
 
 std::mutex g_attr_mu;
-bool g_attr_done[64] = {};
+bool g_attr_done[2][64] = {};  // [block_size == 1][device]
 
 }  // namespace
 
@@ -569,7 +632,8 @@ size_t kvs_decode_bf16_scratch(int num_seqs, int grid) {
 }
 
 bool kvs_decode_bf16_supported(const kvs_cache* c, const kvs_batch* b, int n_heads) {
-  return c->dtype == KVS_BF16 && c->head_dim == D && c->block_size == BS && c->n_kv_heads == HKV &&
+  return c->dtype == KVS_BF16 && c->head_dim == D && (c->block_size == BS || c->block_size == 1) &&
+         c->n_kv_heads == HKV &&
          n_heads == HQ && b->cu_tokens == nullptr && b->num_seqs <= MAX_SEQS;
 }
 
@@ -584,13 +648,14 @@ int kvs_decode_bf16_launch(const kvs_cache* c, const kvs_batch* b, const kvs_dec
   if (a->scratch_bytes < kvs_decode_bf16_scratch(b->num_seqs, grid) || !a->scratch) return KVS_E_SCRATCH;
   int dev = 0;
   cudaGetDevice(&dev);
+  const int one = c->block_size == 1;
+  const auto kernel = one ? decode_bf16_kernel<1> : decode_bf16_kernel<BS>;
   {
     std::lock_guard<std::mutex> lock(g_attr_mu);
-    if (dev < 64 && !g_attr_done[dev]) {
-      if (cudaFuncSetAttribute(decode_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_TOTAL) !=
-          cudaSuccess)
+    if (dev < 64 && !g_attr_done[one][dev]) {
+      if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_TOTAL) != cudaSuccess)
         return KVS_E_LAUNCH;
-      g_attr_done[dev] = true;
+      g_attr_done[one][dev] = true;
     }
   }
   DecodeParams p;
@@ -614,6 +679,6 @@ int kvs_decode_bf16_launch(const kvs_cache* c, const kvs_batch* b, const kvs_dec
   p.part_o = reinterpret_cast<float*>(s + COUNTER_BYTES);
   p.part_ml = reinterpret_cast<float*>(s + COUNTER_BYTES + align_up(slots * HQ * D * 4, 256));
   p.scale_log2 = (float)(a->scale * 1.4426950408889634);
-  decode_bf16_kernel<<<grid, NTHREADS, SMEM_TOTAL, st>>>(p);
+  kernel<<<grid, NTHREADS, SMEM_TOTAL, st>>>(p);
   return launch_rc();
 }

@@ -184,6 +184,7 @@ SIGNATURES = {
     "kvs_paged_attention": (C.c_int, [_P, _P, _I, _P, _P, _I, C.c_double, _P]),
     "kvs_decode_scratch_bytes": (_Z, [_P, _I, _I, _I]),
     "kvs_paged_decode": (C.c_int, [_P, _P, _P, _P]),
+    "kvs_paged_decode_path": (C.c_int, [_P, _P, _P]),
     "kvs_evicted_at": (C.c_int, [_P, _P, _P, _P, _P, _I, _I, _P, _P]),
     "kvs_replay_scratch_bytes": (_Z, [_I, _I]),
     "kvs_replay_attention": (C.c_int, [_P, _P]),

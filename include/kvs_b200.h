@@ -260,6 +260,15 @@ size_t kvs_decode_scratch_bytes(const kvs_cache* c, int32_t num_seqs, int32_t n_
                                 int32_t grid_ctas);
 int kvs_paged_decode(const kvs_cache* c, const kvs_batch* b, const kvs_decode_args* a,
                      kvs_stream_t stream);
+/* Which kernels kvs_paged_decode would run for these arguments, as an OR of KVS_PATH_* bits
+ * (a mixed step reports both sub-batches), or KVS_E_ARG.  Launches nothing; no reference
+ * counterpart (the reference has one attention path). */
+enum kvs_decode_path {
+  KVS_PATH_FUSED_DECODE = 1, /* fused RoPE + append + split-K paged decode (bf16, D 128, 32q/8kv, bs 16 or 1) */
+  KVS_PATH_TC_PREFILL = 2,   /* RoPE + append, then the tensor-core paged prefill (bf16 chunks, bs 16) */
+  KVS_PATH_EXACT = 4         /* the exact SIMT kernels (every dtype and shape) */
+};
+int kvs_paged_decode_path(const kvs_cache* c, const kvs_batch* b, const kvs_decode_args* a);
 
 /* CompactionLog.evicted_at (events.py:66-74), batched: for stream i, events are
  * triples (span_start, span_end, time) j in cu_spans[i]..cu_spans[i+1].
