@@ -31,12 +31,10 @@ _FLAG_PROTECTED, _FLAG_PARTIAL = 1, 2
 
 def policy_code(policy: CompactionPolicy) -> tuple[int, int]:
     """(kvs_policy_code, param) of a policy instance."""
-    try:
-        code = N.POLICY_CODES[policy.name]
-    except KeyError as exc:
-        raise ValueError(f"policy {policy.name!r} has no device implementation") from exc
-    param = getattr(policy, "window") if policy.name == "token_window" else getattr(policy, "keep_last")
-    return code, int(param)
+    code = getattr(policy, "device_code", None)
+    if code is None or N.POLICY_CODES.get(policy.name) != code:
+        raise ValueError(f"policy {policy.name!r} has no device implementation")
+    return int(code), int(policy.device_param)
 
 
 class DeviceCompaction:

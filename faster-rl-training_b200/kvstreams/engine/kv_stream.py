@@ -7,19 +7,19 @@ the block table on the device, and no retained token is ever forwarded twice.
 
 from __future__ import annotations
 
-from ..utils.spans import Span
-from .base import BaseEngine, _Run
+from ..utils.spans import Span, in_spans
+from .base import BaseEngine, _Episode
 
 
 class KVStreamEngine(BaseEngine):
     name = "kvstream"
 
-    def _positions(self, run: _Run, idx: list[int]) -> list[int]:
+    def _positions(self, ep: _Episode, idx: list[int]) -> list[int]:
         return list(idx)
 
-    def _evict(self, run: _Run, spans: list[Span]) -> list[Span]:
-        evicted = self.cache.evict_positions(run.seq_id, spans)
+    def _evict(self, ep: _Episode, spans: list[Span]):
+        evicted = self.cache.evict_positions(ep.seq_id, spans)
         if evicted:
-            run.context = [i for i in run.context if not any(s <= i < e for s, e in evicted)]
-            self.cache.check_invariants(run.seq_id)
-        return evicted
+            ep.context = [i for i in ep.context if not in_spans(i, evicted)]
+            self.cache.check_invariants(ep.seq_id)
+        return evicted, None

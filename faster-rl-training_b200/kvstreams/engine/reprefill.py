@@ -1,30 +1,28 @@
-"""Re-prefill baseline (engine/reprefill.py:1-35): after a compaction the sequence is
-rebuilt from the retained tokens, renumbered from 0, and forwarded again."""
+"""Re-prefill baseline (the comparison arm of the KV-streams paper, engine/reprefill.py:22-35 in
+the reference): compaction drops the sequence's cache and forwards the retained tokens again,
+renumbered from 0, so every compaction costs a prefill of the whole retained context."""
 
 from __future__ import annotations
 
-from ..utils.spans import Span, positions_to_spans
-from .base import BaseEngine, _Run
+from ..utils.spans import Span, in_spans, positions_to_spans
+from .base import BaseEngine, _Episode
 
 
 class RePrefillEngine(BaseEngine):
     name = "reprefill"
 
-    def _positions(self, run: _Run, idx: list[int]) -> list[int]:
-        first = len(run.context)
-        return list(range(first, first + len(idx)))
+    def _positions(self, ep: _Episode, idx: list[int]) -> list[int]:
+        # the cache holds exactly ep.context, renumbered 0..len-1; new tokens follow it
+        base = len(ep.context)
+        return list(range(base, base + len(idx)))
 
-    def _evict(self, run: _Run, spans: list[Span]) -> list[Span]:
-        current = run.context + run.pending
-        dropped = [i for i in current if any(s <= i < e for s, e in spans)]
-        if not dropped:
-            return []
-        gone = set(dropped)
-        retained = [i for i in current if i not in gone]
-        self.cache.free_sequence(run.seq_id)
-        self.cache.add_sequence(run.seq_id)
-        run.context, run.pending = [], []
-        if retained:
-            self._forward(run, retained, "reprefill")
-        self._uncommit_tail(run)
-        return positions_to_spans(dropped)
+    def _evict(self, ep: _Episode, spans: list[Span]):
+        keep, gone = [], []
+        for i in ep.context + ep.pending:
+            (gone if in_spans(i, spans) else keep).append(i)
+        if not gone:
+            return [], None
+        self.cache.free_sequence(ep.seq_id)
+        self.cache.add_sequence(ep.seq_id)
+        ep.context, ep.pending = [], []
+        return positions_to_spans(gone), keep

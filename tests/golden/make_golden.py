@@ -268,18 +268,19 @@ def make_rollouts():
     tok = CharTokenizer()
     arrays, meta = {}, {}
 
-    def dump(tag, model, rollouts):
+    def dump(tag, model, rollouts, mode="kvstream"):
         for i, r in enumerate(rollouts):
             key = f"{tag}_{i}"
             arrays[key + "_tokens"] = np.asarray(r.tokens, dtype=np.int64)
             arrays[key + "_loss"] = np.asarray(r.loss_mask, dtype=bool)
             arrays[key + "_inf"] = np.asarray(r.inf_logprobs, dtype=np.float64)
             arrays[key + "_evicted_at"] = r.log.evicted_at(r.length).numpy()
-            seq = build_sequences(r, "kvstream")[0]
-            batch = collate([seq])
-            with torch.no_grad():
-                lp = token_logprobs(model, batch, r.temperature)[0]
-            arrays[key + "_replay"] = lp.double().numpy()
+            if mode == "kvstream":
+                seq = build_sequences(r, "kvstream")[0]
+                batch = collate([seq])
+                with torch.no_grad():
+                    lp = token_logprobs(model, batch, r.temperature)[0]
+                arrays[key + "_replay"] = lp.double().numpy()
             meta[key] = {"events": [e.to_dict() for e in r.log], "stats": r.stats.to_dict(), "reward": r.reward,
                          "completions": r.completions, "segments": [s.to_dict() for s in r.segments]}
 
@@ -296,6 +297,18 @@ def make_rollouts():
                            RolloutConfig(context_budget=160), SamplingConfig(max_new_tokens=12))
         rs = [eng.rollout(build_env("recall", seed=i, num_distractors=6), teacher_forcing=True) for i in range(2)]
         dump(tag, m64, rs)
+    # the other engine paths: re-prefill, uncommitted partial blocks recomputed, summary turns
+    for tag, engine, bs, pad, commit, policy, kw in (
+        ("f64_reprefill_bs16", "reprefill", 16, True, True, "keep_recent", {"keep_last": 2}),
+        ("f64_reprefill_bs4_recompute", "reprefill", 4, False, False, "keep_recent", {"keep_last": 1}),
+        ("f64_bs16_recompute", "kvstream", 16, False, False, "keep_recent", {"keep_last": 2}),
+        ("f64_bs8_summary", "kvstream", 8, True, True, "summary", {"keep_last": 1}),
+    ):
+        eng = build_engine(engine, m64, tok, build_policy(policy, **kw),
+                           CacheConfig(block_size=bs, num_blocks=1024, pad_to_block=pad, commit_partial_blocks=commit),
+                           RolloutConfig(context_budget=160), SamplingConfig(max_new_tokens=12))
+        rs = [eng.rollout(build_env("recall", seed=i, num_distractors=6), teacher_forcing=True) for i in range(2)]
+        dump(tag, m64, rs, mode="auto")
     arrays.update({f"m64::{k}": v.numpy() for k, v in m64.state_dict().items()})
 
     # fp32 default model at the repo's CPU bench config (keep_recent 2, bs 16 padded, budget 256).
@@ -304,6 +317,13 @@ def make_rollouts():
                      rollout_cfg=RolloutConfig(context_budget=256, max_turns=128), dtype="float32", seed=0)
     rs = [st.engine.rollout(build_env("recall", seed=0, num_distractors=24, filler_len=64), teacher_forcing=True)]
     dump("f32_c1", st.model, rs)
+    # the same episode through the re-prefill engine (the comparison arm of this configuration)
+    rp = build_stack(engine="reprefill", policy="keep_recent", policy_kwargs={"keep_last": 2},
+                     cache_cfg=CacheConfig(16, pad_to_block=True),
+                     rollout_cfg=RolloutConfig(context_budget=256, max_turns=128), model=st.model,
+                     dtype="float32", seed=0)
+    rs = [rp.engine.rollout(build_env("recall", seed=0, num_distractors=24, filler_len=64), teacher_forcing=True)]
+    dump("f32_c1_reprefill", st.model, rs, mode="auto")
     arrays.update({f"m32::{k}": v.numpy() for k, v in st.model.state_dict().items()})
     np.savez_compressed(HERE / "rollouts.npz", **arrays)
     (HERE / "rollouts.json").write_text(json.dumps(meta))

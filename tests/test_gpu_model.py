@@ -89,16 +89,16 @@ def test_rope_relative_position_invariance():
     assert torch.allclose(x.norm(dim=-1), y.norm(dim=-1))
 
 
-def _engine(model, bs, pad, policy, kw, budget=160, max_new=12):
+def _engine(model, bs, pad, policy, kw, budget=160, max_new=12, engine="kvstream", commit=True):
     from kvstreams.compaction import build_policy
     from kvstreams.config import CacheConfig, RolloutConfig, SamplingConfig
-    from kvstreams.engine import KVStreamEngine
+    from kvstreams.engine import build_engine
     from kvstreams.tokenizer import CharTokenizer
 
-    return KVStreamEngine(model, CharTokenizer(), build_policy(policy, **kw),
-                          CacheConfig(block_size=bs, num_blocks=1024, pad_to_block=pad),
-                          RolloutConfig(context_budget=budget, record_full_logprobs=True),
-                          SamplingConfig(max_new_tokens=max_new))
+    return build_engine(engine, model, CharTokenizer(), build_policy(policy, **kw),
+                        CacheConfig(block_size=bs, num_blocks=1024, pad_to_block=pad, commit_partial_blocks=commit),
+                        RolloutConfig(context_budget=budget, record_full_logprobs=True),
+                        SamplingConfig(max_new_tokens=max_new))
 
 
 @pytest.mark.parametrize("tag,bs,pad,policy,kw", [
@@ -161,3 +161,73 @@ def test_bf16_replay_gate(golden_rollouts):
     r = eng.rollout(build_env("recall", seed=0, num_distractors=24, filler_len=64), teacher_forcing=True)
     rep = measure_mismatch(m, [r], "kvstream")
     assert rep.max_abs_logprob_diff <= 2e-2, rep
+
+
+@pytest.mark.parametrize("tag,engine,bs,pad,commit,policy,kw", [
+    ("f64_reprefill_bs16", "reprefill", 16, True, True, "keep_recent", {"keep_last": 2}),
+    ("f64_reprefill_bs4_recompute", "reprefill", 4, False, False, "keep_recent", {"keep_last": 1}),
+    ("f64_bs16_recompute", "kvstream", 16, False, False, "keep_recent", {"keep_last": 2}),
+    ("f64_bs8_summary", "kvstream", 8, True, True, "summary", {"keep_last": 1}),
+])
+def test_fp64_engine_paths_match_reference(golden_rollouts, tag, engine, bs, pad, commit, policy, kw):
+    """Re-prefill, recomputed partial blocks and summary turns through the kernels: tokens and
+    events equal the reference's, inference log-probs within 1e-9 of the reference's own."""
+    from kvstreams.envs import build_env
+
+    arrays, meta = golden_rollouts
+    m = _model(arrays, "m64::", torch.float64, {"init_std": 0.1})
+    eng = _engine(m, bs, pad, policy, kw, engine=engine, commit=commit)
+    for i in range(2):
+        r = eng.rollout(build_env("recall", seed=i, num_distractors=6), teacher_forcing=True)
+        key = f"{tag}_{i}"
+        assert r.tokens == arrays[key + "_tokens"].tolist()
+        assert [e.to_dict() for e in r.log] == meta[key]["events"]
+        assert r.stats.tokens_forwarded == meta[key]["stats"]["tokens_forwarded"]
+        assert r.stats.reprefill_tokens == meta[key]["stats"]["reprefill_tokens"]
+        loss = arrays[key + "_loss"]
+        np.testing.assert_allclose(np.asarray(r.inf_logprobs)[loss], arrays[key + "_inf"][loss], rtol=0, atol=1e-9)
+
+
+def test_fp32_bench_config_reprefill_arm(golden_rollouts):
+    """The comparison arm of the CPU bench configuration: the same episode through the
+    re-prefill engine forwards 6816 tokens (KV-streams: 2032), with the reference's tokens,
+    events and log-probs."""
+    from kvstreams.envs import build_env
+
+    arrays, meta = golden_rollouts
+    m = _model(arrays, "m32::", torch.float32)
+    eng = _engine(m, 16, True, "keep_recent", {"keep_last": 2}, budget=256, engine="reprefill")
+    eng.rollout_cfg.max_turns = 128
+    r = eng.rollout(build_env("recall", seed=0, num_distractors=24, filler_len=64), teacher_forcing=True)
+    key = "f32_c1_reprefill_0"
+    assert r.tokens == arrays[key + "_tokens"].tolist()
+    assert [e.to_dict() for e in r.log] == meta[key]["events"]
+    assert r.stats.tokens_forwarded == 6816 == meta[key]["stats"]["tokens_forwarded"]
+    loss = arrays[key + "_loss"]
+    np.testing.assert_allclose(np.asarray(r.inf_logprobs)[loss], arrays[key + "_inf"][loss], rtol=0, atol=1e-4)
+
+
+@pytest.mark.parametrize("engine", ["kvstream", "reprefill"])
+def test_rollout_batch_equals_one_at_a_time(golden_rollouts, engine):
+    """rollout_batch plays several episodes with one batched forward per step; every episode
+    equals its own rollout() (fp64: tokens, events, stats; log-probs within 1e-10), teacher
+    forced and sampled (greedy, so the draws do not depend on batching)."""
+    from kvstreams.envs import build_env
+
+    arrays, _ = golden_rollouts
+    m = _model(arrays, "m64::", torch.float64, {"init_std": 0.1})
+    for forcing in (True, False):
+        eng = _engine(m, 8, True, "keep_recent", {"keep_last": 1}, engine=engine)
+        eng.sampling.greedy = not forcing
+        envs = [build_env("recall", seed=i, num_distractors=4 + i) for i in range(4)]
+        batch = eng.rollout_batch(envs, teacher_forcing=forcing)
+        singles = [eng.rollout(build_env("recall", seed=i, num_distractors=4 + i), teacher_forcing=forcing)
+                   for i in range(4)]
+        assert eng.cache.allocator.num_used == 0
+        for a, b in zip(batch, singles):
+            assert a.tokens == b.tokens and a.loss_mask == b.loss_mask and a.completions == b.completions
+            assert [e.to_dict() for e in a.log] == [e.to_dict() for e in b.log]
+            sa, sb = a.stats.to_dict(), b.stats.to_dict()
+            sa.pop("wall_time"), sb.pop("wall_time")
+            assert sa == sb
+            np.testing.assert_allclose(a.inf_logprobs, b.inf_logprobs, rtol=0, atol=1e-10)

@@ -104,18 +104,31 @@ class _ConstantModel:
         return torch.zeros(toks.numel(), self.cfg.vocab_size, dtype=torch.float64)
 
 
-@pytest.mark.parametrize("tag,bs,pad,policy,kw", [
-    ("f64_bs16", 16, True, "keep_recent", {"keep_last": 2}),
-    ("f64_bs1", 1, False, "keep_recent", {"keep_last": 2}),
-    ("f64_bs8_markov", 8, True, "markovian", {"keep_last": 1}),
-])
-def test_teacher_forced_stream_and_events_match_reference(golden_rollouts, tag, bs, pad, policy, kw):
+ENGINE_CASES = [
+    # tag, engine, block size, pad to block, commit partial blocks, policy, policy kwargs
+    ("f64_bs16", "kvstream", 16, True, True, "keep_recent", {"keep_last": 2}),
+    ("f64_bs1", "kvstream", 1, False, True, "keep_recent", {"keep_last": 2}),
+    ("f64_bs8_markov", "kvstream", 8, True, True, "markovian", {"keep_last": 1}),
+    ("f64_reprefill_bs16", "reprefill", 16, True, True, "keep_recent", {"keep_last": 2}),
+    ("f64_reprefill_bs4_recompute", "reprefill", 4, False, False, "keep_recent", {"keep_last": 1}),
+    ("f64_bs16_recompute", "kvstream", 16, False, False, "keep_recent", {"keep_last": 2}),
+    ("f64_bs8_summary", "kvstream", 8, True, True, "summary", {"keep_last": 1}),
+]
+
+
+@pytest.mark.parametrize("tag,engine,bs,pad,commit,policy,kw", ENGINE_CASES)
+def test_teacher_forced_stream_and_events_match_reference(golden_rollouts, tag, engine, bs, pad, commit, policy, kw):
+    """Token streams, loss masks, compaction events, stats, segments and completions of the
+    rollout loop (both engines, padded / unpadded, committed / recomputed partial blocks, three
+    policies) equal the reference's, with the model replaced by uniform logits."""
+    from kvstreams.engine import build_engine
+
     arrays, meta = golden_rollouts
     tok = CharTokenizer()
     cache = _OracleBackedCache(bs, 1024)
-    eng = KVStreamEngine(_ConstantModel(tok.vocab_size), tok, build_policy(policy, **kw),
-                         CacheConfig(block_size=bs, num_blocks=1024, pad_to_block=pad),
-                         RolloutConfig(context_budget=160), SamplingConfig(max_new_tokens=12), cache=cache)
+    eng = build_engine(engine, _ConstantModel(tok.vocab_size), tok, build_policy(policy, **kw),
+                       CacheConfig(block_size=bs, num_blocks=1024, pad_to_block=pad, commit_partial_blocks=commit),
+                       RolloutConfig(context_budget=160), SamplingConfig(max_new_tokens=12), cache=cache)
     for i in range(2):
         r = eng.rollout(build_env("recall", seed=i, num_distractors=6), teacher_forcing=True)
         key = f"{tag}_{i}"
@@ -123,7 +136,9 @@ def test_teacher_forced_stream_and_events_match_reference(golden_rollouts, tag, 
         assert r.loss_mask == arrays[key + "_loss"].tolist()
         want = meta[key]["events"]
         assert [e.to_dict() for e in r.log] == want
-        assert r.stats.tokens_forwarded == meta[key]["stats"]["tokens_forwarded"]
-        assert r.stats.compactions == meta[key]["stats"]["compactions"]
+        got_stats = r.stats.to_dict()
+        for name, value in meta[key]["stats"].items():
+            if name != "wall_time":
+                assert got_stats[name] == value, (name, got_stats[name], value)
         assert [s.to_dict() for s in r.segments] == meta[key]["segments"]
         assert r.completions == meta[key]["completions"]
