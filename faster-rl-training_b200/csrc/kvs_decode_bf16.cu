@@ -594,8 +594,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
       acc[mt][2] *= al0;
       acc[mt][3] *= al1;
     }
-    const uint32_t pb0 = movm_t(pack_bf16(p0, p1));  // P[head g][tokens 2t, 2t+1]
-    const uint32_t pb1 = movm_t(pack_bf16(p2, p3));  // P[head g][tokens 8+2t, 9+2t]
+    // P as the sum of two bf16 terms, hi = bf16(p) and lo = bf16(p - hi): 16 significant bits
+    // for P V at two MMAs per fragment instead of one (free in this HBM-bound kernel), so the
+    // decode and the masked replay kernel round P far less differently
+    const uint32_t h01 = pack_bf16(p0, p1), h23 = pack_bf16(p2, p3);
+    const float2 r01 = unpack_bf16(h01), r23 = unpack_bf16(h23);
+    const uint32_t pb0 = movm_t(h01);  // P[head g][tokens 2t, 2t+1]
+    const uint32_t pb1 = movm_t(h23);  // P[head g][tokens 8+2t, 9+2t]
+    const uint32_t pl0 = movm_t(pack_bf16(p0 - r01.x, p1 - r01.y));
+    const uint32_t pl1 = movm_t(pack_bf16(p2 - r23.x, p3 - r23.y));
     // ---- O^T += V^T . P^T
     {
       const int mi = lane >> 3, rr = lane & 7;
@@ -606,6 +613,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
         uint32_t a0, a1, a2, a3;
         ldsm_x4_t(vbase + swz(row, 2 * mt + (mi & 1)), a0, a1, a2, a3);
         mma_bf16(acc[mt], a0, a1, a2, a3, pb0, pb1);
+        mma_bf16(acc[mt], a0, a1, a2, a3, pl0, pl1);
       }
     }
     __syncthreads();  // the stage is refilled by the next iteration's prefetch

@@ -97,6 +97,16 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
   __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&v);
 }
+// (a, b) as an f16 pair, a in the low half; finite inputs beyond the f16 range saturate
+__device__ __forceinline__ uint32_t pack2h(float a, float b) {
+  uint32_t r;
+  asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;\n" : "=r"(r) : "f"(b), "f"(a));
+  return r;
+}
+// a bf16 pair re-encoded as an f16 pair (exact for magnitudes in [2^-14, 65504])
+__device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t x) {
+  return pack2h(__uint_as_float(x << 16), __uint_as_float(x & 0xffff0000u));
+}
 
 __global__ void __launch_bounds__(NT, 1)
 replay_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -438,8 +448,9 @@ constexpr int OFF2_K = OFF2_Q + 2 * TILE_BYTES;    // 2 slots
 constexpr int OFF2_V = OFF2_K + 2 * TILE_BYTES;    // 2 slots
 constexpr int OFF2_E = OFF2_V + 2 * TILE_BYTES;    // 2 slots of 128 int32
 constexpr int OFF2_LIST = OFF2_E + 2 * E_BYTES;
-constexpr int OFF2_BAR = OFF2_LIST + MAX_KT * 2;
-constexpr int NBAR2 = 14;
+constexpr int OFF2_ROWS = OFF2_LIST + MAX_KT * 2;  // paged: pool row of each 16-key block of the list
+constexpr int OFF2_BAR = OFF2_ROWS + MAX_KT * (BN / 16) * 4;
+constexpr int NBAR2 = 16;
 constexpr int OFF2_MISC = OFF2_BAR + NBAR2 * 8;
 constexpr int SMEM2_BYTES = OFF2_MISC + 64 + 33 * 4 + 1024;
 static_assert(SMEM2_BYTES <= 232448, "head-pair replay kernel shared memory");
@@ -452,7 +463,8 @@ __host__ __device__ constexpr uint32_t s_step(int kk) { return (uint32_t)(((kk >
 __host__ __device__ constexpr uint32_t pv_step(int kk) { return (uint32_t)((kk * 2048) >> 4); }
 
 enum { C_KFULL0 = 0, C_KFULL1, C_VFULL0, C_VFULL1, C_KEMPTY0, C_KEMPTY1, C_VEMPTY0, C_VEMPTY1, C_QFULL,
-       C_SFULL0, C_SFULL1, C_PFULL0, C_PFULL1, C_FINAL };
+       C_SFULL0, C_SFULL1, C_PFULL0, C_PFULL1, C_FINAL, C_VCONV0, C_VCONV1 };
+constexpr int NCONV = 64;  // warps 2 and 3: V tiles to f16 in place
 
 template <bool PAGED>
 __global__ void __launch_bounds__(NT2, 1)
@@ -523,6 +535,8 @@ pair_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     for (int i = 0; i < NBAR2; ++i) mbar_init(&bar[i], 1);
     mbar_init(&bar[C_PFULL0], 128);
     mbar_init(&bar[C_PFULL1], 128);
+    mbar_init(&bar[C_VCONV0], NCONV);
+    mbar_init(&bar[C_VCONV1], NCONV);
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -562,24 +576,35 @@ pair_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     if (tid == 0) *s_n = carry;
   }
   __syncthreads();
-  tc_fence_after();
   const int n = *s_n;  // >= 1: the diagonal tile is always active
+  int* rows = reinterpret_cast<int*>(smem + OFF2_ROWS);
+  if (PAGED) {
+    // pool rows of every block the producer will gather, read once by all threads (its loads
+    // then issue back to back); blocks past the sequence read past the pool, i.e. zeros
+    for (int e = tid; e < n * (BN / 16); e += NT2) {
+      const int j = list[e >> 3] & 0x7fff, b8 = e & 7;
+      rows[e] = (j * BN + b8 * 16 < n_all)
+                    ? g.tables[(int64_t)seq_slot * g.max_blocks + j * (BN / 16) + b8] * 16
+                    : g.pool_rows;
+    }
+    __syncthreads();
+  }
+  tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   // one 128-key x 128-dim tile of K or V into a 128-byte swizzled shared tile: replay rows
   // are contiguous; paged keys come as eight 16-token pool blocks (2 KB per half each),
   // and blocks past the sequence are read out of bounds of the pool, i.e. as zeros.
-  auto load_kv = [&](uint8_t* dst, const CUtensorMap* map, int j, uint64_t* bb) {
+  auto load_kv = [&](uint8_t* dst, const CUtensorMap* map, int k, uint64_t* bb) {
     if (!PAGED) {
-      const int row = b * p.T + j * BN;
+      const int row = b * p.T + (list[k] & 0x7fff) * BN;
       tma_load_3d(dst, map, 0, hk, row, bb);
       tma_load_3d(dst + HALF_BYTES, map, 64, hk, row, bb);
     } else {
-      const int32_t* tab = g.tables + (int64_t)seq_slot * g.max_blocks + j * (BN / 16);
-#pragma unroll 1
+      const int* r8 = rows + k * (BN / 16);
+#pragma unroll
       for (int b8 = 0; b8 < BN / 16; ++b8) {
-        const int row = (j * BN + b8 * 16 < n_all) ? tab[b8] * 16 : g.pool_rows;
-        tma_load_3d(dst + b8 * 2048, map, 0, hk, row, bb);
-        tma_load_3d(dst + HALF_BYTES + b8 * 2048, map, 64, hk, row, bb);
+        tma_load_3d(dst + b8 * 2048, map, 0, hk, r8[b8], bb);
+        tma_load_3d(dst + HALF_BYTES + b8 * 2048, map, 64, hk, r8[b8], bb);
       }
     }
   };
@@ -600,10 +625,9 @@ pair_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
           fail_site(1);
           break;
         }
-        const int j = list[k] & 0x7fff;
         uint8_t* Ks = smem + OFF2_K + ks * TILE_BYTES;
         mbar_arrive_expect_tx(&bar[C_KFULL0 + ks], TILE_BYTES);
-        load_kv(Ks, &tm_k, j, &bar[C_KFULL0 + ks]);
+        load_kv(Ks, &tm_k, k, &bar[C_KFULL0 + ks]);
       }
     } else if (warp == 0 && lane == 1) {
       // ---------------------------------------------------------- producer: V ring + evicted_at
@@ -617,7 +641,7 @@ pair_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         const int j = list[k] & 0x7fff;
         uint8_t* Vs = smem + OFF2_V + vs * TILE_BYTES;
         mbar_arrive_expect_tx(&bar[C_VFULL0 + vs], TILE_BYTES + (PAGED ? 0 : E_BYTES));
-        load_kv(Vs, &tm_v, j, &bar[C_VFULL0 + vs]);
+        load_kv(Vs, &tm_v, k, &bar[C_VFULL0 + vs]);
         if (!PAGED)
           bulk_load(smem + OFF2_E + vs * E_BYTES, p.e32 + (int64_t)b * p.T_pad + j * BN, E_BYTES,
                     &bar[C_VFULL0 + vs]);
@@ -626,7 +650,7 @@ pair_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       // ---------------------------------------------------------- UMMA issuer (whole warp,
       // one elected lane issues; every value on this path is warp-uniform)
       constexpr uint32_t ID_QK = idesc_bf16(128, 128, 0);
-      constexpr uint32_t ID_PV = idesc_bf16(128, 128, 1);
+      constexpr uint32_t ID_PV = idesc_f16(128, 128, 1);  // P and V in f16
       // Descriptors are built once; each K16 step adds its byte offset >> 4 to the start-address
       // field (no carry: shared addresses stay below 2^18).
       const uint64_t dq0 = desc_kmajor_sw128(smem_addr(Qs)), dq1 = desc_kmajor_sw128(smem_addr(Qs + TILE_BYTES));
@@ -674,9 +698,9 @@ pair_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         issue_s(1, slot);
         umma_commit_warp(&bar[C_KEMPTY0 + slot]);
         umma_commit_warp(&bar[C_SFULL1]);
-        // V(k) normally landed long ago: take its wait before head 0's P, which is on the
-        // softmax -> P V -> S critical path
-        ok = wait(&bar[C_VFULL0 + slot], ph);
+        // V(k) normally landed (and was converted to f16) long ago: take its wait before head
+        // 0's P, which is on the softmax -> P V -> S critical path
+        ok = wait(&bar[C_VCONV0 + slot], ph);
         if (ok) ok = wait(&bar[C_PFULL0], k & 1);
         if (!ok) break;
         tc_fence_after();
@@ -697,6 +721,34 @@ pair_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       umma_commit_warp(&bar[C_FINAL]);
       mbar_wait(&bar[C_FINAL], 0, nullptr);
       __syncwarp();
+    } else if (warp >= 2) {
+      // ---------------------------------------------------------- warps 2, 3: each V tile to f16
+      // in place once it lands, for the f16 P V products (P keeps 11 significant bits instead
+      // of bf16's 8, so the replay and the paged decode agree far more closely).  The swizzled
+      // layout is unchanged: every 16-byte chunk is converted where it lies.
+      const int ct = tid - 64;
+      bool ok = true;
+      for (int k = 0; k < n; ++k) {
+        const int vs = k & 1;
+        ok = mbar_wait(&bar[C_VFULL0 + vs], (k >> 1) & 1, abort_flag);
+        if (!ok) break;
+        uint4* v4 = reinterpret_cast<uint4*>(smem + OFF2_V + vs * TILE_BYTES);
+#pragma unroll 2
+        for (int c = ct; c < TILE_BYTES / 16; c += NCONV) {
+          uint4 x = v4[c];
+          x.x = bf16x2_to_f16x2(x.x);
+          x.y = bf16x2_to_f16x2(x.y);
+          x.z = bf16x2_to_f16x2(x.z);
+          x.w = bf16x2_to_f16x2(x.w);
+          v4[c] = x;
+        }
+        fence_proxy_async_smem();  // the UMMA reads the tile through the async proxy
+        mbar_arrive(&bar[C_VCONV0 + vs]);
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        fail_site(4);
+      }
     }
   } else {
     regs_alloc<REGS_SOFT>();
@@ -786,7 +838,7 @@ pair_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        uint32_t pk[16];  // bf16 pairs of keys 32c .. 32c+31
+        uint32_t pk[16];  // f16 pairs of keys 32c .. 32c+31
 #pragma unroll
         for (int i = 0; i < 32; i += 4) {
           const int e = 32 * c + i;
@@ -797,8 +849,8 @@ pair_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
           const float p0 = ex2_approx(x0), p1 = ex2_approx(x1), p2 = ex2_approx(x2), p3 = ex2_approx(x3);
           fadd2(a0, a1, p0, p1);
           fadd2(a2, a3, p2, p3);
-          pk[i >> 1] = pack2(p0, p1);
-          pk[(i >> 1) + 1] = pack2(p2, p3);
+          pk[i >> 1] = pack2h(p0, p1);  // p <= 2^8 (lazy rescale): within the f16 range
+          pk[(i >> 1) + 1] = pack2h(p2, p3);
         }
         tmem_st16(tl + S_col + c * 16, pk);
       }

@@ -300,6 +300,10 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, int b_mn) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)b_mn << 16) | ((uint32_t)(N >> 3) << 17) |
          ((uint32_t)(M >> 4) << 24);
 }
+// f16 x f16 -> f32 (A and B format fields 0), otherwise as idesc_bf16
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, int b_mn) {
+  return (1u << 4) | ((uint32_t)b_mn << 16) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
 
 }  // namespace sm100
 }  // namespace kvs

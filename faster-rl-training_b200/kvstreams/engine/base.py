@@ -94,7 +94,7 @@ class BaseEngine:
         self.sampling = sampling or SamplingConfig()
         # a cache may be shared between engines (or be a test double)
         self.cache = cache if cache is not None else PagedKVCache.from_config(
-            model.cfg, self.cache_cfg, device=model.device, dtype=model.dtype)
+            model.cfg, self.cache_cfg, device=model.device, dtype=getattr(model, "attention_dtype", model.dtype))
         self._seq_counter = 0
 
     @property

@@ -241,6 +241,17 @@ class TinyLM(nn.Module):
     def dtype(self) -> torch.dtype:
         return self.embed.weight.dtype
 
+    @property
+    def attention_dtype(self) -> torch.dtype:
+        """Element type of q/k/v, the KV cache and the attention kernels: the model's dtype unless
+        set otherwise (e.g. ``torch.bfloat16`` under float32 weights: bf16 KV pool and bf16
+        attention kernels, everything else in float32).  The paged cache must have this dtype."""
+        return self.__dict__.get("_attention_dtype") or self.dtype
+
+    @attention_dtype.setter
+    def attention_dtype(self, dtype: Optional[torch.dtype]) -> None:
+        self.__dict__["_attention_dtype"] = dtype
+
     def num_parameters(self) -> int:
         return sum(p.numel() for p in self.parameters())
 
@@ -264,14 +275,15 @@ class TinyLM(nn.Module):
             positions = torch.arange(T, device=dev).expand(B, T)
         positions = positions.to(dev)
         rm = as_replay_mask(mask, B, T, dev)
-        inv = self.rope.table(dev, self.dtype)
+        adt = self.attention_dtype
+        inv = self.rope.table(dev, adt)
         x = self.embed(tokens)
         for blk in self.layers:
             at = blk.attn
             qkv = at.project_qkv(blk.attn_norm(x))
-            a = _ReplayAttention.apply(qkv, (at.n_heads, at.n_kv_heads, at.head_dim), positions, rm.evicted_at,
-                                       rm.lengths, inv, at.scale)
-            x2 = blk.attn_residual(x.reshape(B * T, -1), a.reshape(B * T, -1))
+            a = _ReplayAttention.apply(qkv.to(adt), (at.n_heads, at.n_kv_heads, at.head_dim), positions,
+                                       rm.evicted_at, rm.lengths, inv, at.scale)
+            x2 = blk.attn_residual(x.reshape(B * T, -1), a.reshape(B * T, -1).to(x.dtype))
             x = blk.mlp_residual(x2).view(B, T, -1)
         return self.norm(x)
 
@@ -319,13 +331,16 @@ class TinyLM(nn.Module):
         if counts is not None:
             while tail < len(counts) and counts[len(counts) - 1 - tail] == 1:
                 tail += 1
-        inv = self.rope.table(self.device, self.dtype)
+        adt = self.attention_dtype
+        inv = self.rope.table(self.device, adt)
         x = self.embed(tokens)
         for i, blk in enumerate(self.layers):
             q, k, v = blk.attn.project(blk.attn_norm(x))
+            if adt != q.dtype:
+                q, k, v = q.to(adt), k.to(adt), v.to(adt)
             a = ops.paged_forward(cache, None, counts, i, q, k, v, positions, mapping, inv, blk.attn.scale,
                                   batch=batch, tail_singles=tail)
-            x = blk.mlp_residual(blk.attn_residual(x, a.reshape(N, -1)))
+            x = blk.mlp_residual(blk.attn_residual(x, a.reshape(N, -1).to(x.dtype)))
         if rows is not None:
             x = x.index_select(0, rows)
         return self.logits(self.norm(x))

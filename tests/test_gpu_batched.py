@@ -67,16 +67,18 @@ def test_batched_equals_one_at_a_time_fp64():
 
 
 def test_batched_rollouts_bf16_llama_heads():
-    """Llama-3-8B attention geometry (32 q / 8 kv heads, D 128, d_model 4096, two layers):
-    decode steps run the fused paged decode kernel, turn chunks the tensor-core paged
-    prefill, the replay the tcgen05 replay kernel.
+    """Llama-3-8B attention geometry (32 q / 8 kv heads, D 128, d_model 4096, two layers), the
+    whole model in bf16: decode steps run the fused paged decode kernel, turn chunks the
+    tensor-core paged prefill, the replay the tcgen05 replay kernel.
 
-    Tolerance: at this width with random-init weights the logits are O(4) and two correct
-    bf16 computations of the same stream (the decode kernel's and the replay kernel's, with
-    different GEMM shapes) differ by up to ~0.06 in log-prob, mean ~0.01 (each is ~0.13 from
-    the float32 computation); an indexing or masking error shows up as O(1) (a scratch-reuse
-    bug measured max 7.2, mean 0.87).  The 2e-2 bf16 gate is checked on the TinyLM
-    configuration (test_gpu_model)."""
+    Tolerance, from measurements of these rollouts (seed 0): replay vs inference differs by
+    0.041 max / 0.0086 mean in log-prob with the whole model in bf16, by 0.012 / 0.0023 with
+    only attention in bf16 (test_gpu_bf16_gate.py, which holds the 2e-2 gate), and by 0 in
+    float32; the replay itself is batch-invariant (a batch of 8 and one stream at a time give
+    identical log-probs).  The rest of the whole-bf16 difference is the dense layers: their
+    bf16-rounded GEMM outputs differ between the inference steps (a few to a few hundred rows
+    per GEMM) and the replay (thousands of rows), and the rounding differences propagate.  An
+    indexing or masking error shows up as O(1) (a scratch-reuse bug measured max 7.2, mean 0.87)."""
     from kvstreams.config import ModelConfig
     from kvstreams.engine.batched import synthetic_episodes
     from kvstreams.training.mismatch import measure_mismatch
@@ -88,8 +90,8 @@ def test_batched_rollouts_bf16_llama_heads():
     rolls = eng.run(eps)
     assert sum(len(r.log.events) for r in rolls) >= 4
     rep = measure_mismatch(model, rolls)
-    assert rep.max_abs_logprob_diff <= 0.08, rep
-    assert rep.mean_abs_logprob_diff <= 0.02, rep
+    assert rep.max_abs_logprob_diff <= 0.06, rep
+    assert rep.mean_abs_logprob_diff <= 0.015, rep
 
 
 def test_decode_cuda_graphs_equal_eager_bf16():
