@@ -15,8 +15,8 @@ Sections:
   * evicted_at -- CompactionLog.evicted_at (compaction/events.py:66-74)
   * merge_spans / positions_to_spans (utils/spans.py:10-23)
   * rope_* -- RotaryEmbedding + apply_rope (rope.py:21-46)
-  * gqa_attention / replay_attention -- Attention.forward math (model.py:50-75)
-    with the KV-streams mask (training/replay.py:55-63, collate :132-149)
+  * gqa_attention / replay_attention / replay_attention_rows -- Attention.forward math
+    (model.py:50-75) with the KV-streams mask (training/replay.py:55-63, collate :132-149)
   * tinylm_forward -- TinyLM.forward (model.py:132-157) for small models
 """
 
@@ -293,6 +293,31 @@ def replay_attention(q, k, v, ev, lengths, scale, dtype=np.float64):
         n = int(lengths[b])
         m[:n, :n] = kvstream_mask(ev[b, :n])
         out[b] = gqa_attention(q[b], k[b], v[b], m, scale, dtype)
+    return out
+
+
+def replay_attention_rows(q, k, v, ev, rows, scale, dtype=np.float64):
+    """Selected rows of the masked replay attention of one full-length stream, for sizes where
+    the dense [T, T] mask does not fit: q [T, Hq, D], k/v [T, Hkv, D], ev [T]; row t attends to
+    the keys s <= t with t < ev[s] (replay.py:55-63) with the math of model.py:67-74 (query
+    head h reads KV head h // (Hq / Hkv), softmax of scaled scores, weighted values), computed
+    per KV head as one small GEMM.  Returns [len(rows), Hq, D]."""
+    T, Hq, D = q.shape
+    Hkv = k.shape[1]
+    rep = Hq // Hkv
+    kh = np.ascontiguousarray(np.transpose(k, (1, 0, 2)).astype(dtype))  # [Hkv, T, D]
+    vh = np.ascontiguousarray(np.transpose(v, (1, 0, 2)).astype(dtype))
+    out = np.zeros((len(rows), Hq, D), dtype=dtype)
+    for i, t in enumerate(np.asarray(rows, dtype=np.int64)):
+        vis = ev[: t + 1] > t
+        for g in range(Hkv):
+            qs = q[t, g * rep:(g + 1) * rep].astype(dtype)              # [rep, D]
+            sc = (qs @ kh[g, : t + 1].T) * dtype(scale)                  # [rep, t + 1]
+            sc = np.where(vis[None], sc, -np.inf)
+            sc -= sc.max(axis=-1, keepdims=True)
+            pr = np.exp(sc)
+            pr /= pr.sum(axis=-1, keepdims=True)
+            out[i, g * rep:(g + 1) * rep] = pr @ vh[g, : t + 1]
     return out
 
 

@@ -71,3 +71,15 @@ def test_oracle_replay_matches_reference_logprobs(golden_rollouts, tag):
     loss = arrays[tag + "_loss"]
     # the reference's core claim, reproduced by the oracle: replay == inference
     assert np.abs(got[loss] - arrays[tag + "_inf"][loss]).max() < 1e-9
+
+
+def test_row_sampled_replay_oracle_equals_dense():
+    """replay_attention_rows (the full-length checker) equals the dense-mask replay oracle."""
+    rng = np.random.default_rng(0)
+    T = 300
+    q, k, v = rng.standard_normal((T, 8, 16)), rng.standard_normal((T, 2, 16)), rng.standard_normal((T, 2, 16))
+    ev = np.full(T, O.NEVER, dtype=np.int64)
+    ev[40:80], ev[100:120] = 150, 200
+    rows = [0, 1, 79, 149, 150, 199, 200, 299]
+    dense = O.replay_attention(q[None], k[None], v[None], ev[None], np.array([T]), 0.25)[0]
+    np.testing.assert_allclose(O.replay_attention_rows(q, k, v, ev, rows, 0.25), dense[rows], rtol=0, atol=1e-12)
