@@ -14,9 +14,12 @@ split-K paged GQA attention for one new token per stream.  The per-step KV read
 Also reported (same line, `secondary`): the batched whole-block compaction kernel
 on 256 streams x 512-block tables (pool 200000).
 
-`--impl reference` times the oracle port of the reference's CPU path (gather +
-GQA softmax attention, paged_cache.py:176-182 and model.py:67-74) on the host
-cores for a bounded sample of the same workload.
+`--impl reference` times the reference's own CPU implementation (the package installed
+in baseline/_ref) on the host cores, on bounded samples of the same workloads: the decode
+step through its PagedKVCache (append_slots, write, gather; paged_cache.py:145-182) and
+RoPE (rope.py:21-46) with the attention math of model.py:67-74, its evict_positions on
+the 256-stream compaction trace, and its KV-streams and re-prefill rollouts at the CPU
+bench configuration.  Without baseline/_ref the oracle port stands in (kind "port").
 """
 
 from __future__ import annotations
@@ -35,9 +38,36 @@ from pathlib import Path
 import numpy as np
 
 REPO = Path(__file__).resolve().parent
-for p in (str(REPO / "faster-rl-training_b200"), str(REPO)):
-    if p not in sys.path:
-        sys.path.insert(0, p)
+PKG_DIR = REPO / "faster-rl-training_b200"
+REF_DIR = REPO / "baseline" / "_ref"  # the reference package, installed there unmodified
+
+
+def _use_package() -> None:
+    """This library's ``kvstreams`` (and the oracle) on the import path."""
+    for p in (str(PKG_DIR), str(REPO)):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+
+
+def _use_reference() -> bool:
+    """The reference's own ``kvstreams`` on the import path (a process that runs it never
+    imports this library's package of the same name).  False when it is not installed."""
+    if not (REF_DIR / "kvstreams" / "__init__.py").exists():
+        return False
+    sys.path.insert(0, str(REF_DIR))
+    return True
+
+
+def _workloads():
+    """The seeded workload generators (kvstreams/workloads.py of this package, numpy only),
+    loaded by path, so that a process running the reference's package uses the same streams."""
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("kvs_b200_workloads", PKG_DIR / "kvstreams" / "workloads.py")
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[spec.name] = mod  # dataclasses resolve their module by name
+    spec.loader.exec_module(mod)
+    return mod
 
 METRIC = "rollout decode tok/s/GPU + replay tok/s; paged-attn HBM GB/s; replay TC util"
 S, HQ, HKV, D, BS, NB = 64, 32, 8, 128, 16, 131072
@@ -192,77 +222,224 @@ def decode_bs1_bench(dev, args, rank: int) -> dict:
 
 
 # ---------------------------------------------------------------------- cpu baseline
-def cpu_decode_sample(seed: int, n_streams: int = 4):
-    """Reference CPU path on a bounded sample: per stream, gather the live K/V in table
-    order and run GQA softmax attention in float32 (numpy, BLAS threads)."""
-    from kvstreams.workloads import decode_state
+CPU_STREAMS = 4  # decode streams of the 64-stream workload per CPU step
 
+
+def _cpu_threads() -> int:
+    import torch
+
+    n = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    torch.set_num_threads(n)
+    return torch.get_num_threads()
+
+
+def _ref_attend(q, k, v):
+    """The attention of the reference's Attention.forward (model.py:67-74) for one decode
+    query: GQA heads expanded by repeat_interleave, scaled scores, the (all-visible) mask,
+    softmax, weighted values.  q [1, 1, Hq, D], k/v [1, n, Hkv, D]."""
+    import torch
+
+    rep = q.shape[2] // k.shape[2]
+    k = k.repeat_interleave(rep, dim=2)
+    v = v.repeat_interleave(rep, dim=2)
+    mask = torch.ones(1, q.shape[1], k.shape[1], dtype=torch.bool)
+    scores = torch.einsum("bqhd,bkhd->bhqk", q, k) * (q.shape[-1] ** -0.5)
+    scores = scores.masked_fill(~mask[:, None, :, :], float("-inf"))
+    return torch.einsum("bhqk,bkhd->bqhd", scores.softmax(dim=-1), v)
+
+
+def ref_decode_leg(seed: int):
+    """The decode step of the first CPU_STREAMS streams of the headline workload through the
+    reference's own code, bf16 as the GPU arm: its RotaryEmbedding / apply_rope on the new q
+    and k (rope.py:21-46), PagedKVCache.append_slots + write + gather (paged_cache.py:145-182),
+    then the model.py:67-74 attention.  Returns (step, context tokens in the sample)."""
+    import torch
+    from kvstreams.paged_cache import PagedKVCache
+    from kvstreams.rope import RotaryEmbedding, apply_rope
+
+    st = _workloads().decode_state(num_streams=S, ctx_range=CTX, block_size=BS, num_blocks=NB, seed=seed)
+    sample = list(range(CPU_STREAMS))
+    cache = PagedKVCache(1, HKV, D, block_size=BS, num_blocks=sum(len(st.tables[s]) + 8 for s in sample),
+                         dtype=torch.bfloat16)
+    g = torch.Generator().manual_seed(seed)
+    for s in sample:
+        cache.add_sequence(s)
+        pos = torch.from_numpy(st.positions[s])
+        slots = cache.append_slots(s, pos)
+        n = pos.numel()
+        cache.write(0, slots, torch.randn(n, HKV, D, generator=g).bfloat16(),
+                    torch.randn(n, HKV, D, generator=g).bfloat16())
+    rope = RotaryEmbedding(D, THETA)
+    q = torch.randn(len(sample), 1, 1, HQ, D, generator=g).bfloat16()
+    k = torch.randn(len(sample), 1, 1, HKV, D, generator=g).bfloat16()
+    v = torch.randn(len(sample), 1, HKV, D, generator=g).bfloat16()
+    nxt = [int(st.next_positions[s]) for s in sample]
+
+    def step() -> int:
+        for i, s in enumerate(sample):
+            p = torch.tensor([[nxt[i]]])
+            nxt[i] += 1
+            cos, sin = rope(p)
+            qr, kr = apply_rope(q[i], cos, sin), apply_rope(k[i], cos, sin)
+            slots = cache.append_slots(s, p[0])
+            cache.write(0, slots, kr[0], v[i])
+            kk, vv = cache.gather(s, 0)
+            _ref_attend(qr, kk[None], vv[None])
+        return len(sample)
+
+    return step, int(sum(st.positions[s].size for s in sample))
+
+
+def port_decode_leg(seed: int):
+    """The same sample through the oracle port (numpy float32), when the reference package is
+    not installed."""
     from oracle import kvs_oracle as O
 
-    st = decode_state(num_streams=S, ctx_range=CTX, block_size=BS, num_blocks=NB, seed=seed)
+    st = _workloads().decode_state(num_streams=S, ctx_range=CTX, block_size=BS, num_blocks=NB, seed=seed)
     rng = np.random.default_rng(seed)
-    sample = list(range(n_streams))
-    pools = {}
-    for s in sample:
-        nb = len(st.tables[s])
-        pools[s] = (rng.standard_normal((nb, BS, HKV, D), dtype=np.float32),
-                    rng.standard_normal((nb, BS, HKV, D), dtype=np.float32))
-    q = rng.standard_normal((n_streams, HQ, D), dtype=np.float32)
-    knew = rng.standard_normal((n_streams, HKV, D), dtype=np.float32)
-    vnew = rng.standard_normal((n_streams, HKV, D), dtype=np.float32)
+    sample = list(range(CPU_STREAMS))
+    pools = {s: (rng.standard_normal((st.positions[s].size, HKV, D), dtype=np.float32),
+                 rng.standard_normal((st.positions[s].size, HKV, D), dtype=np.float32)) for s in sample}
+    q = rng.standard_normal((len(sample), HQ, D), dtype=np.float32)
+    knew = rng.standard_normal((len(sample), HKV, D), dtype=np.float32)
+    vnew = rng.standard_normal((len(sample), HKV, D), dtype=np.float32)
 
-    def step():
-        toks = 0
+    def step() -> int:
         for i, s in enumerate(sample):
             kp, vp = pools[s]
-            n = st.positions[s].size
             pos = np.asarray([st.next_positions[s]])
             qr = O.rope_apply(q[i:i + 1], pos, THETA, np.float32)
-            kr = O.rope_apply(knew[i:i + 1], pos, THETA, np.float32)
-            keys = np.concatenate([kp.reshape(-1, HKV, D)[:n], kr])
-            vals = np.concatenate([vp.reshape(-1, HKV, D)[:n], vnew[i:i + 1]])
-            O.gqa_attention(qr, keys, vals, np.ones((1, n + 1), bool), D ** -0.5, np.float32)
-            toks += 1
-        return toks
+            keys = np.concatenate([kp, O.rope_apply(knew[i:i + 1], pos, THETA, np.float32)])
+            vals = np.concatenate([vp, vnew[i:i + 1]])
+            O.gqa_attention(qr, keys, vals, np.ones((1, keys.shape[0]), bool), D ** -0.5, np.float32)
+        return len(sample)
 
-    return step, sum(st.positions[s].size for s in sample)
+    return step, int(sum(st.positions[s].size for s in sample))
 
 
-def time_cpu(step, min_seconds: float = 10.0, max_iters: int = 50):
-    step()  # warm
+def ref_compaction_leg(bs: int, n_streams: int, seed: int) -> dict:
+    """The compaction workload (256 streams x 512-block tables, pool 200000, 1-8 keep-recent
+    events) through the reference's PagedKVCache: the first ``n_streams`` streams filled by its
+    append_slots, then its evict_positions for their first eviction round, timed per stream."""
+    import torch
+    from kvstreams.paged_cache import PagedKVCache
+
+    rounds = _workloads().compaction_plan(num_streams=256, blocks_per_stream=512, block_size=bs,
+                                          num_events_range=(1, 8), seed=seed)
+    cache = PagedKVCache(1, 1, 2, block_size=bs, num_blocks=200000)
+    keep = set(range(n_streams))
+    for s in sorted(keep):
+        cache.add_sequence(s)
+    for s, pos in zip(rounds[0].append_seqs, rounds[0].append_positions):
+        if s in keep:
+            cache.append_slots(s, torch.from_numpy(pos))
+    ev = rounds[1]
+    work = [(s, spans) for s, spans in zip(ev.evict_seqs, ev.evict_spans) if s in keep]
     t0 = time.perf_counter()
-    toks, it = 0, 0
-    while (time.perf_counter() - t0 < min_seconds and it < max_iters) or it == 0:
-        toks += step()
-        it += 1
-    return toks / (time.perf_counter() - t0), it
+    for s, spans in work:
+        cache.evict_positions(s, spans)
+    sec = time.perf_counter() - t0
+    per = sec / max(len(work), 1)
+    return {"streams": len(work), "ms_per_stream": per * 1e3, "ms_per_256_streams": per * 256e3}
+
+
+def ref_rollout_leg() -> dict:
+    """The CPU bench configuration through the reference's own engines (fp32 default TinyLM,
+    keep_recent keep_last=2, 16-token blocks padded, budget 256, recall env with 24
+    distractors x filler 64, seeds 0-7, teacher-forced): KV-streams and re-prefill, 8
+    rollouts each; tokens forwarded, wall time and the KV-streams replay mismatch."""
+    from kvstreams.config import CacheConfig, RolloutConfig
+    from kvstreams.envs import build_env
+    from kvstreams.factory import build_stack
+    from kvstreams.training import measure_mismatch
+
+    out = {}
+    for engine in ("kvstream", "reprefill"):
+        st = build_stack(engine=engine, policy="keep_recent", policy_kwargs={"keep_last": 2},
+                         cache_cfg=CacheConfig(16, pad_to_block=True),
+                         rollout_cfg=RolloutConfig(context_budget=256, max_turns=128), dtype="float32", seed=0)
+        t0 = time.perf_counter()
+        rs = [st.engine.rollout(build_env("recall", seed=i, num_distractors=24, filler_len=64), teacher_forcing=True)
+              for i in range(8)]
+        out[f"{engine}_s"] = time.perf_counter() - t0
+        out[f"{engine}_tokens_forwarded"] = sum(r.stats.tokens_forwarded for r in rs)
+        if engine == "kvstream":
+            out["kvstream_replay_max_dlogp"] = measure_mismatch(st.model, rs, "kvstream").max_abs_logprob_diff
+    return out
+
+
+def cpu_legs(args) -> dict:
+    """Every CPU measurement of this run in one process: the reference's own code when it is
+    installed (kind "reference"), else the oracle port for the decode step."""
+    reference = _use_reference()
+    if not reference:
+        _use_package()  # the oracle port and its workloads
+    cores = _cpu_threads()
+    step, ctx = ref_decode_leg(0) if reference else port_decode_leg(0)
+    for _ in range(args.warmup):
+        step()
+    rates = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        n = step()
+        rates.append(n / (time.perf_counter() - t0))
+    value = statistics.median(rates)
+    out = {"kind": "reference" if reference else "port", "cores": cores, "decode_tok_s": value,
+           "decode_sample": f"{CPU_STREAMS} of the {S} streams ({ctx} context tokens) per step, "
+                            + ("the reference's PagedKVCache + RoPE + model.py:67-74 attention in bf16 (torch CPU)"
+                               if reference else "oracle port, numpy float32")}
+    if reference:
+        out["compaction_bs16"] = ref_compaction_leg(16, 32, 0)
+        out["compaction_bs1"] = ref_compaction_leg(1, 256, 0)
+        out["config1"] = ref_rollout_leg()
+    return out
+
+
+def workload_config() -> dict:
+    """The ``config`` of both arms' lines (the same workload)."""
+    return {"workload": f"paged decode+append (one layer), 32q/8kv heads, D128, bs16, {S} streams/GPU, "
+                        f"ctx U[{CTX[0]},{CTX[1]}], pool {NB} blocks, 1-6 evicted spans/stream, theta 5e5",
+            "streams_per_gpu": S, "l2": "per-step KV read ~2.3 GB > 126 MB L2 (no flush needed)"}
 
 
 # ---------------------------------------------------------------------- main arms
 def run_reference(args, rank: int, world: int) -> None:
+    """The reference arm: rank 0 alone times the CPU path (the other ranks exit)."""
     if rank != 0:
         return
-    step, ctx_tokens = cpu_decode_sample(seed=0)
-    cores = os.cpu_count() or 1
-    rate_samples = []
-    for _ in range(args.warmup):
-        step()
-    for _ in range(args.steps):
-        t0 = time.perf_counter()
-        n = step()
-        rate_samples.append(n / (time.perf_counter() - t0))
-    value = statistics.median(rate_samples)
+    cpu = cpu_legs(args)
+    value = cpu["decode_tok_s"]
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "decode tok/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * 4 / value, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "paged decode+append, 32q/8kv heads, D128, bs16, 64 streams, ctx U[1024,16384]",
-                   "sample": "4 of the 64 streams per step"},
-        "cpu_baseline": {"value": value, "unit": "decode tok/s", "cores": cores, "kind": "port",
-                         "sample": f"4 streams ({ctx_tokens} context tokens) of the 64-stream workload per step"},
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * CPU_STREAMS / value,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16" if cpu["kind"] == "reference" else "f32", "data": "synthetic",
+        "config": workload_config(),
+        "cpu_baseline": {"value": value, "unit": "decode tok/s", "cores": cpu["cores"], "kind": cpu["kind"],
+                         "sample": cpu["decode_sample"]},
         "e2e": {"value": value, "unit": "decode tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    if "compaction_bs16" in cpu:
+        line["secondary"] = {"compaction_bs16_ms_per_256_streams": cpu["compaction_bs16"]["ms_per_256_streams"],
+                             "compaction_bs1_ms_per_256_streams": cpu["compaction_bs1"]["ms_per_256_streams"],
+                             **{f"config1_{k}": v for k, v in cpu["config1"].items()}}
+    if args.cpu_json:
+        print(json.dumps(cpu), flush=True)
+    else:
+        print(json.dumps(line), flush=True)
+
+
+def cpu_baseline_subprocess(args) -> dict:
+    """cpu_legs in a process of its own (it imports the reference's package, whose name is
+    this library's), on the same steps and warm-up."""
+    env = {k: v for k, v in os.environ.items() if k not in ("RANK", "WORLD_SIZE", "LOCAL_RANK", "MASTER_ADDR",
+                                                            "MASTER_PORT", "LOCAL_WORLD_SIZE")}
+    cmd = [sys.executable, str(REPO / "bench.py"), "--impl", "reference", "--cpu-json", "--steps", str(args.steps),
+           "--warmup", str(args.warmup), "--streams", str(S), "--pool-blocks", str(NB), "--ctx-max", str(CTX[1])]
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=900)
+    if r.returncode != 0:
+        raise RuntimeError(f"CPU baseline process failed:\n{r.stderr[-2000:]}")
+    return json.loads(r.stdout.strip().splitlines()[-1])
 
 
 def run_b200(args, rank: int, world: int, local_rank: int) -> None:
@@ -374,25 +551,28 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hpos))
     d2h = hout[0].numel() * hout[0].element_size()
 
-    secondary = None
+    detail = {}
     if not args.skip_secondary:
         del hq, hk, hv, hout
-        secondary = compaction_bench(dev, args, rank)
-        secondary["decode_bs1"] = decode_bs1_bench(dev, args, rank)
-        secondary["replay_attention"] = replay_bench(dev, args, rank)
-        secondary["replay_backward"] = replay_backward_bench(dev, args, rank)
-        secondary["compaction_policy"] = compaction_policy_bench(dev, args, rank)
-        secondary["lm_head_logprobs"] = lm_head_logprobs_bench(dev, args, rank)
-        secondary["rollout"] = rollout_bench(dev, args, rank)
-        secondary["prefill"] = prefill_bench(dev, args, rank)
-        secondary["replay_model"] = replay_model_bench(dev, args, rank)
-        secondary["replay_train"] = replay_train_bench(dev, args, rank)
+        detail = compaction_bench(dev, args, rank)
+        detail["decode_bs1"] = decode_bs1_bench(dev, args, rank)
+        detail["replay_attention"] = replay_bench(dev, args, rank)
+        detail["replay_backward"] = replay_backward_bench(dev, args, rank)
+        detail["compaction_policy"] = compaction_policy_bench(dev, args, rank)
+        detail["lm_head_logprobs"] = lm_head_logprobs_bench(dev, args, rank)
+        detail["config1"] = config1_bench(dev, args, rank)
+        detail["rollout"] = rollout_bench(dev, args, rank, world)
+        detail["prefill"] = prefill_bench(dev, args, rank)
+        detail["replay_model"] = replay_model_bench(dev, args, rank)
+        detail["replay_train"] = replay_train_bench(dev, args, rank)
 
     if rank != 0:
         return
     peaks = _peaks()
-    step_cpu, ctx_tokens = cpu_decode_sample(seed=0)
-    cpu_rate, cpu_iters = time_cpu(step_cpu, min_seconds=args.cpu_seconds)
+    # the CPU baseline: rank 0 at one GPU only
+    cpu = cpu_baseline_subprocess(args) if world == 1 and not args.skip_cpu else None
+    if cpu is not None:
+        detail["cpu"] = cpu
     # DRAM bytes of one decode launch: ncu-measured traffic/algorithmic ratio (small-case
     # capture, profiles/) scaled by this launch's algorithmic bytes
     ratio = _traffic().get("paged_decode", {}).get("traffic_over_algorithmic")
@@ -410,11 +590,7 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic",
-        "config": {"workload": "paged decode+append (one layer), 32q/8kv heads, D128, bs16, 64 streams/GPU, "
-                               "ctx U[1024,16384], pool 131072 blocks, 1-6 evicted spans/stream, theta 5e5",
-                   "streams_per_gpu": S, "kv_bytes_per_step": int(alg_bytes),
-                   "l2": "per-step KV read ~2.3 GB > 126 MB L2 (no flush needed)",
-                   "per_gpu_decode_tok_s": S * args.steps / (ms * 1e-3)},
+        "config": workload_config(),
         "e2e": {"value": world * S * args.steps / (e2e_ms * 1e-3), "unit": "decode tok/s",
                 "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                 "ms_per_step": e2e_ms / args.steps,
@@ -424,21 +600,78 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
         "gpu_launches": int(launches),
         "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved_gbs / peaks["hbm_gbs"], "peak_src": peaks["src"],
-                     "frac_of_8tbs_spec": achieved_gbs / 8000.0,
-                     "traffic": traffic, "kernel": "kvs_paged_decode", "kernel_ms": attn_ms},
-        "cpu_baseline": {"value": cpu_rate, "unit": "decode tok/s", "cores": os.cpu_count() or 1, "kind": "port",
-                         "sample": f"4 of 64 streams ({ctx_tokens} context tokens), {cpu_iters} passes, "
-                                   "numpy float32 gather + GQA attention"},
+                     "frac_of_8tbs_spec": achieved_gbs / 8000.0, "bytes_per_launch": int(alg_bytes),
+                     "traffic": traffic, "kernel": "decode_bf16_kernel (kvs_paged_decode)", "kernel_ms": attn_ms},
         "clocks": clocks,
     }
-    if secondary:
-        line["secondary"] = secondary
+    if cpu is not None:
+        line["cpu_baseline"] = {"value": cpu["decode_tok_s"], "unit": "decode tok/s", "cores": cpu["cores"],
+                                "kind": cpu["kind"], "sample": cpu["decode_sample"]}
+    if "rollout" in detail:
+        r = detail["rollout"]
+        line["rollout_decode_tok_s"] = r["rollout_decode_tok_s_total"]
+        line["rollout_decode_tok_s_per_gpu"] = r["rollout_decode_tok_s_total"] / world
+        line["rollout_ms_per_iteration"] = r["ms_per_iteration"]
+    if detail:
+        line["secondary"] = flat_secondary(detail)
+    if args.detail:
+        Path(args.detail).write_text(json.dumps(detail, indent=1))
     print(json.dumps(line), flush=True)
 
 
+def flat_secondary(d: dict) -> dict:
+    """The measurements beside the headline as one short flat dict of numbers (4 significant
+    digits), last on the line so that a reader of the line's tail sees them; the nested
+    ``--detail`` file holds everything.  Keys: *_tc / *_hbm = fraction of the measured bf16 /
+    HBM peak; c1_* = the CPU bench configuration (8 rollouts, KV-streams vs re-prefill) on the
+    GPU and through the reference on the host cores; *_cpu_ref_* = the reference on the host."""
+    out = {}
+
+    def put(key, *path):
+        v = d
+        for k in path:
+            if not isinstance(v, dict) or k not in v:
+                return
+            v = v[k]
+        out[key] = float(f"{v:.4g}") if isinstance(v, float) else v
+
+    put("bs1_decode_hbm", "decode_bs1", "hbm_frac")
+    put("prefill_tc", "prefill", "tc_frac")
+    put("replay_tc", "replay_attention", "tc_frac")
+    put("replay_bwd_tc", "replay_backward", "tc_frac")
+    put("lse_gather_hbm", "lm_head_logprobs", "lse_gather_hbm_frac")
+    put("bs1_decode_ms", "decode_bs1", "ms")
+    put("prefill_ms", "prefill", "ms")
+    put("replay_ms", "replay_attention", "ms")
+    put("replay_bwd_ms", "replay_backward", "ms")
+    put("compact16_ms", "compaction_bs16", "ms_per_call")
+    put("compact1_ms", "compaction_bs1", "ms_per_call")
+    put("compact16_cpu_ref_ms", "cpu", "compaction_bs16", "ms_per_256_streams")
+    put("compact1_cpu_ref_ms", "cpu", "compaction_bs1", "ms_per_256_streams")
+    put("round_host_ms", "compaction_policy", "host_policy_ms_per_round")
+    put("round_dev_ms", "compaction_policy", "device_policy_gpu_ms_per_round")
+    put("lmhead_fused_ms", "lm_head_logprobs", "fused_fwd_ms")
+    put("lmhead_torch_ms", "lm_head_logprobs", "torch_fwd_ms")
+    put("sample_ms", "lm_head_logprobs", "sampling", "kvs_sample_kernel_ms")
+    put("rollout_prefill_tok_s", "rollout", "prefill_tok_s_per_gpu")
+    put("replay_model_tok_s", "replay_model", "replay_tok_s_per_gpu")
+    put("train_tok_s", "replay_train", "train_tok_s_per_gpu")
+    put("train_flop_frac", "replay_train", "model_flop_frac")
+    put("c1_tok_kvs", "config1", "kvstream_tokens_forwarded")
+    put("c1_tok_reprefill", "config1", "reprefill_tokens_forwarded")
+    put("c1_gpu_kvs_s", "config1", "kvstream_s")
+    put("c1_gpu_reprefill_s", "config1", "reprefill_s")
+    put("c1_gpu_dlogp", "config1", "kvstream_replay_max_dlogp")
+    put("c1_cpu_ref_kvs_s", "cpu", "config1", "kvstream_s")
+    put("c1_cpu_ref_reprefill_s", "cpu", "config1", "reprefill_s")
+    put("c1_cpu_ref_dlogp", "cpu", "config1", "kvstream_replay_max_dlogp")
+    return out
+
+
 def compaction_bench(dev, args, rank: int) -> dict:
-    """256 streams x 512-block tables (pool 200000): one batched evict_positions over
-    all streams per step (keep-recent turn spans), state restored between steps."""
+    """256 streams x 512-block tables (pool 200000), 1-8 keep-recent events per stream: the
+    first eviction round (every stream evicts its turn spans) as one batched evict_positions
+    per step, state restored between steps."""
     import torch
 
     from kvstreams.paged_cache import PagedKVCache
@@ -447,7 +680,7 @@ def compaction_bench(dev, args, rank: int) -> dict:
     out = {}
     for bs, blocks in ((16, 512), (1, 512)):
         rounds = compaction_plan(num_streams=256, blocks_per_stream=blocks, block_size=bs, seed=rank,
-                                 num_events_range=(1, 1))
+                                 num_events_range=(1, 8))
         nb = 200000
         cache = PagedKVCache(1, 1, 2, block_size=bs, num_blocks=nb, dtype=torch.bfloat16, device=dev,
                              max_seqs=256, max_blocks_per_seq=blocks + 64)
@@ -690,7 +923,40 @@ def lm_head_logprobs_bench(dev, args, rank: int) -> dict:
     return out
 
 
-def rollout_bench(dev, args, rank: int) -> dict:
+def config1_bench(dev, args, rank: int) -> dict:
+    """The CPU bench configuration on the GPU (fp32 default TinyLM, keep_recent keep_last=2,
+    16-token blocks padded, budget 256, recall env with 24 distractors x filler 64, seeds 0-7,
+    teacher-forced): 8 rollouts per engine in one rollout_batch call (KV-streams, re-prefill),
+    tokens forwarded, wall time, and the KV-streams replay mismatch (gate 1e-5)."""
+    import torch
+
+    from kvstreams.config import CacheConfig, RolloutConfig
+    from kvstreams.envs import build_env
+    from kvstreams.factory import build_stack
+    from kvstreams.training import measure_mismatch
+
+    out = {}
+    for engine in ("kvstream", "reprefill"):
+        st = build_stack(engine=engine, policy="keep_recent", policy_kwargs={"keep_last": 2},
+                         cache_cfg=CacheConfig(16, pad_to_block=True),
+                         rollout_cfg=RolloutConfig(context_budget=256, max_turns=128), dtype="float32",
+                         device=str(dev), seed=0)
+        envs = [build_env("recall", seed=i, num_distractors=24, filler_len=64) for i in range(8)]
+        st.engine.rollout_batch(envs[:1], teacher_forcing=True)  # warm-up
+        torch.cuda.synchronize(dev)
+        envs = [build_env("recall", seed=i, num_distractors=24, filler_len=64) for i in range(8)]
+        t0 = time.perf_counter()
+        rs = st.engine.rollout_batch(envs, teacher_forcing=True)
+        torch.cuda.synchronize(dev)
+        out[f"{engine}_s"] = time.perf_counter() - t0
+        out[f"{engine}_tokens_forwarded"] = sum(r.stats.tokens_forwarded for r in rs)
+        if engine == "kvstream":
+            out["kvstream_replay_max_dlogp"] = measure_mismatch(st.model, rs, "kvstream").max_abs_logprob_diff
+        del st
+    return out
+
+
+def rollout_bench(dev, args, rank: int, world: int = 1) -> dict:
     """Config 5 on one GPU: batched KV-streams rollouts of the Llama-3-8B architecture
     (random init, bf16; 32 layers, d 4096, 32/8 heads, FFN 14336, vocab 128256), 64 rollouts
     of 24 turns with observation and reply lengths ~U[64, 512] (uniform random ids), Markovian
@@ -757,12 +1023,16 @@ def rollout_bench(dev, args, rank: int) -> dict:
     torch.cuda.synchronize(dev)
     ms = ev[0].elapsed_time(ev[1])
     ms = reduce_max(ms, dev)
+    from kvstreams.distributed import reduce_sum
+
+    total_decode = reduce_sum(tally["decode"], dev)  # every rank's rollouts over the slowest rank's time
     out = {
         "workload": f"{n} rollouts/GPU x {turns} turns, obs/reply ~U[64,512], Llama-3-8B arch "
                     f"({cfg.n_layers} layers) bf16 random init, Markovian keep_last=1, budget {budget}, bs16",
         "iterations_timed": K, "ms": ms,
         "decode_tokens": tally["decode"], "prefill_tokens": tally["prefill"],
         "rollout_decode_tok_s_per_gpu": tally["decode"] / (ms * 1e-3),
+        "rollout_decode_tok_s_total": total_decode / (ms * 1e-3), "ranks": world,
         "prefill_tok_s_per_gpu": tally["prefill"] / (ms * 1e-3),
         "ms_per_iteration": ms / K,
         "library_launches": N.lib().kvs_launch_count() - launches0,
@@ -1053,7 +1323,9 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--cpu-json", action="store_true", help=argparse.SUPPRESS)  # the CPU legs' process
+    ap.add_argument("--skip-cpu", action="store_true", help="no CPU baseline leg")
+    ap.add_argument("--detail", default="", help="write every measurement, nested, to this JSON file")
     ap.add_argument("--skip-secondary", action="store_true")
     ap.add_argument("--streams", type=int, default=S, help="decode streams per GPU (profiling: smaller case)")
     ap.add_argument("--pool-blocks", type=int, default=NB)
@@ -1096,10 +1368,22 @@ def main() -> int:
     if args.impl == "reference":
         run_reference(args, rank, world)
         return 0
+    _use_package()
     import datetime
 
     import torch
     import torch.distributed as dist
+
+    local_world = int(os.environ.get("LOCAL_WORLD_SIZE", world))
+    if local_world > 1 and hasattr(os, "sched_setaffinity"):
+        # one rank per GPU on a shared host: each rank's engine loop and launches get their own
+        # slice of the host cores instead of all ranks' threads competing for every core
+        cores = sorted(os.sched_getaffinity(0))
+        per = len(cores) // local_world
+        if per >= 2:
+            mine = cores[local_rank * per:(local_rank + 1) * per]
+            os.sched_setaffinity(0, mine)
+            torch.set_num_threads(len(mine))
 
     if world > 1:
         torch.cuda.set_device(local_rank)
