@@ -9,7 +9,7 @@
 // internal scratch (per-sequence counts, drop flags, dropped block ids) is taken
 // from a fixed array compiled into the library instead of from the caller.
 //
-// The scratch lives in `g_evict_scratch`, a file-scope __device__ array of
+// The scratch lives in `g_evict_scratch`, a file-scope static __device__ array of
 // kNoAllocScratchBytes (about 1.25 MiB).  Every GPU that loads the library holds
 // one copy until the process exits.  Limits: at most kNoAllocMaxSeqs sequences
 // per call and a cache whose tables hold at most kNoAllocMaxBlocks entries per
@@ -25,7 +25,9 @@
 // name is only a host-side stand-in for the symbol.  The device address is
 // obtained once per device with cudaGetSymbolAddress while that device is
 // current, on the first call that runs on it; make that first call before any
-// stream capture begins.
+// stream capture begins.  The address stays cached for the life of the process, so
+// do not call cudaDeviceReset (or otherwise tear down the device's context) while
+// the library is in use: the reloaded module may place the array elsewhere.
 #include "kvs_common.cuh"
 
 #include <mutex>
@@ -39,7 +41,11 @@ constexpr int kMaxDevices = 64;
 // 256-byte aligned snapshot word, counts, drop flags, dropped block ids.
 constexpr size_t kNoAllocScratchBytes = 256 + 2048 + 262144 + 1048576;
 
-__device__ __align__(256) unsigned char g_evict_scratch[kNoAllocScratchBytes];
+}  // namespace
+
+static __device__ __align__(256) unsigned char g_evict_scratch[kNoAllocScratchBytes];
+
+namespace {
 
 std::mutex g_mu;
 void* g_scratch_ptr[kMaxDevices] = {};

@@ -173,7 +173,8 @@ int kvs_evict_positions(const kvs_cache* c, const kvs_batch* b, const int32_t* c
  * KVS_E_NOALLOC_LIMIT and nothing is launched.  Calls share that array, so calls
  * whose kernels overlap on the GPU race.  The first call on each device looks up
  * the array's device address (cudaGetSymbolAddress); make it before any stream
- * capture.  Allocates nothing. */
+ * capture.  The address is cached until exit: do not cudaDeviceReset a device
+ * while the library is in use.  Allocates nothing. */
 int kvs_evict_positions_noalloc(const kvs_cache* c, const kvs_batch* b, const int32_t* cu_spans,
                                 const int64_t* span_start, const int64_t* span_end,
                                 int64_t* out_spans, int32_t* out_counts, int32_t span_cap,

@@ -61,3 +61,21 @@ def test_null_arguments_are_rejected_before_launch(lib):
     assert lib.kvs_append_slots(None, None, None, None, None, None) == -1
     assert lib.kvs_replay_attention(None, None) == -1
     assert lib.kvs_rope(None, 0, None, 0, 1, 2, None, None) == -1
+
+
+def test_noalloc_limits_are_checked_on_the_host(lib):
+    """kvs_evict_positions_noalloc refuses a batch beyond its built-in scratch -- more than 256
+    sequences, or tables longer than 1024 entries -- with KVS_E_NOALLOC_LIMIT before any CUDA
+    call, and an empty batch is a no-op (struct pointers are never dereferenced on the device
+    here: nothing may be launched)."""
+    import ctypes as C
+
+    from kvstreams import _native as N
+
+    cache = N.KvsCache(n_layers=1, num_blocks=4096, block_size=16, n_kv_heads=1, head_dim=2, max_seqs=512,
+                       max_blocks=1024, dtype=N.KVS_F32)
+    for num_seqs, max_blocks, want in ((257, 1024, -5), (1, 1025, -5), (0, 1024, 0)):
+        cache.max_blocks = max_blocks
+        batch = N.KvsBatch(seq_slots=None, cu_tokens=None, num_seqs=num_seqs, total_tokens=num_seqs)
+        rc = lib.kvs_evict_positions_noalloc(C.byref(cache), C.byref(batch), None, None, None, None, None, 1, None)
+        assert rc == want, (num_seqs, max_blocks, rc)

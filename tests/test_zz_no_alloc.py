@@ -106,6 +106,61 @@ def test_noalloc_eviction_equals_allocating_entry_point_twice():
         assert _state(a) == _state(b)
 
 
+def test_noalloc_on_a_second_stream_after_synchronising():
+    """The supported reuse pattern: a later call on another stream, once the earlier calls have
+    finished, finds the shared array (and this device's cached address) as good as new."""
+    a, rounds = _build()
+    b, _ = _build()
+    cap = 64
+    for rd in rounds[:2]:  # a round evicts first, then appends its refills
+        if rd.evict_seqs:
+            a.evict_positions_async(rd.evict_seqs, rd.evict_spans, span_cap=cap)
+            torch.cuda.synchronize()
+            a.refresh(rd.evict_seqs)
+            _noalloc_evict(b, rd.evict_seqs, rd.evict_spans, cap)
+        _append_round(a, rd)
+        _append_round(b, rd)
+    rd = rounds[2]
+    out_a, counts_a, _ = a.evict_positions_async(rd.evict_seqs, rd.evict_spans, span_cap=cap)
+    torch.cuda.synchronize()
+    a.refresh(rd.evict_seqs)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        out_b, counts_b = _noalloc_evict(b, rd.evict_seqs, rd.evict_spans, cap)
+    torch.cuda.synchronize()
+    ca = counts_a.cpu().numpy()
+    assert np.array_equal(ca, counts_b.cpu().numpy())
+    oa, ob = out_a.cpu().numpy(), out_b.cpu().numpy()
+    for i, n in enumerate(ca):
+        assert np.array_equal(oa[i, :n], ob[i, :n])
+    assert _state(a) == _state(b)
+
+
+def test_noalloc_rejects_more_sequences_than_its_limit():
+    """257 sequences (one more than the built-in scratch holds): KVS_E_NOALLOC_LIMIT, and the
+    cache is untouched."""
+    from kvstreams import _native as N
+    from kvstreams.paged_cache import PagedKVCache
+
+    n = 257
+    cache = PagedKVCache(1, 1, 2, block_size=16, num_blocks=n * 4, dtype=torch.float32, max_seqs=n,
+                         max_blocks_per_seq=4)
+    for s in range(n):
+        cache.add_sequence(s)
+    cache.append_slots_batch(list(range(n)), torch.arange(n * 32) % 32, [32] * n)
+    before = (cache._tables.clone(), cache._lengths.clone(), cache._free_stack.clone(), cache.slot_pos.clone())
+    b, keep = cache._batch([cache.slot(s) for s in range(n)])
+    dummy = torch.zeros(n * 4, dtype=torch.long, device=cache.device)
+    rc = N.lib().kvs_evict_positions_noalloc(C.byref(cache.struct), C.byref(b), dummy.data_ptr(), dummy.data_ptr(),
+                                             dummy.data_ptr(), dummy.data_ptr(), dummy.data_ptr(), 1,
+                                             N.stream_ptr(cache.device))
+    torch.cuda.synchronize()
+    assert rc == -5
+    after = (cache._tables, cache._lengths, cache._free_stack, cache.slot_pos)
+    assert all(torch.equal(x, y) for x, y in zip(before, after))
+
+
 def test_noalloc_rejects_batches_beyond_its_limit():
     from kvstreams import _native as N
     from kvstreams.paged_cache import PagedKVCache
