@@ -962,7 +962,8 @@ def rollout_bench(dev, args, rank: int, world: int = 1) -> dict:
     of 24 turns with observation and reply lengths ~U[64, 512] (uniform random ids), Markovian
     keep_last=1, context budget 8192, 16-token blocks padded.  Timed: ``--rollout-iters`` engine
     iterations (each one decode step of the generating rollouts plus one batched chunk call
-    for turn starts and reply ends) after ``--rollout-warmup`` iterations, by CUDA events."""
+    for turn starts and reply ends) after ``--rollout-warmup`` iterations, by CUDA events,
+    preceded by an untimed run of ``--rollout-warmup-run`` iterations on other episodes."""
     import torch
 
     from kvstreams.compaction.policies import MarkovianPolicy
@@ -989,8 +990,18 @@ def rollout_bench(dev, args, rank: int, world: int = 1) -> dict:
     blocks = n * ((budget + 512 + 16 + 16) // 16 + 1)
     cache = PagedKVCache(cfg.n_layers, cfg.n_kv_heads, cfg.head_dim, block_size=16, num_blocks=blocks,
                          dtype=torch.bfloat16, device=dev, max_seqs=n)
-    eng = BatchedKVStreams(model, cache, MarkovianPolicy(keep_last=1), context_budget=budget, seed=rank,
-                           cuda_graphs=not args.rollout_eager, device_policy=args.rollout_device_policy)
+    def engine():
+        return BatchedKVStreams(model, cache, MarkovianPolicy(keep_last=1), context_budget=budget, seed=rank,
+                                cuda_graphs=not args.rollout_eager, device_policy=args.rollout_device_policy)
+
+    # untimed warm-up on other episodes: the first use of each GEMM shape family loads and
+    # selects its cuBLAS kernels (milliseconds per call), a one-time cost of the process that a
+    # long run amortises and a 100-iteration window would otherwise carry
+    if args.rollout_warmup_run > 0:
+        engine().run(synthetic_episodes(n, turns=turns, turn_range=(64, 512), prompt_len=64, vocab=cfg.vocab_size,
+                                        seed=7000 + rank), max_iterations=args.rollout_warmup_run)
+        torch.cuda.synchronize(dev)
+    eng = engine()
     eps = synthetic_episodes(n, turns=turns, turn_range=(64, 512), prompt_len=64, vocab=cfg.vocab_size,
                              seed=1000 + rank)
     W, K = args.rollout_warmup, args.rollout_iters
@@ -1342,6 +1353,8 @@ def main() -> int:
     ap.add_argument("--rollout-streams", type=int, default=64)
     ap.add_argument("--rollout-layers", type=int, default=32)
     ap.add_argument("--rollout-warmup", type=int, default=20)
+    ap.add_argument("--rollout-warmup-run", type=int, default=300,
+                    help="engine iterations of an untimed warm-up run on other episodes first")
     ap.add_argument("--rollout-iters", type=int, default=100)
     ap.add_argument("--rollout-full", action="store_true", help="play the whole episodes (minutes)")
     ap.add_argument("--rollout-eager", action="store_true", help="decode steps without CUDA graphs")

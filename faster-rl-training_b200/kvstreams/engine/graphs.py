@@ -9,9 +9,13 @@ time.  :class:`DecodeGraphs` records that sequence once per batch size ``n`` and
   runs inside the graph on them (``PagedKVCache.append_slots_device``), its host half
   (``reserve_slots``: pool check, host-mirror lengths) runs before each replay;
 * the paged-decode scratch is sized once for the largest batch, so no replay reallocates it;
-* the first step of a new size runs eagerly (it also warms cuBLAS and the library's one-time
-  kernel attributes), the graph is recorded right after (recording executes nothing) and is
-  replayed from the next step of that size on.  All graphs share one memory pool.
+* the first decode step runs eagerly (it also warms cuBLAS and the library's one-time kernel
+  attributes); right after it the graphs of every batch size 1..max_batch are recorded
+  (recording executes nothing), so that no later step pays for a capture -- a rollout batch
+  changes size whenever a rollout starts or ends a turn, and capturing a size on its first
+  appearance spread ~0.1 s captures over the run.  All graphs share one memory pool (each
+  graph's output stays referenced, and one graph's intermediates are dead before the next
+  replays).
 """
 
 from __future__ import annotations
@@ -55,6 +59,13 @@ class DecodeGraphs:
         self.cache.append_slots_device(b, pos, blocks, offsets)
         return self.model.forward_layers(self.tok[:n], pos, self.cache, (b, [self.slots]), SlotMapping(blocks, offsets))
 
+    def _record(self, n: int) -> None:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, pool=self.pool):
+            out = self._body(n)
+        self.pool = g.pool()
+        self.graphs[n] = (g, out)
+
     @torch.no_grad()
     def step(self, seq_ids: Sequence[int], tokens: torch.Tensor, positions: Sequence[int]) -> torch.Tensor:
         """Logits ``[n, vocab]`` of one new token per sequence (same effect on the cache as
@@ -63,14 +74,11 @@ class DecodeGraphs:
         if n > self.max_batch:
             raise ValueError(f"{n} sequences exceed the graph batch capacity {self.max_batch}")
         if n not in self.graphs:
-            pos_t = torch.as_tensor(np.asarray(positions, dtype=np.int64), device=self.model.device)
+            pos_t = N.to_device(np.asarray(positions, dtype=np.int64), torch.long, self.model.device)
             logits = self.model.forward_cached_batch(tokens, pos_t, self.cache, seq_ids)
             torch.cuda.current_stream().synchronize()
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, pool=self.pool):
-                out = self._body(n)
-            self.pool = g.pool()
-            self.graphs[n] = (g, out)
+            for m in ([n] if self.graphs else range(1, self.max_batch + 1)):
+                self._record(m)
             return logits
         self.cache.reserve_slots(seq_ids)
         cache = self.cache
