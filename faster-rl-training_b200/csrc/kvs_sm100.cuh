@@ -270,6 +270,73 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
 
+// ------------------------------------------------------------------ CTA pairs (cta_group::2)
+// Two CTAs of a 2-CTA cluster work as one MMA unit: the even CTA issues M = 256 UMMAs whose
+// A rows and B columns come half from each CTA's shared memory (same offsets), and whose
+// accumulator rows 0..127 / 128..255 land in the even / odd CTA's TMEM.
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
+  return r;
+}
+// every thread of both CTAs; orders shared-memory writes (barrier inits) across the cluster
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+// the shared::cluster address of the same shared-memory offset in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t mapa_shared(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(r) : "r"(smem_addr(p)), "r"(rank));
+  return r;
+}
+// arrive on a barrier given by its shared::cluster address (possibly the peer CTA's)
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster_addr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];\n" ::"r"(bar_cluster_addr) : "memory");
+}
+// 2-D tiled TMA load into this CTA's shared memory whose completion is counted on a barrier
+// of either CTA of the pair (shared::cluster address); each CTA loads only its own tile.
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, int x, int y,
+                                                 uint32_t bar_cluster_addr) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];\n" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar_cluster_addr)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_addr(dst_smem)),
+               "r"(ncols));
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;\n" ::);
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;\n" ::"r"(taddr), "r"(ncols));
+}
+// D (+)= A * B^T over the pair, both operands from shared memory (warp-collective, one lane
+// issues); A_OFF / B_OFF are added to the descriptors' start-address fields
+template <uint32_t A_OFF, uint32_t B_OFF>
+__device__ __forceinline__ void umma_pair_warp_at(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                                  uint32_t accumulate) {
+  asm volatile(
+      "{\n.reg .pred p, e;\n.reg .b64 a, b;\n"
+      "add.s64 a, %1, %5;\n"
+      "add.s64 b, %2, %6;\n"
+      "elect.sync _|e, 0xffffffff;\n"
+      "setp.ne.b32 p, %4, 0;\n"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], a, b, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "n"(A_OFF), "n"(B_OFF));
+}
+// arrive once on the barrier at shared::cluster address `bar` (this CTA's or the peer's) when
+// this thread's pair UMMAs so far have completed (warp-collective, one lane issues)
+__device__ __forceinline__ void umma_commit_pair_warp(uint32_t bar_cluster_addr) {
+  asm volatile(
+      "{\n.reg .pred e;\n"
+      "elect.sync _|e, 0xffffffff;\n"
+      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n}\n" ::"r"(bar_cluster_addr)
+      : "memory");
+}
+
 // ------------------------------------------------------------------ descriptors
 // K-major operand, 128-byte swizzle: rows of 128 B (64 bf16 of K), 8-row atoms
 // 1024 B apart (SBO); tiles of 64 K-columns are separate regions (the caller

@@ -305,6 +305,48 @@ def lse_gather(logits: torch.Tensor, targets: torch.Tensor, temperature: float =
     return logp, lse
 
 
+_LMHEAD_OK: dict = {}
+
+
+def lm_head_logprobs_supported(h: torch.Tensor, weight: torch.Tensor) -> bool:
+    """Whether :func:`lm_head_logprobs` can take these operands on this device."""
+    if not (h.is_cuda and weight.is_cuda and h.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16):
+        return False
+    if h.dim() != 2 or weight.dim() != 2 or h.stride(1) != 1 or weight.stride(1) != 1:
+        return False
+    K = h.shape[1]
+    if weight.shape[1] != K or K % 64 or h.stride(0) % 8 or weight.stride(0) % 8:
+        return False
+    if h.data_ptr() % 16 or weight.data_ptr() % 16:
+        return False
+    key = (h.device.index, K)
+    if key not in _LMHEAD_OK:
+        with torch.cuda.device(h.device):
+            _LMHEAD_OK[key] = bool(N.lib().kvs_lm_head_logprobs_supported(K))
+    return _LMHEAD_OK[key]
+
+
+def lm_head_logprobs(h: torch.Tensor, weight: torch.Tensor, targets: torch.Tensor, temperature: float = 1.0):
+    """``(logp, lse)`` of ``log_softmax((h @ weight.T) / T)`` at ``targets`` and its log-sum-exp,
+    float32, without storing the ``[rows, vocab]`` logits (training/logprobs.py:17-20): one
+    tensor-core GEMM whose epilogue reduces each 256-wide vocab tile, then a merge of the tiles.
+    h ``[rows, K]`` and weight ``[vocab, K]`` bf16 (see :func:`lm_head_logprobs_supported`)."""
+    _check_cuda(h, weight, targets)
+    n, K = h.shape
+    V = weight.shape[0]
+    t = targets.to(torch.long).contiguous().reshape(-1)
+    logp = torch.empty(n, dtype=torch.float32, device=h.device)
+    lse = torch.empty(n, dtype=torch.float32, device=h.device)
+    lib = N.lib()
+    nbytes = int(lib.kvs_lm_head_logprobs_scratch_bytes(n, V))
+    scratch = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=h.device)
+    rc = lib.kvs_lm_head_logprobs(h.data_ptr(), h.stride(0), weight.data_ptr(), weight.stride(0), n, V, K,
+                                  t.data_ptr(), float(temperature), logp.data_ptr(), lse.data_ptr(),
+                                  scratch.data_ptr(), scratch.numel(), N.stream_ptr(h.device))
+    N.check(rc, "kvs_lm_head_logprobs")
+    return logp, lse
+
+
 def sample(logits: torch.Tensor, temperature: float = 1.0, greedy: bool = False, seed: int = 0, offset: int = 0):
     """``(tokens, logp)``: one next token per row of 2-D float32/float64 CUDA logits and its
     ``log_softmax(logits / T)`` value (engine/base.py:180-193), in one launch.  Greedy takes the

@@ -422,6 +422,22 @@ int kvs_lse_gather_backward(const void* logits, int64_t ld, int32_t n_rows, int3
                             const void* lse, const void* grad, double temperature, int32_t dtype, void* dlogits,
                             int64_t ld_out, int32_t out_dtype, kvs_stream_t stream);
 
+/* The same log-prob and log-sum-exp straight from the lm_head's inputs, the logits never
+ * stored (training/logprobs.py:17-20 with model.py:110-114's lm_head): h [n_rows][ld_h] and
+ * the lm_head weight w [vocab][ld_w], both bf16, give x = h w^T (float32 accumulation) and
+ * logp[r] = x[r][t_r]/T - lse[r], lse[r] = log sum_v exp(x[r][v]/T), float32.  One tensor-core
+ * GEMM (pairs of CTAs, M = 256 per MMA) reduces every 256-wide vocab tile of a row in its
+ * epilogue; a second kernel merges the tiles.  Needs hidden % 64 == 0, ld_h and ld_w multiples
+ * of 8, 16-byte aligned h and w (KVS_E_UNSUPPORTED otherwise), and scratch of
+ * kvs_lm_head_logprobs_scratch_bytes(n_rows, vocab) bytes.  A target outside [0, vocab), or a
+ * bounded wait inside the GEMM kernel that ran out, gives NaN.  kvs_lm_head_logprobs_supported
+ * says whether this device can run it (0: use a GEMM and kvs_lse_gather). */
+size_t kvs_lm_head_logprobs_scratch_bytes(int32_t n_rows, int32_t vocab);
+int kvs_lm_head_logprobs_supported(int32_t hidden);
+int kvs_lm_head_logprobs(const void* h, int64_t ld_h, const void* w, int64_t ld_w, int32_t n_rows, int32_t vocab,
+                         int32_t hidden, const int64_t* targets, double temperature, float* logp, float* lse,
+                         void* scratch, size_t scratch_bytes, kvs_stream_t stream);
+
 /* The rollout's next-token step (engine/base.py:180-193: log_softmax(logits / T), then
  * multinomial or argmax, and the token's log-prob) for a batch of logits rows [n_rows][ld]
  * (KVS_F32 or KVS_F64) in one pass over each row.  greedy != 0: tokens[r] = the row's argmax
