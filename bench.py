@@ -650,7 +650,9 @@ def flat_secondary(d: dict) -> dict:
     put("compact1_cpu_ref_ms", "cpu", "compaction_bs1", "ms_per_256_streams")
     put("round_host_ms", "compaction_policy", "host_policy_ms_per_round")
     put("round_dev_ms", "compaction_policy", "device_policy_gpu_ms_per_round")
-    put("lmhead_fused_ms", "lm_head_logprobs", "fused_fwd_ms")
+    put("lmhead_epilogue_ms", "lm_head_logprobs", "epilogue_kernel_ms")
+    put("lmhead_epilogue_tc", "lm_head_logprobs", "epilogue_kernel_tc_frac")
+    put("lmhead_gemm_lse_ms", "lm_head_logprobs", "fused_fwd_ms")
     put("lmhead_torch_ms", "lm_head_logprobs", "torch_fwd_ms")
     put("sample_ms", "lm_head_logprobs", "sampling", "kvs_sample_kernel_ms")
     put("rollout_prefill_tok_s", "rollout", "prefill_tok_s_per_gpu")
@@ -808,7 +810,9 @@ def lm_head_logprobs_bench(dev, args, rank: int) -> dict:
     fused chunk (GEMM + kvs_lse_gather; backward recomputes the logits, kvs_lse_gather_backward,
     two GEMMs).  The torch forward + backward uses bf16 logits cast to float32 (the float32-result
     GEMM has no autograd derivative).  The kvs_lse_gather kernel alone against the measured HBM bandwidth: it reads
-    each float32 logit once (algorithmic bytes = rows x vocab x 4 + 16 B per row)."""
+    each float32 logit once (algorithmic bytes = rows x vocab x 4 + 16 B per row).  And the lm_head GEMM with
+    the log-sum-exp in its epilogue (kvs_lm_head_logprobs, 2 x rows x vocab x d FLOP) against the
+    measured bf16 peak; the fused forward + backward takes it for its forward."""
     import torch
 
     from kvstreams import ops
@@ -874,6 +878,14 @@ def lm_head_logprobs_bench(dev, args, rank: int) -> dict:
            "lse_gather_kernel_ms": k_ms, "lse_gather_gbs": gbs, "lse_gather_hbm_frac": gbs / peaks["hbm_gbs"],
            "peak_src": peaks["src"]}
     del logits
+    # the GEMM with the log-sum-exp in its epilogue (the logits never stored)
+    if ops.lm_head_logprobs_supported(h, w):
+        e_ms = ev_time(lambda: ops.lm_head_logprobs(h, w, tgt, temp))
+        tf = 2.0 * n * V * d / (e_ms * 1e-3) / 1e12
+        out.update({"epilogue_kernel_ms": e_ms, "epilogue_kernel_tflops": tf,
+                    "epilogue_kernel_tc_frac": tf / peaks["bf16_tflops"],
+                    "epilogue_kernel_max_abs_diff": float((ops.lm_head_logprobs(h, w, tgt, temp)[0]
+                                                           - fused_fwd()).abs().max())})
     torch.cuda.empty_cache()
     torch.cuda.reset_peak_memory_stats(dev)
     out["torch_fwd_bwd_ms"] = ev_time(torch_fb, reps=2)

@@ -189,7 +189,7 @@ lmhead_lse_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constan
         for (int j = 0; j < 32; ++j) {
           const float x = __uint_as_float(v[j]);
           if (j < cv) cm = fmaxf(cm, x);
-          if (c * 32 + j == tcol) {
+          if (j < cv && c * 32 + j == tcol) {  // a target past the vocabulary stays NaN
             tv = x;
             found = true;
           }

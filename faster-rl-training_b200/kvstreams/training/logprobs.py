@@ -14,18 +14,22 @@ _CHUNK_TOKENS = 8192
 class _LmHeadLogprob(torch.autograd.Function):
     """One chunk of lm_head -> log_softmax(logits / T) -> gather (logprobs.py:17-20).
 
-    Forward: the lm_head GEMM (cuBLAS; float32 result for half-precision models), then one
-    pass over each logits row (``kvs_lse_gather``).  Only the hidden states and each row's
-    log-sum-exp are kept; backward recomputes the chunk's logits, turns them into
-    dlogits = g (onehot - softmax) / T in place (``kvs_lse_gather_backward``, in the weight's
-    dtype) and runs the two GEMMs of dh and dW."""
+    Forward: for a bf16 lm_head, one tensor-core GEMM whose epilogue reduces each 256-wide
+    vocab tile of every row (``kvs_lm_head_logprobs``: the logits are never stored); otherwise
+    the lm_head GEMM (cuBLAS) and one pass over each logits row (``kvs_lse_gather``).  Only the
+    hidden states and each row's log-sum-exp are kept; backward recomputes the chunk's logits,
+    turns them into dlogits = g (onehot - softmax) / T in place (``kvs_lse_gather_backward``,
+    in the weight's dtype) and runs the two GEMMs of dh and dW."""
 
     @staticmethod
     def forward(ctx, h, weight, targets, temperature, model):
-        logits = model.logits(h)
-        if logits.dtype in (torch.bfloat16, torch.float16):
-            logits = logits.float()
-        logp, lse = ops.lse_gather(logits, targets, temperature)
+        if ops.lm_head_logprobs_supported(h, weight):
+            logp, lse = ops.lm_head_logprobs(h, weight, targets, temperature)
+        else:
+            logits = model.logits(h)
+            if logits.dtype in (torch.bfloat16, torch.float16):
+                logits = logits.float()
+            logp, lse = ops.lse_gather(logits, targets, temperature)
         ctx.save_for_backward(h, weight, targets, lse)
         ctx.temperature, ctx.model = temperature, model
         return logp
