@@ -968,6 +968,32 @@ def config1_bench(dev, args, rank: int) -> dict:
     return out
 
 
+def lmhead_bench(dev, args, rank: int) -> dict:
+    """The lm_head GEMM with the log-sum-exp epilogue alone: ``--lmhead-rows`` rows x d 4096 x
+    vocab 128256 (bf16), CUDA events around kvs_lm_head_logprobs (2 x rows x vocab x d FLOP)."""
+    import torch
+
+    from kvstreams import ops
+
+    n, d, V = args.lmhead_rows, 4096, 128256
+    g = torch.Generator(device=dev).manual_seed(rank)
+    w = (torch.randn(V, d, generator=g, device=dev) * 0.02).bfloat16()
+    h = torch.randn(n, d, generator=g, device=dev).bfloat16()
+    tgt = torch.randint(0, V, (n,), generator=g, device=dev)
+    ts = []
+    for i in range(args.warmup + args.steps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        ops.lm_head_logprobs(h, w, tgt, 1.0)
+        b.record()
+        torch.cuda.synchronize(dev)
+        if i >= args.warmup:
+            ts.append(a.elapsed_time(b))
+    ms = statistics.median(ts)
+    tf = 2.0 * n * V * d / (ms * 1e-3) / 1e12
+    return {"rows": n, "ms": ms, "tflops": tf, "tc_frac": tf / _peaks()["bf16_tflops"]}
+
+
 def rollout_bench(dev, args, rank: int, world: int = 1) -> dict:
     """Config 5 on one GPU: batched KV-streams rollouts of the Llama-3-8B architecture
     (random init, bf16; 32 layers, d 4096, 32/8 heads, FFN 14336, vocab 128256), 64 rollouts
@@ -1383,6 +1409,8 @@ def main() -> int:
     ap.add_argument("--prefill-streams", type=int, default=64)
     ap.add_argument("--prefill-only", action="store_true", help="only the paged prefill measurement")
     ap.add_argument("--decode-bs1-only", action="store_true", help="only the one-token-block decode measurement")
+    ap.add_argument("--lmhead-only", action="store_true", help="only the lm_head log-sum-exp GEMM")
+    ap.add_argument("--lmhead-rows", type=int, default=8192)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -1435,6 +1463,11 @@ def main() -> int:
             r = replay_backward_bench(torch.device("cuda", local_rank), args, rank)
             if rank == 0:
                 print(json.dumps({"replay_backward": r}), flush=True)
+        elif args.lmhead_only:
+            torch.cuda.set_device(local_rank)
+            r = lmhead_bench(torch.device("cuda", local_rank), args, rank)
+            if rank == 0:
+                print(json.dumps({"lmhead": r}), flush=True)
         elif args.decode_bs1_only:
             torch.cuda.set_device(local_rank)
             r = decode_bs1_bench(torch.device("cuda", local_rank), args, rank)
