@@ -1256,10 +1256,11 @@ replay_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
 #pragma unroll
         for (int e = 0; e < GCOLS; e += 4) {
           const float4 n4 = *reinterpret_cast<const float4*>(nl + e);
-          pf[e] = ex2_approx(fmaf(__uint_as_float(sv[e]), sl2, n4.x));
-          pf[e + 1] = ex2_approx(fmaf(__uint_as_float(sv[e + 1]), sl2, n4.y));
-          pf[e + 2] = ex2_approx(fmaf(__uint_as_float(sv[e + 2]), sl2, n4.z));
-          pf[e + 3] = ex2_approx(fmaf(__uint_as_float(sv[e + 3]), sl2, n4.w));
+          float x[4];
+          ffma2v(x[0], x[1], __uint_as_float(sv[e]), __uint_as_float(sv[e + 1]), sl2, n4.x, n4.y);
+          ffma2v(x[2], x[3], __uint_as_float(sv[e + 2]), __uint_as_float(sv[e + 3]), sl2, n4.z, n4.w);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) pf[e + u] = ex2_approx(x[u]);
         }
         if (!full) {
 #pragma unroll
@@ -1297,8 +1298,9 @@ replay_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
 #pragma unroll
         for (int e = 0; e < GCOLS; e += 4) {
           const float4 n4 = *reinterpret_cast<const float4*>(nd + e);
-          float d[4] = {pf[e] * (__uint_as_float(dp[e]) + n4.x), pf[e + 1] * (__uint_as_float(dp[e + 1]) + n4.y),
-                        pf[e + 2] * (__uint_as_float(dp[e + 2]) + n4.z), pf[e + 3] * (__uint_as_float(dp[e + 3]) + n4.w)};
+          float d[4];
+          addmul2(d[0], d[1], __uint_as_float(dp[e]), __uint_as_float(dp[e + 1]), n4.x, n4.y, pf[e], pf[e + 1]);
+          addmul2(d[2], d[3], __uint_as_float(dp[e + 2]), __uint_as_float(dp[e + 3]), n4.z, n4.w, pf[e + 2], pf[e + 3]);
           if (!full) {  // D past the stream is not defined: select, do not multiply
 #pragma unroll
             for (int u = 0; u < 4; ++u) d[u] = (e + u >= lo && e + u < hi) ? d[u] : 0.f;
@@ -1363,8 +1365,10 @@ constexpr int OFFQ_SLOT = 2 * TILE_BYTES;            // 4 slots: K and V tiles o
 constexpr int OFFQ_E = OFFQ_SLOT + 4 * TILE_BYTES;   // 4 slots of 128 int32, loaded with K
 constexpr int OFFQ_LIST = OFFQ_E + 4 * E_BYTES;
 constexpr int OFFQ_BAR = OFFQ_LIST + MAX_KT * 2;
-// Q_SREAD: every softmax warp has S of the step in registers (S may be overwritten)
-enum { Q_QFULL = 0, Q_FULL0, Q_EMPTY0 = Q_FULL0 + 4, Q_SFULL = Q_EMPTY0 + 4, Q_DPFULL, Q_SREAD, Q_DSFULL, Q_FINAL, NBARQ };
+// Q_SREAD: every softmax warp has S of the step in registers (S may be overwritten);
+// Q_AFULL: the softmax warps have copied Q and dO into TMEM (the A operands of S and dP)
+enum { Q_QFULL = 0, Q_FULL0, Q_EMPTY0 = Q_FULL0 + 4, Q_SFULL = Q_EMPTY0 + 4, Q_DPFULL, Q_SREAD, Q_DSFULL, Q_AFULL,
+       Q_FINAL, NBARQ };
 constexpr int OFFQ_MISC = OFFQ_BAR + NBARQ * 8;
 constexpr int SMEMQ_BYTES = OFFQ_MISC + 64 + 33 * 4;
 static_assert(SMEMQ_BYTES <= 232448, "dQ kernel shared memory");
@@ -1404,6 +1408,7 @@ replay_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     for (int i = 0; i < NBARQ; ++i) mbar_init(&bar[i], 1);
     mbar_init(&bar[Q_SREAD], 4 * NGRP);
     mbar_init(&bar[Q_DSFULL], 4 * NGRP);
+    mbar_init(&bar[Q_AFULL], 4 * NGRP);
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -1436,7 +1441,9 @@ replay_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   tc_fence_after();
   const int n = *s_n;
   const uint32_t tmem = *tmem_slot;
-  // TMEM: S [0,128), dP [128,256), dQ [256,384), dS bf16 [384,448) (group g over [384+16g, +16))
+  // TMEM: S [0,128), dP [128,256) (dS bf16 of group g over [128+32g, +16) once dP is read),
+  // dQ [256,384), Q [384,448) and dO [448,512) as bf16 A operands.  Q and dO are the same for
+  // every step, so S = Q K^T and dP = dO V^T read only K and V from shared memory.
 
   if (warp == 0) {
     if (lane == 0) {
@@ -1492,28 +1499,26 @@ replay_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     // ---------------------------------------------------------- UMMA issuer (whole warp)
     // per step k: S(k+1) once S(k) is read; dQ += dS(k) K(k); dP(k+1).  K(k) is released by
     // dQ(k), V(k) by dP(k): K(k+2) takes V(k)'s slot and V(k+2) K(k)'s.
-    constexpr uint32_t ID_K = idesc_bf16(128, 128, 0);   // S, dP: both operands K-major
+    constexpr uint32_t ID_K = idesc_bf16(128, 128, 0);   // S, dP: A from TMEM, B K-major
     constexpr uint32_t ID_MN = idesc_bf16(128, 128, 1);  // dQ: B (K) MN-major
-    const uint64_t dq_ = desc_kmajor_sw128(smem_addr(smem + OFFQ_Q));
-    const uint64_t ddo_ = desc_kmajor_sw128(smem_addr(smem + OFFQ_DO));
     auto wait = [&](uint64_t* bb, int parity) {
       return __all_sync(0xffffffffu, mbar_wait_fast(bb, parity, abort_flag));
     };
-    auto issue_s = [&](int sl) {  // S = Q K^T into [0,128)
+    auto issue_s = [&](int sl) {  // S = Q K^T into [0,128), Q from TMEM [384,448)
       const uint64_t dk_k = desc_kmajor_sw128(smem_addr(smem + OFFQ_SLOT + sl * TILE_BYTES));
-      const uint32_t d = tmem;
-#define KVS_S(kk) umma_bf16_warp_at<kq_step(kk), kq_step(kk)>(d, dq_, dk_k, ID_K, kk > 0)
+      const uint32_t d = tmem, a = tmem + 384;
+#define KVS_S(kk) umma_bf16_tmem_a_warp_at<kk * 8, kq_step(kk)>(d, a, dk_k, ID_K, kk > 0)
       KVS_S(0); KVS_S(1); KVS_S(2); KVS_S(3); KVS_S(4); KVS_S(5); KVS_S(6); KVS_S(7);
 #undef KVS_S
     };
-    auto issue_dp = [&](int sl) {  // dP = dO V^T into [128,256)
+    auto issue_dp = [&](int sl) {  // dP = dO V^T into [128,256), dO from TMEM [448,512)
       const uint64_t dv_k = desc_kmajor_sw128(smem_addr(smem + OFFQ_SLOT + sl * TILE_BYTES));
-      const uint32_t d = tmem + 128;
-#define KVS_DP(kk) umma_bf16_warp_at<kq_step(kk), kq_step(kk)>(d, ddo_, dv_k, ID_K, kk > 0)
+      const uint32_t d = tmem + 128, a = tmem + 448;
+#define KVS_DP(kk) umma_bf16_tmem_a_warp_at<kk * 8, kq_step(kk)>(d, a, dv_k, ID_K, kk > 0)
       KVS_DP(0); KVS_DP(1); KVS_DP(2); KVS_DP(3); KVS_DP(4); KVS_DP(5); KVS_DP(6); KVS_DP(7);
 #undef KVS_DP
     };
-    bool ok = wait(&bar[Q_QFULL], 0);
+    bool ok = wait(&bar[Q_AFULL], 0);
     if (ok) ok = wait(&bar[Q_FULL0 + slot_a(0)], 0);
     if (ok) {
       tc_fence_after();
@@ -1544,9 +1549,9 @@ replay_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       {
         const uint64_t dk_mn =
             desc_mnmajor_sw128(smem_addr(smem + OFFQ_SLOT + slot_a(k) * TILE_BYTES), HALF_BYTES);
-        const uint32_t d = tmem + 256, a = tmem + 384;
+        const uint32_t d = tmem + 256, a = tmem + 128;
         const uint32_t acc = k > 0;
-#define KVS_DQ(kk) umma_bf16_tmem_a_warp_at<kk * 8, mn_step(kk)>(d, a, dk_mn, ID_MN, (kk > 0) || acc)
+#define KVS_DQ(kk) umma_bf16_tmem_a_warp_at<split_col(kk), mn_step(kk)>(d, a, dk_mn, ID_MN, (kk > 0) || acc)
         KVS_DQ(0); KVS_DQ(1); KVS_DQ(2); KVS_DQ(3); KVS_DQ(4); KVS_DQ(5); KVS_DQ(6); KVS_DQ(7);
 #undef KVS_DQ
       }
@@ -1580,8 +1585,30 @@ replay_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     const int64_t vrow = ((int64_t)b * p.Hq + h) * p.T_pad + t;
     const float nlse = t < p.T ? p.nlse[vrow] : 0.f;
     const float nd = t < p.T ? p.nd[vrow] : 0.f;
-    bool ok = true;
-    for (int k = 0; k < n; ++k) {
+    // Q and dO of row r into TMEM: dims [32 grp, +32) of each, 16-byte chunks of the 128-byte
+    // swizzled row, as 16 columns of bf16 pairs at 384 + 16 grp and 448 + 16 grp
+    bool ok = __all_sync(0xffffffffu, mbar_wait(&bar[Q_QFULL], 0, abort_flag));
+    if (ok) {
+      const int c0 = (grp & 1) * 4, sw = r & 7;
+#pragma unroll
+      for (int which = 0; which < 2; ++which) {
+        const uint8_t* row = smem + (which ? OFFQ_DO : OFFQ_Q) + (grp >> 1) * HALF_BYTES + r * 128;
+        uint32_t w[16];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const uint4 x = *reinterpret_cast<const uint4*>(row + (((c0 + c) ^ sw) << 4));
+          w[4 * c] = x.x;
+          w[4 * c + 1] = x.y;
+          w[4 * c + 2] = x.z;
+          w[4 * c + 3] = x.w;
+        }
+        tmem_st16(tl + 384 + 64 * which + 16 * grp, w);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      warp_arrive(&bar[Q_AFULL]);
+    }
+    for (int k = 0; ok && k < n; ++k) {
       const int j = list[k] & 0x7fff;
       const bool masked = (list[k] >> 15) & 1;
       ok = mbar_wait_fast(&bar[Q_SFULL], k & 1, abort_flag);
@@ -1598,7 +1625,12 @@ replay_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         tc_fence_before();
         warp_arrive(&bar[Q_SREAD]);
 #pragma unroll
-        for (int e = 0; e < GCOLS; ++e) pf[e] = ex2_approx(fmaf(__uint_as_float(sv[e]), sl2, nlse));
+        for (int e = 0; e < GCOLS; e += 2) {
+          float x0, x1;
+          ffma2(x0, x1, __uint_as_float(sv[e]), __uint_as_float(sv[e + 1]), sl2, nlse);
+          pf[e] = ex2_approx(x0);
+          pf[e + 1] = ex2_approx(x1);
+        }
       }
       // visibility bits of this thread's 32 keys (all set for an unmasked tile)
       uint32_t bits = 0xffffffffu;
@@ -1632,7 +1664,8 @@ replay_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         tmem_wait_ld();
 #pragma unroll
         for (int e = 0; e < GCOLS; e += 2) {
-          float d0 = pf[e] * (__uint_as_float(dp[e]) + nd), d1 = pf[e + 1] * (__uint_as_float(dp[e + 1]) + nd);
+          float d0, d1;
+          addmul2(d0, d1, __uint_as_float(dp[e]), __uint_as_float(dp[e + 1]), nd, nd, pf[e], pf[e + 1]);
           if (masked) {
             d0 = ((bits >> e) & 1) ? d0 : 0.f;
             d1 = ((bits >> (e + 1)) & 1) ? d1 : 0.f;
@@ -1640,7 +1673,7 @@ replay_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
           dk[e >> 1] = pack2(d0, d1);
         }
       }
-      tmem_st16(tl + 384 + (GCOLS / 2) * grp, dk);
+      tmem_st16(tl + 128 + cb, dk);
       tmem_wait_st();
       tc_fence_before();
       warp_arrive(&bar[Q_DSFULL]);

@@ -114,6 +114,31 @@ __device__ __forceinline__ void fadd2(float& s0, float& s1, float a0, float a1) 
       : "f"(a0), "f"(a1));
 }
 
+// (d0, d1) = (a0, a1) * b + (c0, c1)
+__device__ __forceinline__ void ffma2v(float& d0, float& d1, float a0, float a1, float b, float c0, float c1) {
+  asm("{\n.reg .b64 a, b, c, d;\n"
+      "mov.b64 a, {%2, %3};\n"
+      "mov.b64 b, {%4, %4};\n"
+      "mov.b64 c, {%5, %6};\n"
+      "fma.rn.f32x2 d, a, b, c;\n"
+      "mov.b64 {%0, %1}, d;\n}\n"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b), "f"(c0), "f"(c1));
+}
+// (d0, d1) = ((a0, a1) + (b0, b1)) * (c0, c1), each step rounded as in scalar code
+__device__ __forceinline__ void addmul2(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0,
+                                        float c1) {
+  asm("{\n.reg .b64 a, b, c, d;\n"
+      "mov.b64 a, {%2, %3};\n"
+      "mov.b64 b, {%4, %5};\n"
+      "mov.b64 c, {%6, %7};\n"
+      "add.rn.f32x2 d, a, b;\n"
+      "mul.rn.f32x2 d, d, c;\n"
+      "mov.b64 {%0, %1}, d;\n}\n"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+
 // max of three (sm_100 three-input form)
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;
@@ -289,7 +314,9 @@ __device__ __forceinline__ uint32_t mapa_shared(const void* p, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(r) : "r"(smem_addr(p)), "r"(rank));
   return r;
 }
-// arrive on a barrier given by its shared::cluster address (possibly the peer CTA's)
+// arrive on a barrier given by its shared::cluster address (possibly the peer CTA's).  The
+// arrivals order tcgen05 work (after tcgen05.fence::before_thread_sync), not memory writes, so
+// the default release scope is used: a cluster-scope release costs about a thousand cycles.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster_addr) {
   asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];\n" ::"r"(bar_cluster_addr) : "memory");
 }
