@@ -222,6 +222,59 @@ def decode_bs1_bench(dev, args, rank: int) -> dict:
             "decode_tok_s": S / (ms * 1e-3), "fused_kernel": path == [1]}
 
 
+def decode_short_bench(dev, args, rank: int) -> dict:
+    """The paged decode at rollout contexts: 64 streams of ~U[300, 500] live tokens (16-token
+    blocks, 1-6 evicted spans), 32 layers per step sharing one batch descriptor, as one
+    decode iteration of the rollout engine issues them; CUDA events around each step's 32
+    kvs_paged_decode calls.  Per-launch fixed costs (batch scan, table gather, first blocks in
+    flight, combine) weigh here, where each layer streams only ~105 MB."""
+    import torch
+
+    from kvstreams import ops
+    from kvstreams.paged_cache import PagedKVCache
+    from kvstreams.rope import RotaryEmbedding
+    from kvstreams.workloads import decode_state
+
+    layers, ctx, nb = 32, (300, 500), 4096
+    st = decode_state(num_streams=S, ctx_range=ctx, block_size=BS, num_blocks=nb, seed=7)
+    cache = PagedKVCache(layers, HKV, D, block_size=BS, num_blocks=nb, dtype=torch.bfloat16, device=dev,
+                         max_seqs=S, max_blocks_per_seq=64)
+    cache.load_state(range(S), st.tables, st.positions, st.free_list)
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    for t in (cache.k, cache.v):
+        t.view(-1)[:] = torch.randn(t.numel(), generator=g, device=dev, dtype=torch.float32).bfloat16()
+    q = torch.randn(S, HQ, D, generator=g, device=dev).bfloat16()
+    k = torch.randn(S, HKV, D, generator=g, device=dev).bfloat16()
+    v = torch.randn(S, HKV, D, generator=g, device=dev).bfloat16()
+    inv = RotaryEmbedding(D, THETA).table(dev, torch.bfloat16)
+    seqs = list(range(S))
+    pos = torch.as_tensor(st.next_positions, device=dev)
+    out = torch.empty_like(q)
+    batch = cache._batch(seqs)
+    steps, warm = 8, 3
+    times = []
+    for i in range(warm + steps):
+        p = pos + i
+        mapping = cache.append_slots_batch(seqs, p)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for layer in range(layers):
+            ops.paged_forward(cache, seqs, None, layer, q, k, v, p, mapping, inv, D ** -0.5, out=out, batch=batch)
+        b.record()
+        if i >= warm:
+            times.append((a, b))
+    torch.cuda.synchronize(dev)
+    ms = statistics.mean(x.elapsed_time(y) for x, y in times) / layers
+    alg = decode_bytes(st.lengths + warm + steps // 2 + 1)
+    gbs = alg / (ms * 1e-3) / 1e9
+    peaks = _peaks()
+    del cache, q, k, v, out
+    torch.cuda.empty_cache()
+    return {"workload": f"{S} streams, ctx U[{ctx[0]},{ctx[1]}] (mean {st.lengths.mean():.0f}), {layers} layers per "
+                        "step, bs16", "us_per_layer": ms * 1e3, "gbs": gbs, "hbm_frac": gbs / peaks["hbm_gbs"],
+            "kv_bytes_per_layer": int(alg), "ideal_us": alg / (peaks["hbm_gbs"] * 1e9) * 1e6}
+
+
 # ---------------------------------------------------------------------- cpu baseline
 CPU_STREAMS = 4  # decode streams of the 64-stream workload per CPU step
 
@@ -1415,6 +1468,8 @@ def main() -> int:
     ap.add_argument("--prefill-streams", type=int, default=64)
     ap.add_argument("--prefill-only", action="store_true", help="only the paged prefill measurement")
     ap.add_argument("--decode-bs1-only", action="store_true", help="only the one-token-block decode measurement")
+    ap.add_argument("--decode-short-only", action="store_true",
+                    help="only the paged decode at rollout contexts (~400 tokens, 32 layers per step)")
     ap.add_argument("--lmhead-only", action="store_true", help="only the lm_head log-sum-exp GEMM")
     ap.add_argument("--lmhead-rows", type=int, default=8192)
     args = ap.parse_args()
@@ -1474,6 +1529,11 @@ def main() -> int:
             r = lmhead_bench(torch.device("cuda", local_rank), args, rank)
             if rank == 0:
                 print(json.dumps({"lmhead": r}), flush=True)
+        elif args.decode_short_only:
+            torch.cuda.set_device(local_rank)
+            r = decode_short_bench(torch.device("cuda", local_rank), args, rank)
+            if rank == 0:
+                print(json.dumps({"decode_short": r}), flush=True)
         elif args.decode_bs1_only:
             torch.cuda.set_device(local_rank)
             r = decode_bs1_bench(torch.device("cuda", local_rank), args, rank)
