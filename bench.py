@@ -252,27 +252,36 @@ def decode_short_bench(dev, args, rank: int) -> dict:
     out = torch.empty_like(q)
     batch = cache._batch(seqs)
     steps, warm = 8, 3
-    times = []
-    for i in range(warm + steps):
-        p = pos + i
-        mapping = cache.append_slots_batch(seqs, p)
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        for layer in range(layers):
-            ops.paged_forward(cache, seqs, None, layer, q, k, v, p, mapping, inv, D ** -0.5, out=out, batch=batch)
-        b.record()
-        if i >= warm:
-            times.append((a, b))
-    torch.cuda.synchronize(dev)
-    ms = statistics.mean(x.elapsed_time(y) for x, y in times) / layers
-    alg = decode_bytes(st.lengths + warm + steps // 2 + 1)
+    from kvstreams import _native as N
+
+    def run(step0: int, planned: bool) -> float:
+        times = []
+        for i in range(warm + steps):
+            p = pos + step0 + i
+            mapping = cache.append_slots_batch(seqs, p)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for layer in range(layers):
+                plan = (N.PLAN_BUILD if layer == 0 else N.PLAN_REUSE) if planned else N.PLAN_NONE
+                ops.paged_forward(cache, seqs, None, layer, q, k, v, p, mapping, inv, D ** -0.5, out=out, batch=batch,
+                                  plan=plan)
+            b.record()
+            if i >= warm:
+                times.append((a, b))
+        torch.cuda.synchronize(dev)
+        return statistics.mean(x.elapsed_time(y) for x, y in times) / layers
+
+    ms_noplan = run(0, False)
+    ms = run(warm + steps, True)  # as the engine runs a step: the first layer stores the plan
+    alg = decode_bytes(st.lengths + 2 * (warm + steps) - steps // 2)
     gbs = alg / (ms * 1e-3) / 1e9
     peaks = _peaks()
     del cache, q, k, v, out
     torch.cuda.empty_cache()
     return {"workload": f"{S} streams, ctx U[{ctx[0]},{ctx[1]}] (mean {st.lengths.mean():.0f}), {layers} layers per "
                         "step, bs16", "us_per_layer": ms * 1e3, "gbs": gbs, "hbm_frac": gbs / peaks["hbm_gbs"],
-            "kv_bytes_per_layer": int(alg), "ideal_us": alg / (peaks["hbm_gbs"] * 1e9) * 1e6}
+            "us_per_layer_without_plan": ms_noplan * 1e3, "kv_bytes_per_layer": int(alg),
+            "ideal_us": alg / (peaks["hbm_gbs"] * 1e9) * 1e6}
 
 
 # ---------------------------------------------------------------------- cpu baseline

@@ -65,7 +65,9 @@ constexpr int SMEM_Q = HQ * D * 2;
 constexpr int SMEM_NEW = 2 * HKV * D * 2;
 constexpr int SMEM_PREF = (MAX_SEQS + 1) * 4;
 constexpr int SMEM_TAB = TAB_CAP * 4;
-constexpr int SEQ_COST = 2;  // a stream's start + finish, in blocks of streaming time (work split)
+constexpr int SEQ_COST = 4;  // a stream's start + finish + merge, in blocks of streaming time (work split)
+constexpr int PLAN_HDR = 16;  // ints of the batch plan's header (16-token blocks)
+constexpr int PLAN_MAGIC = 0x6B76706C;  // header word 2 of a stored plan
 constexpr int SMEM_TOTAL = SMEM_STAGES + SMEM_Q + SMEM_NEW + SMEM_PREF + SMEM_TAB + 256;
 static_assert(HQ * 8 == NTHREADS, "start(): one thread per (query head, 16-byte chunk)");
 
@@ -86,6 +88,8 @@ struct DecodeParams {
   float* part_o;               // [slots][HQ][D]
   float* part_ml;              // [slots][HQ][2]
   int32_t* counters;           // [S]
+  int32_t* plan;               // the step's batch plan (16-token blocks), or null
+  int plan_mode;               // KVS_PLAN_*
   float scale_log2;            // D^-0.5 * log2(e)
 };
 
@@ -154,11 +158,14 @@ __device__ __forceinline__ float warp_sum_rows(float v) {
 }
 
 // the global inputs of one sequence's start: its q chunk, new k / v chunks, inv_freq slice,
-// logical position and append row (owner = this CTA holds the sequence's last block)
+// logical position and append slot (owner = this CTA holds the sequence's last block).  Kept
+// as loaded: nothing is computed from them until the sequence starts, so issuing the loads
+// never waits for them.
 struct SeqIn {
   uint4 q_lo, q_hi, k_lo, k_hi, v_c;
   float4 f_lo, f_hi;
-  int64_t pos, row;
+  int64_t pos;
+  int32_t blk, off;
   bool owner;
 };
 
@@ -182,9 +189,40 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
   const kvs_cache& c = p.c;
   const int S = p.num_seqs;
 
+  // The batch plan of a decode step (16-token blocks): per-sequence prefix sums of the
+  // groups, each CTA's group range and the block ids of every group, the same for all layers
+  // of the step.  A launch in KVS_PLAN_BUILD mode computes them as below and stores them; one
+  // in KVS_PLAN_REUSE mode reads them back in two rounds of independent loads instead of the
+  // scan's and the table gather's dependent ones (it computes them if the stored plan is for
+  // another batch size or grid).
+  int32_t* const plan_pref = p.plan ? p.plan + PLAN_HDR : nullptr;
+  int32_t* const plan_range = p.plan ? plan_pref + S + 1 : nullptr;
+  int32_t* const plan_tab = p.plan ? plan_range + 2 * gridDim.x : nullptr;
+  const bool build = BSZ == BS && p.plan && p.plan_mode == KVS_PLAN_BUILD;
+  bool reuse = false;
+  int pg0 = 0, pg1 = 0;
+  if (BSZ == BS && p.plan && p.plan_mode == KVS_PLAN_REUSE) {
+    const int hs = p.plan[0], hg = p.plan[1], hm = p.plan[2];
+    pg0 = plan_range[2 * blockIdx.x];
+    pg1 = plan_range[2 * blockIdx.x + 1];
+    int pv[5];
+#pragma unroll
+    for (int k = 0; k < 5; ++k) {
+      const int i = tid + k * NTHREADS;
+      pv[k] = i <= S ? plan_pref[i] : 0;
+    }
+    reuse = hs == S && hg == (int)gridDim.x && hm == PLAN_MAGIC;  // the same loads in every thread
+    if (reuse) {
+#pragma unroll
+      for (int k = 0; k < 5; ++k) {
+        const int i = tid + k * NTHREADS;
+        if (i <= S) s_pref[i] = pv[k];
+      }
+    }
+  }
   // prefix sums of table lengths (blocks) over the batch: thread tid owns sequences
   // 4*tid .. 4*tid+3 (MAX_SEQS = 4 * NTHREADS), one block-wide scan
-  {
+  if (!reuse) {
     int nb[4], sum = 0;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
@@ -204,8 +242,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
   }
   __syncthreads();
   // Cost units: every block is one, and every stream adds SEQ_COST in front of its first block
-  // (the start and finish work of a stream, ~2 blocks of streaming time), so a CTA that carries
-  // a stream boundary gets fewer blocks.  Global block gb of stream i sits at unit
+  // (the start, finish and merge work of a stream, a few blocks of streaming time), so a CTA
+  // that carries a stream boundary gets fewer blocks.  Global block gb of stream i sits at unit
   // gb + SEQ_COST (i + 1); CTA c takes the units [c RU, (c + 1) RU).
   const int total = s_pref[S];
   const int total_units = total + SEQ_COST * S;
@@ -220,8 +258,22 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
     const int j = u - (s_pref[lo] + SEQ_COST * (lo + 1));
     return j <= 0 ? s_pref[lo] : min(s_pref[lo] + j, s_pref[lo + 1]);
   };
-  const int g0 = first_block(blockIdx.x * RU);
-  const int g1 = first_block(blockIdx.x * RU + RU);
+  const int g0 = reuse ? pg0 : first_block(blockIdx.x * RU);
+  const int g1 = reuse ? pg1 : first_block(blockIdx.x * RU + RU);
+  if (build) {
+    if (tid == 0) {
+      plan_range[2 * blockIdx.x] = g0;
+      plan_range[2 * blockIdx.x + 1] = g1;
+    }
+    if (blockIdx.x == 0) {
+      for (int i = tid; i <= S; i += NTHREADS) plan_pref[i] = s_pref[i];
+      if (tid == 0) {
+        p.plan[0] = S;
+        p.plan[1] = gridDim.x;
+        p.plan[2] = PLAN_MAGIC;
+      }
+    }
+  }
   if (g0 >= g1) return;
 
   const uint8_t* Kpool = static_cast<const uint8_t*>(c.k);
@@ -252,9 +304,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
     s.f_lo = *reinterpret_cast<const float4*>(p.inv_freq + d0);
     s.f_hi = *reinterpret_cast<const float4*>(p.inv_freq + d0 + 4);
     s.k_lo = s.k_hi = s.v_c = make_uint4(0, 0, 0, 0);
-    s.row = 0;
+    s.blk = s.off = 0;
     if (s.owner) {
-      s.row = ((layer_rows + p.slot_blocks[i]) * BSZ + p.slot_offsets[i]) * HKV;
+      s.blk = p.slot_blocks[i];
+      s.off = p.slot_offsets[i];
       if (tid < HKV * 8) {
         const uint4* ksrc = reinterpret_cast<const uint4*>(p.k_new + (int64_t)i * p.kv_stride + h * D + d0);
         s.k_lo = ksrc[0];
@@ -266,6 +319,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
   };
   // the first sequence's loads overlap the table gather and the prologue's KV copies
   const int first = seq_of(g0);
+  const int last_seq = seq_of(g1 - 1);
   const SeqIn first_in = load_seq(first);
 
   // block ids of this CTA's range, gathered once (the copies below then need no global lookups).
@@ -288,10 +342,22 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
     __syncthreads();
   } else if (tab_in_smem) {
     for (int gb = g0 + tid; gb < g1; gb += NTHREADS) {
-      const int i = seq_of(gb);
-      s_tab[gb - g0] = c.tables[(int64_t)p.seq_slots[i] * c.max_blocks + (gb - s_pref[i])];
+      int blk;
+      if (reuse) {
+        blk = plan_tab[gb];
+      } else {
+        const int i = seq_of(gb);
+        blk = c.tables[(int64_t)p.seq_slots[i] * c.max_blocks + (gb - s_pref[i])];
+        if (build) plan_tab[gb] = blk;
+      }
+      s_tab[gb - g0] = blk;
     }
     __syncthreads();
+  } else if (build) {
+    for (int gb = g0 + tid; gb < g1; gb += NTHREADS) {
+      const int i = seq_of(gb);
+      plan_tab[gb] = c.tables[(int64_t)p.seq_slots[i] * c.max_blocks + (gb - s_pref[i])];
+    }
   }
 
   auto issue = [&](int gb, int st) {
@@ -313,6 +379,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
       int64_t blk;
       if (tab_in_smem) {
         blk = s_tab[gb - g0];
+      } else if (reuse) {
+        blk = plan_tab[gb];
       } else {
         const int i = seq_of(gb);
         blk = c.tables[(int64_t)p.seq_slots[i] * c.max_blocks + (gb - s_pref[i])];
@@ -342,11 +410,23 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
   int cur = -1;
 
-  auto finish = [&](int i) {
-    // sequence i: this CTA's part is done; write it (or the final output) and merge if last
+  // CTAs [c0, c0 + expected) share sequence i (the ranges that hold one of its blocks)
+  auto seq_ctas = [&](int i, int& c0) {
     const int P0 = s_pref[i], nb = s_pref[i + 1] - P0;
-    const int c0 = (P0 + SEQ_COST * (i + 1)) / RU, c1 = (P0 + nb - 1 + SEQ_COST * (i + 1)) / RU;
-    const int expected = c1 - c0 + 1;
+    c0 = (P0 + SEQ_COST * (i + 1)) / RU;
+    return (P0 + nb - 1 + SEQ_COST * (i + 1)) / RU - c0 + 1;
+  };
+  // Streams shared with other CTAs: at most the first and the last of this CTA's range.  Each
+  // CTA writes its partial when it leaves the stream and arrives on the stream's counter; the
+  // last to arrive merges.  A stream left mid-range arrives at once but reads the counter's
+  // answer only at the end of the kernel (e_seq), the stream the range ends in arrives at the
+  // end (t_seq), so moving on to the next stream waits for no global round trip.
+  int e_seq = -1, t_seq = -1;
+  int arrived0 = 0;  // thread 0: the counter value the early arrival for e_seq returned
+  auto finish = [&](int i) {
+    // sequence i: this CTA's part is done; write the output, or this CTA's partial
+    int c0;
+    const int expected = seq_ctas(i, c0);
     const float lt0 = warp_sum_rows(l0), lt1 = warp_sum_rows(l1);
     const int hq0 = warp * G + 2 * t;  // query heads hq0, hq0+1 (valid for t < 2)
     if (expected == 1) {
@@ -383,83 +463,90 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
         ml[3] = lt1;
       }
     }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-      const int arrived = atomicAdd(&p.counters[i], 1);
-      *s_flag = (arrived == expected - 1);
-    }
-    __syncthreads();
-    if (*s_flag) {
-      __threadfence();
-      // thread -> head h = tid / 8, dims d0 = 16 (tid % 8) .. +16.  The partials are read four at
-      // a time with all their loads in flight and combined under a running maximum:
-      // out = sum_k 2^(m_k - M) o_k / sum_k 2^(m_k - M) l_k
-      const int h = tid >> 3, d0 = (tid & 7) * 16;
-      float M = -INFINITY, den = 0.f;
-      float4 o[4];
-#pragma unroll
-      for (int v = 0; v < 4; ++v) o[v] = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int k0 = 0; k0 < expected; k0 += 4) {
-        float mk[4], lk[4];
-        float4 xk[4][4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          mk[u] = -INFINITY;
-          lk[u] = 0.f;
-#pragma unroll
-          for (int v = 0; v < 4; ++v) xk[u][v] = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (k0 + u < expected) {
-            const int64_t slot = c0 + k0 + u + i;
-            const float* ml = p.part_ml + (slot * HQ + h) * 2;
-            mk[u] = __ldcg(ml);
-            lk[u] = __ldcg(ml + 1);
-            const float4* src = reinterpret_cast<const float4*>(p.part_o + (slot * HQ + h) * D + d0);
-#pragma unroll
-            for (int v = 0; v < 4; ++v) xk[u][v] = __ldcg(src + v);
-          }
-        }
-        float Mn = M;
-#pragma unroll
-        for (int u = 0; u < 4; ++u) Mn = fmaxf(Mn, mk[u]);
-        const float sc = exp2f(M - Mn);  // 0 on the first group (M = -inf)
-        den *= sc;
-#pragma unroll
-        for (int v = 0; v < 4; ++v) o[v] = make_float4(o[v].x * sc, o[v].y * sc, o[v].z * sc, o[v].w * sc);
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float w = exp2f(mk[u] - Mn);  // 0 for the slots beyond `expected`
-          den += w * lk[u];
-#pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            o[v].x += w * xk[u][v].x;
-            o[v].y += w * xk[u][v].y;
-            o[v].z += w * xk[u][v].z;
-            o[v].w += w * xk[u][v].w;
-          }
-        }
-        M = Mn;
+    if (i == last_seq) {
+      t_seq = i;
+    } else {
+      e_seq = i;
+      // a stream this CTA leaves mid-range (its first one): arrive now, with every thread's
+      // partial writes ordered before the arrival by the barrier and thread 0's fence; the
+      // value returned is only read at the end of the kernel, so nothing waits for it here
+      __syncthreads();
+      if (tid == 0) {
+        __threadfence();
+        arrived0 = atomicAdd(&p.counters[i], 1);
       }
-      const float inv = 1.f / den;
-      uint32_t packed[8];
-#pragma unroll
-      for (int v = 0; v < 4; ++v) {
-        packed[2 * v] = pack_bf16(o[v].x * inv, o[v].y * inv);
-        packed[2 * v + 1] = pack_bf16(o[v].z * inv, o[v].w * inv);
-      }
-      int4* dst = reinterpret_cast<int4*>(p.out + ((int64_t)i * HQ + h) * D + d0);
-      dst[0] = make_int4(packed[0], packed[1], packed[2], packed[3]);
-      dst[1] = make_int4(packed[4], packed[5], packed[6], packed[7]);
-      if (tid == 0) p.counters[i] = 0;  // ready for the next launch
     }
-    __syncthreads();
+  };
+  // the last CTA to arrive for sequence i combines the partials of its `expected` CTAs
+  auto merge = [&](int i) {
+    int c0;
+    const int expected = seq_ctas(i, c0);
+    // thread -> head h = tid / 8, dims d0 = 16 (tid % 8) .. +16.  The partials are read four at
+    // a time with all their loads in flight and combined under a running maximum:
+    // out = sum_k 2^(m_k - M) o_k / sum_k 2^(m_k - M) l_k
+    const int h = tid >> 3, d0 = (tid & 7) * 16;
+    float M = -INFINITY, den = 0.f;
+    float4 o[4];
+#pragma unroll
+    for (int v = 0; v < 4; ++v) o[v] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k0 = 0; k0 < expected; k0 += 4) {
+      float mk[4], lk[4];
+      float4 xk[4][4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        mk[u] = -INFINITY;
+        lk[u] = 0.f;
+#pragma unroll
+        for (int v = 0; v < 4; ++v) xk[u][v] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (k0 + u < expected) {
+          const int64_t slot = c0 + k0 + u + i;
+          const float* ml = p.part_ml + (slot * HQ + h) * 2;
+          mk[u] = __ldcg(ml);
+          lk[u] = __ldcg(ml + 1);
+          const float4* src = reinterpret_cast<const float4*>(p.part_o + (slot * HQ + h) * D + d0);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) xk[u][v] = __ldcg(src + v);
+        }
+      }
+      float Mn = M;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) Mn = fmaxf(Mn, mk[u]);
+      const float sc = exp2f(M - Mn);  // 0 on the first group (M = -inf)
+      den *= sc;
+#pragma unroll
+      for (int v = 0; v < 4; ++v) o[v] = make_float4(o[v].x * sc, o[v].y * sc, o[v].z * sc, o[v].w * sc);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float w = exp2f(mk[u] - Mn);  // 0 for the slots beyond `expected`
+        den += w * lk[u];
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          o[v].x += w * xk[u][v].x;
+          o[v].y += w * xk[u][v].y;
+          o[v].z += w * xk[u][v].z;
+          o[v].w += w * xk[u][v].w;
+        }
+      }
+      M = Mn;
+    }
+    const float inv = 1.f / den;
+    uint32_t packed[8];
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      packed[2 * v] = pack_bf16(o[v].x * inv, o[v].y * inv);
+      packed[2 * v + 1] = pack_bf16(o[v].z * inv, o[v].w * inv);
+    }
+    int4* dst = reinterpret_cast<int4*>(p.out + ((int64_t)i * HQ + h) * D + d0);
+    dst[0] = make_int4(packed[0], packed[1], packed[2], packed[3]);
+    dst[1] = make_int4(packed[4], packed[5], packed[6], packed[7]);
+    if (tid == 0) p.counters[i] = 0;  // ready for the next launch
   };
 
   // RoPE of q into shared memory, and the append of the rotated new k and of v (same rotation
   // as every other kernel of the library); pairs (d, d + D/2) of each head
   auto apply_seq = [&](const SeqIn& in) {
     const int h = tid >> 3, d0 = (tid & 7) * 8;
-    const int64_t pos = in.pos, row = in.row;
+    const int64_t pos = in.pos, row = ((layer_rows + in.blk) * BSZ + in.off) * HKV;
     const float fr[8] = {in.f_lo.x, in.f_lo.y, in.f_lo.z, in.f_lo.w, in.f_hi.x, in.f_hi.y, in.f_hi.z, in.f_hi.w};
     // words w of lo / hi hold elements (d0 + 2w, d0 + 2w + 1) and (d0 + D/2 + 2w, ...)
     auto rot2 = [&](uint32_t lo, uint32_t hi, int w, uint32_t& out_lo, uint32_t& out_hi) {
@@ -507,10 +594,17 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
     m0 = m1 = -INFINITY;
     l0 = l1 = 0.f;
   };
-  auto start = [&](int i) { apply_seq(load_seq(i)); };
+  // the next sequence of the range, its inputs loaded while the current one streams
+  int nxt = -1;
+  SeqIn nxt_in;
+  auto prefetch_after = [&](int i) {
+    nxt = (i + 1 < S && s_pref[i + 1] < g1) ? i + 1 : -1;
+    if (nxt >= 0) nxt_in = load_seq(nxt);
+  };
 
   cur = first;
   apply_seq(first_in);
+  prefetch_after(first);
 
   for (int gb = g0; gb < g1; ++gb) {
     const int it = gb - g0;
@@ -532,7 +626,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
     const int i = seq_of(gb);
     if (i != cur) {
       if (cur >= 0) finish(cur);
-      start(i);
+      apply_seq(i == nxt ? nxt_in : load_seq(i));
+      prefetch_after(i);
       cur = i;
     }
     const int j = gb - s_pref[i];
@@ -620,6 +715,24 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
   }
   cp_async_wait<0>();
   if (cur >= 0) finish(cur);
+  // arrivals for the shared streams (each after this CTA's partial writes are visible), then
+  // the merges of those for which this CTA arrived last
+  if (e_seq >= 0 || t_seq >= 0) {
+    __syncthreads();
+    if (tid == 0) {
+      int c0;
+      s_flag[0] = e_seq >= 0 && arrived0 == seq_ctas(e_seq, c0) - 1;
+      s_flag[1] = 0;
+      if (t_seq >= 0) {
+        __threadfence();
+        s_flag[1] = atomicAdd(&p.counters[t_seq], 1) == seq_ctas(t_seq, c0) - 1;
+      }
+    }
+    __syncthreads();
+    if (s_flag[0] | s_flag[1]) __threadfence();
+    if (s_flag[0]) merge(e_seq);
+    if (s_flag[1]) merge(t_seq);
+  }
 }
 
 std::mutex g_attr_mu;
@@ -634,9 +747,19 @@ bool g_attr_done[2][64] = {};  // [block_size == 1][device]
 constexpr size_t COUNTER_BYTES = (size_t)MAX_SEQS * 4;
 static_assert(COUNTER_BYTES % 256 == 0, "partials stay 256-byte aligned");
 
-size_t kvs_decode_bf16_scratch(int num_seqs, int grid) {
+// the batch plan: header, num_seqs + 1 prefix sums, 2 ints per CTA, one block id per group
+// (at most max_blocks per sequence); 16-token blocks only
+static size_t plan_bytes(const kvs_cache* c, int num_seqs, int grid) {
+  if (c->block_size != BS) return 0;
+  return align_up(((size_t)PLAN_HDR + num_seqs + 1 + 2 * (size_t)grid + (size_t)num_seqs * c->max_blocks) * 4, 256);
+}
+static size_t partial_bytes(int num_seqs, int grid) {
   const size_t slots = (size_t)grid + num_seqs;
-  return COUNTER_BYTES + align_up(slots * HQ * D * 4, 256) + align_up(slots * HQ * 2 * 4, 256);
+  return align_up(slots * HQ * D * 4, 256) + align_up(slots * HQ * 2 * 4, 256);
+}
+
+size_t kvs_decode_bf16_scratch(const kvs_cache* c, int num_seqs, int grid) {
+  return COUNTER_BYTES + partial_bytes(num_seqs, grid) + plan_bytes(c, num_seqs, grid);
 }
 
 bool kvs_decode_bf16_supported(const kvs_cache* c, const kvs_batch* b, int n_heads) {
@@ -653,7 +776,8 @@ int kvs_decode_bf16_grid(int override_ctas) {
 
 int kvs_decode_bf16_launch(const kvs_cache* c, const kvs_batch* b, const kvs_decode_args* a, int grid,
                            cudaStream_t st) {
-  if (a->scratch_bytes < kvs_decode_bf16_scratch(b->num_seqs, grid) || !a->scratch) return KVS_E_SCRATCH;
+  if (a->scratch_bytes < kvs_decode_bf16_scratch(c, b->num_seqs, grid) || !a->scratch) return KVS_E_SCRATCH;
+  if (a->plan < KVS_PLAN_NONE || a->plan > KVS_PLAN_REUSE) return KVS_E_ARG;
   int dev = 0;
   cudaGetDevice(&dev);
   const int one = c->block_size == 1;
@@ -686,6 +810,10 @@ int kvs_decode_bf16_launch(const kvs_cache* c, const kvs_batch* b, const kvs_dec
   p.counters = reinterpret_cast<int32_t*>(s);
   p.part_o = reinterpret_cast<float*>(s + COUNTER_BYTES);
   p.part_ml = reinterpret_cast<float*>(s + COUNTER_BYTES + align_up(slots * HQ * D * 4, 256));
+  p.plan = plan_bytes(c, b->num_seqs, grid)
+               ? reinterpret_cast<int32_t*>(s + COUNTER_BYTES + partial_bytes(b->num_seqs, grid))
+               : nullptr;
+  p.plan_mode = a->plan;
   p.scale_log2 = (float)(a->scale * 1.4426950408889634);
   kernel<<<grid, NTHREADS, SMEM_TOTAL, st>>>(p);
   return launch_rc();

@@ -3,7 +3,7 @@
 #include "kvs_common.cuh"
 
 int kvs_decode_generic(const kvs_cache* c, const kvs_batch* b, const kvs_decode_args* a, cudaStream_t st);
-size_t kvs_decode_bf16_scratch(int num_seqs, int grid);
+size_t kvs_decode_bf16_scratch(const kvs_cache* c, int num_seqs, int grid);
 bool kvs_decode_bf16_supported(const kvs_cache* c, const kvs_batch* b, int n_heads);
 int kvs_decode_bf16_grid(int override_ctas);
 int kvs_decode_bf16_launch(const kvs_cache* c, const kvs_batch* b, const kvs_decode_args* a, int grid,
@@ -32,7 +32,7 @@ KVS_API long long kvs_launch_count(void) { return g_launches.load(std::memory_or
 static size_t decode_region_bytes(const kvs_cache* c, int num_seqs, int n_heads, int grid_ctas) {
   const kvs_batch probe = {nullptr, nullptr, num_seqs, num_seqs};
   if (!kvs_decode_bf16_supported(c, &probe, n_heads)) return 0;
-  return kvs_decode_bf16_scratch(num_seqs, kvs_decode_bf16_grid(grid_ctas));
+  return kvs_decode_bf16_scratch(c, num_seqs, kvs_decode_bf16_grid(grid_ctas));
 }
 
 KVS_API size_t kvs_decode_scratch_bytes(const kvs_cache* c, int32_t num_seqs, int32_t n_heads,
@@ -89,6 +89,9 @@ static bool split_mixed(const kvs_cache* c, const kvs_batch* b, const kvs_decode
   as_->slot_offsets = a->slot_offsets + tok1;
   as_->out = static_cast<uint8_t*>(a->out) + tok1 * orow * esz;
   as_->tail_singles = 0;
+  // the chunks' prefill region of the scratch may cover where a stored plan of the singles
+  // would lie: a mixed step computes its decode plan in every layer
+  as_->plan = KVS_PLAN_NONE;
   *bc = {b->seq_slots, b->cu_tokens, nc, tok1};
   *ac = *a;
   ac->tail_singles = 0;

@@ -111,7 +111,11 @@ class KvsDecodeArgs(C.Structure):
         ("tail_singles", C.c_int32),
         ("q_stride", C.c_int64),
         ("kv_stride", C.c_int64),
+        ("plan", C.c_int32),
     ]
+
+
+PLAN_NONE, PLAN_BUILD, PLAN_REUSE = 0, 1, 2  # kvs_decode_plan
 
 
 class KvsReplayArgs(C.Structure):

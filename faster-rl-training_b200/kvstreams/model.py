@@ -22,6 +22,7 @@ import torch
 import torch.nn.functional as F
 from torch import nn
 
+from . import _native
 from . import _native as N
 from . import ops
 from .config import ModelConfig
@@ -338,8 +339,11 @@ class TinyLM(nn.Module):
             q, k, v = blk.attn.project(blk.attn_norm(x))
             if adt != q.dtype:
                 q, k, v = q.to(adt), k.to(adt), v.to(adt)
+            # every layer has the same batch: the first stores the decode kernel's plan, the
+            # others reuse it
             a = ops.paged_forward(cache, None, counts, i, q, k, v, positions, mapping, inv, blk.attn.scale,
-                                  batch=batch, tail_singles=tail)
+                                  batch=batch, tail_singles=tail,
+                                  plan=_native.PLAN_BUILD if i == 0 else _native.PLAN_REUSE)
             x = blk.mlp_residual(blk.attn_residual(x, a.reshape(N, -1).to(x.dtype)))
         if rows is not None:
             x = x.index_select(0, rows)

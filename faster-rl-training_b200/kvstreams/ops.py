@@ -190,7 +190,7 @@ def paged_forward(cache, slots: Sequence[int], counts: Optional[Sequence[int]], 
                   k_new: torch.Tensor, v_new: torch.Tensor, positions: torch.Tensor, mapping,
                   inv_freq: torch.Tensor, scale: float, out: Optional[torch.Tensor] = None,
                   grid_ctas: int = 0, batch=None, tail_singles: int = 0,
-                  report_path: Optional[list] = None) -> torch.Tensor:
+                  report_path: Optional[list] = None, plan: int = 0) -> torch.Tensor:
     """One layer of the paged incremental forward (model.py:50-75 + hook :182-185) for the
     new tokens of a batch of sequences: RoPE of q/k, append of k/v, paged GQA attention.
 
@@ -198,7 +198,10 @@ def paged_forward(cache, slots: Sequence[int], counts: Optional[Sequence[int]], 
     is the SlotMapping returned by append_slots for the same tokens; ``batch`` a descriptor from
     ``cache._batch(slots, counts)`` that the layers of one forward can share; ``tail_singles``
     the number of trailing sequences with exactly one new token (they then run on the decode
-    kernel while the chunks before them run on the prefill path, in one call).  ``report_path``
+    kernel while the chunks before them run on the prefill path, in one call).  ``plan``: 1 on
+    the first layer of a decode step stores the decode kernel's batch plan, 2 on the later
+    layers of the same step reuses it (same batch, lengths and tables; ``kvs_decode_plan``).
+    ``report_path``
     (a list) receives the call's kernel families as ``kvs_paged_decode_path`` bits: 1 fused
     decode, 2 tensor-core prefill, 4 exact kernels."""
     # q, k_new, v_new may be row-strided views (the column blocks of a fused q|k|v projection
@@ -224,7 +227,7 @@ def paged_forward(cache, slots: Sequence[int], counts: Optional[Sequence[int]], 
                         scratch_bytes=scratch.numel() if scratch is not None else 0, scale=float(scale),
                         layer=int(layer), n_heads=int(q.shape[1]), grid_ctas=int(grid_ctas),
                         tail_singles=int(tail_singles) if counts is not None else 0,
-                        q_stride=q_stride, kv_stride=kv_stride)
+                        q_stride=q_stride, kv_stride=kv_stride, plan=int(plan))
     if report_path is not None:
         report_path.append(int(lib.kvs_paged_decode_path(C.byref(cache.struct), C.byref(b), C.byref(a))))
     N.check(lib.kvs_paged_decode(C.byref(cache.struct), C.byref(b), C.byref(a), N.stream_ptr(q.device)),

@@ -252,7 +252,18 @@ typedef struct kvs_decode_args {
   int64_t q_stride;         /* elements from one token's q row to the next (0: packed, n_heads*head_dim);
                                e.g. the q columns of a fused [tokens][q|k|v] projection output */
   int64_t kv_stride;        /* the same for k_new and v_new (0: packed, n_kv_heads*head_dim) */
+  int32_t plan;             /* KVS_PLAN_*: the batch plan of a decode step (below) */
 } kvs_decode_args;
+/* The batch plan of the fused decode kernel (16-token blocks): how the step's groups of 16
+ * live entries are split over the CTAs, and the block id of every group.  The layers of one
+ * decode step all have the same plan, so the first layer's call can store it in the scratch
+ * (KVS_PLAN_BUILD) and the later layers' calls read it back (KVS_PLAN_REUSE) instead of
+ * recomputing it from the block tables.  REUSE is valid only while the batch, its sequences'
+ * lengths and block tables and grid_ctas are those of the last BUILD call on the same scratch
+ * (one decode step); a REUSE call whose stored plan has another batch size or grid computes
+ * the plan itself.  No reference counterpart (the reference's decode recomputes nothing per
+ * layer: it gathers every sequence's K/V in PyTorch). */
+enum kvs_decode_plan { KVS_PLAN_NONE = 0, KVS_PLAN_BUILD = 1, KVS_PLAN_REUSE = 2 };
 /* scratch of kvs_paged_decode: split partials and per-sequence arrival counters of the
  * fused decode kernel, then (bf16, head_dim 128, 16-token blocks, even GQA group) the
  * query-tile offsets of the tensor-core chunked prefill.  Zero it once when allocated:

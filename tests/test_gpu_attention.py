@@ -283,6 +283,69 @@ def test_prefill_then_decode_share_scratch_any_slot_order():
             nxt[s] += n
 
 
+@pytest.mark.parametrize("S,ctx,grid", [
+    (40, (50, 900), 0),      # one CTA per SM, every range's block ids staged in shared memory
+    (4, (8500, 9500), 1),    # one CTA over > 2048 groups: block ids read from the plan in global memory
+])
+def test_decode_plan_reuse_equals_recompute(S, ctx, grid):
+    """The layers of a decode step with the batch plan stored by the first layer and read back
+    by the others (KVS_PLAN_BUILD / KVS_PLAN_REUSE) give the same bits as layers that each
+    compute it; a REUSE call after a BUILD for another batch size computes the plan itself."""
+    from kvstreams import _native as N
+    from kvstreams import ops
+    from kvstreams.paged_cache import PagedKVCache
+    from kvstreams.rope import RotaryEmbedding
+    from kvstreams.workloads import decode_state
+
+    dtype, D, Hq, Hkv, bs, L = torch.bfloat16, 128, 32, 8, 16, 3
+    st = decode_state(num_streams=S, ctx_range=ctx, block_size=bs, num_blocks=S * (ctx[1] // bs + 16), seed=11)
+    cache = PagedKVCache(L, Hkv, D, block_size=bs, num_blocks=st.num_blocks, dtype=dtype, max_seqs=S,
+                         max_blocks_per_seq=ctx[1] // bs + 16)
+    cache.load_state(range(S), st.tables, st.positions, st.free_list)
+    g = torch.Generator(device="cuda").manual_seed(4)
+    cache.k.copy_(torch.randn(cache.k.shape, generator=g, device="cuda").to(dtype))
+    cache.v.copy_(torch.randn(cache.v.shape, generator=g, device="cuda").to(dtype))
+    inv = RotaryEmbedding(D, 5e5).table("cuda", dtype)
+    pos = torch.as_tensor(st.next_positions, device="cuda")
+    for step in range(3):
+        seqs = list(range(S)) if step != 1 else list(range(S - 1))  # step 1: another batch size
+        p = pos[: len(seqs)] + step
+        q = torch.randn(len(seqs), L, Hq, D, generator=g, device="cuda").to(dtype)
+        k = torch.randn(len(seqs), L, Hkv, D, generator=g, device="cuda").to(dtype)
+        v = torch.randn(len(seqs), L, Hkv, D, generator=g, device="cuda").to(dtype)
+        mapping = cache.append_slots_batch(seqs, p)
+        batch = cache._batch(seqs)
+        for mode in ("plan", "none"):
+            outs = []
+            for layer in range(L):
+                if mode == "none":
+                    plan = N.PLAN_NONE
+                elif step == 1:
+                    plan = N.PLAN_REUSE  # the stored plan is for S sequences: computed instead
+                else:
+                    plan = N.PLAN_BUILD if layer == 0 else N.PLAN_REUSE
+                path = []
+                outs.append(ops.paged_forward(cache, seqs, None, layer, q[:, layer], k[:, layer], v[:, layer], p,
+                                              mapping, inv, D ** -0.5, grid_ctas=grid, batch=batch, plan=plan,
+                                              report_path=path))
+                assert path == [FUSED]
+            if mode == "plan":
+                with_plan = outs
+        for layer in range(L):
+            assert torch.equal(with_plan[layer], outs[layer]), f"step {step} layer {layer}"
+    # the plan path against the oracle on the last step's first layer
+    pn = p.cpu().numpy()
+    q_rot = O.rope_apply(_np(q[:, 0]), pn, 5e5, np.float32).astype(np.float64)
+    got = _np(with_plan[0])
+    for s in (0, S - 1):
+        tab = torch.as_tensor(cache.block_table(s), device="cuda")
+        n = cache.num_tokens(s)
+        keys = _np(cache.k[0].index_select(0, tab).reshape(-1, Hkv, D)[:n])
+        vals = _np(cache.v[0].index_select(0, tab).reshape(-1, Hkv, D)[:n])
+        want = O.gqa_attention(q_rot[s:s + 1], keys, vals, np.ones((1, n), dtype=bool), D ** -0.5)
+        np.testing.assert_allclose(got[s:s + 1], want, rtol=0, atol=TOL[dtype], err_msg=f"stream {s}")
+
+
 @pytest.mark.parametrize("dtype,D,Hq,Hkv,counts", [
     (torch.bfloat16, 128, 32, 8, [1] * 9),               # fused decode kernel
     (torch.bfloat16, 128, 32, 8, [40, 17, 1, 1, 1]),     # mixed step: prefill chunks + decode tail
