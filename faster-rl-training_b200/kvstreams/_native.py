@@ -55,7 +55,7 @@ STAT_FIELDS = (
 )
 STAT_COUNT = 8
 STATUS_WORDS = 4
-ABI_VERSION = 3  # KVS_ABI_VERSION of include/kvs_b200.h
+ABI_VERSION = 4  # KVS_ABI_VERSION of include/kvs_b200.h
 NEVER = (1 << 63) - 1
 
 

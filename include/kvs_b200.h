@@ -30,7 +30,7 @@ extern "C" {
 
 typedef struct CUstream_st* kvs_stream_t; /* == cudaStream_t */
 
-#define KVS_ABI_VERSION 3
+#define KVS_ABI_VERSION 4
 
 /* element types of K/V pools and activations */
 enum kvs_dtype { KVS_F32 = 0, KVS_F64 = 1, KVS_BF16 = 2, KVS_F16 = 3 };

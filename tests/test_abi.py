@@ -46,7 +46,7 @@ def test_struct_layouts_match(lib):
 
     for which, st in N.STRUCTS.items():
         assert lib.kvs_abi_struct_size(which) == C.sizeof(st)
-    assert lib.kvs_abi_version() == 3
+    assert lib.kvs_abi_version() == 4
 
 
 def test_host_only_size_queries(lib):
