@@ -919,30 +919,52 @@ pair_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
 // of one head and loops over its active key tiles (the forward's list).  P and dS are
 // rounded to bf16 as UMMA operands (as P is in the forward).
 
-// -lse2 and -D of each (stream, head, row) (one warp per row and head); both kernels add them
-__global__ void replay_rowdot_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ o,
-                                     const float* __restrict__ lse, float* __restrict__ nlse,
-                                     float* __restrict__ nd, int B, int T, int T_pad, int Hq) {
-  const int64_t gw = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (gw >= (int64_t)B * T * Hq) return;
-  const int lane = threadIdx.x & 31;
-  const int h = (int)(gw % Hq), t = (int)((gw / Hq) % T), b = (int)(gw / ((int64_t)Hq * T));
-  const uint2 x = reinterpret_cast<const uint2*>(dout + gw * HD)[lane];
-  const uint2 y = reinterpret_cast<const uint2*>(o + gw * HD)[lane];
-  const __nv_bfloat162* xa = reinterpret_cast<const __nv_bfloat162*>(&x);
-  const __nv_bfloat162* ya = reinterpret_cast<const __nv_bfloat162*>(&y);
-  float s = 0.f;
+// -lse2 and -D of each (stream, head, row); both kernels add them.  A warp takes four
+// consecutive rows of one head, half a warp per row and 16 bytes of dO and of O per lane, with
+// every load of a lane (and the rows' lse) issued before the first product: a pure stream of
+// dO and O whose outputs land in consecutive words.
+constexpr int ROWDOT_PER_WARP = 4;
+__global__ void __launch_bounds__(256) replay_rowdot_kernel(const __nv_bfloat16* __restrict__ dout,
+                                                            const __nv_bfloat16* __restrict__ o,
+                                                            const float* __restrict__ lse, float* __restrict__ nlse,
+                                                            float* __restrict__ nd, int B, int T, int T_pad, int Hq) {
+  const int nt4 = (T + ROWDOT_PER_WARP - 1) / ROWDOT_PER_WARP;
+  const int64_t w = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (w >= (int64_t)B * Hq * nt4) return;
+  const int tq = (int)(w % nt4), h = (int)((w / nt4) % Hq), b = (int)(w / ((int64_t)nt4 * Hq));
+  const int lane = threadIdx.x & 31, half = lane >> 4, l16 = lane & 15;
+  const int64_t vrow = ((int64_t)b * Hq + h) * T_pad;  // this head's row vectors
+  uint4 x[ROWDOT_PER_WARP / 2], y[ROWDOT_PER_WARP / 2];
+  float ls[ROWDOT_PER_WARP / 2];
 #pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const float2 a = __bfloat1622float2(xa[i]), c = __bfloat1622float2(ya[i]);
-    s += a.x * c.x + a.y * c.y;
+  for (int it = 0; it < ROWDOT_PER_WARP / 2; ++it) {
+    const int t = tq * ROWDOT_PER_WARP + 2 * it + half;
+    x[it] = y[it] = make_uint4(0u, 0u, 0u, 0u);
+    ls[it] = 0.f;
+    if (t < T) {
+      const int64_t row = ((int64_t)b * T + t) * Hq + h;
+      x[it] = reinterpret_cast<const uint4*>(dout + row * HD)[l16];
+      y[it] = reinterpret_cast<const uint4*>(o + row * HD)[l16];
+      if (l16 == 0) ls[it] = lse[vrow + t];
+    }
   }
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-  if (lane == 0) {
-    const int64_t v = ((int64_t)b * Hq + h) * T_pad + t;
-    nd[v] = -s;
-    nlse[v] = -lse[v];
+  for (int it = 0; it < ROWDOT_PER_WARP / 2; ++it) {
+    const __nv_bfloat162* xa = reinterpret_cast<const __nv_bfloat162*>(&x[it]);
+    const __nv_bfloat162* ya = reinterpret_cast<const __nv_bfloat162*>(&y[it]);
+    float s = 0.f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 a = __bfloat1622float2(xa[e]), c = __bfloat1622float2(ya[e]);
+      s += a.x * c.x + a.y * c.y;
+    }
+#pragma unroll
+    for (int off = 8; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    const int t = tq * ROWDOT_PER_WARP + 2 * it + half;
+    if (l16 == 0 && t < T) {
+      nd[vrow + t] = -s;
+      nlse[vrow + t] = -ls[it];
+    }
   }
 }
 
@@ -2059,8 +2081,8 @@ int kvs_replay_tc_backward(const kvs_replay_args* a, const void* dout, void* dq,
   replay_prepass_kernel<<<dim3(n_kt, B), BN, 0, st>>>(a->evicted_at, T, T_pad, n_kt, s.e32, s.tmin, s.tmax);
   int rc = launch_rc();
   if (rc) return rc;
-  const int64_t rows = (int64_t)B * T * a->n_heads;
-  replay_rowdot_kernel<<<(unsigned)((rows + 3) / 4), 128, 0, st>>>(static_cast<const __nv_bfloat16*>(dout),
+  const int64_t rowdot_warps = (int64_t)B * a->n_heads * ((T + ROWDOT_PER_WARP - 1) / ROWDOT_PER_WARP);
+  replay_rowdot_kernel<<<(unsigned)((rowdot_warps + 7) / 8), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(dout),
                                                                     static_cast<const __nv_bfloat16*>(a->out),
                                                                     a->row_lse, nlse, nd, B, T, T_pad, a->n_heads);
   if ((rc = launch_rc())) return rc;
