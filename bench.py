@@ -519,12 +519,14 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     st, cache, q, k, v, rope = build_decode(dev, seed=1000, value_seed=1000 + rank)
     inv = rope.table(dev, torch.bfloat16)
     seqs = list(range(S))
-    pos = torch.as_tensor(st.next_positions, device=dev)
+    steps_all = max(args.warmup, args.steps)
+    # every step's positions, resident before the timed region (an input like q/k/v)
+    pos_steps = torch.as_tensor(st.next_positions, device=dev)[None, :] + torch.arange(steps_all, device=dev)[:, None]
     out = torch.empty_like(q)
     snap = cache.snapshot_state()
 
     def step(i: int, ev=None):
-        p = pos + i
+        p = pos_steps[i]
         mapping = cache.append_slots_batch(seqs, p)
         if ev is not None:
             ev[0].record()
@@ -566,7 +568,8 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     # overlap step i's kernels; every copy of every step stays inside the timed region.
     cache.restore_state(snap)
     hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
-    hpos = torch.as_tensor(st.next_positions).pin_memory()
+    hpos_steps = pos_steps.cpu().pin_memory()  # row i: step i's positions, uploaded with its q/k/v
+    hpos = hpos_steps[0]
     hout = [torch.empty(out.shape, dtype=out.dtype).pin_memory() for _ in range(2)]
     bufs = [tuple(torch.empty_like(t, device=dev) for t in (hq, hk, hv, hpos)) for _ in range(2)]
     outs = [out, torch.empty_like(out)]
@@ -580,7 +583,7 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
         with torch.cuda.stream(copy):
             if i >= 2:
                 copy.wait_event(done[i - 2])  # step i-2 has read this buffer
-            for d_t, h_t in zip(bufs[i % 2], (hq, hk, hv, hpos)):
+            for d_t, h_t in zip(bufs[i % 2], (hq, hk, hv, hpos_steps[i])):
                 d_t.copy_(h_t, non_blocking=True)
             in_ready[i].record(copy)
 
@@ -598,9 +601,8 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
         if i >= 2:
             comp.wait_event(fetched[i - 2])  # the output buffer of step i-2 is on the host
         dq, dk, dv, dpos = bufs[i % 2]
-        p = dpos + i
-        mapping = cache.append_slots_batch(seqs, p)
-        ops.paged_forward(cache, seqs, None, 0, dq, dk, dv, p, mapping, inv, D ** -0.5, out=outs[i % 2])
+        mapping = cache.append_slots_batch(seqs, dpos)
+        ops.paged_forward(cache, seqs, None, 0, dq, dk, dv, dpos, mapping, inv, D ** -0.5, out=outs[i % 2])
         done[i].record(comp)
         with torch.cuda.stream(copy):
             copy.wait_event(done[i])

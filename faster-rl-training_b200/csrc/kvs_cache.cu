@@ -43,6 +43,70 @@ __global__ void reset_kernel(kvs_cache c) {
 // One CTA: the allocation order is a prefix sum over the batch (canonical order).
 constexpr int kAppendThreads = 1024;
 
+// The decode step's append (one new token per sequence, at most kAppendThreads sequences): a
+// thread per sequence, every value loaded once and kept in registers, the token's slot taken
+// from the table entry it already has or from the block it pops.  Same allocation order,
+// checks and status words as append_slots_kernel, in fewer dependent global round trips.
+__global__ void __launch_bounds__(kAppendThreads)
+append_one_kernel(kvs_cache c, kvs_batch b, const int64_t* __restrict__ positions,
+                  int32_t* __restrict__ out_blocks, int32_t* __restrict__ out_offsets) {
+  __shared__ int s_scan[33];
+  __shared__ long long s_red[32];
+  const int tid = threadIdx.x, bs = c.block_size;
+  const int top = *c.free_top;  // read by every thread before the first barrier; written last
+  const bool valid = tid < b.num_seqs;
+  int slot = 0, n = 0, nb = 0, need = 0, tab = -1;
+  int64_t pos = 0;
+  if (valid) {
+    slot = b.seq_slots[tid];
+    pos = positions[tid];
+    n = c.lengths[slot];
+    nb = c.n_blocks[slot];
+    need = n / bs + 1 - nb;  // ceil_div(n + 1, bs) - nb
+    need = need < 0 ? 0 : need;
+    if (need == 0) tab = c.tables[(int64_t)slot * c.max_blocks + n / bs];
+  }
+  const int over = valid && nb + need > c.max_blocks;
+  int total = 0;
+  const int off = block_exclusive_scan(need, s_scan, &total);
+  // the batch must fit as a whole (no partial state on failure)
+  if (total > top) {
+    if (tid == 0) set_status(c.status, KVS_ST_OUT_OF_BLOCKS, total, top, 0);
+    return;
+  }
+  if (__syncthreads_or(over)) {
+    const long long overflow = block_sum_ll(over, s_red);
+    if (tid == 0) set_status(c.status, KVS_ST_TABLE_OVERFLOW, (int)overflow, c.max_blocks, 0);
+    return;
+  }
+  if (valid) {
+    // paged_cache.py:152-155 -- a block is taken from the end of the free list whenever the
+    // token index reaches a new table entry
+    int blk_tok = tab;
+    for (int k = 0; k < need; ++k) {
+      const int blk = c.free_stack[top - 1 - (off + k)];
+      c.tables[(int64_t)slot * c.max_blocks + nb + k] = blk;
+      if (c.block_owner[blk] != -1) set_status(c.status, KVS_ST_OWNER, blk, slot, c.block_owner[blk]);
+      c.block_owner[blk] = slot;
+      if (nb + k == n / bs) blk_tok = blk;
+    }
+    c.n_blocks[slot] = nb + need;
+    // paged_cache.py:152,161 -- slot of token n is (table[n // bs], n % bs)
+    const int o = n % bs;
+    c.slot_pos[(int64_t)blk_tok * bs + o] = pos;
+    out_blocks[tid] = blk_tok;
+    out_offsets[tid] = o;
+    c.lengths[slot] = n + 1;
+  }
+  if (tid == 0) {
+    const int new_top = top - total;
+    *c.free_top = new_top;
+    c.stats[KVS_STAT_WRITTEN_TOKENS] += b.total_tokens;
+    const long long used = c.num_blocks - new_top;  // paged_cache.py:164
+    if (used > c.stats[KVS_STAT_PEAK_BLOCKS]) c.stats[KVS_STAT_PEAK_BLOCKS] = used;
+  }
+}
+
 __global__ void __launch_bounds__(kAppendThreads)
 append_slots_kernel(kvs_cache c, kvs_batch b, const int64_t* __restrict__ positions,
                     int32_t* __restrict__ out_blocks, int32_t* __restrict__ out_offsets) {
@@ -503,8 +567,11 @@ KVS_API int kvs_append_slots(const kvs_cache* c, const kvs_batch* b, const int64
   if (!c || !b || b->num_seqs < 0 || b->total_tokens < 0) return KVS_E_ARG;
   if (b->num_seqs == 0) return KVS_OK;
   if (b->total_tokens > 0 && (!positions || !out_blocks || !out_offsets)) return KVS_E_ARG;
-  append_slots_kernel<<<1, kAppendThreads, 0, to_cuda(stream)>>>(*c, *b, positions, out_blocks,
-                                                                 out_offsets);
+  if (b->cu_tokens == nullptr && b->total_tokens == b->num_seqs && b->num_seqs <= kAppendThreads)
+    append_one_kernel<<<1, kAppendThreads, 0, to_cuda(stream)>>>(*c, *b, positions, out_blocks, out_offsets);
+  else
+    append_slots_kernel<<<1, kAppendThreads, 0, to_cuda(stream)>>>(*c, *b, positions, out_blocks,
+                                                                   out_offsets);
   return launch_rc();
 }
 
