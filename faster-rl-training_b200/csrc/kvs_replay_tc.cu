@@ -2179,6 +2179,37 @@ int kvs_prefill_tc_launch(const kvs_cache* c, const kvs_batch* b, int layer, voi
   return launch_rc();
 }
 
+namespace {
+// One warp waits on an mbarrier with the library's bounded waits.  mode bit 0: the fast wait
+// (default time slices) instead of the suspending one; bit 1: thread 0 arrives first, so the
+// wait completes.  out[0] = 1 if the wait gave up, 0 if it saw the phase complete; out[1..2] =
+// the wait's clock64 cycles (low, high word).
+__global__ void wait_selftest_kernel(int mode, uint32_t limit, int32_t* out) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    mbar_fence_init();
+  }
+  __syncwarp();
+  if ((mode & 2) && threadIdx.x == 0) mbar_arrive(&bar);
+  __syncwarp();
+  const long long t0 = clock64();
+  const bool ok = (mode & 1) ? mbar_wait_fast(&bar, 0, nullptr, limit) : mbar_wait(&bar, 0, nullptr, limit);
+  const long long dt = clock64() - t0;
+  if (threadIdx.x == 0) {
+    out[0] = ok ? 0 : 1;
+    out[1] = (int32_t)(dt & 0xffffffffLL);
+    out[2] = (int32_t)(dt >> 32);
+  }
+}
+}  // namespace
+
+KVS_API int kvs_selftest_wait(int32_t mode, uint32_t limit, int32_t* out, kvs_stream_t stream) {
+  if (!out || mode < 0 || mode > 3 || limit == 0) return KVS_E_ARG;
+  wait_selftest_kernel<<<1, 32, 0, to_cuda(stream)>>>(mode, limit, out);
+  return launch_rc();
+}
+
 KVS_API int kvs_selftest_umma(const void* a, const void* b, float* c, int32_t mode, int32_t* error,
                               kvs_stream_t stream) {
   if (!a || !b || !c || !error || mode < 0 || mode > 3) return KVS_E_ARG;

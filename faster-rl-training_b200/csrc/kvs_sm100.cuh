@@ -50,11 +50,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity, ui
       : "memory");
   return ok != 0;
 }
-// Wait for phase `parity` of `bar` to complete, giving up after `limit` suspended
-// polls of at most 100 us each (~2 s in all).  Returns false on timeout; the caller
-// records an error and winds down instead of hanging.
+// Wait for phase `parity` of `bar` to complete, giving up after `limit` suspended polls.
+// Returns false on timeout; the caller records an error and winds down instead of hanging.
+// An unanswered poll lasts ~4 us on B200 (the 100 us hint is an upper bound the hardware does
+// not reach), so the default bound is ~1.6 s.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const volatile int* abort_flag,
-                                          uint32_t limit = 20000) {
+                                          uint32_t limit = 400000) {
   for (uint32_t i = 0; i < limit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if (abort_flag && *abort_flag) return false;
@@ -74,9 +75,10 @@ __device__ __forceinline__ bool mbar_try_wait_default(uint64_t* bar, uint32_t pa
       : "memory");
   return ok != 0;
 }
-// Latency-critical wait: default time slices, bounded by `limit` polls (several seconds).
+// Latency-critical wait: default time slices, bounded by `limit` polls.  An unanswered poll
+// lasts ~4 us on B200, so the default bound is ~2 s.
 __device__ __forceinline__ bool mbar_wait_fast(uint64_t* bar, uint32_t parity, const volatile int* abort_flag,
-                                               uint32_t limit = 1u << 24) {
+                                               uint32_t limit = 1u << 19) {
   for (uint32_t i = 0; i < limit; ++i) {
     if (mbar_try_wait_default(bar, parity)) return true;
     if (abort_flag && *abort_flag) return false;

@@ -208,6 +208,7 @@ SIGNATURES = {
     "kvs_silu_mul_backward": (C.c_int, [_P, _P, _P, C.c_int64, _I, C.c_int64, C.c_int64, C.c_int64, _I, _P]),
     "kvs_lse_gather_backward": (C.c_int, [_P, C.c_int64, _I, _I, _P, _P, _P, C.c_double, _I, _P, C.c_int64, _I, _P]),
     "kvs_selftest_umma": (C.c_int, [_P, _P, _P, _I, _P, _P]),
+    "kvs_selftest_wait": (C.c_int, [_I, C.c_uint32, _P, _P]),
     "kvs_lm_head_logprobs_scratch_bytes": (_Z, [_I, _I]),
     "kvs_lm_head_logprobs_supported": (C.c_int, [_I]),
     "kvs_lm_head_logprobs": (C.c_int, [_P, C.c_int64, _P, C.c_int64, _I, _I, _I, _P, C.c_double, _P, _P, _P, _Z,

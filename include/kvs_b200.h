@@ -492,6 +492,13 @@ int kvs_silu_mul_backward(const void* gu, const void* grad, void* dgu, int64_t n
  * descriptors, TMA swizzle and TMEM layouts that the replay kernel relies on. */
 int kvs_selftest_umma(const void* a, const void* b, float* c, int32_t mode, int32_t* error,
                       kvs_stream_t stream);
+/* Self-test of the bounded waits every kernel of this library uses on its mbarriers (no
+ * reference counterpart): one warp waits, at most `limit` polls, on a barrier that nothing
+ * arrives on (mode bit 1 = 0) or that one thread arrives on first (bit 1 = 1), with the
+ * suspending wait (bit 0 = 0) or the fast one (bit 0 = 1).  out[0] = 1 if the wait gave up
+ * (the kernels then record an error and wind down), 0 if it completed; out[1], out[2] = the
+ * wait's SM cycles (low, high 32 bits).  A timeout leaves the context usable. */
+int kvs_selftest_wait(int32_t mode, uint32_t limit, int32_t* out, kvs_stream_t stream);
 
 #ifdef __cplusplus
 }
