@@ -7,7 +7,7 @@ the block table on the device, and no retained token is ever forwarded twice.
 
 from __future__ import annotations
 
-from ..utils.spans import Span, in_spans
+from ..utils.spans import Span, split_by_spans
 from .base import BaseEngine, _Episode
 
 
@@ -18,8 +18,8 @@ class KVStreamEngine(BaseEngine):
         return list(idx)
 
     def _evict(self, ep: _Episode, spans: list[Span]):
-        evicted = self.cache.evict_positions(ep.seq_id, spans)
+        # the eviction and the cache's invariant check come back in one device round trip
+        evicted = self.cache.evict_positions(ep.seq_id, spans, check=True)
         if evicted:
-            ep.context = [i for i in ep.context if not in_spans(i, evicted)]
-            self.cache.check_invariants(ep.seq_id)
+            ep.context = split_by_spans(ep.context, evicted)[0]
         return evicted, None

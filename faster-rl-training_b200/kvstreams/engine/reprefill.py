@@ -4,7 +4,7 @@ renumbered from 0, so every compaction costs a prefill of the whole retained con
 
 from __future__ import annotations
 
-from ..utils.spans import Span, in_spans, positions_to_spans
+from ..utils.spans import Span, positions_to_spans, split_by_spans
 from .base import BaseEngine, _Episode
 
 
@@ -17,9 +17,7 @@ class RePrefillEngine(BaseEngine):
         return list(range(base, base + len(idx)))
 
     def _evict(self, ep: _Episode, spans: list[Span]):
-        keep, gone = [], []
-        for i in ep.context + ep.pending:
-            (gone if in_spans(i, spans) else keep).append(i)
+        keep, gone = split_by_spans(ep.context + ep.pending, spans)
         if not gone:
             return [], None
         self.cache.free_sequence(ep.seq_id)

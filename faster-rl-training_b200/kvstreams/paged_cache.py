@@ -496,20 +496,43 @@ class PagedKVCache:
             self._h_top += rem // bs
         return removed
 
-    def evict_positions(self, seq_id: int, spans: Iterable[Span]) -> list[Span]:
+    def evict_positions(self, seq_id: int, spans: Iterable[Span], check: bool = False) -> list[Span]:
         """paged_cache.py:219-240: evict every full block whose tokens all lie in ``spans``;
-        returns the logical spans actually removed."""
-        return self.evict_positions_batch([seq_id], [spans])[0]
+        returns the logical spans actually removed.  ``check``: also run
+        :meth:`check_invariants` on the sequence, read back with the eviction's results."""
+        return self.evict_positions_batch([seq_id], [spans], check=check)[0]
 
-    def evict_positions_batch(self, seq_ids: Sequence[int], spans: Sequence[Iterable[Span]]) -> list[list[Span]]:
-        """Batched evict_positions in canonical (given) order; one device round trip."""
-        out_t, counts_t, slots = self.evict_positions_async(seq_ids, spans)
-        if out_t is None:
+    def evict_positions_batch(self, seq_ids: Sequence[int], spans: Sequence[Iterable[Span]],
+                              check: bool = False) -> list[list[Span]]:
+        """Batched evict_positions in canonical (given) order.  One device round trip: the
+        evicted spans, the sequences' new lengths and table sizes, the free count, the status
+        word and (with ``check``) the invariant codes of the evicted sequences come back in one
+        read."""
+        req = self.prepare_evict(seq_ids, spans)
+        if req is None:
             return [[] for _ in seq_ids]
-        counts = counts_t.cpu().numpy()
-        spans_h = out_t.cpu().numpy()
-        self._refresh(slots)
-        return [[(int(a), int(b)) for a, b in spans_h[i, : counts[i]]] for i in range(len(slots))]
+        self.evict_prepared(req)
+        slots, n = req.slots, len(req.slots)
+        idx = req.keep[0].long()  # the batch's slot ids, already on the device
+        parts = [req.counts.long(), req.out.reshape(-1), self._lengths.index_select(0, idx).long(),
+                 self._n_blocks.index_select(0, idx).long(), self._free_top.long(), self._status.long()]
+        if check:
+            parts.append(self._launch_check(req.batch).long())
+        vals = torch.cat(parts).cpu().numpy()
+        counts = vals[:n]
+        spans_h = vals[n : n + n * req.cap * 2].reshape(n, req.cap, 2)
+        o = n + n * req.cap * 2
+        self._h_len[list(slots)] = vals[o : o + n]
+        self._h_nb[list(slots)] = vals[o + n : o + 2 * n]
+        self._h_top = int(vals[o + 2 * n])
+        self._stale.difference_update(int(sl) for sl in slots)
+        if vals[o + 2 * n + 1] != 0:
+            self._raise_status()
+        if check:
+            for code in vals[o + 2 * n + 2 :].tolist():
+                if code != N.ST_OK:
+                    raise AssertionError(self._INV_MESSAGES.get(code, f"invariant {code} violated"))
+        return [[(int(a), int(b)) for a, b in spans_h[i, : counts[i]]] for i in range(n)]
 
     def evict_positions_async(self, seq_ids: Sequence[int], spans: Sequence[Iterable[Span]],
                               span_cap: int = 0):
@@ -529,17 +552,22 @@ class PagedKVCache:
         merged = [merge_spans(sp) for sp in spans]
         if not any(merged) or not any(self._h_len[s] for s in slots):
             return None
-        cu = np.zeros(len(slots) + 1, dtype=np.int32)
-        np.cumsum([len(m) for m in merged], out=cu[1:])
+        # starts (int64), ends (int64) and the per-sequence prefix (int32) in one upload
+        ns = sum(len(m) for m in merged)
+        buf = np.zeros(16 * ns + 4 * (len(slots) + 1), dtype=np.uint8)
         flat = np.asarray([x for m in merged for x in m], dtype=np.int64).reshape(-1, 2)
+        buf[: 8 * ns].view(np.int64)[:] = flat[:, 0]
+        buf[8 * ns : 16 * ns].view(np.int64)[:] = flat[:, 1]
+        np.cumsum([len(m) for m in merged], out=buf[16 * ns :].view(np.int32)[1:])
         cap = int(span_cap) or max(1, int(max(self._h_len[s] for s in slots)))
         dev = self.device
         b, keep = self._batch(slots)
+        up = torch.from_numpy(buf).to(dev)
         return EvictRequest(
-            slots=slots, batch=b, keep=keep,
-            cu=torch.from_numpy(cu).to(dev),
-            starts=torch.from_numpy(np.ascontiguousarray(flat[:, 0])).to(dev),
-            ends=torch.from_numpy(np.ascontiguousarray(flat[:, 1])).to(dev),
+            slots=slots, batch=b, keep=keep + [up],
+            cu=up[16 * ns :].view(torch.int32),
+            starts=up[: 8 * ns].view(torch.int64),
+            ends=up[8 * ns : 16 * ns].view(torch.int64),
             out=torch.empty((len(slots), cap, 2), dtype=torch.long, device=dev),
             counts=torch.empty(len(slots), dtype=torch.int32, device=dev),
             cap=cap,
@@ -590,17 +618,22 @@ class PagedKVCache:
         """paged_cache.py:262-273, run by the device validation kernel."""
         self.check_invariants_batch([seq_id])
 
+    def _launch_check(self, batch) -> torch.Tensor:
+        """Launch the invariant check of ``batch``'s sequences; their codes, on the device."""
+        codes = torch.empty(batch.num_seqs, dtype=torch.int32, device=self.device)
+        nbytes = self._lib.kvs_check_scratch_bytes(self.num_blocks)
+        scratch = self._scratch_buf(nbytes)
+        rc = self._lib.kvs_check_invariants(C.byref(self._struct), C.byref(batch), codes.data_ptr(),
+                                            scratch.data_ptr(), scratch.numel(), self._stream())
+        N.check(rc, "kvs_check_invariants")
+        return codes
+
     def check_invariants_batch(self, seq_ids: Sequence[int]) -> None:
         slots = [self._slot_of[s] for s in seq_ids]
         if not slots:
             return
-        codes = torch.empty(len(slots), dtype=torch.int32, device=self.device)
-        nbytes = self._lib.kvs_check_scratch_bytes(self.num_blocks)
-        scratch = self._scratch_buf(nbytes)
         b, keep = self._batch(slots)
-        rc = self._lib.kvs_check_invariants(C.byref(self._struct), C.byref(b), codes.data_ptr(), scratch.data_ptr(),
-                                            scratch.numel(), self._stream())
-        N.check(rc, "kvs_check_invariants")
+        codes = self._launch_check(b)
         for code in codes.cpu().tolist():
             if code != N.ST_OK:
                 raise AssertionError(self._INV_MESSAGES.get(code, f"invariant {code} violated"))

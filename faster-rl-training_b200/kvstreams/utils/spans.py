@@ -2,6 +2,7 @@
 
 from __future__ import annotations
 
+from bisect import bisect_right
 from typing import Iterable
 
 Span = tuple[int, int]
@@ -31,3 +32,16 @@ def span_length(spans: Iterable[Span]) -> int:
 
 def in_spans(position: int, spans: Iterable[Span]) -> bool:
     return any(a <= position < b for a, b in spans)
+
+
+def split_by_spans(positions: Iterable[int], spans: Iterable[Span]) -> tuple[list[int], list[int]]:
+    """(positions in none of the spans, positions in one), each in the given order: a binary
+    search per position over the merged spans instead of a scan of every span."""
+    merged = merge_spans(spans)
+    starts = [a for a, _ in merged]
+    outside: list[int] = []
+    inside: list[int] = []
+    for p in positions:
+        j = bisect_right(starts, p) - 1
+        (inside if j >= 0 and p < merged[j][1] else outside).append(p)
+    return outside, inside

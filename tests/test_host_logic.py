@@ -72,8 +72,11 @@ class _OracleBackedCache:
     def append(self, s, positions):
         self.c.append_slots(s, positions)
 
-    def evict_positions(self, s, spans):
-        return self.c.evict_positions(s, spans)
+    def evict_positions(self, s, spans, check=False):
+        evicted = self.c.evict_positions(s, spans)
+        if check:
+            self.check_invariants(s)
+        return evicted
 
     def check_invariants(self, s):
         msg = self.c.check_invariants(s)
