@@ -184,6 +184,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
   int* s_flag = s_tab + TAB_CAP;
   int* s_scan = s_flag + 4;  // 33 ints
 
+  // Launched with programmatic stream serialization: the grid may become resident while the
+  // previous kernel of the stream (the q|k|v projection, or the previous layer's decode) is
+  // finishing; everything it reads waits for that kernel's completion here.
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;
   const kvs_cache& c = p.c;
@@ -815,6 +819,19 @@ int kvs_decode_bf16_launch(const kvs_cache* c, const kvs_batch* b, const kvs_dec
                : nullptr;
   p.plan_mode = a->plan;
   p.scale_log2 = (float)(a->scale * 1.4426950408889634);
-  kernel<<<grid, NTHREADS, SMEM_TOTAL, st>>>(p);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(NTHREADS, 1, 1);
+  cfg.dynamicSmemBytes = SMEM_TOTAL;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kernel, p) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return KVS_E_LAUNCH;
+  }
   return launch_rc();
 }
