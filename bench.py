@@ -1110,6 +1110,7 @@ def rollout_bench(dev, args, rank: int, world: int = 1) -> dict:
     W, K = args.rollout_warmup, args.rollout_iters
     ev = [torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
     tally = {"decode": 0, "prefill": 0}
+    clk = ClockSampler(dev.index or 0)  # seconds of GEMM-heavy work: the power cap may lower the clock
 
     prof = args.rollout_profile_iter
 
@@ -1124,11 +1125,13 @@ def rollout_bench(dev, args, rank: int, world: int = 1) -> dict:
             torch.cuda.profiler.stop()
         if i == W:
             ev[0].record()
+            clk.__enter__()
         elif W < i <= W + K:
             tally["decode"] += n_dec
             tally["prefill"] += n_pre
             if i == W + K:
                 ev[1].record()
+                clk.__exit__(None, None, None)
 
     from kvstreams import _native as N
 
@@ -1153,6 +1156,7 @@ def rollout_bench(dev, args, rank: int, world: int = 1) -> dict:
         "engine_iterations": eng.last_iterations,
         "cuda_graphs": not args.rollout_eager,
         "device_policy": bool(args.rollout_device_policy),
+        "clocks": clk.summary(),
     }
     if args.rollout_full:
         out["compactions"] = sum(r.stats.compactions for r in rolls)
