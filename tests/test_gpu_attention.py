@@ -286,6 +286,7 @@ def test_prefill_then_decode_share_scratch_any_slot_order():
 @pytest.mark.parametrize("S,ctx,grid", [
     (40, (50, 900), 0),      # one CTA per SM, every range's block ids staged in shared memory
     (4, (8500, 9500), 1),    # one CTA over > 2048 groups: block ids read from the plan in global memory
+    (2, (40, 60), 0),        # fewer groups than CTAs: most stored ranges are empty
 ])
 def test_decode_plan_reuse_equals_recompute(S, ctx, grid):
     """The layers of a decode step with the batch plan stored by the first layer and read back
