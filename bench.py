@@ -1111,6 +1111,7 @@ def rollout_bench(dev, args, rank: int, world: int = 1) -> dict:
     ev = [torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
     tally = {"decode": 0, "prefill": 0}
     clk = ClockSampler(dev.index or 0)  # seconds of GEMM-heavy work: the power cap may lower the clock
+    host_t = [0.0, 0.0]  # host wall clock at the first and last timed iteration
 
     prof = args.rollout_profile_iter
 
@@ -1125,12 +1126,14 @@ def rollout_bench(dev, args, rank: int, world: int = 1) -> dict:
             torch.cuda.profiler.stop()
         if i == W:
             ev[0].record()
+            host_t[0] = time.perf_counter()
             clk.__enter__()
         elif W < i <= W + K:
             tally["decode"] += n_dec
             tally["prefill"] += n_pre
             if i == W + K:
                 ev[1].record()
+                host_t[1] = time.perf_counter()
                 clk.__exit__(None, None, None)
 
     from kvstreams import _native as N
@@ -1152,6 +1155,9 @@ def rollout_bench(dev, args, rank: int, world: int = 1) -> dict:
         "rollout_decode_tok_s_total": total_decode / (ms * 1e-3), "ranks": world,
         "prefill_tok_s_per_gpu": tally["prefill"] / (ms * 1e-3),
         "ms_per_iteration": ms / K,
+        # the engine loop never waits on the GPU: the host's time per iteration, against the
+        # device's, says whether the host kept the launch queue full
+        "host_ms_per_iteration": (host_t[1] - host_t[0]) * 1e3 / K,
         "library_launches": N.lib().kvs_launch_count() - launches0,
         "engine_iterations": eng.last_iterations,
         "cuda_graphs": not args.rollout_eager,
