@@ -68,7 +68,8 @@ constexpr int SMEM_TAB = TAB_CAP * 4;
 constexpr int SEQ_COST = 4;  // a stream's start + finish + merge, in blocks of streaming time (work split)
 constexpr int PLAN_HDR = 16;  // ints of the batch plan's header (16-token blocks)
 constexpr int PLAN_MAGIC = 0x6B76706C;  // header word 2 of a stored plan
-constexpr int SMEM_TOTAL = SMEM_STAGES + SMEM_Q + SMEM_NEW + SMEM_PREF + SMEM_TAB + 256;
+constexpr int SMEM_ROPE = 2 * (D / 2) * 4;  // sin and cos of the D/2 angles of a stream's position
+constexpr int SMEM_TOTAL = SMEM_STAGES + SMEM_Q + SMEM_NEW + SMEM_PREF + SMEM_TAB + 256 + SMEM_ROPE;
 static_assert(HQ * 8 == NTHREADS, "start(): one thread per (query head, 16-byte chunk)");
 
 struct DecodeParams {
@@ -163,7 +164,6 @@ __device__ __forceinline__ float warp_sum_rows(float v) {
 // never waits for them.
 struct SeqIn {
   uint4 q_lo, q_hi, k_lo, k_hi, v_c;
-  float4 f_lo, f_hi;
   int64_t pos;
   int32_t blk, off;
   bool owner;
@@ -183,6 +183,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
   int* s_tab = s_pref + MAX_SEQS + 1;
   int* s_flag = s_tab + TAB_CAP;
   int* s_scan = s_flag + 4;  // 33 ints
+  float* s_sin = reinterpret_cast<float*>(smem + SMEM_STAGES + SMEM_Q + SMEM_NEW + SMEM_PREF + SMEM_TAB + 256);
+  float* s_cos = s_sin + D / 2;
 
   // Launched with programmatic stream serialization: the grid may become resident while the
   // previous kernel of the stream (the q|k|v projection, or the previous layer's decode) is
@@ -192,6 +194,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
   const int g = lane >> 2, t = lane & 3;
   const kvs_cache& c = p.c;
   const int S = p.num_seqs;
+  const float my_freq = tid < D / 2 ? p.inv_freq[tid] : 0.f;  // inv_freq[tid]: the angle table's row
 
   // The batch plan of a decode step (16-token blocks): per-sequence prefix sums of the
   // groups, each CTA's group range and the block ids of every group, the same for all layers
@@ -305,8 +308,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
     const uint4* qsrc = reinterpret_cast<const uint4*>(p.q + (int64_t)i * p.q_stride + h * D + d0);
     s.q_lo = qsrc[0];
     s.q_hi = qsrc[D / 16];
-    s.f_lo = *reinterpret_cast<const float4*>(p.inv_freq + d0);
-    s.f_hi = *reinterpret_cast<const float4*>(p.inv_freq + d0 + 4);
     s.k_lo = s.k_hi = s.v_c = make_uint4(0, 0, 0, 0);
     s.blk = s.off = 0;
     if (s.owner) {
@@ -551,13 +552,17 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
   auto apply_seq = [&](const SeqIn& in) {
     const int h = tid >> 3, d0 = (tid & 7) * 8;
     const int64_t pos = in.pos, row = ((layer_rows + in.blk) * BSZ + in.off) * HKV;
-    const float fr[8] = {in.f_lo.x, in.f_lo.y, in.f_lo.z, in.f_lo.w, in.f_hi.x, in.f_hi.y, in.f_hi.z, in.f_hi.w};
+    // the D/2 angles of this position, once per stream (every head of q and of the new k
+    // rotates by the same ones): one sincos per thread of the first D/2 instead of eight each
+    if (tid < D / 2) rope_sincos<float, float>(pos, my_freq, s_sin[tid], s_cos[tid]);
+    __syncthreads();
     // words w of lo / hi hold elements (d0 + 2w, d0 + 2w + 1) and (d0 + D/2 + 2w, ...)
     auto rot2 = [&](uint32_t lo, uint32_t hi, int w, uint32_t& out_lo, uint32_t& out_hi) {
       const float2 a = unpack_bf16(lo), b = unpack_bf16(hi);
       float r0, r1, r2, r3;
-      rope_rotate<float, float>(a.x, b.x, pos, fr[2 * w], r0, r1);
-      rope_rotate<float, float>(a.y, b.y, pos, fr[2 * w + 1], r2, r3);
+      const int f = d0 + 2 * w;
+      rope_apply(a.x, b.x, s_sin[f], s_cos[f], r0, r1);
+      rope_apply(a.y, b.y, s_sin[f + 1], s_cos[f + 1], r2, r3);
       out_lo = pack_bf16(r0, r2);
       out_hi = pack_bf16(r1, r3);
     };
