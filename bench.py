@@ -621,6 +621,7 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
         del hq, hk, hv, hout
         detail = compaction_bench(dev, args, rank)
         detail["decode_bs1"] = decode_bs1_bench(dev, args, rank)
+        detail["decode_short"] = decode_short_bench(dev, args, rank)
         detail["replay_attention"] = replay_bench(dev, args, rank)
         detail["replay_backward"] = replay_backward_bench(dev, args, rank)
         detail["compaction_policy"] = compaction_policy_bench(dev, args, rank)
@@ -701,6 +702,8 @@ def flat_secondary(d: dict) -> dict:
         out[key] = float(f"{v:.4g}") if isinstance(v, float) else v
 
     put("bs1_decode_hbm", "decode_bs1", "hbm_frac")
+    put("rollout_ctx_decode_hbm", "decode_short", "hbm_frac")
+    put("rollout_ctx_decode_us", "decode_short", "us_per_layer")
     put("prefill_tc", "prefill", "tc_frac")
     put("replay_tc", "replay_attention", "tc_frac")
     put("replay_bwd_tc", "replay_backward", "tc_frac")
