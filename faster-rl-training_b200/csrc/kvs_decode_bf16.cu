@@ -17,10 +17,11 @@
 //
 // Work split ("stream-K"): the groups of all sequences, concatenated in batch order,
 // are cut into gridDim.x contiguous ranges of equal cost, one per CTA (one CTA per SM):
-// a group costs one unit and each sequence two more (its start and finish), so every SM
-// streams about the same number of KV bytes whatever the context lengths.  A
-// sequence cut by range boundaries yields one partial (m, l, O) per CTA; the last
-// CTA to finish a sequence (per-sequence arrival counter) merges its partials.
+// a group costs one unit and each sequence SEQ_COST = 4 more (its start, finish and
+// merge of partials), so every SM streams about the same number of KV bytes whatever
+// the context lengths.  A sequence cut by range boundaries yields one partial
+// (m, l, O) per CTA; the last CTA to finish a sequence (per-sequence arrival
+// counter) merges its partials.
 //
 // Per CTA: 8 warps, warp w <-> KV head w (4 query heads).  A 3-stage cp.async
 // pipeline stages whole 16-token groups (K and V of all heads, 64 KiB) in shared
