@@ -68,10 +68,12 @@ constexpr int SMEM_PREF = (MAX_SEQS + 1) * 4;
 constexpr int SMEM_TAB = TAB_CAP * 4;
 constexpr int SEQ_COST = 4;  // a stream's start + finish + merge, in blocks of streaming time (work split)
 constexpr int PLAN_HDR = 16;  // ints of the batch plan's header (16-token blocks)
+constexpr int PLAN_REC = 8;   // ints of a CTA's start record: g0, g1, block ids of groups g0, g0 + 1
 constexpr int PLAN_MAGIC = 0x6B76706C;  // header word 2 of a stored plan
 constexpr int SMEM_ROPE = 2 * (D / 2) * 4;  // sin and cos of the D/2 angles of a stream's position
 constexpr int SMEM_TOTAL = SMEM_STAGES + SMEM_Q + SMEM_NEW + SMEM_PREF + SMEM_TAB + 256 + SMEM_ROPE;
 static_assert(HQ * 8 == NTHREADS, "start(): one thread per (query head, 16-byte chunk)");
+static_assert(STAGES == 3, "a start record holds the block ids of the prologue's two stages");
 
 struct DecodeParams {
   kvs_cache c;
@@ -197,22 +199,41 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
   const int S = p.num_seqs;
   const float my_freq = tid < D / 2 ? p.inv_freq[tid] : 0.f;  // inv_freq[tid]: the angle table's row
 
-  // The batch plan of a decode step (16-token blocks): per-sequence prefix sums of the
-  // groups, each CTA's group range and the block ids of every group, the same for all layers
-  // of the step.  A launch in KVS_PLAN_BUILD mode computes them as below and stores them; one
-  // in KVS_PLAN_REUSE mode reads them back in two rounds of independent loads instead of the
-  // scan's and the table gather's dependent ones (it computes them if the stored plan is for
-  // another batch size or grid).
-  int32_t* const plan_pref = p.plan ? p.plan + PLAN_HDR : nullptr;
-  int32_t* const plan_range = p.plan ? plan_pref + S + 1 : nullptr;
-  int32_t* const plan_tab = p.plan ? plan_range + 2 * gridDim.x : nullptr;
+  const uint8_t* Kpool = static_cast<const uint8_t*>(c.k);
+  const uint8_t* Vpool = static_cast<const uint8_t*>(c.v);
+  const int64_t layer_rows = (int64_t)p.layer * c.num_blocks;
+  // K and V of one 16-token block (all heads) into pipeline stage st, 16-byte copies into the
+  // swizzled rows
+  auto issue_blk = [&](int64_t blk, int st) {
+    const uint32_t kd = smem_u32(stages + st * STAGE_BYTES);
+    const uint32_t vd = kd + KV_BLOCK_BYTES;
+    const uint8_t* ks = Kpool + (layer_rows + blk) * KV_BLOCK_BYTES;
+    const uint8_t* vs = Vpool + (layer_rows + blk) * KV_BLOCK_BYTES;
+#pragma unroll
+    for (int k = 0; k < CHUNKS / NTHREADS; ++k) {
+      const int q = tid + k * NTHREADS;
+      const int r = q >> 4, ch = q & 15;
+      cp_async16(kd + swz(r, ch), ks + (q << 4));
+      cp_async16(vd + swz(r, ch), vs + (q << 4));
+    }
+  };
+
+  // The batch plan of a decode step (16-token blocks): each CTA's start record (its group
+  // range and the block ids of its first two groups), per-sequence prefix sums of the groups
+  // and the block ids of every group, the same for all layers of the step.  A launch in
+  // KVS_PLAN_BUILD mode computes them as below and stores them; one in KVS_PLAN_REUSE mode
+  // reads the record and the prefix sums in one round of independent loads, issues the copies
+  // of its first two blocks at once and gathers the other block ids while they fly (it computes
+  // everything if the stored plan is for another batch size or grid).
+  int32_t* const plan_rec = p.plan ? p.plan + PLAN_HDR : nullptr;
+  int32_t* const plan_pref = p.plan ? plan_rec + PLAN_REC * gridDim.x : nullptr;
+  int32_t* const plan_tab = p.plan ? plan_pref + S + 1 : nullptr;
   const bool build = BSZ == BS && p.plan && p.plan_mode == KVS_PLAN_BUILD;
   bool reuse = false;
   int pg0 = 0, pg1 = 0;
   if (BSZ == BS && p.plan && p.plan_mode == KVS_PLAN_REUSE) {
     const int hs = p.plan[0], hg = p.plan[1], hm = p.plan[2];
-    pg0 = plan_range[2 * blockIdx.x];
-    pg1 = plan_range[2 * blockIdx.x + 1];
+    const int4 rec = *reinterpret_cast<const int4*>(plan_rec + PLAN_REC * blockIdx.x);
     int pv[5];
 #pragma unroll
     for (int k = 0; k < 5; ++k) {
@@ -221,6 +242,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
     }
     reuse = hs == S && hg == (int)gridDim.x && hm == PLAN_MAGIC;  // the same loads in every thread
     if (reuse) {
+      pg0 = rec.x;
+      pg1 = rec.y;
+      // the pipeline's first two stages, as the prologue below would issue them
+      if (pg0 < pg1) issue_blk(rec.z, 0);
+      cp_async_commit();
+      if (pg0 + 1 < pg1) issue_blk(rec.w, 1);
+      cp_async_commit();
 #pragma unroll
       for (int k = 0; k < 5; ++k) {
         const int i = tid + k * NTHREADS;
@@ -270,8 +298,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
   const int g1 = reuse ? pg1 : first_block(blockIdx.x * RU + RU);
   if (build) {
     if (tid == 0) {
-      plan_range[2 * blockIdx.x] = g0;
-      plan_range[2 * blockIdx.x + 1] = g1;
+      plan_rec[PLAN_REC * blockIdx.x] = g0;
+      plan_rec[PLAN_REC * blockIdx.x + 1] = g1;
     }
     if (blockIdx.x == 0) {
       for (int i = tid; i <= S; i += NTHREADS) plan_pref[i] = s_pref[i];
@@ -283,10 +311,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
     }
   }
   if (g0 >= g1) return;
-
-  const uint8_t* Kpool = static_cast<const uint8_t*>(c.k);
-  const uint8_t* Vpool = static_cast<const uint8_t*>(c.v);
-  const int64_t layer_rows = (int64_t)p.layer * c.num_blocks;
 
   auto seq_of = [&](int gb) {
     int lo = 0, hi = S - 1;  // last i with s_pref[i] <= gb
@@ -354,7 +378,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
       } else {
         const int i = seq_of(gb);
         blk = c.tables[(int64_t)p.seq_slots[i] * c.max_blocks + (gb - s_pref[i])];
-        if (build) plan_tab[gb] = blk;
+        if (build) {
+          plan_tab[gb] = blk;
+          if (gb - g0 < 2) plan_rec[PLAN_REC * blockIdx.x + 2 + (gb - g0)] = blk;
+        }
       }
       s_tab[gb - g0] = blk;
     }
@@ -362,14 +389,16 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
   } else if (build) {
     for (int gb = g0 + tid; gb < g1; gb += NTHREADS) {
       const int i = seq_of(gb);
-      plan_tab[gb] = c.tables[(int64_t)p.seq_slots[i] * c.max_blocks + (gb - s_pref[i])];
+      const int blk = c.tables[(int64_t)p.seq_slots[i] * c.max_blocks + (gb - s_pref[i])];
+      plan_tab[gb] = blk;
+      if (gb - g0 < 2) plan_rec[PLAN_REC * blockIdx.x + 2 + (gb - g0)] = blk;
     }
   }
 
   auto issue = [&](int gb, int st) {
-    const uint32_t kd = smem_u32(stages + st * STAGE_BYTES);
-    const uint32_t vd = kd + KV_BLOCK_BYTES;
     if constexpr (BSZ == 1) {
+      const uint32_t kd = smem_u32(stages + st * STAGE_BYTES);
+      const uint32_t vd = kd + KV_BLOCK_BYTES;
       // chunk q = tid + k NTHREADS is 16-byte chunk (q & 127) of token q >> 7 (row q >> 4)
       const int* ent = s_tab + (gb - w0) * BS;
 #pragma unroll
@@ -391,23 +420,17 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
         const int i = seq_of(gb);
         blk = c.tables[(int64_t)p.seq_slots[i] * c.max_blocks + (gb - s_pref[i])];
       }
-      const uint8_t* ks = Kpool + (layer_rows + blk) * KV_BLOCK_BYTES;
-      const uint8_t* vs = Vpool + (layer_rows + blk) * KV_BLOCK_BYTES;
-#pragma unroll
-      for (int k = 0; k < CHUNKS / NTHREADS; ++k) {
-        const int q = tid + k * NTHREADS;
-        const int r = q >> 4, ch = q & 15;
-        cp_async16(kd + swz(r, ch), ks + (q << 4));
-        cp_async16(vd + swz(r, ch), vs + (q << 4));
-      }
+      issue_blk(blk, st);
     }
   };
 
-  // prologue
+  // prologue (a reusing launch issued it from its start record)
+  if (!reuse) {
 #pragma unroll
-  for (int k = 0; k < STAGES - 1; ++k) {
-    if (g0 + k < g1) issue(g0 + k, k);
-    cp_async_commit();
+    for (int k = 0; k < STAGES - 1; ++k) {
+      if (g0 + k < g1) issue(g0 + k, k);
+      cp_async_commit();
+    }
   }
 
   // per-warp state of the current segment (one sequence inside this CTA's range)
@@ -757,11 +780,12 @@ bool g_attr_done[2][64] = {};  // [block_size == 1][device]
 constexpr size_t COUNTER_BYTES = (size_t)MAX_SEQS * 4;
 static_assert(COUNTER_BYTES % 256 == 0, "partials stay 256-byte aligned");
 
-// the batch plan: header, num_seqs + 1 prefix sums, 2 ints per CTA, one block id per group
-// (at most max_blocks per sequence); 16-token blocks only
+// the batch plan: header, a start record per CTA (8 ints, 16-byte aligned), num_seqs + 1
+// prefix sums, one block id per group (at most max_blocks per sequence); 16-token blocks only
 static size_t plan_bytes(const kvs_cache* c, int num_seqs, int grid) {
   if (c->block_size != BS) return 0;
-  return align_up(((size_t)PLAN_HDR + num_seqs + 1 + 2 * (size_t)grid + (size_t)num_seqs * c->max_blocks) * 4, 256);
+  return align_up(((size_t)PLAN_HDR + PLAN_REC * (size_t)grid + num_seqs + 1 + (size_t)num_seqs * c->max_blocks) * 4,
+                  256);
 }
 static size_t partial_bytes(int num_seqs, int grid) {
   const size_t slots = (size_t)grid + num_seqs;
