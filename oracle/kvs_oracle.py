@@ -3,7 +3,7 @@
 A plain numpy / Python restatement of the reference algorithms
 (thanhauco/faster-RL-training, package kvstreams 0.2.0).  Only the tests,
 ``__graft_entry__.smoke()`` and the CPU-baseline leg of ``bench.py`` may import
-this module, and only as the checker (or the timed CPU baseline); the product
+this module, and only as the expected result (or the timed CPU baseline); the product
 (the ``kvstreams`` package and libkvs_b200.so) never calls it.
 
 Pinned against golden vectors produced by running the reference itself
