@@ -217,9 +217,22 @@ def decode_bs1_bench(dev, args, rank: int) -> dict:
     gbs = alg / (ms * 1e-3) / 1e9
     peaks = _peaks()
     del cache, q, k, v, out
-    torch.cuda.empty_cache()
+    _release_device_memory()
     return {"ms": ms, "gbs": gbs, "hbm_frac": gbs / peaks["hbm_gbs"], "kv_bytes": int(alg),
             "decode_tok_s": S / (ms * 1e-3), "fused_kernel": path == [1]}
+
+
+def _release_device_memory() -> None:
+    """Return the freed blocks of the legs before to the device.  A leg's engine, CUDA graphs and
+    model can sit in reference cycles that only Python's cycle collector frees; without a
+    collection here, whether a rank still held the previous leg's tens of GB when the next leg
+    allocated depended on when each rank's collector last ran."""
+    import gc
+
+    import torch
+
+    gc.collect()
+    torch.cuda.empty_cache()
 
 
 def decode_short_bench(dev, args, rank: int) -> dict:
@@ -277,7 +290,7 @@ def decode_short_bench(dev, args, rank: int) -> dict:
     gbs = alg / (ms * 1e-3) / 1e9
     peaks = _peaks()
     del cache, q, k, v, out
-    torch.cuda.empty_cache()
+    _release_device_memory()
     return {"workload": f"{S} streams, ctx U[{ctx[0]},{ctx[1]}] (mean {st.lengths.mean():.0f}), {layers} layers per "
                         "step, bs16", "us_per_layer": ms * 1e3, "gbs": gbs, "hbm_frac": gbs / peaks["hbm_gbs"],
             "us_per_layer_without_plan": ms_noplan * 1e3, "kv_bytes_per_layer": int(alg),
@@ -954,11 +967,11 @@ def lm_head_logprobs_bench(dev, args, rank: int) -> dict:
                     "epilogue_kernel_tc_frac": tf / peaks["bf16_tflops"],
                     "epilogue_kernel_max_abs_diff": float((ops.lm_head_logprobs(h, w, tgt, temp)[0]
                                                            - fused_fwd()).abs().max())})
-    torch.cuda.empty_cache()
+    _release_device_memory()
     torch.cuda.reset_peak_memory_stats(dev)
     out["torch_fwd_bwd_ms"] = ev_time(torch_fb, reps=2)
     out["torch_fwd_bwd_peak_gb"] = torch.cuda.max_memory_allocated(dev) / 1e9
-    torch.cuda.empty_cache()
+    _release_device_memory()
     torch.cuda.reset_peak_memory_stats(dev)
     out["fused_fwd_bwd_ms"] = ev_time(fused_fb, reps=2)
     out["fused_fwd_bwd_peak_gb"] = torch.cuda.max_memory_allocated(dev) / 1e9
@@ -966,7 +979,7 @@ def lm_head_logprobs_bench(dev, args, rank: int) -> dict:
     a, b = torch_fwd(), fused_fwd()
     out["max_abs_diff_vs_torch"] = float((a - b).abs().max())
     del w, h
-    torch.cuda.empty_cache()
+    _release_device_memory()
     # the rollout's next-token step for 64 rollouts (engine/base.py:180-193): torch's
     # log_softmax + exp + multinomial + gather against one kvs_sample launch
     rows = 64
@@ -1079,7 +1092,7 @@ def rollout_bench(dev, args, rank: int, world: int = 1) -> dict:
     from kvstreams.model import TinyLM
     from kvstreams.paged_cache import PagedKVCache
 
-    torch.cuda.empty_cache()
+    _release_device_memory()
     n, budget, turns = args.rollout_streams, 8192, 24
     cfg = ModelConfig(vocab_size=128256, d_model=4096, n_layers=args.rollout_layers, n_heads=32, n_kv_heads=8,
                       d_ff=14336, rope_theta=5e5)
@@ -1173,7 +1186,7 @@ def rollout_bench(dev, args, rank: int, world: int = 1) -> dict:
         out["decode_tokens_total"] = sum(r.stats.decode_tokens for r in rolls)
         out["rollout_decode_tok_s_per_gpu_whole_episode"] = out["decode_tokens_total"] / eng.last_wall
     del model, cache, eng, rolls
-    torch.cuda.empty_cache()
+    _release_device_memory()
     return out
 
 
@@ -1230,7 +1243,7 @@ def prefill_bench(dev, args, rank: int) -> dict:
     tf = float(np.mean(flops_all)) / (ms * 1e-3) / 1e12
     peaks = _peaks()
     del cache, q, kn, vn
-    torch.cuda.empty_cache()
+    _release_device_memory()
     return {"workload": f"{n} sequences x chunk U[64,512] ({N} new tokens) onto contexts U[1024,8192], 32q/8kv D128 "
                         "bs16 bf16, one layer", "ms": ms, "tflops": tf, "tc_frac": tf / peaks["bf16_tflops"],
             "peak_src": peaks["src"], "prefill_tok_s": N / (ms * 1e-3),
@@ -1254,7 +1267,7 @@ def replay_train_bench(dev, args, rank: int) -> dict:
     from kvstreams.training.replay import Batch
     from kvstreams.workloads import replay_evicted_at, visible_pairs
 
-    torch.cuda.empty_cache()
+    _release_device_memory()
     B, T = 1, args.replay_train_t
     cfg = ModelConfig(vocab_size=128256, d_model=4096, n_layers=args.rollout_layers, n_heads=32, n_kv_heads=8,
                       d_ff=14336, rope_theta=5e5)
@@ -1296,7 +1309,7 @@ def replay_train_bench(dev, args, rank: int) -> dict:
     tf = flops / (ms * 1e-3) / 1e12
     peak_gb = torch.cuda.max_memory_allocated(dev) / 1e9
     del model, batch, tokens, adv
-    torch.cuda.empty_cache()
+    _release_device_memory()
     return {"workload": f"B={B} T={T}, Llama-3-8B arch ({cfg.n_layers} layers) bf16 random init, 3-8 keep-recent "
                         "events: forward + backward of sum(advantage * token_logprobs)",
             "ms": ms, "train_tok_s_per_gpu": B * T / (ms * 1e-3), "model_tflops": tf,
@@ -1320,7 +1333,7 @@ def replay_model_bench(dev, args, rank: int) -> dict:
     from kvstreams.workloads import replay_evicted_at
     from kvstreams.distributed import reduce_max
 
-    torch.cuda.empty_cache()
+    _release_device_memory()
     B, T = args.replay_model_b, args.replay_model_t
     cfg = ModelConfig(vocab_size=128256, d_model=4096, n_layers=args.rollout_layers, n_heads=32, n_kv_heads=8,
                       d_ff=14336, rope_theta=5e5)
@@ -1350,7 +1363,7 @@ def replay_model_bench(dev, args, rank: int) -> dict:
     ms = reduce_max(e0.elapsed_time(e1), dev)
     finite = bool(torch.isfinite(lp).all())
     del model, lp, batch, tokens
-    torch.cuda.empty_cache()
+    _release_device_memory()
     return {"workload": f"B={B} T={T}, Llama-3-8B arch ({cfg.n_layers} layers) bf16 random init, 3-8 keep-recent "
                         f"events/stream: token_logprobs (masked forward + lm_head + log-softmax + gather)",
             "ms": ms, "replay_tok_s_per_gpu": B * T / (ms * 1e-3), "logprobs_finite": finite}
