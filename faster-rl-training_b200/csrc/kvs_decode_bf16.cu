@@ -104,6 +104,15 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src));
 }
+// An arrival on a stream's counter with acquire-release semantics at GPU scope: this thread's
+// (and, through the barrier before it, its CTA's) partial writes are visible to whoever
+// observes the count, and the partials of earlier arrivals are visible to this CTA after the
+// barrier that follows (the same ordering as a full fence on each side, without its cost).
+__device__ __forceinline__ int arrive_acq_rel(int32_t* counter) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;\n" : "=r"(old) : "l"(counter) : "memory");
+  return old;
+}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
 // 16-byte copy that reads `src_bytes` (16 or 0) bytes and zero-fills the rest
 __device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const void* src, int src_bytes) {
@@ -497,13 +506,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
     } else {
       e_seq = i;
       // a stream this CTA leaves mid-range (its first one): arrive now, with every thread's
-      // partial writes ordered before the arrival by the barrier and thread 0's fence; the
-      // value returned is only read at the end of the kernel, so nothing waits for it here
+      // partial writes ordered before the arrival by the barrier and the release; the value
+      // returned is only read at the end of the kernel, so nothing waits for it here
       __syncthreads();
-      if (tid == 0) {
-        __threadfence();
-        arrived0 = atomicAdd(&p.counters[i], 1);
-      }
+      if (tid == 0) arrived0 = arrive_acq_rel(&p.counters[i]);
     }
   };
   // the last CTA to arrive for sequence i combines the partials of its `expected` CTAs
@@ -756,13 +762,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_bf16_kernel(const DecodePa
       int c0;
       s_flag[0] = e_seq >= 0 && arrived0 == seq_ctas(e_seq, c0) - 1;
       s_flag[1] = 0;
-      if (t_seq >= 0) {
-        __threadfence();
-        s_flag[1] = atomicAdd(&p.counters[t_seq], 1) == seq_ctas(t_seq, c0) - 1;
-      }
+      if (t_seq >= 0) s_flag[1] = arrive_acq_rel(&p.counters[t_seq]) == seq_ctas(t_seq, c0) - 1;
     }
     __syncthreads();
-    if (s_flag[0] | s_flag[1]) __threadfence();
     if (s_flag[0]) merge(e_seq);
     if (s_flag[1]) merge(t_seq);
   }
